@@ -1,0 +1,392 @@
+#!/usr/bin/env python3
+"""Benchmark: quantized MoE decode layer, microseconds per layer per token, on 1..8 B200s.
+
+One step = one FP8 MoE layer (the stack's layers 0-19) followed by one FP4 MoE layer (layers
+20-39), each on B fresh bf16 tokens: router (fp32 logits, top-6 of 384, sigmoid, bias, x2.5),
+6 routed experts + 1 FP8 shared expert (H 5120, I 2048, SwiGLU), routing-weighted combine, and at
+N > 1 the fp32 all-reduce of the tensor-parallel partials (each GPU holds I/N rows of every
+expert). With equal FP8 and FP4 layer counts, the mean over the two is the 40-layer stack's mean
+per-layer time. Weights are seeded synthetic N(0, 0.02), generated and resident in HBM.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+
+Prints one JSON line (rank 0). ``value`` is device time (CUDA events on the launching stream,
+L2 flushed between steps, max over ranks); ``e2e`` is the same metric through the public API
+with the step's tokens copied from pinned host memory and its outputs read back every step.
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "tenstorrent-wormhole-deepseek-v41-flash_b200")
+for _p in (ROOT, PKG_DIR):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "FP8/FP4 MoE layer us/token + HBM GB/s vs 8 TB/s peak at 1/2/4/8 B200"
+UNIT = "us/layer/token"
+H, I, E, TOPK = 5120, 2048, 384, 6
+ROUTE_SCALE = 2.5
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+
+# algorithmic bytes (weights + scales) per expert and per router (fp32 weight + bias)
+ROUTER_BYTES = E * H * 4 + E * 4
+FP8_W13 = 2 * (H * I + (I // 128) * (H // 128) * 4)
+FP8_W2 = H * I + (H // 128) * (I // 128) * 4
+FP4_W13 = 2 * (H * I // 2 + H * I // 32)
+FP4_W2 = H * I // 2 + H * I // 32
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=2024)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline sampling")
+    return ap.parse_args()
+
+
+def workload_config(args, world):
+    return {"workload": "one FP8 + one FP4 MoE decode layer per step (experts resident, TP over GPUs)",
+            "hidden": H, "inter": I, "experts": E, "topk": TOPK, "shared_experts": 1, "batch": args.batch,
+            "score_func": "sigmoid", "route_scale": ROUTE_SCALE, "layers_per_step": ["fp8-block128", "fp4-e2m1-e8m0"],
+            "parallelism": f"tp{world}", "l2": "flushed between steps (256 MiB write, outside the timed events)"}
+
+
+# ------------------------------------------------------------------ reference arm (CPU)
+
+def cpu_layers_setup(seed, pool=6):
+    """Router at full size; the chosen experts' weights come from a pool of ``pool`` experts per
+    format (expert e -> pool[e % pool]); the arithmetic per step is the full layer's."""
+    import torch
+    from dsmoe import synth
+    gen = torch.Generator().manual_seed(seed)
+    layers = []
+    for fmt in ("fp8", "fp4"):
+        rw = synth.make_router(E, H, gen)
+        experts = [synth.make_expert(fmt, H, I, gen) for _ in range(pool)]
+        shared = synth.make_expert("fp8", H, I, gen)
+        layers.append((rw, experts, shared))
+    toks = synth.make_tokens(64, H, gen)
+    return layers, toks
+
+
+def run_cpu(args, steps, warmup, budget_s=None):
+    import torch
+    from oracle import cpu_baseline as CB
+    cores = CB.use_all_cores()
+    layers, toks = cpu_layers_setup(args.seed)
+    B = args.batch
+
+    def step(i):
+        for li, (rw, experts, shared) in enumerate(layers):
+            j = (2 * i + li) % (64 - B + 1)
+            CB.layer(toks[j:j + B], rw.wg, rw.bias, lambda e, ex=experts: ex[e % len(ex)], shared, TOPK, ROUTE_SCALE)
+
+    with torch.inference_mode():
+        sec, n = CB.time_steps(step, steps, warmup, min_steps=1, budget_s=budget_s)
+    us = sec * 1e6 / (2 * B)
+    from oracle import ref_fp4lib
+    sample = (f"{n} steps of {{FP8 layer + FP4 layer}} at batch {B}, torch CPU fp32 (kernel.py fp8_gemm/fp4_gemm "
+              f"math, weights re-dequantized per call), FP4 unpack via "
+              f"{'the reference fp4lib.c (oracle/_ref)' if ref_fp4lib.available() else 'the torch LUT'}; "
+              f"{CB.cpu_model()}")
+    return {"value": round(us, 2), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
+            "ms_per_step": round(sec * 1e3, 3), "steps": n}
+
+
+def reference_arm(args):
+    rank, _, world = int(os.environ.get("RANK", 0)), 0, int(os.environ.get("WORLD_SIZE", 1))
+    if rank != 0:
+        return
+    cb = run_cpu(args, args.steps, args.warmup)
+    line = {"metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": cb["steps"],
+            "warmup": args.warmup, "ms_per_step": cb["ms_per_step"], "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args, world), "impl": "reference",
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU arm
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the timed region runs."""
+    Q = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid):
+        self.uuid, self.proc, self.path = uuid, None, None
+
+    def __enter__(self):
+        import tempfile
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                f = [c.strip() for c in line.split(",")]
+                if len(f) >= 10 and (self.uuid is None or f[1] == self.uuid):
+                    rows.append(f)
+            os.unlink(self.path)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[6:10]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][3]) if rows[0][3].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ours(args):
+    import torch
+    import torch.distributed as dist
+    import dsmoe
+    from dsmoe import _lib as L
+    from dsmoe.tp import env_rank_world, max_over_ranks
+
+    rank, local, world = env_rank_world()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    B = args.batch
+    if not 1 <= B <= L.MAX_DECODE_TOKENS:
+        raise SystemExit(f"--batch must be in 1..{L.MAX_DECODE_TOKENS}")
+
+    # ---- resident layers (same seed on every rank: rank r packs its slice)
+    t_setup = time.time()
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    layers = []
+    for fmt in ("fp8", "fp4"):
+        m = dsmoe.MoE(H, I, E, TOPK, fmt, "sigmoid", ROUTE_SCALE, rank=rank, world=world, device=dev, max_tokens=B)
+        m.load_router(dsmoe.make_router(E, H, gen, device=dev))
+        m.load_shared(dsmoe.make_expert("fp8", H, I, gen, device=dev))
+        for e in range(E):
+            m.load_expert(e, dsmoe.make_expert(fmt, H, I, gen, device=dev))
+        layers.append(m)
+    pool = 256
+    toks = dsmoe.make_tokens(pool + B, H, gen, device=dev)
+    torch.cuda.synchronize()
+    setup_s = time.time() - t_setup
+
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    K, W = args.steps, args.warmup
+    n_layers = len(layers)
+    stream = torch.cuda.current_stream(dev)
+    st = stream.cuda_stream
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_layers)] for _ in range(K + W)]
+    ev_end = [[torch.cuda.Event(enable_timing=True) for _ in range(n_layers)] for _ in range(K + W)]
+    for row in ev:                      # materialize the CUDA events before handing them to the library
+        for evs in row:
+            for e_ in evs:
+                e_.record(stream)
+    torch.cuda.synchronize()
+    idx_log = torch.zeros((K + W, n_layers, B, TOPK), dtype=torch.int64, device=dev)
+    part = [torch.empty((B, H), dtype=torch.float32, device=dev) for _ in range(n_layers)]
+    yout = [torch.empty((B, H), dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
+    launches_per_layer = 5 + (1 if world > 1 else 0)
+
+    def layer_step(s, li, m):
+        x = toks[(s * n_layers + li) * 7 % pool:][:B]
+        evp = (ctypes.c_void_p * 4)(*[e_.cuda_event for e_ in ev[s][li]])
+        y_t, y_dt = (part[li], L.DTYPE_F32) if world > 1 else (yout[li], L.DTYPE_BF16)
+        L.call("dsmoe_moe_decode_profiled", m._layer, L.ptr(x), B, None, L.ptr(y_t), y_dt,
+               L.ptr(idx_log[s, li]), None, None, L.ptr(m.workspace), m.workspace.numel(), st, evp)
+        if world > 1:
+            dist.all_reduce(part[li])
+            L.call("dsmoe_f32_to_bf16", L.ptr(part[li]), L.ptr(yout[li]), part[li].numel(), st)
+        ev_end[s][li].record(stream)
+
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    except Exception:
+        pass
+
+    if world > 1:
+        dist.barrier()
+    for s in range(W):
+        for li, m in enumerate(layers):
+            layer_step(s, li, m)
+        flush.zero_()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(uuid) as clk:
+        for s in range(W, W + K):
+            for li, m in enumerate(layers):
+                layer_step(s, li, m)
+            flush.zero_()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    # ---- per-step and per-kernel device times
+    step_ms, stage = [], {(li, k): [] for li in range(n_layers) for k in ("router", "w13", "w2", "allreduce")}
+    for s in range(W, W + K):
+        step_ms.append(ev[s][0][0].elapsed_time(ev_end[s][n_layers - 1]))
+        for li in range(n_layers):
+            e4 = ev[s][li]
+            stage[(li, "router")].append(e4[0].elapsed_time(e4[1]))
+            stage[(li, "w13")].append(e4[1].elapsed_time(e4[2]))
+            stage[(li, "w2")].append(e4[2].elapsed_time(e4[3]))
+            stage[(li, "allreduce")].append(e4[3].elapsed_time(ev_end[s][li]))
+    ms_per_step = max_over_ranks(sum(step_ms) / K, dev)
+    value = ms_per_step * 1e3 / (n_layers * B)
+
+    # unique experts per step -> algorithmic bytes
+    uniq = [[len(set(idx_log[s, li].flatten().tolist())) for li in range(n_layers)] for s in range(W, W + K)]
+    names = ["fp8", "fp4"]
+    w13_b = {"fp8": FP8_W13, "fp4": FP4_W13}
+    w2_b = {"fp8": FP8_W2, "fp4": FP4_W2}
+    kern = {}
+    for li, nm in enumerate(names):
+        u = statistics.mean(uq[li] for uq in uniq)
+        b13 = (u * w13_b[nm] + FP8_W13) / world
+        b2 = (u * w2_b[nm] + FP8_W2) / world
+        for k, byts in (("router", ROUTER_BYTES), ("w13", b13), ("w2", b2), ("allreduce", 0)):
+            t = statistics.mean(stage[(li, k)])
+            kern[f"{nm}_{k}"] = {"us": round(t * 1e3, 2), "bytes": int(byts),
+                                 "gbs": round(byts / (t * 1e-3) / 1e9, 1) if byts and t > 0 else None}
+    tot_us = sum(v["us"] for v in kern.values())
+    for v in kern.values():
+        v["share"] = round(v["us"] / tot_us, 3) if tot_us else None
+    step_bytes = sum(v["bytes"] for v in kern.values())
+    dom_name = max((k for k in kern if kern[k]["bytes"]), key=lambda k: kern[k]["us"])
+    dom = kern[dom_name]
+    peak, peak_kind = measured_peak()
+    achieved = dom["gbs"]
+    traffic = read_traffic(dom_name, B, world)
+
+    # ---- e2e through the public API (pinned host tokens in, outputs read back every step)
+    xh = torch.empty((pool + B, H), dtype=torch.bfloat16).pin_memory()
+    xh.copy_(toks.cpu())
+    yh = [torch.empty((B, H), dtype=torch.bfloat16).pin_memory() for _ in range(n_layers)]
+    xd = [torch.empty((B, H), dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
+
+    def e2e_step(s):
+        for li, m in enumerate(layers):
+            j = (s * n_layers + li) * 7 % pool
+            xd[li].copy_(xh[j:j + B], non_blocking=True)
+            yh[li].copy_(m.forward(xd[li]), non_blocking=True)
+        torch.cuda.synchronize()
+
+    for s in range(W):
+        e2e_step(s)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for s in range(K):
+        e2e_step(W + s)
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / K, dev)
+    e2e_val = e2e_ms * 1e3 / (n_layers * B)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = run_cpu(args, steps=1000, warmup=1, budget_s=args.cpu_budget)
+        cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    clocks = clk.summary()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": round(ms_per_step, 5), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "e4m3/e2m1 weights x f16 tokens -> f32 (tensor cores)",
+            "data": "synthetic (seeded N(0,0.02) weights quantized per the config, N(0,1) bf16 tokens)",
+            "config": workload_config(args, world),
+            "hbm_gbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9, 1),
+            "hbm_frac_of_8tbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9 / NOMINAL_HBM_GBS, 3),
+            "hbm_frac_of_measured": round(step_bytes / (ms_per_step * 1e-3) / 1e9 / peak, 3),
+            "bytes_per_step_per_gpu": int(step_bytes),
+            "unique_experts_per_layer": [round(statistics.mean(uq[li] for uq in uniq), 2) for li in range(n_layers)],
+            "kernels": kern,
+            "roofline": {"kernel": dom_name, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 3) if achieved else None,
+                         "peak_source": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
+                         "traffic": traffic},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_val, 3), "unit": UNIT, "h2d_bytes_per_step": n_layers * B * H * 2,
+                    "d2h_bytes_per_step": n_layers * B * H * 2},
+            "gpu_launches": K * n_layers * launches_per_layer,
+            "clocks": clocks,
+            "setup_s": round(setup_s, 1),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def read_traffic(kernel_name, B, world):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if present.
+
+    The summary file lists lines ``traffic <kernel> b<B> tp<N> <bytes>``."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    try:
+        for line in open(path):
+            f = line.split()
+            if len(f) == 5 and f[0] == "traffic" and f[1] == kernel_name and f[2] == f"b{B}" and f[3] == f"tp{world}":
+                return int(f[4])
+    except OSError:
+        pass
+    return None
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,186 @@
+/*
+ * dsmoe -- B200 (sm_100a) quantized MoE expert layer: C ABI.
+ *
+ * The drop-in boundary for the reference's MoE hot path. Every entry point takes plain device
+ * pointers, sizes and a cudaStream_t (passed as void*), returns an int status (DSMOE_OK = 0,
+ * negative on error; dsmoe_last_error() gives the message), launches asynchronously on that
+ * stream, and allocates nothing: the caller owns every buffer, including the workspace.
+ * This follows the reference's native binding convention (dsv41/ref/fp4lib.py:5-11: raw pointers,
+ * integer sizes, caller-owned buffers), with status codes in place of Python-side asserts.
+ *
+ * Formats:
+ *   DSMOE_FMT_FP8  e4m3 weight bytes [out, in] + fp32 scales [ceil(out/128), ceil(in/128)]
+ *                  (dsv41/ref/kernel.py:75-78)
+ *   DSMOE_FMT_FP4  e2m1 codes [out, in/2], low nibble first + e8m0 scales [out, in/32]
+ *                  (dsv41/ref/kernel.py:91-98; dsv41/ref/fp4lib.c:12-30; dsv41/ckpt.py:41-50)
+ */
+#ifndef DSMOE_H_
+#define DSMOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DSMOE_API __attribute__((visibility("default")))
+#else
+#define DSMOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSMOE_OK 0
+#define DSMOE_ERR_ARG (-1)         /* bad shape, null pointer, unsupported combination */
+#define DSMOE_ERR_ALIGN (-2)       /* pointer not 16-byte aligned */
+#define DSMOE_ERR_CUDA (-3)        /* a CUDA call or launch failed */
+#define DSMOE_ERR_WORKSPACE (-4)   /* workspace too small */
+#define DSMOE_ERR_TIMEOUT (-5)     /* a bounded device-side wait gave up */
+#define DSMOE_ERR_UNSUPPORTED (-6)
+
+#define DSMOE_FMT_FP8 0
+#define DSMOE_FMT_FP4 1
+
+#define DSMOE_SCORE_SIGMOID 0
+#define DSMOE_SCORE_SQRTSOFTPLUS 1
+
+#define DSMOE_DTYPE_F32 0
+#define DSMOE_DTYPE_BF16 1
+#define DSMOE_DTYPE_E4M3 2
+
+/* Largest decode batch of dsmoe_moe_decode (tokens per call). */
+#define DSMOE_MAX_DECODE_TOKENS 64
+/* Tokens per expert slot in a decode step: an expert chosen by more tokens gets more slots,
+ * the "virtual bucket" rule of dsv41/tt/moe.py:184-187 with a bucket of 8 rows. */
+#define DSMOE_SLOT_TOKENS 8
+
+/* One expert set of one layer on this GPU, in the packed resident layout written by
+ * dsmoe_store_pack_expert (each expert's w1|w3 tiles, then its w2 tiles, scales co-located). */
+typedef struct dsmoe_store {
+  const uint8_t* w13;          /* [n_experts][w13_expert_bytes] */
+  const uint8_t* w2;           /* [n_experts][w2_expert_bytes]  */
+  long long w13_expert_bytes;  /* dsmoe_store_expert_bytes() */
+  long long w2_expert_bytes;
+  int fmt;                     /* DSMOE_FMT_* */
+  int n_experts;
+} dsmoe_store_t;
+
+/* One MoE layer on this GPU: router, routed experts and the shared expert.
+ * With tensor parallelism over W GPUs, each GPU holds inter_local = I / W rows of every expert's
+ * intermediate dimension (w1/w3 column-parallel, w2 row-parallel; dsv41/tt/moe.py:2-3) and the
+ * layer output on each GPU is a partial sum to be all-reduced. */
+typedef struct dsmoe_layer {
+  int hidden;                  /* H */
+  int inter_local;             /* intermediate rows per expert on this GPU */
+  int n_experts;               /* routed experts E */
+  int topk;                    /* k <= 8 */
+  int score_func;              /* DSMOE_SCORE_* */
+  float route_scale;
+  const float* gate_w;         /* [E, H] fp32 router weight (checkpoint [out, in] layout) */
+  const float* gate_bias;      /* [E] fp32, selection-only bias */
+  const float* gate_bias_vl;   /* [E] fp32 or NULL: bias for image-span tokens */
+  dsmoe_store_t routed;
+  dsmoe_store_t shared;        /* one expert */
+} dsmoe_layer_t;
+
+DSMOE_API const char* dsmoe_last_error(void);
+DSMOE_API int dsmoe_version(void);
+
+/* ---- weight unpack (kernel-surface dequant) ------------------------------------------------ */
+
+/* FP8 block dequant: b [N, K] e4m3, b_s [ceil(N/block), ceil(K/block)] fp32 -> out [N, K].
+ * Replaces `_deq_fp8_weight` (dsv41/ref/kernel.py:75-78) and the `weight_dequant` kernel entry
+ * point of DeepSeek's inference/kernel.py. out_dtype: DSMOE_DTYPE_F32 or DSMOE_DTYPE_BF16. */
+DSMOE_API int dsmoe_fp8_block_dequant(const uint8_t* b, const float* b_s, long long N, long long K, int block,
+                            void* out, int out_dtype, void* stream);
+
+/* FP4 dequant: b [N, K/2] packed e2m1, b_s [N, K/32] e8m0 -> out [N, K].
+ * Replaces `dequant_fp4_weight` (dsv41/ref/kernel.py:91-98) and `dequant_fp4`
+ * (dsv41/ref/fp4lib.c:12-30). */
+DSMOE_API int dsmoe_fp4_dequant(const uint8_t* b, const uint8_t* b_s, long long N, long long K,
+                      void* out, int out_dtype, void* stream);
+
+/* ---- kernel-surface GEMMs and activation quant ------------------------------------------- */
+
+/* out[M, N] = (a * a_s per 128-K block) @ dequant(b, b_s)^T, rounded to out_dtype.
+ * a: [M, K] in a_dtype (F32, BF16 or E4M3), a_s: [M, K/128] fp32 or NULL (all ones).
+ * Replaces `fp8_gemm` (dsv41/ref/kernel.py:105-107). */
+DSMOE_API int dsmoe_fp8_gemm(const void* a, int a_dtype, const float* a_s, long long M, long long K,
+                   const uint8_t* b, const float* b_s, long long N, void* out, int out_dtype,
+                   void* stream);
+
+/* Same with FP4 weights b [N, K/2] + e8m0 b_s [N, K/32]. Replaces `fp4_gemm`
+ * (dsv41/ref/kernel.py:110-112). */
+DSMOE_API int dsmoe_fp4_gemm(const void* a, int a_dtype, const float* a_s, long long M, long long K,
+                   const uint8_t* b, const uint8_t* b_s, long long N, void* out, int out_dtype,
+                   void* stream);
+
+/* Per-(row, block) e4m3 activation quant: s = amax/448 (or its power-of-2 ceiling when pow2 != 0),
+ * q = e4m3(clamp(x / s, +-448)), amax clamped below at 1e-4. Replaces the quantizing branch of
+ * `act_quant` (dsv41/ref/kernel.py:44-55). x: [M, K] in x_dtype (F32 or BF16). */
+DSMOE_API int dsmoe_act_quant(const void* x, int x_dtype, long long M, long long K, int block, int pow2,
+                    uint8_t* q, float* s, void* stream);
+
+/* ---- expert store (one-time repack; replaces the host ExpertStore / tile packer) ---------- */
+
+/* Bytes of one expert's w1|w3 part and w2 part in the packed store. */
+DSMOE_API int dsmoe_store_expert_bytes(int fmt, int hidden, int inter_local, long long* w13_bytes,
+                             long long* w2_bytes);
+
+/* Repack one expert from checkpoint layout (device memory) into the packed store, keeping
+ * intermediate rows [row0, row0 + inter_local) -- this GPU's tensor-parallel slice.
+ *   FP8: w1,w3 [I, H] e4m3, s1,s3 fp32 [ceil(I/128), H/128]; w2 [H, I] e4m3, s2 fp32 [H/128, ceil(I/128)]
+ *   FP4: w1,w3 [I, H/2] u8, s1,s3 e8m0 [I, H/32];         w2 [H, I/2] u8,  s2 e8m0 [H, I/32]
+ * Replaces ExpertStore._pack_one_proj / pack_expert_fp4_shards (dsv41/tt/store.py:66-89;
+ * dsv41/ref/fp4lib.c:116-186), which packed Tenstorrent tiles on the host. */
+DSMOE_API int dsmoe_store_pack_expert(int fmt, int hidden, int inter, int row0, int inter_local,
+                            const uint8_t* w1, const void* s1, const uint8_t* w3, const void* s3,
+                            const uint8_t* w2, const void* s2, uint8_t* w13_dst, uint8_t* w2_dst,
+                            void* stream);
+
+/* Inverse of dsmoe_store_pack_expert, dequantized to fp32: w1,w3 [inter_local, H], w2 [H, inter_local].
+ * Used to prove the packed store is lossless (bit-exact against the reference dequant). */
+DSMOE_API int dsmoe_store_unpack_expert(int fmt, int hidden, int inter, int row0, int inter_local,
+                              const uint8_t* w13_src, const uint8_t* w2_src, float* w1, float* w3,
+                              float* w2, void* stream);
+
+/* ---- router and MoE forward --------------------------------------------------------------- */
+
+/* Workspace bytes for dsmoe_router / dsmoe_moe_decode at batch B. */
+DSMOE_API size_t dsmoe_moe_workspace_bytes(const dsmoe_layer_t* layer, int B);
+
+/* On-device router: logits = x @ gate_w^T (fp64 accumulation, rounded to fp32), scores =
+ * score_func(logits), top-k of scores + bias (ties -> lower expert index), weights = the unbiased
+ * scores at those indices / (sum + 1e-20) * route_scale.
+ * Replaces MoE.scores + MoE.pick_from_host (dsv41/tt/moe.py:108-125), which read the scores back
+ * to the host every layer. x [B, H] bf16; image_mask [B] u8 or NULL selects gate_bias_vl per token.
+ * Outputs: idx [B, k] int64, wt [B, k] fp32, scores [B, E] fp32 (scores may be NULL). */
+DSMOE_API int dsmoe_router(const dsmoe_layer_t* layer, const void* x, int B, const uint8_t* image_mask,
+                 int64_t* idx, float* wt, float* scores, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/* Whole MoE layer for B <= DSMOE_MAX_DECODE_TOKENS tokens: router, routed experts (each weight
+ * tile read once per step for all tokens that chose it), shared expert, routing-weighted combine.
+ * Replaces MoE.decode / verify_batched (dsv41/tt/moe.py:148-180, 202-241).
+ * y: [B, H]; y_dtype DSMOE_DTYPE_BF16 (final output) or DSMOE_DTYPE_F32 (this GPU's partial sum,
+ * before the all-reduce). idx/wt/scores as in dsmoe_router (each may be NULL). */
+DSMOE_API int dsmoe_moe_decode(const dsmoe_layer_t* layer, const void* x, int B, const uint8_t* image_mask,
+                     void* y, int y_dtype, int64_t* idx, float* wt, float* scores,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* dsmoe_moe_decode that also records four caller-created CUDA events on the stream: before the
+ * router kernels, before the w1|w3 kernel, before the w2 kernel and after it. Same work, same
+ * results; used by the benchmark to time each kernel on its own stream (no counterpart in the
+ * reference, whose bench times whole traces, bench/bench_layer.py:34-51). */
+DSMOE_API int dsmoe_moe_decode_profiled(const dsmoe_layer_t* layer, const void* x, int B,
+                                        const uint8_t* image_mask, void* y, int y_dtype, int64_t* idx,
+                                        float* wt, float* scores, void* workspace, size_t workspace_bytes,
+                                        void* stream, void* const* events);
+
+/* fp32 [n] -> bf16 [n] (the last step after an fp32 all-reduce of the partial sums). */
+DSMOE_API int dsmoe_f32_to_bf16(const float* src, void* dst, long long n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DSMOE_H_ */

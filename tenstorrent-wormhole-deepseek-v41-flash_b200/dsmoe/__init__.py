@@ -1,0 +1,14 @@
+"""dsmoe -- B200-native quantized MoE expert layer (host side).
+
+The compute lives in libdsmoe.so (CUDA, sm_100a) behind the C ABI in include/dsmoe.h; this package
+binds it (``_lib``), keeps the resident expert store (``store``), and exposes the reference's
+Gate / Expert / MoE surface (``moe``). Synthetic seeded weights for tests and benchmarks are in
+``synth``.
+"""
+from . import _lib
+from .moe import MoE, Gate, Expert
+from .store import ExpertStore, expert_bytes
+from .synth import ExpertWeights, RouterWeights, make_expert, make_router, make_tokens
+
+__all__ = ["MoE", "Gate", "Expert", "ExpertStore", "expert_bytes", "ExpertWeights", "RouterWeights",
+           "make_expert", "make_router", "make_tokens", "_lib"]

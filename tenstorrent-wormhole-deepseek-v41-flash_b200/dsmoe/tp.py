@@ -1,0 +1,46 @@
+"""Tensor-parallel plumbing for the MoE layer (one process per GPU, torch.distributed).
+
+The reference runs the experts TP-8 over its 8-chip mesh: w1/w3 column-parallel, w2 row-parallel,
+one all_gather+sum all-reduce of the routed + shared partials per layer (dsv41/tt/moe.py:2-3,
+162, 180; dsv41/tt/attn.py:19-21). Here each rank holds a contiguous 1/world slice of every
+expert's intermediate dimension and the partials are summed in fp32 with one all-reduce.
+"""
+import os
+
+import torch
+
+
+def slice_of(inter: int, rank: int, world: int):
+    """(row0, inter_local) of ``rank``'s slice; the slice must keep the packed store's alignment."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world {world}")
+    if inter % world:
+        raise ValueError(f"inter {inter} does not split evenly over {world} ranks")
+    loc = inter // world
+    if loc % 32:
+        raise ValueError(f"per-rank slice {loc} must be a multiple of 32")
+    return rank * loc, loc
+
+
+def allreduce_partial_(part: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum the per-rank fp32 partials in place (one all-reduce, as attn.all_reduce_sum does)."""
+    if part.dtype != torch.float32:
+        raise TypeError("partials are summed in fp32")
+    if torch.distributed.is_initialized() and torch.distributed.get_world_size(group) > 1:
+        torch.distributed.all_reduce(part, op=torch.distributed.ReduceOp.SUM, group=group)
+    return part
+
+
+def max_over_ranks(value: float, device=None, group=None) -> float:
+    """The slowest rank's value (benchmark times are the max over ranks)."""
+    if not (torch.distributed.is_initialized() and torch.distributed.get_world_size(group) > 1):
+        return float(value)
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=group)
+    return float(t.item())
+
+
+def env_rank_world():
+    """(rank, local_rank, world) from torchrun's environment (1 process when absent)."""
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
