@@ -162,16 +162,27 @@ DSMOE_API int dsmoe_router(const dsmoe_layer_t* layer, const void* x, int B, con
 /* Whole MoE layer for B <= DSMOE_MAX_DECODE_TOKENS tokens: router, routed experts (each weight
  * tile read once per step for all tokens that chose it), shared expert, routing-weighted combine.
  * Replaces MoE.decode / verify_batched (dsv41/tt/moe.py:148-180, 202-241).
+ * For B <= 8 (hidden a multiple of 512, <= 1024 experts) the layer runs as one persistent kernel
+ * that keeps counters and a grid barrier in the workspace: the workspace must be zero-filled once
+ * before its first use (calls leave it reusable), and calls sharing one workspace must not overlap
+ * on the GPU. Every device-side wait is bounded; dsmoe_moe_check reports an expired wait.
  * y: [B, H]; y_dtype DSMOE_DTYPE_BF16 (final output) or DSMOE_DTYPE_F32 (this GPU's partial sum,
  * before the all-reduce). idx/wt/scores as in dsmoe_router (each may be NULL). */
 DSMOE_API int dsmoe_moe_decode(const dsmoe_layer_t* layer, const void* x, int B, const uint8_t* image_mask,
                      void* y, int y_dtype, int64_t* idx, float* wt, float* scores,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* Synchronizes `stream` and reads the status word of the persistent path: DSMOE_OK, or
+ * DSMOE_ERR_TIMEOUT when a bounded device-side wait expired in an earlier call (the workspace
+ * counters are then reset). Failure detection for the path; no counterpart in the reference. */
+DSMOE_API int dsmoe_moe_check(const dsmoe_layer_t* layer, int B, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
 /* dsmoe_moe_decode that also records four caller-created CUDA events on the stream: before the
  * router kernels, before the w1|w3 kernel, before the w2 kernel and after it. Same work, same
  * results; used by the benchmark to time each kernel on its own stream (no counterpart in the
- * reference, whose bench times whole traces, bench/bench_layer.py:34-51). */
+ * reference, whose bench times whole traces, bench/bench_layer.py:34-51). On the persistent path
+ * the first three events are recorded together before its single kernel. */
 DSMOE_API int dsmoe_moe_decode_profiled(const dsmoe_layer_t* layer, const void* x, int B,
                                         const uint8_t* image_mask, void* y, int y_dtype, int64_t* idx,
                                         float* wt, float* scores, void* workspace, size_t workspace_bytes,

@@ -19,6 +19,16 @@
 
 namespace dsmoe {
 
+// fused persistent path (moe_fused.cu)
+struct FusedScratch {
+  size_t rl, p13, p2, hf, cnt13, cnt2, gbar, status, total;
+  int p13max, qmax, slots;
+};
+FusedScratch fused_scratch(int H, int I_loc, int E, int B, int topk, int r_fmt);
+bool fused_supported(const dsmoe_layer_t* L, int B);
+int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image_mask, void* y, int y_dtype,
+                 int64_t* idx, float* wt, float* scores, uint8_t* ws, cudaStream_t st);
+
 struct DecodeArgs {
   int H, I_loc, E, B;
   int r_fmt;
@@ -322,10 +332,10 @@ struct WsLayout {
 
 static size_t al(size_t v) { return (v + 255) & ~size_t(255); }
 
-static WsLayout ws_layout(int B, int H, int E, int topk, int I_loc) {
+static WsLayout ws_layout(int B, int H, int E, int topk, int I_loc, size_t base) {
   WsLayout w{};
   const int S = max_slots(B, topk);
-  size_t o = 0;
+  size_t o = base;
   w.logits = o; o += al((size_t)B * E * 4);
   w.idx32 = o; o += al((size_t)B * topk * 4);
   w.wt32 = o; o += al((size_t)B * topk * 4);
@@ -339,6 +349,19 @@ static WsLayout ws_layout(int B, int H, int E, int topk, int I_loc) {
   w.hf = o; o += al((size_t)S * DSMOE_SLOT_TOKENS * I_loc * 2);
   w.total = o;
   return w;
+}
+
+// The persistent path's scratch sits at the front of the workspace, at a size and position that
+// depend only on the layer geometry (never on the batch), so calls of any batch share it safely.
+static size_t fused_region(const dsmoe_layer_t* L) {
+  if (L->inter_local <= 0 || L->inter_local % 32 || L->hidden % 512 ||
+      (L->routed.fmt != DSMOE_FMT_FP8 && L->routed.fmt != DSMOE_FMT_FP4))
+    return 0;
+  return fused_scratch(L->hidden, L->inter_local, L->n_experts, 8, L->topk, L->routed.fmt).total;
+}
+
+static WsLayout ws_layout_for(const dsmoe_layer_t* L, int B) {
+  return ws_layout(B, L->hidden, L->n_experts, L->topk, L->inter_local > 0 ? L->inter_local : 0, fused_region(L));
 }
 
 static int validate(const dsmoe_layer_t* L, int B, bool need_experts) {
@@ -413,7 +436,7 @@ using namespace dsmoe;
 
 extern "C" size_t dsmoe_moe_workspace_bytes(const dsmoe_layer_t* L, int B) {
   if (!L || B < 1) return 0;
-  return ws_layout(B, L->hidden, L->n_experts, L->topk, L->inter_local > 0 ? L->inter_local : 0).total;
+  return ws_layout_for(L, B).total;
 }
 
 extern "C" int dsmoe_router(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image_mask, int64_t* idx,
@@ -423,7 +446,7 @@ extern "C" int dsmoe_router(const dsmoe_layer_t* L, const void* x, int B, const 
   DSMOE_REQUIRE(x && workspace, DSMOE_ERR_ARG, "router: x / workspace null");
   DSMOE_REQUIRE(((uintptr_t)x & 7) == 0 && ((uintptr_t)workspace & 255) == 0, DSMOE_ERR_ALIGN,
                 "router: x must be 8-byte and workspace 256-byte aligned");
-  const WsLayout w = ws_layout(B, L->hidden, L->n_experts, L->topk, L->inter_local > 0 ? L->inter_local : 0);
+  const WsLayout w = ws_layout_for(L, B);
   DSMOE_REQUIRE(workspace_bytes >= w.total, DSMOE_ERR_WORKSPACE, "router: workspace %zu < %zu", workspace_bytes, w.total);
   RouterArgs a = router_args(L, x, B, image_mask, idx, wt, scores, (uint8_t*)workspace, w);
   return launch_router(a, false, (cudaStream_t)stream);
@@ -438,11 +461,21 @@ static int moe_decode_impl(const dsmoe_layer_t* L, const void* x, int B, const u
   DSMOE_REQUIRE(y_dtype == DSMOE_DTYPE_BF16 || y_dtype == DSMOE_DTYPE_F32, DSMOE_ERR_ARG, "moe_decode: y_dtype %d", y_dtype);
   DSMOE_REQUIRE(((uintptr_t)x & 7) == 0 && ((uintptr_t)workspace & 255) == 0, DSMOE_ERR_ALIGN,
                 "moe_decode: x must be 8-byte and workspace 256-byte aligned");
-  const WsLayout w = ws_layout(B, L->hidden, L->n_experts, L->topk, L->inter_local);
+  const WsLayout w = ws_layout_for(L, B);
   DSMOE_REQUIRE(workspace_bytes >= w.total, DSMOE_ERR_WORKSPACE, "moe_decode: workspace %zu < %zu", workspace_bytes,
                 w.total);
   uint8_t* ws = (uint8_t*)workspace;
   cudaStream_t st = (cudaStream_t)stream;
+  if (fused_region(L) > 0 && fused_supported(L, B)) {
+    if (events) {
+      cudaEventRecord((cudaEvent_t)events[0], st);
+      cudaEventRecord((cudaEvent_t)events[1], st);
+      cudaEventRecord((cudaEvent_t)events[2], st);
+    }
+    rc = launch_fused(L, x, B, image_mask, y, y_dtype, idx, wt, scores, ws, st);
+    if (events) cudaEventRecord((cudaEvent_t)events[3], st);
+    return rc;
+  }
   RouterArgs ra = router_args(L, x, B, image_mask, idx, wt, scores, ws, w);
   if (events) cudaEventRecord((cudaEvent_t)events[0], st);
   rc = launch_router(ra, true, st);
@@ -501,6 +534,28 @@ extern "C" int dsmoe_moe_decode_profiled(const dsmoe_layer_t* L, const void* x, 
                 "moe_decode_profiled: four events required");
   return moe_decode_impl(L, x, B, image_mask, y, y_dtype, idx, wt, scores, workspace, workspace_bytes, stream,
                          events);
+}
+
+extern "C" int dsmoe_moe_check(const dsmoe_layer_t* L, int B, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  int rc = validate(L, B, true);
+  if (rc) return rc;
+  DSMOE_REQUIRE(workspace, DSMOE_ERR_ARG, "moe_check: workspace null");
+  const WsLayout w = ws_layout_for(L, B);
+  if (fused_region(L) == 0 || workspace_bytes < w.total) return DSMOE_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return cuda_status("moe_check: synchronize");
+  const FusedScratch f = fused_scratch(L->hidden, L->inter_local, L->n_experts, 8, L->topk, L->routed.fmt);
+  uint8_t* base = (uint8_t*)workspace;
+  unsigned status = 0;
+  if (cudaMemcpy(&status, base + f.status, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return cuda_status("moe_check: read status");
+  if (status == 0) return DSMOE_OK;
+  // a bounded wait expired: clear the scratch counters so the next call starts clean
+  cudaMemsetAsync(base + f.gbar, 0, f.rl - f.gbar, st);
+  cudaStreamSynchronize(st);
+  set_error("moe_decode: a bounded device wait expired (status 0x%x); workspace counters were reset", status);
+  return DSMOE_ERR_TIMEOUT;
 }
 
 extern "C" int dsmoe_f32_to_bf16(const float* src, void* dst, long long n, void* stream) {

@@ -58,6 +58,7 @@ _SIGS = {
     "dsmoe_moe_decode": ([ctypes.POINTER(Layer), _P, _I, _P, _P, _I, _P, _P, _P, _P, ctypes.c_size_t, _P], _I),
     "dsmoe_moe_decode_profiled": ([ctypes.POINTER(Layer), _P, _I, _P, _P, _I, _P, _P, _P, _P, ctypes.c_size_t, _P,
                                    ctypes.POINTER(_P)], _I),
+    "dsmoe_moe_check": ([ctypes.POINTER(Layer), _I, _P, ctypes.c_size_t, _P], _I),
     "dsmoe_f32_to_bf16": ([_P, _P, _LL, _P], _I),
 }
 

@@ -59,7 +59,8 @@ class MoE:
         self.max_tokens = min(max_tokens, L.MAX_DECODE_TOKENS)
         self._layer = self._make_layer()
         nbytes = L.lib.dsmoe_moe_workspace_bytes(self._layer, self.max_tokens)
-        self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        # zero-filled once: the persistent kernel keeps counters and a grid barrier here
+        self.workspace = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
 
     # ---------------------------------------------------------------- loading
     def _make_layer(self) -> L.Layer:
@@ -130,6 +131,11 @@ class MoE:
 
     __call__ = forward
     decode = forward
+
+    def check(self, B: int = 1) -> None:
+        """Synchronize and raise if a bounded device-side wait expired in an earlier call."""
+        L.call("dsmoe_moe_check", self._layer, min(B, self.max_tokens), L.ptr(self.workspace),
+               self.workspace.numel(), L.stream_of(self.workspace))
 
     def _run(self, x, image_mask, out, y_dtype, idx=None, wt=None):
         x = _check_x(x, self.hidden, self.device)

@@ -346,3 +346,20 @@ def test_errors_are_raised_not_launched(dev):
                L.stream_of())                                                    # batch too large
     assert ei.value.code == L.ERR_ARG
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "fp4"])
+def test_workspace_reuse_across_calls_and_batches(dev, fmt):
+    """One workspace, many calls: the persistent path (B <= 8) and the multi-kernel path (B > 8)
+    alternate; every output matches the oracle and no bounded wait expires."""
+    spec = make_layer_cpu(fmt, 1024, 256, 32, seed=55)
+    m = to_gpu_moe(spec, device=dev)
+    ref = to_oracle_layer(spec)
+    gen = torch.Generator().manual_seed(12)
+    for B in (1, 8, 13, 2, 1, 64, 5, 1, 1):
+        x = torch.randn((B, 1024), generator=gen).to(torch.bfloat16)
+        y = bf16_np(m.forward(x.to(dev)))
+        yr, _, _ = OM.moe_forward(ref, x.float().numpy())
+        mar, cos = OM.compare(y, yr)
+        assert mar < MAR_TOL and cos > COS_TOL, (B, mar, cos)
+    m.check(8)
