@@ -10,19 +10,21 @@
 //              item's weight bytes into a ring of up to 16 x 8.5 KB shared-memory stages,
 //              completion counted on per-stage mbarriers; it runs ahead across phase boundaries
 //              (w2 weights stream in while the grid waits for the last w1|w3 tiles).
-//   consumers  each item is consumed by one warp: dequantize the A fragments from the stage,
-//              mma.sync m16n8k16 (f16 x f16 -> fp32) against the tokens' f16 fragments (shared
-//              memory), block scales on the fp32 partials, partial sums to global scratch.
-// Phases (items are dealt round-robin over the CTAs, rotating across phases so every CTA gets the
-// same amount of work):
+//   consumers  dequantize A fragments from the stage, mma.sync m16n8k16 (f16 x f16 -> fp32)
+//              against the tokens' f16 fragments (shared memory), block scales on fp32 partials.
+// Work distribution: every phase is a flat list of items (4-8.5 KB of packed chunks each); each
+// CTA takes a contiguous span and each consumer warp a contiguous run of that span, so a warp
+// accumulates the consecutive parts of a 16-row tile in registers and publishes one partial per
+// tile it shares with other warps. The last contributor of a tile (counter in the workspace)
+// re-derives the tile's segments from the same deterministic distribution and sums them in order,
+// so results do not depend on timing.
+// Phases:
 //   R  router quarter-rows (fp64 accumulation) + the shared expert's w1|w3 parts (no routing
-//      needed); a CTA arrives at grid barrier A as soon as its router items are done, so the
-//      shared-expert work hides the barrier.
-//   P  every CTA computes the same top-k and slot plan from the router partials (no extra barrier).
-//   1  routed w1|w3 parts. The last part of each 16-row tile (a counter) sums the tile's partials
-//      in a fixed order and applies clamp / SiLU / up / routing weight -> h (f16).
-//   2  (after grid barrier B) w2 parts per 16 output rows x slot x K range; the last part of each
-//      16-row tile sums the partials in a fixed order -> y. Results are deterministic.
+//      needed); a CTA arrives at grid barrier A when its router rows are done, and the shared-
+//      expert work hides the barrier.
+//   P  every CTA computes the same top-k and slot plan from the router partials.
+//   1  routed w1|w3 parts; tile epilogue: clamp / SiLU / up / routing weight -> h (f16).
+//   2  after grid barrier B: w2 parts (16 output rows x slot x 256 K); tile epilogue -> y.
 // Every wait (mbarrier, grid barrier) is bounded by %globaltimer; on expiry the kernel records a
 // status bit in the workspace, stops issuing work, lets its own copies land and returns.
 #include "router.cuh"
@@ -31,8 +33,9 @@ namespace dsmoe {
 
 constexpr int FW = 8;                  // consumer warps
 constexpr int FT = (FW + 1) * 32;      // + producer warp
-constexpr int FCH = 8;                 // packed chunks per w1|w3 or w2 item
+constexpr int FCH = 8;                 // packed chunks per w1|w3 item
 constexpr int FSTAGE = FCH * 1088;     // bytes per ring stage (8 FP4 w1|w3 chunks, the largest item)
+constexpr int FK2 = 256;               // K values per w2 item (8 FP8 chunks or 4 FP4 chunks)
 constexpr int FMAXB = 8;               // tokens per call
 constexpr int FMAXK = DSMOE_MAX_TOPK;
 constexpr int FMAXS = FMAXB * FMAXK + 1;
@@ -61,15 +64,15 @@ struct FusedArgs {
   float* wt;
   float* scores;
   // scratch (workspace)
-  double* rl;        // [B][E][4] router quarter-row partial logits
-  float* p13;        // [slots][T][p13max][32][8] w1|w3 partials
-  float* p2;         // [NT][qmax][32][4] w2 partials (token columns)
+  double* rl;        // [8][E][4] router quarter-row partial logits
+  float* p13;        // [slots][T][p13max][32][8] w1|w3 tile-segment partials
+  float* p2;         // [NT][qmax][32][4] w2 tile-segment partials (token columns)
   uint16_t* hf;      // [slots * 8][I_loc] h, f16, fragment order
   unsigned* cnt13;   // [slots][T]
   unsigned* cnt2;    // [NT]
   unsigned* gbar;    // [0] arrivals, [1] generation
   unsigned* status;  // [0]
-  int sh_idx;        // scratch slot index of the shared expert (= B * topk)
+  int sh_idx;        // scratch slot index of the shared expert
   int nstage, xrow, p13max, qmax;
 };
 
@@ -90,8 +93,8 @@ struct FPlan {
 };
 
 struct Geo {
-  int T, NT, KB, NR, NS, P13s, P13r, KC2s, KC2r, P2s, P2r;
-  int chunk13r, chunk2r;
+  int T, NT, KB, NR, NS, P13s, P13r, P2;
+  int chunk13r, chunk2r, nch2r;
   long long tile13r, tile13s, tile2r, tile2s;
 };
 
@@ -104,12 +107,10 @@ __device__ __forceinline__ Geo make_geo(const FusedArgs& a) {
   g.P13s = (a.H / 32) / FCH;
   g.P13r = a.r_fmt == DSMOE_FMT_FP8 ? (a.H / 32) / FCH : (a.H / 64) / FCH;
   g.NS = g.T * g.P13s;
-  g.KC2s = a.I_loc / 32;
-  g.KC2r = a.r_fmt == DSMOE_FMT_FP8 ? a.I_loc / 32 : a.I_loc / 64;
-  g.P2s = (g.KC2s + FCH - 1) / FCH;
-  g.P2r = (g.KC2r + FCH - 1) / FCH;
+  g.P2 = (a.I_loc + FK2 - 1) / FK2;
   g.chunk13r = a.r_fmt == DSMOE_FMT_FP8 ? 1024 : 1088;
   g.chunk2r = a.r_fmt == DSMOE_FMT_FP8 ? 512 : 544;
+  g.nch2r = a.r_fmt == DSMOE_FMT_FP8 ? FK2 / 32 : FK2 / 64;
   g.tile13r = w13_tile_bytes(a.r_fmt, a.H);
   g.tile13s = fp8_w13_tile_bytes(a.H);
   g.tile2r = w2_tile_bytes(a.r_fmt, a.I_loc);
@@ -117,10 +118,34 @@ __device__ __forceinline__ Geo make_geo(const FusedArgs& a) {
   return g;
 }
 
-// first item of CTA c in a phase whose items are dealt from CTA (base % G)
-__device__ __forceinline__ int first_item(int base, int c, int G) {
-  int f = c - base % G;
-  return f < 0 ? f + G : f;
+// ------------------------------------------------------------------ deterministic distribution
+struct Span {
+  int s, e;
+};
+__device__ __forceinline__ Span cta_span(int n, int c, int G) {
+  return {(int)((long long)n * c / G), (int)((long long)n * (c + 1) / G)};
+}
+__device__ __forceinline__ Span warp_run(Span cs, int w) {
+  const int nc = cs.e - cs.s, L = nc / FW, r = nc % FW;
+  const int rs = cs.s + w * L + min(w, r);
+  return {rs, rs + L + (w < r ? 1 : 0)};
+}
+// Calls f(first item of the segment - a) for every warp run that intersects [a, b), in order.
+template <class F>
+__device__ __forceinline__ void for_segments(int n, int G, int a, int b, F&& f) {
+  int c = (int)(((long long)a * G) / n);
+  while (c + 1 < G && cta_span(n, c + 1, G).s <= a) ++c;
+  while (c > 0 && cta_span(n, c, G).s > a) --c;
+  for (; c < G; ++c) {
+    const Span cs = cta_span(n, c, G);
+    if (cs.s >= b) break;
+    for (int w = 0; w < FW; ++w) {
+      const Span r = warp_run(cs, w);
+      if (r.e <= a || r.s >= r.e) continue;
+      if (r.s >= b) break;
+      f(max(r.s, a) - a);
+    }
+  }
 }
 
 __device__ __forceinline__ float fscore(float l, int func) {
@@ -177,7 +202,7 @@ __device__ __forceinline__ bool grid_wait(unsigned* gbar, unsigned g0, const uns
   return true;
 }
 
-// ------------------------------------------------------------------ items (one warp each)
+// ------------------------------------------------------------------ router
 // Router quarter-row: 1/4 of gate_w[r] (H/4 fp32, in the stage) . x[b] for every token, fp64.
 __device__ void router_item(const FusedArgs& a, const uint8_t* stage, int r, int q, int lane) {
   double acc[FMAXB];
@@ -208,45 +233,17 @@ __device__ void router_item(const FusedArgs& a, const uint8_t* stage, int r, int
   }
 }
 
-// Sum a w1|w3 tile's partials in order and write h (clamp, SiLU, up, routing weight).
-__device__ void finalize_w13(const FusedArgs& a, const Geo& G, const FPlan& pl, int sidx, int t, int nparts,
-                             int ntok, const int* toks, const float* wts, int lane) {
-  float s[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) s[j] = 0.f;
-  for (int q = 0; q < nparts; ++q) {
-    const float* src = a.p13 + ((((long long)sidx * G.T + t) * a.p13max + q) * 32 + lane) * 8;
-    const uint4 v0 = ld_cg16(src), v1 = ld_cg16(src + 4);
-    s[0] += __uint_as_float(v0.x); s[1] += __uint_as_float(v0.y);
-    s[2] += __uint_as_float(v0.z); s[3] += __uint_as_float(v0.w);
-    s[4] += __uint_as_float(v1.x); s[5] += __uint_as_float(v1.y);
-    s[6] += __uint_as_float(v1.z); s[7] += __uint_as_float(v1.w);
-  }
-  const int g = lane >> 2, tq = lane & 3;
-#pragma unroll
-  for (int q4 = 0; q4 < 4; ++q4) {
-    const int row = q4 >= 2 ? g + 8 : g, col = 2 * tq + (q4 & 1);
-    if (col < ntok) {
-      const float xs = pl.xscale[toks[col]];
-      const float gv = fminf(s[q4] * xs, 10.0f);
-      const float uv = fminf(fmaxf(s[4 + q4] * xs, -10.0f), 10.0f);
-      const float h = silu_f(gv) * uv * wts[col];
-      a.hf[(long long)(sidx * 8 + col) * a.I_loc + frag_pos(16 * t + row)] = __half_as_ushort(__float2half_rn(h));
-    }
-  }
-}
-
-// One w1|w3 item: 8 chunks of a 16-row tile against the slot's tokens.
+// ------------------------------------------------------------------ w1|w3
+// One item (8 chunks of a 16-row tile, part p) accumulated into acc1 / acc3.
 template <int FMT>
-__device__ void w13_item(const FusedArgs& a, const Geo& G, const FPlan& pl, const uint8_t* stage, const uint8_t* xf,
-                         const uint8_t* tile_g, int sidx, int t, int p, int nparts, int ntok, const int* toks,
-                         const float* wts, int lane) {
+__device__ __forceinline__ void w13_accum(const FusedArgs& a, const Geo& G, const uint8_t* stage, const uint8_t* xrow,
+                                          const uint8_t* tile_g, int p, int lane, float (&acc1)[4], float (&acc3)[4]) {
   const int g = lane >> 2, tq = lane & 3;
-  const uint8_t* xrow = xf + (long long)toks[min(g, ntok - 1)] * a.xrow;
-  float acc1[4] = {0.f, 0.f, 0.f, 0.f}, acc3[4] = {0.f, 0.f, 0.f, 0.f};
   float t1[4] = {0.f, 0.f, 0.f, 0.f}, t3[4] = {0.f, 0.f, 0.f, 0.f};
   if (FMT == DSMOE_FMT_FP8) {
     const float* sc = reinterpret_cast<const float*>(tile_g + (long long)(a.H / 32) * 1024);
+    const float s1a = __ldg(sc + 2 * p), s1b = __ldg(sc + 2 * p + 1);
+    const float s3a = __ldg(sc + G.KB + 2 * p), s3b = __ldg(sc + G.KB + 2 * p + 1);
 #pragma unroll
     for (int c = 0; c < FCH; ++c) {
       const int gc = p * FCH + c;
@@ -258,10 +255,12 @@ __device__ void w13_item(const FusedArgs& a, const Geo& G, const FPlan& pl, cons
       a_frag_fp8(A, A3.x, A3.y); mma16816(t3, A, X.x, X.y);
       a_frag_fp8(A, A1.z, A1.w); mma16816(t1, A, X.z, X.w);
       a_frag_fp8(A, A3.z, A3.w); mma16816(t3, A, X.z, X.w);
-      if ((c & 3) == 3) {
-        const int kb = gc >> 2;
-        fma4s(acc1, t1, __ldg(sc + kb));
-        fma4s(acc3, t3, __ldg(sc + G.KB + kb));
+      if (c == 3) {
+        fma4s(acc1, t1, s1a);
+        fma4s(acc3, t3, s3a);
+      } else if (c == 7) {
+        fma4s(acc1, t1, s1b);
+        fma4s(acc3, t3, s3b);
       }
     }
   } else {
@@ -287,57 +286,95 @@ __device__ void w13_item(const FusedArgs& a, const Geo& G, const FPlan& pl, cons
       fma4r(acc3, t3, e8m0_to_f32(S3 >> 8), e8m0_to_f32(S3 >> 24));
     }
   }
-  float* dst = a.p13 + ((((long long)sidx * G.T + t) * a.p13max + p) * 32 + lane) * 8;
-  *reinterpret_cast<float4*>(dst) = make_float4(acc1[0], acc1[1], acc1[2], acc1[3]);
-  *reinterpret_cast<float4*>(dst + 4) = make_float4(acc3[0], acc3[1], acc3[2], acc3[3]);
-  __threadfence();
-  __syncwarp();
-  unsigned old = 0;
-  if (lane == 0) old = atomicAdd(a.cnt13 + sidx * G.T + t, 1u);
-  old = __shfl_sync(0xffffffffu, old, 0);
-  if (old == (unsigned)nparts - 1) {
-    __threadfence();
-    finalize_w13(a, G, pl, sidx, t, nparts, ntok, toks, wts, lane);
-    if (lane == 0) a.cnt13[sidx * G.T + t] = 0u;
+}
+
+// Tile epilogue: clamp, SiLU(gate) * up * routing weight -> h (f16, w2's fragment order).
+__device__ __forceinline__ void w13_epilogue(const FusedArgs& a, const FPlan& pl, int sidx, int t, const float (&s)[8],
+                                             int ntok, const int* toks, const float* wts, int lane) {
+  const int g = lane >> 2, tq = lane & 3;
+#pragma unroll
+  for (int q4 = 0; q4 < 4; ++q4) {
+    const int row = q4 >= 2 ? g + 8 : g, col = 2 * tq + (q4 & 1);
+    if (col < ntok) {
+      const float xs = pl.xscale[toks[col]];
+      const float gv = fminf(s[q4] * xs, 10.0f);
+      const float uv = fminf(fmaxf(s[4 + q4] * xs, -10.0f), 10.0f);
+      const float h = silu_f(gv) * uv * wts[col];
+      a.hf[(long long)(sidx * 8 + col) * a.I_loc + frag_pos(16 * t + row)] = __half_as_ushort(__float2half_rn(h));
+    }
   }
 }
 
-// One w2 item: up to 8 chunks of one slot's 16 output rows x K range; partial in token columns.
-template <int FMT>
-__device__ void w2_item(const FusedArgs& a, const Geo& G, const FPlan& pl, const uint8_t* stage,
-                        const uint8_t* tile_g, int s, int sidx, int nt, int p, int nch, int q, int Q, int lane) {
+// A warp's contribution to one tile ends: publish it, or finish the tile if it is complete.
+// [a0, a0 + P) are the tile's items in the phase (n items); the warp covered seg_np of them from seg_first.
+__device__ void w13_flush(const FusedArgs& a, const Geo& G, const FPlan& pl, int n, int a0, int P, int seg_first,
+                          int seg_np, int sidx, int t, const float (&acc1)[4], const float (&acc3)[4], int ntok,
+                          const int* toks, const float* wts, int lane) {
+  float s[8] = {acc1[0], acc1[1], acc1[2], acc1[3], acc3[0], acc3[1], acc3[2], acc3[3]};
+  if (seg_np == P) {
+    w13_epilogue(a, pl, sidx, t, s, ntok, toks, wts, lane);
+    return;
+  }
+  float* base = a.p13 + (((long long)sidx * G.T + t) * a.p13max) * 32 * 8;
+  float* dst = base + ((long long)(seg_first - a0) * 32 + lane) * 8;
+  *reinterpret_cast<float4*>(dst) = make_float4(s[0], s[1], s[2], s[3]);
+  *reinterpret_cast<float4*>(dst + 4) = make_float4(s[4], s[5], s[6], s[7]);
+  __threadfence();
+  __syncwarp();
+  unsigned old = 0;
+  if (lane == 0) old = atomicAdd(a.cnt13 + sidx * G.T + t, (unsigned)seg_np);
+  old = __shfl_sync(0xffffffffu, old, 0);
+  if ((int)old + seg_np != P) return;
+  __threadfence();
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s[j] = 0.f;
+  for_segments(n, gridDim.x, a0, a0 + P, [&](int q) {
+    const float* src = base + ((long long)q * 32 + lane) * 8;
+    const uint4 v0 = ld_cg16(src), v1 = ld_cg16(src + 4);
+    s[0] += __uint_as_float(v0.x); s[1] += __uint_as_float(v0.y);
+    s[2] += __uint_as_float(v0.z); s[3] += __uint_as_float(v0.w);
+    s[4] += __uint_as_float(v1.x); s[5] += __uint_as_float(v1.y);
+    s[6] += __uint_as_float(v1.z); s[7] += __uint_as_float(v1.w);
+  });
+  w13_epilogue(a, pl, sidx, t, s, ntok, toks, wts, lane);
+  if (lane == 0) a.cnt13[sidx * G.T + t] = 0u;
+}
+
+// ------------------------------------------------------------------ w2
+// The 8 k32 blocks of h this lane feeds to one w2 item (slot row sidx*8+g, K range p*256..).
+__device__ __forceinline__ void load_h(const FusedArgs& a, int sidx, int p, int lane, uint4 (&hb)[8]) {
   const int g = lane >> 2, tq = lane & 3;
+  const int kc = a.I_loc / 32;
   const uint8_t* hrow = reinterpret_cast<const uint8_t*>(a.hf + (long long)(sidx * 8 + g) * a.I_loc) + tq * 16;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (p * 8 + i < kc) hb[i] = ld_cg16(hrow + (long long)(p * 8 + i) * 64);
+}
+
+// One w2 item of slot s accumulated into out[] (token columns: rows g, g+8 x tokens 2tq, 2tq+1).
+template <int FMT>
+__device__ __forceinline__ void w2_accum(const FusedArgs& a, const FPlan& pl, const uint8_t* stage, const uint8_t* tile_g,
+                                         int s, int p, const uint4 (&hb)[8], int lane, float (&out)[4]) {
+  const int g = lane >> 2, tq = lane & 3;
   float acc[4] = {0.f, 0.f, 0.f, 0.f}, tt[4] = {0.f, 0.f, 0.f, 0.f};
   if (FMT == DSMOE_FMT_FP8) {
     const int KC = a.I_loc / 32;
     const float* sc = reinterpret_cast<const float*>(tile_g + (long long)KC * 512);
-    uint4 hb[FCH];
 #pragma unroll
-    for (int i = 0; i < FCH; ++i)
-      if (i < nch) hb[i] = ld_cg16(hrow + (long long)(p * FCH + i) * 64);
-#pragma unroll
-    for (int i = 0; i < FCH; ++i) {
-      if (i < nch) {
+    for (int i = 0; i < 8; ++i) {
+      if (p * 8 + i < KC) {
         const uint4 A0 = lds16(stage + i * 512 + lane * 16);
         uint32_t A[4];
         a_frag_fp8(A, A0.x, A0.y); mma16816(tt, A, hb[i].x, hb[i].y);
         a_frag_fp8(A, A0.z, A0.w); mma16816(tt, A, hb[i].z, hb[i].w);
-        fma4s(acc, tt, __ldg(sc + p * FCH + i));
+        fma4s(acc, tt, __ldg(sc + p * 8 + i));
       }
     }
   } else {
-    uint4 hb[2 * FCH];
+    const int KC = a.I_loc / 64;
 #pragma unroll
-    for (int i = 0; i < FCH; ++i) {
-      if (i < nch) {
-        hb[2 * i] = ld_cg16(hrow + (long long)(2 * (p * FCH + i)) * 64);
-        hb[2 * i + 1] = ld_cg16(hrow + (long long)(2 * (p * FCH + i) + 1) * 64);
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < FCH; ++i) {
-      if (i < nch) {
+    for (int i = 0; i < 4; ++i) {
+      if (p * 4 + i < KC) {
         const uint8_t* ch = stage + i * 544;
         const uint4 A0 = lds16(ch + lane * 16);
         const uint32_t S = lds32(ch + 512 + 4 * g);
@@ -351,8 +388,7 @@ __device__ void w2_item(const FusedArgs& a, const Geo& G, const FPlan& pl, const
       }
     }
   }
-  // slot columns -> token columns: lane (g, tq) collects tokens 2tq, 2tq+1 of rows g, g+8
-  float out[4];
+  // slot columns -> token columns
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int tok = 2 * tq + h;
@@ -360,37 +396,53 @@ __device__ void w2_item(const FusedArgs& a, const Geo& G, const FPlan& pl, const
     const int src = g * 4 + (col < 0 ? 0 : col >> 1);
     const float v0 = __shfl_sync(0xffffffffu, acc[0], src), v1 = __shfl_sync(0xffffffffu, acc[1], src);
     const float v2 = __shfl_sync(0xffffffffu, acc[2], src), v3 = __shfl_sync(0xffffffffu, acc[3], src);
-    out[h] = col < 0 ? 0.f : ((col & 1) ? v1 : v0);
-    out[2 + h] = col < 0 ? 0.f : ((col & 1) ? v3 : v2);
+    if (col >= 0) {
+      out[h] += (col & 1) ? v1 : v0;
+      out[2 + h] += (col & 1) ? v3 : v2;
+    }
   }
-  float* dst = a.p2 + (((long long)nt * a.qmax + q) * 32 + lane) * 4;
-  *reinterpret_cast<float4*>(dst) = make_float4(out[0], out[1], out[2], out[3]);
+}
+
+__device__ __forceinline__ void w2_epilogue(const FusedArgs& a, int nt, const float (&s)[4], int lane) {
+  const int g = lane >> 2, tq = lane & 3;
+#pragma unroll
+  for (int q4 = 0; q4 < 4; ++q4) {
+    const int row = nt * 16 + (q4 >= 2 ? g + 8 : g), tok = 2 * tq + (q4 & 1);
+    if (tok < a.B) {
+      const long long o = (long long)tok * a.H + row;
+      if (a.y_f32)
+        reinterpret_cast<float*>(a.y)[o] = s[q4];
+      else
+        reinterpret_cast<__nv_bfloat16*>(a.y)[o] = __float2bfloat16_rn(s[q4]);
+    }
+  }
+}
+
+__device__ void w2_flush(const FusedArgs& a, int n, int Q, int nt, int seg_first, int seg_np, const float (&out)[4],
+                         int lane) {
+  float s[4] = {out[0], out[1], out[2], out[3]};
+  const int a0 = nt * Q;
+  if (seg_np == Q) {
+    w2_epilogue(a, nt, s, lane);
+    return;
+  }
+  float* base = a.p2 + ((long long)nt * a.qmax) * 32 * 4;
+  *reinterpret_cast<float4*>(base + ((long long)(seg_first - a0) * 32 + lane) * 4) = make_float4(s[0], s[1], s[2], s[3]);
   __threadfence();
   __syncwarp();
   unsigned old = 0;
-  if (lane == 0) old = atomicAdd(a.cnt2 + nt, 1u);
+  if (lane == 0) old = atomicAdd(a.cnt2 + nt, (unsigned)seg_np);
   old = __shfl_sync(0xffffffffu, old, 0);
-  if (old == (unsigned)Q - 1) {
-    __threadfence();
-    float sum[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int qq = 0; qq < Q; ++qq) {
-      const uint4 v = ld_cg16(a.p2 + (((long long)nt * a.qmax + qq) * 32 + lane) * 4);
-      sum[0] += __uint_as_float(v.x); sum[1] += __uint_as_float(v.y);
-      sum[2] += __uint_as_float(v.z); sum[3] += __uint_as_float(v.w);
-    }
-#pragma unroll
-    for (int q4 = 0; q4 < 4; ++q4) {
-      const int row = nt * 16 + (q4 >= 2 ? g + 8 : g), tok = 2 * tq + (q4 & 1);
-      if (tok < a.B) {
-        const long long o = (long long)tok * a.H + row;
-        if (a.y_f32)
-          reinterpret_cast<float*>(a.y)[o] = sum[q4];
-        else
-          reinterpret_cast<__nv_bfloat16*>(a.y)[o] = __float2bfloat16_rn(sum[q4]);
-      }
-    }
-    if (lane == 0) a.cnt2[nt] = 0u;
-  }
+  if ((int)old + seg_np != Q) return;
+  __threadfence();
+  s[0] = s[1] = s[2] = s[3] = 0.f;
+  for_segments(n, gridDim.x, a0, a0 + Q, [&](int q) {
+    const uint4 v = ld_cg16(base + ((long long)q * 32 + lane) * 4);
+    s[0] += __uint_as_float(v.x); s[1] += __uint_as_float(v.y);
+    s[2] += __uint_as_float(v.z); s[3] += __uint_as_float(v.w);
+  });
+  w2_epilogue(a, nt, s, lane);
+  if (lane == 0) a.cnt2[nt] = 0u;
 }
 
 // ------------------------------------------------------------------ the kernel
@@ -409,8 +461,8 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   const int G = gridDim.x, cta = blockIdx.x;
   const Geo geo = make_geo(a);
   const int nR = geo.NR + geo.NS;
-  int my_router = 0;
-  for (int i = first_item(0, cta, G); i < geo.NR; i += G) ++my_router;
+  const Span spanR = cta_span(nR, cta, G);
+  const int my_router = max(0, min(spanR.e, geo.NR) - spanR.s);
 
   if (tid == 0) {
     for (int s = 0; s < a.nstage; ++s) {
@@ -441,14 +493,23 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       bulk_g2s(ring + (size_t)s * FSTAGE, src, bytes, &full[s]);
       ++j;
     };
-    for (int i = first_item(0, cta, G); i < nR && ok; i += G) {
+    // items of a CTA span in the consumers' order: the k-th item of every warp run, warp by warp
+    auto issue_span = [&](Span cs, auto&& item) {
+      const int L = (cs.e - cs.s + FW - 1) / FW;
+      for (int k = 0; k < L && ok; ++k)
+        for (int w = 0; w < FW && ok; ++w) {
+          const Span r = warp_run(cs, w);
+          if (r.s + k < r.e) item(r.s + k);
+        }
+    };
+    issue_span(spanR, [&](int i) {
       if (i < geo.NR) {
         issue(a.wg + (long long)(i >> 2) * a.H + (i & 3) * (a.H / 4), (uint32_t)a.H);
       } else {
         const int i2 = i - geo.NR, t = i2 / geo.P13s, p = i2 % geo.P13s;
         issue(a.s_w13 + t * geo.tile13s + (long long)p * FCH * 1024, FCH * 1024);
       }
-    }
+    });
     if (ok && !mbar_wait(planbar, 0, 4 * kWaitNs)) {
       atomicOr(a.status, ST_PLAN);
       ok = false;
@@ -456,29 +517,25 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     if (ok) {
       const int nr = pl.n_routed;
       const int N1 = nr * geo.T * geo.P13r;
-      for (int i = first_item(nR, cta, G); i < N1 && ok; i += G) {
-        const int per = geo.T * geo.P13r, s = i / per, rem = i % per, t = rem / geo.P13r, p = rem % geo.P13r;
+      issue_span(cta_span(N1, cta, G), [&](int i) {
+        const int tile = i / geo.P13r, p = i % geo.P13r, s = tile / geo.T, t = tile % geo.T;
         const uint8_t* base = a.r_w13 + (long long)pl.expert[s] * a.r_w13_eb + t * geo.tile13r;
         issue(base + (long long)p * FCH * geo.chunk13r, (uint32_t)(FCH * geo.chunk13r));
-      }
-      const int Q = nr * geo.P2r + geo.P2s;
+      });
+      const int Q = (nr + 1) * geo.P2;
       const int N2 = geo.NT * Q;
-      for (int i = first_item(nR + N1, cta, G); i < N2 && ok; i += G) {
-        const int nt = i / Q, jq = i % Q;
-        const uint8_t* src;
-        uint32_t bytes;
-        if (jq < nr * geo.P2r) {
-          const int s = jq / geo.P2r, p = jq % geo.P2r;
-          const int nch = min(FCH, geo.KC2r - p * FCH);
-          src = a.r_w2 + (long long)pl.expert[s] * a.r_w2_eb + nt * geo.tile2r + (long long)p * FCH * geo.chunk2r;
-          bytes = (uint32_t)(nch * geo.chunk2r);
+      issue_span(cta_span(N2, cta, G), [&](int i) {
+        const int nt = i / Q, jq = i % Q, s = jq / geo.P2, p = jq % geo.P2;
+        if (s < nr) {
+          const int kc = a.I_loc / (RFMT == DSMOE_FMT_FP8 ? 32 : 64);
+          const int nch = min(geo.nch2r, kc - p * geo.nch2r);
+          issue(a.r_w2 + (long long)pl.expert[s] * a.r_w2_eb + nt * geo.tile2r + (long long)p * geo.nch2r * geo.chunk2r,
+                (uint32_t)(nch * geo.chunk2r));
         } else {
-          const int p = jq - nr * geo.P2r, nch = min(FCH, geo.KC2s - p * FCH);
-          src = a.s_w2 + nt * geo.tile2s + (long long)p * FCH * 512;
-          bytes = (uint32_t)(nch * 512);
+          const int nch = min(8, a.I_loc / 32 - p * 8);
+          issue(a.s_w2 + nt * geo.tile2s + (long long)p * 8 * 512, (uint32_t)(nch * 512));
         }
-        issue(src, bytes);
-      }
+      });
     }
     // let every copy this thread issued land before the CTA may exit
     for (int jj = max(0, j - a.nstage); jj < j; ++jj) mbar_wait(&full[jj % a.nstage], (jj / a.nstage) & 1, kWaitNs);
@@ -502,17 +559,27 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     if (m > 0.f && m <= 3.0e38f) {
       int e2;
       frexpf(m, &e2);
-      p = e2 - 15;
+      p = e2 - 15;  // m * 2^-p in [2^14, 2^15): inside f16 range with room to spare
     }
     if (lane == 0) pl.xscale[warp] = ldexpf(1.0f, p);
     const float inv = ldexpf(1.0f, -p);
-    for (int i = lane; i < (a.H / 32) * 4; i += 32) {
-      const int c = i >> 2, tq = i & 3, k0 = 32 * c + 2 * tq;
-      auto pr = [&](int k) {
-        return pack_f16x2(__bfloat162float(xr[k]) * inv, __bfloat162float(xr[k + 1]) * inv);
-      };
-      *reinterpret_cast<uint4*>(xf + (long long)warp * a.xrow + c * 64 + tq * 16) =
-          make_uint4(pr(k0), pr(k0 + 8), pr(k0 + 16), pr(k0 + 24));
+    for (int c = lane; c < a.H / 32; c += 32) {
+      float v[32];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr + 32 * c + 8 * q));
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          v[8 * q + 2 * h] = __uint_as_float(w[h] << 16) * inv;
+          v[8 * q + 2 * h + 1] = __uint_as_float(w[h] & 0xFFFF0000u) * inv;
+        }
+      }
+#pragma unroll
+      for (int tq = 0; tq < 4; ++tq)
+        *reinterpret_cast<uint4*>(xf + (long long)warp * a.xrow + c * 64 + tq * 16) =
+            make_uint4(pack_f16x2(v[2 * tq], v[2 * tq + 1]), pack_f16x2(v[2 * tq + 8], v[2 * tq + 9]),
+                       pack_f16x2(v[2 * tq + 16], v[2 * tq + 17]), pack_f16x2(v[2 * tq + 24], v[2 * tq + 25]));
     }
   }
   for (int e = tid; e < a.E; e += FW * 32) emask[e] = 0u;
@@ -527,7 +594,6 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     shared_wts[b] = 1.0f;
   }
 
-  int j = 0;  // CTA item sequence (same order as the producer)
   auto wait_full = [&](int jj) -> bool {
     if (*(volatile int*)&pl.abort) return false;
     if (!mbar_wait(&full[jj % a.nstage], (jj / a.nstage) & 1, kWaitNs)) {
@@ -544,27 +610,51 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     if (lane == 0) mbar_arrive(&empty[jj % a.nstage]);
   };
 
+  int jbase = 0;  // sequence number of the phase's first item in this CTA (the producer's order)
+
   // ---- phase R: router quarter-rows, then the shared expert's w1|w3 parts
-  for (int i = first_item(0, cta, G); i < nR; i += G, ++j) {
-    if (j % FW != warp) continue;
-    if (!wait_full(j)) break;
-    const uint8_t* stage = ring + (size_t)(j % a.nstage) * FSTAGE;
-    if (i < geo.NR) {
-      router_item(a, stage, i >> 2, i & 3, lane);
-      release(j);
-      __threadfence();
-      __syncwarp();
-      if (lane == 0) {
-        const unsigned done = atomicAdd(&pl.router_done, 1u) + 1;
-        if ((int)done == my_router) pl.gen_a = grid_arrive(a.gbar, G);
+  {
+    const Span run = warp_run(spanR, warp);
+    int cur = -1, seg_first = 0, seg_np = 0, n_router = 0;
+    float acc1[4] = {0.f, 0.f, 0.f, 0.f}, acc3[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint8_t* xrow = xf + (long long)shared_toks[min(lane >> 2, a.B - 1)] * a.xrow;
+    for (int i = run.s; i < run.e; ++i) {
+      const int jj = jbase + 8 * (i - run.s) + warp;
+      if (!wait_full(jj)) break;
+      const uint8_t* stage = ring + (size_t)(jj % a.nstage) * FSTAGE;
+      if (i < geo.NR) {
+        router_item(a, stage, i >> 2, i & 3, lane);
+        ++n_router;
+      } else {
+        const int i2 = i - geo.NR, t = i2 / geo.P13s, p = i2 % geo.P13s;
+        if (t != cur) {
+          if (cur >= 0)
+            w13_flush(a, geo, pl, nR, geo.NR + cur * geo.P13s, geo.P13s, seg_first, seg_np, a.sh_idx, cur, acc1, acc3,
+                      a.B, shared_toks, shared_wts, lane);
+          cur = t;
+          seg_first = i;
+          seg_np = 0;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc1[q] = acc3[q] = 0.f;
+        }
+        w13_accum<DSMOE_FMT_FP8>(a, geo, stage, xrow, a.s_w13 + t * geo.tile13s, p, lane, acc1, acc3);
+        ++seg_np;
       }
-    } else {
-      const int i2 = i - geo.NR, t = i2 / geo.P13s, p = i2 % geo.P13s;
-      w13_item<DSMOE_FMT_FP8>(a, geo, pl, stage, xf, a.s_w13 + t * geo.tile13s, a.sh_idx, t, p, geo.P13s, a.B,
-                              shared_toks, shared_wts, lane);
-      release(j);
+      release(jj);
+      if (i + 1 == min(run.e, geo.NR)) {  // this warp's last router row: count its rows toward barrier A
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) {
+          const unsigned done = atomicAdd(&pl.router_done, (unsigned)n_router) + n_router;
+          if ((int)done == my_router) pl.gen_a = grid_arrive(a.gbar, G);
+        }
+      }
     }
+    if (cur >= 0 && !pl.abort)
+      w13_flush(a, geo, pl, nR, geo.NR + cur * geo.P13s, geo.P13s, seg_first, seg_np, a.sh_idx, cur, acc1, acc3, a.B,
+                shared_toks, shared_wts, lane);
   }
+  jbase += spanR.e - spanR.s;
   __threadfence();
   named_bar_sync(1, FW * 32);
   if (tid == 0 && !pl.abort) {
@@ -575,6 +665,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   }
   named_bar_sync(1, FW * 32);
   if (pl.abort) return;
+  __threadfence();
 
   // ---- plan: identical in every CTA
   if (warp < a.B) {
@@ -703,14 +794,40 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   // ---- phase 1: routed w1|w3
   const int nr = pl.n_routed;
   const int N1 = nr * geo.T * geo.P13r;
-  for (int i = first_item(nR, cta, G); i < N1; i += G, ++j) {
-    if (j % FW != warp) continue;
-    if (!wait_full(j)) break;
-    const uint8_t* stage = ring + (size_t)(j % a.nstage) * FSTAGE;
-    const int per = geo.T * geo.P13r, s = i / per, rem = i % per, t = rem / geo.P13r, p = rem % geo.P13r;
-    const uint8_t* tile_g = a.r_w13 + (long long)pl.expert[s] * a.r_w13_eb + t * geo.tile13r;
-    w13_item<RFMT>(a, geo, pl, stage, xf, tile_g, s, t, p, geo.P13r, pl.ntok[s], pl.tok[s], pl.wt[s], lane);
-    release(j);
+  {
+    const Span span = cta_span(N1, cta, G);
+    const Span run = warp_run(span, warp);
+    int cur = -1, seg_first = 0, seg_np = 0;
+    float acc1[4] = {0.f, 0.f, 0.f, 0.f}, acc3[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int i = run.s; i < run.e; ++i) {
+      const int jj = jbase + 8 * (i - run.s) + warp;
+      if (!wait_full(jj)) break;
+      const uint8_t* stage = ring + (size_t)(jj % a.nstage) * FSTAGE;
+      const int tile = i / geo.P13r, p = i % geo.P13r, s = tile / geo.T, t = tile % geo.T;
+      if (tile != cur) {
+        if (cur >= 0) {
+          const int cs = cur / geo.T;
+          w13_flush(a, geo, pl, N1, cur * geo.P13r, geo.P13r, seg_first, seg_np, cs, cur % geo.T, acc1, acc3,
+                    pl.ntok[cs], pl.tok[cs], pl.wt[cs], lane);
+        }
+        cur = tile;
+        seg_first = i;
+        seg_np = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc1[q] = acc3[q] = 0.f;
+      }
+      const uint8_t* xrow = xf + (long long)pl.tok[s][min(lane >> 2, pl.ntok[s] - 1)] * a.xrow;
+      const uint8_t* tile_g = a.r_w13 + (long long)pl.expert[s] * a.r_w13_eb + t * geo.tile13r;
+      w13_accum<RFMT>(a, geo, stage, xrow, tile_g, p, lane, acc1, acc3);
+      ++seg_np;
+      release(jj);
+    }
+    if (cur >= 0 && !pl.abort) {
+      const int cs = cur / geo.T;
+      w13_flush(a, geo, pl, N1, cur * geo.P13r, geo.P13r, seg_first, seg_np, cs, cur % geo.T, acc1, acc3, pl.ntok[cs],
+                pl.tok[cs], pl.wt[cs], lane);
+    }
+    jbase += span.e - span.s;
   }
   __threadfence();
   named_bar_sync(1, FW * 32);
@@ -723,24 +840,51 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   }
   named_bar_sync(1, FW * 32);
   if (pl.abort) return;
+  __threadfence();
 
-  // ---- phase 2: w2
-  const int Q = nr * geo.P2r + geo.P2s;
-  const int N2 = geo.NT * Q;
-  for (int i = first_item(nR + N1, cta, G); i < N2; i += G, ++j) {
-    if (j % FW != warp) continue;
-    if (!wait_full(j)) break;
-    const uint8_t* stage = ring + (size_t)(j % a.nstage) * FSTAGE;
-    const int nt = i / Q, jq = i % Q;
-    if (jq < nr * geo.P2r) {
-      const int s = jq / geo.P2r, p = jq % geo.P2r, nch = min(FCH, geo.KC2r - p * FCH);
-      const uint8_t* tile_g = a.r_w2 + (long long)pl.expert[s] * a.r_w2_eb + nt * geo.tile2r;
-      w2_item<RFMT>(a, geo, pl, stage, tile_g, s, s, nt, p, nch, jq, Q, lane);
-    } else {
-      const int p = jq - nr * geo.P2r, nch = min(FCH, geo.KC2s - p * FCH);
-      w2_item<DSMOE_FMT_FP8>(a, geo, pl, stage, a.s_w2 + nt * geo.tile2s, nr, a.sh_idx, nt, p, nch, jq, Q, lane);
+  // ---- phase 2: w2 (h operands double-buffered in registers)
+  {
+    const int Q = (nr + 1) * geo.P2;
+    const int N2 = geo.NT * Q;
+    const Span span = cta_span(N2, cta, G);
+    const Span run = warp_run(span, warp);
+    int cur = -1, seg_first = 0, seg_np = 0;
+    float out[4] = {0.f, 0.f, 0.f, 0.f};
+    uint4 hA[8], hB[8];
+    auto step = [&](int i, const uint4(&hb)[8]) -> bool {
+      const int jj = jbase + 8 * (i - run.s) + warp;
+      if (!wait_full(jj)) return false;
+      const uint8_t* stage = ring + (size_t)(jj % a.nstage) * FSTAGE;
+      const int nt = i / Q, jq = i % Q, s = jq / geo.P2, p = jq % geo.P2;
+      if (nt != cur) {
+        if (cur >= 0) w2_flush(a, N2, Q, cur, seg_first, seg_np, out, lane);
+        cur = nt;
+        seg_first = i;
+        seg_np = 0;
+        out[0] = out[1] = out[2] = out[3] = 0.f;
+      }
+      if (s < nr)
+        w2_accum<RFMT>(a, pl, stage, a.r_w2 + (long long)pl.expert[s] * a.r_w2_eb + nt * geo.tile2r, s, p, hb, lane, out);
+      else
+        w2_accum<DSMOE_FMT_FP8>(a, pl, stage, a.s_w2 + nt * geo.tile2s, s, p, hb, lane, out);
+      ++seg_np;
+      release(jj);
+      return true;
+    };
+    auto fetch = [&](int i, uint4(&hb)[8]) {
+      const int jq = i % Q, s = jq / geo.P2;
+      load_h(a, s < nr ? s : a.sh_idx, jq % geo.P2, lane, hb);
+    };
+    if (run.s < run.e) fetch(run.s, hA);
+    for (int i = run.s; i < run.e; i += 2) {
+      if (i + 1 < run.e) fetch(i + 1, hB);
+      if (!step(i, hA)) break;
+      if (i + 1 < run.e) {
+        if (i + 2 < run.e) fetch(i + 2, hA);
+        if (!step(i + 1, hB)) break;
+      }
     }
-    release(j);
+    if (cur >= 0 && !pl.abort) w2_flush(a, N2, Q, cur, seg_first, seg_np, out, lane);
   }
 }
 
@@ -764,18 +908,13 @@ static size_t al2(size_t v) { return (v + 255) & ~size_t(255); }
 // same (zero) words there.
 FusedScratch fused_scratch(int H, int I_loc, int E, int B, int topk, int r_fmt) {
   (void)B;
+  (void)r_fmt;
   B = FMAXB;
   FusedScratch f{};
   const int T = I_loc / 16, NT = H / 16;
-  const int P13s = (H / 32) / FCH, P13r = r_fmt == DSMOE_FMT_FP8 ? (H / 32) / FCH : (H / 64) / FCH;
-  const int KC2s = I_loc / 32, KC2r = r_fmt == DSMOE_FMT_FP8 ? I_loc / 32 : I_loc / 64;
-  const int P2s = (KC2s + FCH - 1) / FCH, P2r = (KC2r + FCH - 1) / FCH;
-  const int P13max_any = (H / 32) / FCH;                       // FP8 parts bound both formats
-  const int P2max_any = (I_loc / 32 + FCH - 1) / FCH;
-  (void)P13s; (void)P13r; (void)P2s; (void)P2r;
   f.slots = B * topk + 1;
-  f.p13max = P13max_any;
-  f.qmax = B * topk * P2max_any + P2max_any;
+  f.p13max = (H / 32) / FCH;                        // FP8 parts per tile bound both formats
+  f.qmax = f.slots * ((I_loc + FK2 - 1) / FK2);     // w2 items per 16 output rows
   size_t o = 0;
   f.gbar = o; o += al2(8);
   f.status = o; o += al2(4);
