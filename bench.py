@@ -37,7 +37,7 @@ NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 
 # algorithmic bytes (weights + scales) per expert and per router (fp32 weight + bias)
-ROUTER_BYTES = E * H * 4 + E * 4
+ROUTER_BYTES = E * H * 4 + E * 4  # at the configured 384 experts; scaled to --experts below
 FP8_W13 = 2 * (H * I + (I // 128) * (H // 128) * 4)
 FP8_W2 = H * I + (H // 128) * (I // 128) * 4
 FP4_W13 = 2 * (H * I // 2 + H * I // 32)
@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=2024)
+    ap.add_argument("--experts", type=int, default=E,
+                    help="routed experts kept resident per layer (default 384; smaller only for profiler runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline sampling")
     return ap.parse_args()
@@ -59,7 +61,7 @@ def parse():
 
 def workload_config(args, world):
     return {"workload": "one FP8 + one FP4 MoE decode layer per step (experts resident, TP over GPUs)",
-            "hidden": H, "inter": I, "experts": E, "topk": TOPK, "shared_experts": 1, "batch": args.batch,
+            "hidden": H, "inter": I, "experts": getattr(args, "experts", E), "topk": TOPK, "shared_experts": 1, "batch": args.batch,
             "score_func": "sigmoid", "route_scale": ROUTE_SCALE, "layers_per_step": ["fp8-block128", "fp4-e2m1-e8m0"],
             "parallelism": f"tp{world}", "l2": "flushed between steps (256 MiB write, outside the timed events)"}
 
@@ -203,10 +205,11 @@ def ours(args):
     gen = torch.Generator(device=dev).manual_seed(args.seed)
     layers = []
     for fmt in ("fp8", "fp4"):
-        m = dsmoe.MoE(H, I, E, TOPK, fmt, "sigmoid", ROUTE_SCALE, rank=rank, world=world, device=dev, max_tokens=B)
-        m.load_router(dsmoe.make_router(E, H, gen, device=dev))
+        NE = args.experts
+        m = dsmoe.MoE(H, I, NE, TOPK, fmt, "sigmoid", ROUTE_SCALE, rank=rank, world=world, device=dev, max_tokens=B)
+        m.load_router(dsmoe.make_router(NE, H, gen, device=dev))
         m.load_shared(dsmoe.make_expert("fp8", H, I, gen, device=dev))
-        for e in range(E):
+        for e in range(NE):
             m.load_expert(e, dsmoe.make_expert(fmt, H, I, gen, device=dev))
         layers.append(m)
     pool = 256
@@ -300,6 +303,8 @@ def ours(args):
         else:
             parts = (("router", ROUTER_BYTES, t_r), ("w13", b13, t_13), ("w2", b2, t_2))
         parts += (("allreduce", 0, statistics.mean(stage[(li, "allreduce")])),)
+        parts = tuple((k, byts - (ROUTER_BYTES - args.experts * (H * 4 + 4) if k in ("router", "layer") else 0), t)
+                      for k, byts, t in parts)
         for k, byts, t in parts:
             kern[f"{nm}_{k}"] = {"us": round(t * 1e3, 2), "bytes": int(byts),
                                  "gbs": round(byts / (t * 1e-3) / 1e9, 1) if byts and t > 0 else None}

@@ -27,7 +27,7 @@ struct FusedScratch {
 FusedScratch fused_scratch(int H, int I_loc, int E, int B, int topk, int r_fmt);
 bool fused_supported(const dsmoe_layer_t* L, int B);
 int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image_mask, void* y, int y_dtype,
-                 int64_t* idx, float* wt, float* scores, uint8_t* ws, cudaStream_t st);
+                 int64_t* idx, float* wt, float* scores, uint8_t* ws, cudaStream_t st, void* const* events);
 
 struct DecodeArgs {
   int H, I_loc, E, B;
@@ -466,16 +466,8 @@ static int moe_decode_impl(const dsmoe_layer_t* L, const void* x, int B, const u
                 w.total);
   uint8_t* ws = (uint8_t*)workspace;
   cudaStream_t st = (cudaStream_t)stream;
-  if (fused_region(L) > 0 && fused_supported(L, B)) {
-    if (events) {
-      cudaEventRecord((cudaEvent_t)events[0], st);
-      cudaEventRecord((cudaEvent_t)events[1], st);
-      cudaEventRecord((cudaEvent_t)events[2], st);
-    }
-    rc = launch_fused(L, x, B, image_mask, y, y_dtype, idx, wt, scores, ws, st);
-    if (events) cudaEventRecord((cudaEvent_t)events[3], st);
-    return rc;
-  }
+  if (fused_region(L) > 0 && fused_supported(L, B))
+    return launch_fused(L, x, B, image_mask, y, y_dtype, idx, wt, scores, ws, st, events);
   RouterArgs ra = router_args(L, x, B, image_mask, idx, wt, scores, ws, w);
   if (events) cudaEventRecord((cudaEvent_t)events[0], st);
   rc = launch_router(ra, true, st);

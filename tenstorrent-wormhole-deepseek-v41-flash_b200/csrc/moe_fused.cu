@@ -928,20 +928,33 @@ FusedScratch fused_scratch(int H, int I_loc, int E, int B, int topk, int r_fmt) 
   return f;
 }
 
+// Per-device constants, looked up once (attribute queries cost microseconds per call).
+struct DevInfo {
+  int sms = 0, optin = 0;
+  bool attr_set[2] = {false, false};
+};
+static DevInfo g_dev[64];
+
+static DevInfo& dev_info() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  DevInfo& d = g_dev[dev & 63];
+  if (d.sms == 0) {
+    cudaDeviceGetAttribute(&d.optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return d;
+}
+
 bool fused_supported(const dsmoe_layer_t* L, int B) {
   if (B < 1 || B > FMAXB || L->n_experts > FEMAX || L->hidden % 512 != 0 || L->hidden > FSTAGE) return false;
-  int dev = 0, optin = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  return fused_smem_bytes(L->hidden, B, L->n_experts, 8) <= (size_t)optin;
+  return fused_smem_bytes(L->hidden, B, L->n_experts, 8) <= (size_t)dev_info().optin;
 }
 
 int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image_mask, void* y, int y_dtype,
-                 int64_t* idx, float* wt, float* scores, uint8_t* ws, cudaStream_t st) {
-  int dev = 0, optin = 0, sms = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+                 int64_t* idx, float* wt, float* scores, uint8_t* ws, cudaStream_t st, void* const* events) {
+  DevInfo& d = dev_info();
+  const int optin = d.optin, sms = d.sms;
   int nstage = 16;
   while (nstage > 8 && fused_smem_bytes(L->hidden, B, L->n_experts, nstage) > (size_t)optin) --nstage;
   const size_t smem = fused_smem_bytes(L->hidden, B, L->n_experts, nstage);
@@ -987,12 +1000,14 @@ int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* im
   a.p13max = f.p13max;
   a.qmax = f.qmax;
 
-  void (*kern)(FusedArgs) = L->routed.fmt == DSMOE_FMT_FP8 ? moe_fused_kernel<DSMOE_FMT_FP8> : moe_fused_kernel<DSMOE_FMT_FP4>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return cuda_status("fused: set smem");
-  int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, FT, smem);
-  DSMOE_REQUIRE(per_sm >= 1, DSMOE_ERR_UNSUPPORTED, "fused: kernel does not fit on an SM");
+  const int fi = L->routed.fmt == DSMOE_FMT_FP8 ? 0 : 1;
+  void (*kern)(FusedArgs) = fi == 0 ? moe_fused_kernel<DSMOE_FMT_FP8> : moe_fused_kernel<DSMOE_FMT_FP4>;
+  if (!d.attr_set[fi]) {
+    // the largest dynamic shared memory any call can ask for; set once per device and format
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess)
+      return cuda_status("fused: set smem");
+    d.attr_set[fi] = true;
+  }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(sms);
   cfg.blockDim = dim3(FT);
@@ -1003,7 +1018,13 @@ int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* im
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (events) {
+    cudaEventRecord((cudaEvent_t)events[0], st);
+    cudaEventRecord((cudaEvent_t)events[1], st);
+    cudaEventRecord((cudaEvent_t)events[2], st);
+  }
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (events) cudaEventRecord((cudaEvent_t)events[3], st);
   if (e != cudaSuccess) {
     set_error("fused launch: %s", cudaGetErrorString(e));
     cudaGetLastError();
