@@ -23,11 +23,14 @@ constexpr int kWarp = 32;
 
 // ------------------------------------------------------------------ packed-store geometry
 // FP8 w1|w3 tile (16 rows of w1 and the same 16 rows of w3): H/32 chunks of 1024 B
-// (w1 512 B, w3 512 B), then the tile's scale rows: H/128 fp32 for w1, H/128 for w3, padded to
-// 16 B.  FP8 w2 n-tile (16 output rows): I_loc/32 chunks of 512 B, then one fp32 scale per chunk.
+// (w1 512 B, w3 512 B), then the tile's fp32 scales, 16 B per 256 K (see fp8_w13_scale_index).  FP8 w2 n-tile (16 output rows): I_loc/32 chunks of 512 B, then one fp32 scale per chunk.
 // FP4 w1|w3 tile: H/64 chunks of 1088 B (w1 512, w3 512, w1 scales 32, w3 scales 32).
 // FP4 w2 n-tile: I_loc/64 chunks of 544 B (512 data, 32 scales).
 __host__ __device__ inline long long pad16(long long b) { return (b + 15) & ~15LL; }
+
+// FP8 w1|w3 tile scales are grouped per 256 K values (16 bytes: s1[2p], s1[2p+1], s3[2p], s3[2p+1])
+// so that one aligned 16-byte copy brings a work item's four scales with its weights.
+__host__ __device__ inline int fp8_w13_scale_index(int kb, int m) { return (kb >> 1) * 4 + 2 * m + (kb & 1); }
 
 __host__ __device__ inline long long fp8_w13_tile_bytes(int H) {
   return (long long)(H / 32) * 1024 + pad16(8LL * (H / 128));

@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(256, 2) moe_w13_kernel(DecodeArgs a) {
         w3v[i] = ld_stream16(ch + 512);
         xv[i] = xrow[(4 * kb + i) * 4];
       }
-      const float s1 = __ldg(sc + kb), s3 = __ldg(sc + KB + kb);
+      const float s1 = __ldg(sc + fp8_w13_scale_index(kb, 0)), s3 = __ldg(sc + fp8_w13_scale_index(kb, 1));
       float t1[4] = {0.f, 0.f, 0.f, 0.f}, t3[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {

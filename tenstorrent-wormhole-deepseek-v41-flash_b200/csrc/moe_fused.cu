@@ -6,23 +6,24 @@
 // launch that streams every weight byte the step needs exactly once.
 //
 // Shape: one CTA per SM (cooperative launch), 8 consumer warps + 1 producer warp.
-//   producer   one thread issues 1-D bulk copies (cp.async.bulk, the TMA engine) of each work
-//              item's weight bytes into a ring of up to 16 x 8.5 KB shared-memory stages,
-//              completion counted on per-stage mbarriers; it runs ahead across phase boundaries
-//              (w2 weights stream in while the grid waits for the last w1|w3 tiles).
-//   consumers  dequantize A fragments from the stage, mma.sync m16n8k16 (f16 x f16 -> fp32)
-//              against the tokens' f16 fragments (shared memory), block scales on fp32 partials.
-// Work distribution: every phase is a flat list of items (4-8.5 KB of packed chunks each); each
-// CTA takes a contiguous span and each consumer warp a contiguous run of that span, so a warp
-// accumulates the consecutive parts of a 16-row tile in registers and publishes one partial per
-// tile it shares with other warps. The last contributor of a tile (counter in the workspace)
-// re-derives the tile's segments from the same deterministic distribution and sums them in order,
-// so results do not depend on timing.
+//   producer   one thread issues 1-D bulk copies (cp.async.bulk, the TMA engine) of everything a
+//              work item reads -- its packed weights, their FP8 scales and, for w2 items, the h
+//              rows of its slot -- into a ring of up to 16 x 8.5 KB shared-memory stages, counted
+//              on one mbarrier per stage. It runs ahead across phase boundaries: w2 weights stream
+//              in while the grid still waits for the last w1|w3 tiles; their h rows follow as soon
+//              as grid barrier B has passed.
+//   consumers  read nothing from global memory on the streaming path: dequantize A fragments from
+//              the stage, mma.sync m16n8k16 (f16 x f16 -> fp32) against the tokens' f16 fragments
+//              (shared memory) or the stage's h rows, block scales on the fp32 partials.
+// Work distribution: every phase is a flat list of items (2-8.5 KB each); each CTA takes a
+// contiguous span and each consumer warp a contiguous run of it, so a warp accumulates the
+// consecutive parts of a 16-row tile in registers and publishes one partial per tile it shares.
+// The last contributor of a tile (counter in the workspace) re-derives the tile's segments from
+// the same deterministic distribution and sums them in order: results do not depend on timing.
 // Phases:
-//   R  router quarter-rows (fp64 accumulation) + the shared expert's w1|w3 parts (no routing
-//      needed); a CTA arrives at grid barrier A when its router rows are done, and the shared-
-//      expert work hides the barrier.
-//   P  every CTA computes the same top-k and slot plan from the router partials.
+//   R  router quarter-rows (fp64) and the shared expert's w1|w3 parts (no routing needed), both
+//      spread over all CTAs; a CTA arrives at grid barrier A when its router rows are done.
+//   P  every CTA computes the same scores, top-k and slot plan (shared memory scratch).
 //   1  routed w1|w3 parts; tile epilogue: clamp / SiLU / up / routing weight -> h (f16).
 //   2  after grid barrier B: w2 parts (16 output rows x slot x 256 K); tile epilogue -> y.
 // Every wait (mbarrier, grid barrier) is bounded by %globaltimer; on expiry the kernel records a
@@ -36,6 +37,9 @@ constexpr int FT = (FW + 1) * 32;      // + producer warp
 constexpr int FCH = 8;                 // packed chunks per w1|w3 item
 constexpr int FSTAGE = FCH * 1088;     // bytes per ring stage (8 FP4 w1|w3 chunks, the largest item)
 constexpr int FK2 = 256;               // K values per w2 item (8 FP8 chunks or 4 FP4 chunks)
+constexpr int FSC13 = FCH * 1024;      // FP8 w1|w3 item: weights, then its 16 B of scales
+constexpr int FSC2 = 4096;             // w2 item: weights (<= 4096 B), then FP8 scales (32 B)
+constexpr int FH2 = 4128;              // w2 item: h rows of the slot's tokens, 512 B each
 constexpr int FMAXB = 8;               // tokens per call
 constexpr int FMAXK = DSMOE_MAX_TOPK;
 constexpr int FMAXS = FMAXB * FMAXK + 1;
@@ -130,7 +134,8 @@ __device__ __forceinline__ Span warp_run(Span cs, int w) {
   const int rs = cs.s + w * L + min(w, r);
   return {rs, rs + L + (w < r ? 1 : 0)};
 }
-// Calls f(first item of the segment - a) for every warp run that intersects [a, b), in order.
+// Phases 1 and 2: item i of n belongs to CTA span / warp run as above. Calls f(first item of the
+// segment - a) for every warp run that intersects [a, b), in order.
 template <class F>
 __device__ __forceinline__ void for_segments(int n, int G, int a, int b, F&& f) {
   int c = (int)(((long long)a * G) / n);
@@ -147,6 +152,28 @@ __device__ __forceinline__ void for_segments(int n, int G, int a, int b, F&& f) 
     }
   }
 }
+// Phase R: CTA c's local list is its router span (over NR) followed by its shared-expert span
+// (over NS); warp runs split the local list. Same contract as for_segments, over the NS items.
+template <class F>
+__device__ __forceinline__ void for_segments_R(int NR, int NS, int G, int a, int b, F&& f) {
+  int c = (int)(((long long)a * G) / NS);
+  while (c + 1 < G && cta_span(NS, c + 1, G).s <= a) ++c;
+  while (c > 0 && cta_span(NS, c, G).s > a) --c;
+  for (; c < G; ++c) {
+    const Span ss = cta_span(NS, c, G);
+    if (ss.s >= b) break;
+    const Span rs = cta_span(NR, c, G);
+    const int rc = rs.e - rs.s;
+    const Span local = {0, rc + ss.e - ss.s};
+    for (int w = 0; w < FW; ++w) {
+      const Span r = warp_run(local, w);
+      const int s0 = max(r.s, rc) - rc + ss.s, s1 = r.e - rc + ss.s;  // the run's shared items
+      if (r.e <= rc || s1 <= a || s0 >= s1) continue;
+      if (s0 >= b) break;
+      f(max(s0, a) - a);
+    }
+  }
+}
 
 __device__ __forceinline__ float fscore(float l, int func) {
   const double d = (double)l;
@@ -156,6 +183,7 @@ __device__ __forceinline__ float fscore(float l, int func) {
 
 __device__ __forceinline__ uint4 lds16(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 __device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+__device__ __forceinline__ float ldsf(const uint8_t* p) { return *reinterpret_cast<const float*>(p); }
 
 __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
 
@@ -197,53 +225,52 @@ __device__ __forceinline__ bool grid_wait(unsigned* gbar, unsigned g0, const uns
   while (ld_acquire_u32(gbar + 1) == g0) {
     if (ld_acquire_u32(status) != 0u) return false;
     if (globaltimer_ns() - t0 > kWaitNs) return false;
-    __nanosleep(64);
+    __nanosleep(32);
   }
   return true;
 }
 
 // ------------------------------------------------------------------ router
 // Router quarter-row: 1/4 of gate_w[r] (H/4 fp32, in the stage) . x[b] for every token, fp64.
+// The token's values come from global memory (L1-resident after the first row); each token's
+// loads are all issued before its multiply-adds.
 __device__ void router_item(const FusedArgs& a, const uint8_t* stage, int r, int q, int lane) {
-  double acc[FMAXB];
-#pragma unroll
-  for (int b = 0; b < FMAXB; ++b) acc[b] = 0.0;
   const float4* wv = reinterpret_cast<const float4*>(stage);
-  const int n4 = a.H / 16;  // float4 per quarter
-  for (int f = lane; f < n4; f += 32) {
-    const float4 w = wv[f];
-    const int k = q * (a.H / 4) + 4 * f;
+  const int n4 = a.H / 16;  // float4 per quarter (<= 512 for H <= 8192)
+  for (int b = 0; b < a.B; ++b) {
+    const __nv_bfloat16* xr = a.x + (long long)b * a.H + q * (a.H / 4);
+    uint2 xv[16];
 #pragma unroll
-    for (int b = 0; b < FMAXB; ++b) {
-      if (b < a.B) {
-        const uint2 xv = __ldg(reinterpret_cast<const uint2*>(a.x + (long long)b * a.H + k));
-        acc[b] = fma((double)__uint_as_float(xv.x << 16), (double)w.x, acc[b]);
-        acc[b] = fma((double)__uint_as_float(xv.x & 0xFFFF0000u), (double)w.y, acc[b]);
-        acc[b] = fma((double)__uint_as_float(xv.y << 16), (double)w.z, acc[b]);
-        acc[b] = fma((double)__uint_as_float(xv.y & 0xFFFF0000u), (double)w.w, acc[b]);
+    for (int it = 0; it < 16; ++it) {
+      const int f = lane + 32 * it;
+      if (f < n4) xv[it] = __ldg(reinterpret_cast<const uint2*>(xr + 4 * f));
+    }
+    double acc = 0.0;
+#pragma unroll
+    for (int it = 0; it < 16; ++it) {
+      const int f = lane + 32 * it;
+      if (f < n4) {
+        const float4 w = wv[f];
+        acc = fma((double)__uint_as_float(xv[it].x << 16), (double)w.x, acc);
+        acc = fma((double)__uint_as_float(xv[it].x & 0xFFFF0000u), (double)w.y, acc);
+        acc = fma((double)__uint_as_float(xv[it].y << 16), (double)w.z, acc);
+        acc = fma((double)__uint_as_float(xv[it].y & 0xFFFF0000u), (double)w.w, acc);
       }
     }
-  }
-#pragma unroll
-  for (int b = 0; b < FMAXB; ++b) {
-    if (b < a.B) {
-      const double v = warp_sum_d(acc[b]);
-      if (lane == 0) a.rl[((long long)b * a.E + r) * 4 + q] = v;
-    }
+    acc = warp_sum_d(acc);
+    if (lane == 0) a.rl[((long long)b * a.E + r) * 4 + q] = acc;
   }
 }
 
 // ------------------------------------------------------------------ w1|w3
-// One item (8 chunks of a 16-row tile, part p) accumulated into acc1 / acc3.
+// One item (8 chunks of a 16-row tile, part p) accumulated into acc1 / acc3. Scales come with the
+// weights: FP8 in the 16 bytes after them, FP4 inside each chunk.
 template <int FMT>
-__device__ __forceinline__ void w13_accum(const FusedArgs& a, const Geo& G, const uint8_t* stage, const uint8_t* xrow,
-                                          const uint8_t* tile_g, int p, int lane, float (&acc1)[4], float (&acc3)[4]) {
+__device__ __forceinline__ void w13_accum(const uint8_t* stage, const uint8_t* xrow, int p, int lane, float (&acc1)[4],
+                                          float (&acc3)[4]) {
   const int g = lane >> 2, tq = lane & 3;
   float t1[4] = {0.f, 0.f, 0.f, 0.f}, t3[4] = {0.f, 0.f, 0.f, 0.f};
   if (FMT == DSMOE_FMT_FP8) {
-    const float* sc = reinterpret_cast<const float*>(tile_g + (long long)(a.H / 32) * 1024);
-    const float s1a = __ldg(sc + 2 * p), s1b = __ldg(sc + 2 * p + 1);
-    const float s3a = __ldg(sc + G.KB + 2 * p), s3b = __ldg(sc + G.KB + 2 * p + 1);
 #pragma unroll
     for (int c = 0; c < FCH; ++c) {
       const int gc = p * FCH + c;
@@ -255,12 +282,10 @@ __device__ __forceinline__ void w13_accum(const FusedArgs& a, const Geo& G, cons
       a_frag_fp8(A, A3.x, A3.y); mma16816(t3, A, X.x, X.y);
       a_frag_fp8(A, A1.z, A1.w); mma16816(t1, A, X.z, X.w);
       a_frag_fp8(A, A3.z, A3.w); mma16816(t3, A, X.z, X.w);
-      if (c == 3) {
-        fma4s(acc1, t1, s1a);
-        fma4s(acc3, t3, s3a);
-      } else if (c == 7) {
-        fma4s(acc1, t1, s1b);
-        fma4s(acc3, t3, s3b);
+      if ((c & 3) == 3) {
+        const int h = c >> 2;  // 128-K block within the item
+        fma4s(acc1, t1, ldsf(stage + FSC13 + 4 * fp8_w13_scale_index(h, 0)));
+        fma4s(acc3, t3, ldsf(stage + FSC13 + 4 * fp8_w13_scale_index(h, 1)));
       }
     }
   } else {
@@ -305,18 +330,20 @@ __device__ __forceinline__ void w13_epilogue(const FusedArgs& a, const FPlan& pl
   }
 }
 
-// A warp's contribution to one tile ends: publish it, or finish the tile if it is complete.
-// [a0, a0 + P) are the tile's items in the phase (n items); the warp covered seg_np of them from seg_first.
-__device__ void w13_flush(const FusedArgs& a, const Geo& G, const FPlan& pl, int n, int a0, int P, int seg_first,
-                          int seg_np, int sidx, int t, const float (&acc1)[4], const float (&acc3)[4], int ntok,
-                          const int* toks, const float* wts, int lane) {
+// A warp's contribution to one tile ends: publish it, or finish the tile if the warp covered all
+// of it. seg_rel = the segment's first item minus the tile's first item. `segs` enumerates the
+// tile's segments (same order everywhere) for the last contributor.
+template <class Segs>
+__device__ void w13_flush(const FusedArgs& a, const Geo& G, const FPlan& pl, int P, int seg_rel, int seg_np, int sidx,
+                          int t, const float (&acc1)[4], const float (&acc3)[4], int ntok, const int* toks,
+                          const float* wts, int lane, Segs&& segs) {
   float s[8] = {acc1[0], acc1[1], acc1[2], acc1[3], acc3[0], acc3[1], acc3[2], acc3[3]};
   if (seg_np == P) {
     w13_epilogue(a, pl, sidx, t, s, ntok, toks, wts, lane);
     return;
   }
   float* base = a.p13 + (((long long)sidx * G.T + t) * a.p13max) * 32 * 8;
-  float* dst = base + ((long long)(seg_first - a0) * 32 + lane) * 8;
+  float* dst = base + ((long long)seg_rel * 32 + lane) * 8;
   *reinterpret_cast<float4*>(dst) = make_float4(s[0], s[1], s[2], s[3]);
   *reinterpret_cast<float4*>(dst + 4) = make_float4(s[4], s[5], s[6], s[7]);
   __threadfence();
@@ -328,7 +355,7 @@ __device__ void w13_flush(const FusedArgs& a, const Geo& G, const FPlan& pl, int
   __threadfence();
 #pragma unroll
   for (int j = 0; j < 8; ++j) s[j] = 0.f;
-  for_segments(n, gridDim.x, a0, a0 + P, [&](int q) {
+  segs([&](int q) {
     const float* src = base + ((long long)q * 32 + lane) * 8;
     const uint4 v0 = ld_cg16(src), v1 = ld_cg16(src + 4);
     s[0] += __uint_as_float(v0.x); s[1] += __uint_as_float(v0.y);
@@ -341,49 +368,42 @@ __device__ void w13_flush(const FusedArgs& a, const Geo& G, const FPlan& pl, int
 }
 
 // ------------------------------------------------------------------ w2
-// The 8 k32 blocks of h this lane feeds to one w2 item (slot row sidx*8+g, K range p*256..).
-__device__ __forceinline__ void load_h(const FusedArgs& a, int sidx, int p, int lane, uint4 (&hb)[8]) {
-  const int g = lane >> 2, tq = lane & 3;
-  const int kc = a.I_loc / 32;
-  const uint8_t* hrow = reinterpret_cast<const uint8_t*>(a.hf + (long long)(sidx * 8 + g) * a.I_loc) + tq * 16;
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-    if (p * 8 + i < kc) hb[i] = ld_cg16(hrow + (long long)(p * 8 + i) * 64);
-}
-
-// One w2 item of slot s accumulated into out[] (token columns: rows g, g+8 x tokens 2tq, 2tq+1).
+// One w2 item of slot s (weights, FP8 scales and the slot's h rows all in the stage) accumulated
+// into out[] in token columns: rows g, g+8 x tokens 2tq, 2tq+1.
 template <int FMT>
-__device__ __forceinline__ void w2_accum(const FusedArgs& a, const FPlan& pl, const uint8_t* stage, const uint8_t* tile_g,
-                                         int s, int p, const uint4 (&hb)[8], int lane, float (&out)[4]) {
+__device__ __forceinline__ void w2_accum(const FusedArgs& a, const FPlan& pl, const uint8_t* stage, int s, int p,
+                                         int lane, float (&out)[4]) {
   const int g = lane >> 2, tq = lane & 3;
+  const uint8_t* hrow = stage + FH2 + min(g, pl.ntok[s] - 1) * 512 + tq * 16;
   float acc[4] = {0.f, 0.f, 0.f, 0.f}, tt[4] = {0.f, 0.f, 0.f, 0.f};
   if (FMT == DSMOE_FMT_FP8) {
-    const int KC = a.I_loc / 32;
-    const float* sc = reinterpret_cast<const float*>(tile_g + (long long)KC * 512);
+    const int nch = min(8, a.I_loc / 32 - p * 8);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      if (p * 8 + i < KC) {
+      if (i < nch) {
         const uint4 A0 = lds16(stage + i * 512 + lane * 16);
+        const uint4 hb = lds16(hrow + i * 64);
         uint32_t A[4];
-        a_frag_fp8(A, A0.x, A0.y); mma16816(tt, A, hb[i].x, hb[i].y);
-        a_frag_fp8(A, A0.z, A0.w); mma16816(tt, A, hb[i].z, hb[i].w);
-        fma4s(acc, tt, __ldg(sc + p * 8 + i));
+        a_frag_fp8(A, A0.x, A0.y); mma16816(tt, A, hb.x, hb.y);
+        a_frag_fp8(A, A0.z, A0.w); mma16816(tt, A, hb.z, hb.w);
+        fma4s(acc, tt, ldsf(stage + FSC2 + 4 * i));
       }
     }
   } else {
-    const int KC = a.I_loc / 64;
+    const int nch = min(4, a.I_loc / 64 - p * 4);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      if (p * 4 + i < KC) {
+      if (i < nch) {
         const uint8_t* ch = stage + i * 544;
         const uint4 A0 = lds16(ch + lane * 16);
         const uint32_t S = lds32(ch + 512 + 4 * g);
+        const uint4 h0 = lds16(hrow + (2 * i) * 64), h1 = lds16(hrow + (2 * i + 1) * 64);
         uint32_t A[4];
-        a_frag_fp4(A, A0.x); mma16816(tt, A, hb[2 * i].x, hb[2 * i].y);
-        a_frag_fp4(A, A0.y); mma16816(tt, A, hb[2 * i].z, hb[2 * i].w);
+        a_frag_fp4(A, A0.x); mma16816(tt, A, h0.x, h0.y);
+        a_frag_fp4(A, A0.y); mma16816(tt, A, h0.z, h0.w);
         fma4r(acc, tt, e8m0_to_f32(S), e8m0_to_f32(S >> 16));
-        a_frag_fp4(A, A0.z); mma16816(tt, A, hb[2 * i + 1].x, hb[2 * i + 1].y);
-        a_frag_fp4(A, A0.w); mma16816(tt, A, hb[2 * i + 1].z, hb[2 * i + 1].w);
+        a_frag_fp4(A, A0.z); mma16816(tt, A, h1.x, h1.y);
+        a_frag_fp4(A, A0.w); mma16816(tt, A, h1.z, h1.w);
         fma4r(acc, tt, e8m0_to_f32(S >> 8), e8m0_to_f32(S >> 24));
       }
     }
@@ -453,23 +473,24 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   uint8_t* xf = ring + (size_t)a.nstage * FSTAGE;
   uint64_t* full = reinterpret_cast<uint64_t*>(xf + (size_t)a.B * a.xrow);
   uint64_t* empty = full + a.nstage;
-  uint64_t* planbar = empty + a.nstage;
+  uint64_t* planbar = empty + a.nstage;  // [0] plan ready, [1] grid barrier B passed
   FPlan& pl = *reinterpret_cast<FPlan*>(planbar + 2);
   unsigned* emask = reinterpret_cast<unsigned*>(&pl + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int G = gridDim.x, cta = blockIdx.x;
   const Geo geo = make_geo(a);
-  const int nR = geo.NR + geo.NS;
-  const Span spanR = cta_span(nR, cta, G);
-  const int my_router = max(0, min(spanR.e, geo.NR) - spanR.s);
+  const Span rspan = cta_span(geo.NR, cta, G), sspan = cta_span(geo.NS, cta, G);
+  const int my_router = rspan.e - rspan.s;
+  const Span localR = {0, my_router + sspan.e - sspan.s};  // phase R: router part, then shared part
 
   if (tid == 0) {
     for (int s = 0; s < a.nstage; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(planbar, 1);
+    mbar_init(&planbar[0], 1);
+    mbar_init(&planbar[1], 1);
     pl.router_done = 0;
     pl.abort = 0;
     fence_mbar_init();
@@ -481,19 +502,50 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     if (lane != 0) return;
     int j = 0;
     bool ok = true;
-    auto issue = [&](const void* src, uint32_t bytes) {
-      if (!ok) return;
-      const int s = j % a.nstage, k = j / a.nstage;
-      if (k > 0 && !mbar_wait(&empty[s], (k - 1) & 1, kWaitNs)) {
-        atomicOr(a.status, ST_EMPTY);
+    // w2 items issued before grid barrier B get their h rows later: (stage, slot, part)
+    int def_n = 0, def_stage[16], def_slot[16], def_p[16];
+    bool h_open = false;
+    int j2 = 0x7FFFFFFF;  // sequence number of the first w2 item
+    auto copy_h = [&](int s, int slot, int p) {
+      const int sidx = slot < pl.n_routed ? slot : a.sh_idx;
+      const uint32_t hb = (uint32_t)(min(FK2, a.I_loc - p * FK2) * 2);
+      for (int c = 0; c < pl.ntok[slot]; ++c)
+        bulk_g2s(ring + (size_t)s * FSTAGE + FH2 + c * 512,
+                 a.hf + (long long)(sidx * 8 + c) * a.I_loc + (long long)p * FK2, hb, &full[s]);
+    };
+    auto open_h = [&]() {  // grid barrier B passed: h is complete; send the deferred h rows
+      if (h_open || !ok) return;
+      if (!mbar_wait(&planbar[1], 0, 4 * kWaitNs)) {
+        atomicOr(a.status, ST_PLAN);
         ok = false;
         return;
       }
-      mbar_expect_tx(&full[s], bytes);
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      for (int d = 0; d < def_n; ++d) copy_h(def_stage[d], def_slot[d], def_p[d]);
+      h_open = true;
+    };
+    auto acquire = [&](int& s) -> bool {  // the next stage, free
+      s = j % a.nstage;
+      const int k = j / a.nstage;
+      if (k > 0) {
+        if (j - a.nstage >= j2) open_h();  // that stage's last occupant was a w2 item
+        if (!ok) return false;
+        if (!mbar_wait(&empty[s], (k - 1) & 1, kWaitNs)) {
+          atomicOr(a.status, ST_EMPTY);
+          ok = false;
+          return false;
+        }
+      }
+      return true;
+    };
+    auto issue = [&](const void* src, uint32_t bytes, const void* src2, uint32_t bytes2) {
+      int s;
+      if (!ok || !acquire(s)) return;
+      mbar_expect_tx(&full[s], bytes + bytes2);
       bulk_g2s(ring + (size_t)s * FSTAGE, src, bytes, &full[s]);
+      if (bytes2) bulk_g2s(ring + (size_t)s * FSTAGE + (bytes == FSC13 ? FSC13 : FSC2), src2, bytes2, &full[s]);
       ++j;
     };
-    // items of a CTA span in the consumers' order: the k-th item of every warp run, warp by warp
     auto issue_span = [&](Span cs, auto&& item) {
       const int L = (cs.e - cs.s + FW - 1) / FW;
       for (int k = 0; k < L && ok; ++k)
@@ -502,15 +554,17 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
           if (r.s + k < r.e) item(r.s + k);
         }
     };
-    issue_span(spanR, [&](int i) {
-      if (i < geo.NR) {
-        issue(a.wg + (long long)(i >> 2) * a.H + (i & 3) * (a.H / 4), (uint32_t)a.H);
+    issue_span(localR, [&](int li) {
+      if (li < my_router) {
+        const int i = rspan.s + li;
+        issue(a.wg + (long long)(i >> 2) * a.H + (i & 3) * (a.H / 4), (uint32_t)a.H, nullptr, 0);
       } else {
-        const int i2 = i - geo.NR, t = i2 / geo.P13s, p = i2 % geo.P13s;
-        issue(a.s_w13 + t * geo.tile13s + (long long)p * FCH * 1024, FCH * 1024);
+        const int i = sspan.s + li - my_router, t = i / geo.P13s, p = i % geo.P13s;
+        const uint8_t* tile = a.s_w13 + t * geo.tile13s;
+        issue(tile + (long long)p * FSC13, FSC13, tile + (long long)(a.H / 32) * 1024 + 16 * p, 16);
       }
     });
-    if (ok && !mbar_wait(planbar, 0, 4 * kWaitNs)) {
+    if (ok && !mbar_wait(&planbar[0], 0, 4 * kWaitNs)) {
       atomicOr(a.status, ST_PLAN);
       ok = false;
     }
@@ -520,22 +574,48 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       issue_span(cta_span(N1, cta, G), [&](int i) {
         const int tile = i / geo.P13r, p = i % geo.P13r, s = tile / geo.T, t = tile % geo.T;
         const uint8_t* base = a.r_w13 + (long long)pl.expert[s] * a.r_w13_eb + t * geo.tile13r;
-        issue(base + (long long)p * FCH * geo.chunk13r, (uint32_t)(FCH * geo.chunk13r));
+        if (RFMT == DSMOE_FMT_FP8)
+          issue(base + (long long)p * FSC13, FSC13, base + (long long)(a.H / 32) * 1024 + 16 * p, 16);
+        else
+          issue(base + (long long)p * FCH * 1088, FCH * 1088, nullptr, 0);
       });
       const int Q = (nr + 1) * geo.P2;
       const int N2 = geo.NT * Q;
+      j2 = j;
       issue_span(cta_span(N2, cta, G), [&](int i) {
         const int nt = i / Q, jq = i % Q, s = jq / geo.P2, p = jq % geo.P2;
-        if (s < nr) {
-          const int kc = a.I_loc / (RFMT == DSMOE_FMT_FP8 ? 32 : 64);
-          const int nch = min(geo.nch2r, kc - p * geo.nch2r);
-          issue(a.r_w2 + (long long)pl.expert[s] * a.r_w2_eb + nt * geo.tile2r + (long long)p * geo.nch2r * geo.chunk2r,
-                (uint32_t)(nch * geo.chunk2r));
+        int st;
+        if (!ok || !acquire(st)) return;
+        const uint32_t hbytes = (uint32_t)(pl.ntok[s] * min(FK2, a.I_loc - p * FK2) * 2);
+        uint32_t wbytes, sbytes = 0;
+        const uint8_t *wsrc, *ssrc = nullptr;
+        if (s < nr && RFMT == DSMOE_FMT_FP4) {
+          const int nch = min(4, a.I_loc / 64 - p * 4);
+          wsrc = a.r_w2 + (long long)pl.expert[s] * a.r_w2_eb + nt * geo.tile2r + (long long)p * 4 * 544;
+          wbytes = (uint32_t)(nch * 544);
         } else {
-          const int nch = min(8, a.I_loc / 32 - p * 8);
-          issue(a.s_w2 + nt * geo.tile2s + (long long)p * 8 * 512, (uint32_t)(nch * 512));
+          const uint8_t* tile = s < nr ? a.r_w2 + (long long)pl.expert[s] * a.r_w2_eb + nt * geo.tile2r
+                                       : a.s_w2 + nt * geo.tile2s;
+          const int kc = a.I_loc / 32, nch = min(8, kc - p * 8);
+          wsrc = tile + (long long)p * 8 * 512;
+          wbytes = (uint32_t)(nch * 512);
+          ssrc = tile + (long long)kc * 512 + p * 32;
+          sbytes = (uint32_t)(((nch + 3) / 4) * 16);
         }
+        mbar_expect_tx(&full[st], wbytes + sbytes + hbytes);
+        bulk_g2s(ring + (size_t)st * FSTAGE, wsrc, wbytes, &full[st]);
+        if (sbytes) bulk_g2s(ring + (size_t)st * FSTAGE + FSC2, ssrc, sbytes, &full[st]);
+        if (h_open) {
+          copy_h(st, s, p);
+        } else {
+          def_stage[def_n] = st;
+          def_slot[def_n] = s;
+          def_p[def_n] = p;
+          ++def_n;
+        }
+        ++j;
       });
+      open_h();
     }
     // let every copy this thread issued land before the CTA may exit
     for (int jj = max(0, j - a.nstage); jj < j; ++jj) mbar_wait(&full[jj % a.nstage], (jj / a.nstage) & 1, kWaitNs);
@@ -543,16 +623,35 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   }
 
   // ================================================================ consumer warps
-  // token fragments: amax -> power-of-2 pre-scale -> f16 fragments in shared memory
+  // token fragments: amax -> power-of-2 pre-scale -> f16 fragments in shared memory (one pass,
+  // every load of the row in flight at once)
   if (warp < a.B) {
     const __nv_bfloat16* xr = a.x + (long long)warp * a.H;
+    const int nchunk = a.H / 32;  // <= 256: at most 8 chunks of 32 values per lane
     float m = 0.f;
-    for (int i = lane * 8; i < a.H; i += 256) {
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr + i));
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int h = 0; h < 4; ++h)
-        m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w[h] << 16)), fabsf(__uint_as_float(w[h] & 0xFFFF0000u))));
+    for (int k0 = 0; k0 < 8; k0 += 4) {  // 4 chunks (16 loads) in flight per batch
+      uint4 u[4][4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int c = lane + 32 * (k0 + k);
+        if (c < nchunk) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) u[k][q] = __ldg(reinterpret_cast<const uint4*>(xr + 32 * c + 8 * q));
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (lane + 32 * (k0 + k) < nchunk) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t w[4] = {u[k][q].x, u[k][q].y, u[k][q].z, u[k][q].w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h)
+              m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w[h] << 16)), fabsf(__uint_as_float(w[h] & 0xFFFF0000u))));
+          }
+        }
+      }
     }
     m = warp_max(m);
     int p = 0;
@@ -563,23 +662,38 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     }
     if (lane == 0) pl.xscale[warp] = ldexpf(1.0f, p);
     const float inv = ldexpf(1.0f, -p);
-    for (int c = lane; c < a.H / 32; c += 32) {
-      float v[32];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr + 32 * c + 8 * q));
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    for (int k0 = 0; k0 < 8; k0 += 4) {  // second pass over the (now cached) row: convert
+      uint4 u[4][4];
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          v[8 * q + 2 * h] = __uint_as_float(w[h] << 16) * inv;
-          v[8 * q + 2 * h + 1] = __uint_as_float(w[h] & 0xFFFF0000u) * inv;
+      for (int k = 0; k < 4; ++k) {
+        const int c = lane + 32 * (k0 + k);
+        if (c < nchunk) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) u[k][q] = __ldg(reinterpret_cast<const uint4*>(xr + 32 * c + 8 * q));
         }
       }
 #pragma unroll
-      for (int tq = 0; tq < 4; ++tq)
-        *reinterpret_cast<uint4*>(xf + (long long)warp * a.xrow + c * 64 + tq * 16) =
-            make_uint4(pack_f16x2(v[2 * tq], v[2 * tq + 1]), pack_f16x2(v[2 * tq + 8], v[2 * tq + 9]),
-                       pack_f16x2(v[2 * tq + 16], v[2 * tq + 17]), pack_f16x2(v[2 * tq + 24], v[2 * tq + 25]));
+      for (int k = 0; k < 4; ++k) {
+        const int c = lane + 32 * (k0 + k);
+        if (c < nchunk) {
+          float v[32];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t w[4] = {u[k][q].x, u[k][q].y, u[k][q].z, u[k][q].w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              v[8 * q + 2 * h] = __uint_as_float(w[h] << 16) * inv;
+              v[8 * q + 2 * h + 1] = __uint_as_float(w[h] & 0xFFFF0000u) * inv;
+            }
+          }
+#pragma unroll
+          for (int tq = 0; tq < 4; ++tq)
+            *reinterpret_cast<uint4*>(xf + (long long)warp * a.xrow + c * 64 + tq * 16) =
+                make_uint4(pack_f16x2(v[2 * tq], v[2 * tq + 1]), pack_f16x2(v[2 * tq + 8], v[2 * tq + 9]),
+                           pack_f16x2(v[2 * tq + 16], v[2 * tq + 17]), pack_f16x2(v[2 * tq + 24], v[2 * tq + 25]));
+        }
+      }
     }
   }
   for (int e = tid; e < a.E; e += FW * 32) emask[e] = 0u;
@@ -614,34 +728,39 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
 
   // ---- phase R: router quarter-rows, then the shared expert's w1|w3 parts
   {
-    const Span run = warp_run(spanR, warp);
+    const Span run = warp_run(localR, warp);
     int cur = -1, seg_first = 0, seg_np = 0, n_router = 0;
     float acc1[4] = {0.f, 0.f, 0.f, 0.f}, acc3[4] = {0.f, 0.f, 0.f, 0.f};
     const uint8_t* xrow = xf + (long long)shared_toks[min(lane >> 2, a.B - 1)] * a.xrow;
-    for (int i = run.s; i < run.e; ++i) {
-      const int jj = jbase + 8 * (i - run.s) + warp;
+    auto flush = [&]() {
+      w13_flush(a, geo, pl, geo.P13s, seg_first - cur * geo.P13s, seg_np, a.sh_idx, cur, acc1, acc3, a.B, shared_toks,
+                shared_wts, lane, [&](auto&& f) {
+                  for_segments_R(geo.NR, geo.NS, G, cur * geo.P13s, (cur + 1) * geo.P13s, f);
+                });
+    };
+    for (int li = run.s; li < run.e; ++li) {
+      const int jj = jbase + 8 * (li - run.s) + warp;
       if (!wait_full(jj)) break;
       const uint8_t* stage = ring + (size_t)(jj % a.nstage) * FSTAGE;
-      if (i < geo.NR) {
+      if (li < my_router) {
+        const int i = rspan.s + li;
         router_item(a, stage, i >> 2, i & 3, lane);
         ++n_router;
       } else {
-        const int i2 = i - geo.NR, t = i2 / geo.P13s, p = i2 % geo.P13s;
+        const int i = sspan.s + li - my_router, t = i / geo.P13s, p = i % geo.P13s;
         if (t != cur) {
-          if (cur >= 0)
-            w13_flush(a, geo, pl, nR, geo.NR + cur * geo.P13s, geo.P13s, seg_first, seg_np, a.sh_idx, cur, acc1, acc3,
-                      a.B, shared_toks, shared_wts, lane);
+          if (cur >= 0) flush();
           cur = t;
           seg_first = i;
           seg_np = 0;
 #pragma unroll
           for (int q = 0; q < 4; ++q) acc1[q] = acc3[q] = 0.f;
         }
-        w13_accum<DSMOE_FMT_FP8>(a, geo, stage, xrow, a.s_w13 + t * geo.tile13s, p, lane, acc1, acc3);
+        w13_accum<DSMOE_FMT_FP8>(stage, xrow, p, lane, acc1, acc3);
         ++seg_np;
       }
       release(jj);
-      if (i + 1 == min(run.e, geo.NR)) {  // this warp's last router row: count its rows toward barrier A
+      if (li + 1 == min(run.e, my_router)) {  // this warp's last router row: count its rows toward barrier A
         __threadfence();
         __syncwarp();
         if (lane == 0) {
@@ -650,11 +769,9 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
         }
       }
     }
-    if (cur >= 0 && !pl.abort)
-      w13_flush(a, geo, pl, nR, geo.NR + cur * geo.P13s, geo.P13s, seg_first, seg_np, a.sh_idx, cur, acc1, acc3, a.B,
-                shared_toks, shared_wts, lane);
+    if (cur >= 0 && !pl.abort) flush();
   }
-  jbase += spanR.e - spanR.s;
+  jbase += localR.e;
   __threadfence();
   named_bar_sync(1, FW * 32);
   if (tid == 0 && !pl.abort) {
@@ -667,70 +784,101 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   if (pl.abort) return;
   __threadfence();
 
-  // ---- plan: identical in every CTA
-  if (warp < a.B) {
-    const int b = warp;
-    float scv[FEMAX / 32], biv[FEMAX / 32];
-    const bool vl = a.bias_vl != nullptr && a.image_mask != nullptr && a.image_mask[b] != 0;
-    const float* bias = vl ? a.bias_vl : a.bias;
+  // ---- plan: identical in every CTA. The ring is idle here (phase R consumed, phase 1 not yet
+  // issued), so its first bytes hold the scores.
+  {
+    float* sc_s = reinterpret_cast<float*>(ring);    // [B][E] scores
+    float* bi_s = sc_s + a.B * a.E;                  // [B][E] scores + selection bias
+    const int n = a.B * a.E;
+    for (int i0 = tid; i0 < n; i0 += 4 * FW * 32) {
+      double l4[4][4];
+      float bs[4];
 #pragma unroll
-    for (int i = 0; i < FEMAX / 32; ++i) {
-      const int e = lane + 32 * i;
-      scv[i] = 0.f;
-      biv[i] = -INFINITY;
-      if (e < a.E) {
-        const double* r4 = a.rl + ((long long)b * a.E + e) * 4;
-        const double l = ((ld_cg_f64(r4) + ld_cg_f64(r4 + 1)) + ld_cg_f64(r4 + 2)) + ld_cg_f64(r4 + 3);
-        const float sc = fscore(__double2float_rn(l), a.score_func);
-        scv[i] = sc;
-        biv[i] = sc + bias[e];
-        if (cta == 0 && a.scores) a.scores[(long long)b * a.E + e] = sc;
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * FW * 32;
+        if (i < n) {
+          const int b = i / a.E, e = i % a.E;
+          const double* r4 = a.rl + (long long)i * 4;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) l4[u][q] = ld_cg_f64(r4 + q);
+          const bool vl = a.bias_vl != nullptr && a.image_mask != nullptr && a.image_mask[b] != 0;
+          bs[u] = (vl ? a.bias_vl : a.bias)[e];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * FW * 32;
+        if (i < n) {
+          const float sc = fscore(__double2float_rn(((l4[u][0] + l4[u][1]) + l4[u][2]) + l4[u][3]), a.score_func);
+          sc_s[i] = sc;
+          bi_s[i] = sc + bs[u];
+        }
       }
     }
-    float tot = 0.f;
-    for (int r = 0; r < a.topk; ++r) {
-      float best = -INFINITY;
-      int bi = 0x7FFFFFFF;
+    named_bar_sync(1, FW * 32);
+    if (cta == 0 && a.scores)
+      for (int i = tid; i < n; i += FW * 32) a.scores[i] = sc_s[i];
+    if (warp < a.B) {  // top-k of token `warp`: lane-local top-k lists, then k rounds of warp argmax
+      const int b = warp;
+      float tv[FMAXK];
+      int ti[FMAXK];
 #pragma unroll
-      for (int i = 0; i < FEMAX / 32; ++i) {
-        const int e = lane + 32 * i;
-        if (e < a.E && (biv[i] > best || (biv[i] == best && e < bi))) {
-          best = biv[i];
-          bi = e;
+      for (int r = 0; r < FMAXK; ++r) {
+        tv[r] = -INFINITY;
+        ti[r] = 0x7FFFFFFF;
+      }
+      for (int e = lane; e < a.E; e += 32) {
+        float v = bi_s[b * a.E + e];
+        int vi = e;
+#pragma unroll
+        for (int r = 0; r < FMAXK; ++r) {  // insertion: larger value first, lower index on ties
+          if (v > tv[r] || (v == tv[r] && vi < ti[r])) {
+            const float ov = tv[r];
+            const int oi = ti[r];
+            tv[r] = v;
+            ti[r] = vi;
+            v = ov;
+            vi = oi;
+          }
         }
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > best || (ov == best && oi < bi)) {
-          best = ov;
-          bi = oi;
-        }
-      }
-      if (bi == 0x7FFFFFFF) bi = 0;
-      float scw = 0.f;
-#pragma unroll
-      for (int i = 0; i < FEMAX / 32; ++i) {
-        if (lane + 32 * i == bi) {
-          scw = scv[i];
-          biv[i] = -INFINITY;
-        }
-      }
-      scw = __shfl_sync(0xffffffffu, scw, bi & 31);
-      if (lane == 0) {
-        pl.sel[b][r] = bi;
-        pl.selw[b][r] = scw;
-      }
-      tot += scw;
-    }
-    if (lane == 0) {
+      float tot = 0.f;
       for (int r = 0; r < a.topk; ++r) {
-        const float w = pl.selw[b][r] / (tot + 1e-20f) * a.route_scale;
-        pl.selw[b][r] = w;
+        float best = tv[0];
+        int bi = ti[0];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (ov > best || (ov == best && oi < bi)) {
+            best = ov;
+            bi = oi;
+          }
+        }
+        if (bi == 0x7FFFFFFF) bi = 0;
+        if (ti[0] == bi) {  // the winning lane pops its head
+#pragma unroll
+          for (int q = 0; q < FMAXK - 1; ++q) {
+            tv[q] = tv[q + 1];
+            ti[q] = ti[q + 1];
+          }
+          tv[FMAXK - 1] = -INFINITY;
+          ti[FMAXK - 1] = 0x7FFFFFFF;
+        }
+        const float w = sc_s[b * a.E + bi];
+        if (lane == 0) {
+          pl.sel[b][r] = bi;
+          pl.selw[b][r] = w;
+        }
+        tot += w;
+      }
+      __syncwarp();
+      if (lane < a.topk) {
+        const float w = pl.selw[b][lane] / (tot + 1e-20f) * a.route_scale;
+        pl.selw[b][lane] = w;
         if (cta == 0) {
-          if (a.idx) a.idx[b * a.topk + r] = pl.sel[b][r];
-          if (a.wt) a.wt[b * a.topk + r] = w;
+          if (a.idx) a.idx[b * a.topk + lane] = pl.sel[b][lane];
+          if (a.wt) a.wt[b * a.topk + lane] = w;
         }
       }
     }
@@ -789,7 +937,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     }
   }
   named_bar_sync(1, FW * 32);
-  if (tid == 0) mbar_arrive(planbar);
+  if (tid == 0) mbar_arrive(&planbar[0]);
 
   // ---- phase 1: routed w1|w3
   const int nr = pl.n_routed;
@@ -799,17 +947,19 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     const Span run = warp_run(span, warp);
     int cur = -1, seg_first = 0, seg_np = 0;
     float acc1[4] = {0.f, 0.f, 0.f, 0.f}, acc3[4] = {0.f, 0.f, 0.f, 0.f};
+    auto flush = [&]() {
+      const int cs = cur / geo.T;
+      w13_flush(a, geo, pl, geo.P13r, seg_first - cur * geo.P13r, seg_np, cs, cur % geo.T, acc1, acc3, pl.ntok[cs],
+                pl.tok[cs], pl.wt[cs], lane,
+                [&](auto&& f) { for_segments(N1, G, cur * geo.P13r, (cur + 1) * geo.P13r, f); });
+    };
     for (int i = run.s; i < run.e; ++i) {
       const int jj = jbase + 8 * (i - run.s) + warp;
       if (!wait_full(jj)) break;
       const uint8_t* stage = ring + (size_t)(jj % a.nstage) * FSTAGE;
-      const int tile = i / geo.P13r, p = i % geo.P13r, s = tile / geo.T, t = tile % geo.T;
+      const int tile = i / geo.P13r, p = i % geo.P13r, s = tile / geo.T;
       if (tile != cur) {
-        if (cur >= 0) {
-          const int cs = cur / geo.T;
-          w13_flush(a, geo, pl, N1, cur * geo.P13r, geo.P13r, seg_first, seg_np, cs, cur % geo.T, acc1, acc3,
-                    pl.ntok[cs], pl.tok[cs], pl.wt[cs], lane);
-        }
+        if (cur >= 0) flush();
         cur = tile;
         seg_first = i;
         seg_np = 0;
@@ -817,16 +967,11 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
         for (int q = 0; q < 4; ++q) acc1[q] = acc3[q] = 0.f;
       }
       const uint8_t* xrow = xf + (long long)pl.tok[s][min(lane >> 2, pl.ntok[s] - 1)] * a.xrow;
-      const uint8_t* tile_g = a.r_w13 + (long long)pl.expert[s] * a.r_w13_eb + t * geo.tile13r;
-      w13_accum<RFMT>(a, geo, stage, xrow, tile_g, p, lane, acc1, acc3);
+      w13_accum<RFMT>(stage, xrow, p, lane, acc1, acc3);
       ++seg_np;
       release(jj);
     }
-    if (cur >= 0 && !pl.abort) {
-      const int cs = cur / geo.T;
-      w13_flush(a, geo, pl, N1, cur * geo.P13r, geo.P13r, seg_first, seg_np, cs, cur % geo.T, acc1, acc3, pl.ntok[cs],
-                pl.tok[cs], pl.wt[cs], lane);
-    }
+    if (cur >= 0 && !pl.abort) flush();
     jbase += span.e - span.s;
   }
   __threadfence();
@@ -839,10 +984,10 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     }
   }
   named_bar_sync(1, FW * 32);
+  if (tid == 0 && !pl.abort) mbar_arrive(&planbar[1]);  // the producer may now copy h rows
   if (pl.abort) return;
-  __threadfence();
 
-  // ---- phase 2: w2 (h operands double-buffered in registers)
+  // ---- phase 2: w2
   {
     const int Q = (nr + 1) * geo.P2;
     const int N2 = geo.NT * Q;
@@ -850,10 +995,9 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     const Span run = warp_run(span, warp);
     int cur = -1, seg_first = 0, seg_np = 0;
     float out[4] = {0.f, 0.f, 0.f, 0.f};
-    uint4 hA[8], hB[8];
-    auto step = [&](int i, const uint4(&hb)[8]) -> bool {
+    for (int i = run.s; i < run.e; ++i) {
       const int jj = jbase + 8 * (i - run.s) + warp;
-      if (!wait_full(jj)) return false;
+      if (!wait_full(jj)) break;
       const uint8_t* stage = ring + (size_t)(jj % a.nstage) * FSTAGE;
       const int nt = i / Q, jq = i % Q, s = jq / geo.P2, p = jq % geo.P2;
       if (nt != cur) {
@@ -864,25 +1008,11 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
         out[0] = out[1] = out[2] = out[3] = 0.f;
       }
       if (s < nr)
-        w2_accum<RFMT>(a, pl, stage, a.r_w2 + (long long)pl.expert[s] * a.r_w2_eb + nt * geo.tile2r, s, p, hb, lane, out);
+        w2_accum<RFMT>(a, pl, stage, s, p, lane, out);
       else
-        w2_accum<DSMOE_FMT_FP8>(a, pl, stage, a.s_w2 + nt * geo.tile2s, s, p, hb, lane, out);
+        w2_accum<DSMOE_FMT_FP8>(a, pl, stage, s, p, lane, out);
       ++seg_np;
       release(jj);
-      return true;
-    };
-    auto fetch = [&](int i, uint4(&hb)[8]) {
-      const int jq = i % Q, s = jq / geo.P2;
-      load_h(a, s < nr ? s : a.sh_idx, jq % geo.P2, lane, hb);
-    };
-    if (run.s < run.e) fetch(run.s, hA);
-    for (int i = run.s; i < run.e; i += 2) {
-      if (i + 1 < run.e) fetch(i + 1, hB);
-      if (!step(i, hA)) break;
-      if (i + 1 < run.e) {
-        if (i + 2 < run.e) fetch(i + 2, hA);
-        if (!step(i + 1, hB)) break;
-      }
     }
     if (cur >= 0 && !pl.abort) w2_flush(a, N2, Q, cur, seg_first, seg_np, out, lane);
   }

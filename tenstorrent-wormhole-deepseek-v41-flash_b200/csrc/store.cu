@@ -15,6 +15,7 @@
 //    j: 0 (g, 2t)   1 (g+8, 2t)   2 (g, 2t+8)   3 (g+8, 2t+8)
 //  FP4 chunk scales, 32 bytes: byte 4g + q: q 0 (g, group 2c), 1 (g, 2c+1), 2 (g+8, 2c), 3 (g+8, 2c+1)
 // These are the register orders of the A operand of mma.m16n8k16 (two f16 per 32-bit register).
+// FP8 w1|w3 tile scales: 16 bytes per 256 K (one fused-kernel work item): s1[2p] s1[2p+1] s3[2p] s3[2p+1].
 #include "common.cuh"
 
 namespace dsmoe {
@@ -60,11 +61,12 @@ __global__ void pack_w13_kernel(PackArgs a) {
         v[j] = src[(long long)(rbase + row) * a.H + 32 * c + k];
       }
       *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<uint4*>(v);
-      if (c == 0 && l == 0) {  // this tile's scale row, after its data
+      if (c == 0 && l == 0) {  // this tile's scales after its data, 16 B per 256 K: s1 s1 s3 s3
         const float* s = (const float*)(m ? a.s3 : a.s1);
-        float* sd = reinterpret_cast<float*>(a.w13 + t * tile_b + (long long)KC * 1024) + m * (a.H / 128);
+        float* sd = reinterpret_cast<float*>(a.w13 + t * tile_b + (long long)KC * 1024);
         const int KB = a.H / 128;
-        for (int kb = 0; kb < KB; ++kb) sd[kb] = s[(long long)(rbase / 128) * KB + kb];
+        for (int kb = 0; kb < 2 * ((KB + 1) / 2); ++kb)
+          sd[fp8_w13_scale_index(kb, m)] = kb < KB ? s[(long long)(rbase / 128) * KB + kb] : 0.f;
       }
     } else {
       uint8_t* dst = a.w13 + t * tile_b + (long long)c * 1088 + m * 512 + l * 16;
@@ -159,7 +161,7 @@ __global__ void unpack_w13_kernel(UnpackArgs a) {
     if (a.fmt == DSMOE_FMT_FP8) {
       const uint4 q = ld16(tile + (long long)c * 1024 + m * 512 + l * 16);
       const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-      const float s = reinterpret_cast<const float*>(tile + (long long)KC * 1024)[m * (a.H / 128) + (32 * c) / 128];
+      const float s = reinterpret_cast<const float*>(tile + (long long)KC * 1024)[fp8_w13_scale_index((32 * c) / 128, m)];
 #pragma unroll
       for (int p = 0; p < 8; ++p) {  // p-th byte pair
         const uint32_t h = e4m3x2_to_f16x2((w[p >> 1] >> (16 * (p & 1))) & 0xFFFF);
