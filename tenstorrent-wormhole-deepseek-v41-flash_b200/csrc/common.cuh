@@ -22,21 +22,38 @@ namespace dsmoe {
 constexpr int kWarp = 32;
 
 // ------------------------------------------------------------------ packed-store geometry
-// FP8 w1|w3 tile (16 rows of w1 and the same 16 rows of w3): H/32 chunks of 1024 B
-// (w1 512 B, w3 512 B), then the tile's fp32 scales, 16 B per 256 K (see fp8_w13_scale_index).  FP8 w2 n-tile (16 output rows): I_loc/32 chunks of 512 B, then one fp32 scale per chunk.
+// The store is a sequence of work items, each one contiguous run of bytes that carries its own
+// scales, so that one bulk copy brings everything an item needs.
+// FP8 w1|w3 tile (16 rows of w1 and the same 16 rows of w3): items of 8 chunks of 32 K
+// (chunk = w1 512 B + w3 512 B), each followed by its 16 B of fp32 scales
+// [s1 block 0, s1 block 1, s3 block 0, s3 block 1] (blocks of 128 K); the last item may be short.
+// FP8 w2 n-tile (16 output rows): items of 8 chunks of 32 K (512 B each) followed by 32 B holding
+// one fp32 scale per chunk.
 // FP4 w1|w3 tile: H/64 chunks of 1088 B (w1 512, w3 512, w1 scales 32, w3 scales 32).
 // FP4 w2 n-tile: I_loc/64 chunks of 544 B (512 data, 32 scales).
-__host__ __device__ inline long long pad16(long long b) { return (b + 15) & ~15LL; }
+constexpr int kFp8W13Item = 8 * 1024 + 16;
+constexpr int kFp8W2Item = 8 * 512 + 32;
 
-// FP8 w1|w3 tile scales are grouped per 256 K values (16 bytes: s1[2p], s1[2p+1], s3[2p], s3[2p+1])
-// so that one aligned 16-byte copy brings a work item's four scales with its weights.
-__host__ __device__ inline int fp8_w13_scale_index(int kb, int m) { return (kb >> 1) * 4 + 2 * m + (kb & 1); }
+__host__ __device__ inline long long fp8_w13_chunk_off(int c) { return (long long)(c >> 3) * kFp8W13Item + (c & 7) * 1024; }
+__host__ __device__ inline long long fp8_w13_scale_off(int p, int KC) {
+  const int n = KC - 8 * p;
+  return (long long)p * kFp8W13Item + (n < 8 ? n : 8) * 1024;
+}
+// index (in floats) of the scale of 128-K block `kb` of matrix m (0 = w1, 1 = w3) within its item
+__host__ __device__ inline int fp8_w13_scale_index(int kb, int m) { return 2 * m + (kb & 1); }
+__host__ __device__ inline long long fp8_w2_chunk_off(int c) { return (long long)(c >> 3) * kFp8W2Item + (c & 7) * 512; }
+__host__ __device__ inline long long fp8_w2_scale_off(int p, int KC2) {
+  const int n = KC2 - 8 * p;
+  return (long long)p * kFp8W2Item + (n < 8 ? n : 8) * 512;
+}
 
 __host__ __device__ inline long long fp8_w13_tile_bytes(int H) {
-  return (long long)(H / 32) * 1024 + pad16(8LL * (H / 128));
+  const int KC = H / 32;
+  return (long long)(KC / 8) * kFp8W13Item + (KC % 8 ? (KC % 8) * 1024 + 16 : 0);
 }
 __host__ __device__ inline long long fp8_w2_tile_bytes(int I_loc) {
-  return (long long)(I_loc / 32) * 512 + pad16(4LL * (I_loc / 32));
+  const int KC2 = I_loc / 32;
+  return (long long)(KC2 / 8) * kFp8W2Item + (KC2 % 8 ? (KC2 % 8) * 512 + 32 : 0);
 }
 __host__ __device__ inline long long fp4_w13_tile_bytes(int H) { return (long long)(H / 64) * 1088; }
 __host__ __device__ inline long long fp4_w2_tile_bytes(int I_loc) { return (long long)(I_loc / 64) * 544; }
@@ -66,9 +83,8 @@ __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
 // e8m0 byte -> 2^(b-127) as fp32. b = 0 is the subnormal 2^-127; 0xFF is NaN (torch semantics).
 __device__ __forceinline__ float e8m0_to_f32(uint32_t b) {
   b &= 0xFFu;
-  if (b == 0u) return __uint_as_float(0x00400000u);
-  if (b == 0xFFu) return __uint_as_float(0x7FC00000u);
-  return __uint_as_float(b << 23);
+  const uint32_t bits = b == 0u ? 0x00400000u : (b == 0xFFu ? 0x7FC00000u : b << 23);
+  return __uint_as_float(bits);
 }
 
 __device__ __forceinline__ float f16_lo(uint32_t h2) { return __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFF))); }

@@ -88,18 +88,18 @@ __global__ void __launch_bounds__(256, 2) moe_w13_kernel(DecodeArgs a) {
   if (RFMT == DSMOE_FMT_FP8 || shared) {
     const uint8_t* tile =
         (shared ? a.s_w13 : a.r_w13 + (long long)e * a.r_w13_eb) + (long long)t * fp8_w13_tile_bytes(a.H);
-    const float* sc = reinterpret_cast<const float*>(tile + (long long)(a.H / 32) * 1024);
-    const int KB = a.H / 128;
+    const int KB = a.H / 128, KC = a.H / 32;
     const int kb0 = warp * KB / kWarps, kb1 = (warp + 1) * KB / kWarps;
     for (int kb = kb0; kb < kb1; ++kb) {
       uint4 w1v[4], w3v[4], xv[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const uint8_t* ch = tile + (long long)(4 * kb + i) * 1024 + lane * 16;
+        const uint8_t* ch = tile + fp8_w13_chunk_off(4 * kb + i) + lane * 16;
         w1v[i] = ld_stream16(ch);
         w3v[i] = ld_stream16(ch + 512);
         xv[i] = xrow[(4 * kb + i) * 4];
       }
+      const float* sc = reinterpret_cast<const float*>(tile + fp8_w13_scale_off(kb >> 1, KC));
       const float s1 = __ldg(sc + fp8_w13_scale_index(kb, 0)), s3 = __ldg(sc + fp8_w13_scale_index(kb, 1));
       float t1[4] = {0.f, 0.f, 0.f, 0.f}, t3[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -243,7 +243,6 @@ __global__ void __launch_bounds__(256, 2) moe_w2_kernel(DecodeArgs a) {
     if (RFMT == DSMOE_FMT_FP8 || shared) {
       const uint8_t* tile =
           (shared ? a.s_w2 : a.r_w2 + (long long)e * a.r_w2_eb) + (long long)nt * fp8_w2_tile_bytes(a.I_loc);
-      const float* sc = reinterpret_cast<const float*>(tile + (long long)KC8 * 512);
       for (int cc = c; cc < c + n; cc += 4) {
         const int m = min(4, c + n - cc);
         uint4 wv[4], hv[4];
@@ -251,9 +250,9 @@ __global__ void __launch_bounds__(256, 2) moe_w2_kernel(DecodeArgs a) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           if (i < m) {
-            wv[i] = ld_stream16(tile + (long long)(cc + i) * 512 + lane * 16);
+            wv[i] = ld_stream16(tile + fp8_w2_chunk_off(cc + i) + lane * 16);
             hv[i] = hrow[(cc + i) * 4];
-            s[i] = __ldg(sc + cc + i);
+            s[i] = __ldg(reinterpret_cast<const float*>(tile + fp8_w2_scale_off((cc + i) >> 3, KC8)) + ((cc + i) & 7));
           }
         }
 #pragma unroll

@@ -37,9 +37,8 @@ constexpr int FT = (FW + 1) * 32;      // + producer warp
 constexpr int FCH = 8;                 // packed chunks per w1|w3 item
 constexpr int FSTAGE = FCH * 1088;     // bytes per ring stage (8 FP4 w1|w3 chunks, the largest item)
 constexpr int FK2 = 256;               // K values per w2 item (8 FP8 chunks or 4 FP4 chunks)
-constexpr int FSC13 = FCH * 1024;      // FP8 w1|w3 item: weights, then its 16 B of scales
-constexpr int FSC2 = 4096;             // w2 item: weights (<= 4096 B), then FP8 scales (32 B)
-constexpr int FH2 = 4128;              // w2 item: h rows of the slot's tokens, 512 B each
+constexpr int FH2 = kFp8W2Item;        // w2 item: h rows of the slot's tokens (512 B each) after
+                                       // the packed item (<= 4128 B)
 constexpr int FMAXB = 8;               // tokens per call
 constexpr int FMAXK = DSMOE_MAX_TOPK;
 constexpr int FMAXS = FMAXB * FMAXK + 1;
@@ -264,51 +263,97 @@ __device__ void router_item(const FusedArgs& a, const uint8_t* stage, int r, int
 
 // ------------------------------------------------------------------ w1|w3
 // One item (8 chunks of a 16-row tile, part p) accumulated into acc1 / acc3. Scales come with the
-// weights: FP8 in the 16 bytes after them, FP4 inside each chunk.
+// weights (FP8: 16 bytes after the 8 chunks; FP4: inside each chunk). Every chunk (and FP4 32-K
+// group) accumulates into its own registers and the MMAs are issued k-step by k-step across
+// chunks, so no MMA waits on the one before it.
 template <int FMT>
 __device__ __forceinline__ void w13_accum(const uint8_t* stage, const uint8_t* xrow, int p, int lane, float (&acc1)[4],
                                           float (&acc3)[4]) {
   const int g = lane >> 2, tq = lane & 3;
-  float t1[4] = {0.f, 0.f, 0.f, 0.f}, t3[4] = {0.f, 0.f, 0.f, 0.f};
   if (FMT == DSMOE_FMT_FP8) {
 #pragma unroll
-    for (int c = 0; c < FCH; ++c) {
-      const int gc = p * FCH + c;
-      const uint4 A1 = lds16(stage + c * 1024 + lane * 16);
-      const uint4 A3 = lds16(stage + c * 1024 + 512 + lane * 16);
-      const uint4 X = lds16(xrow + gc * 64 + tq * 16);
-      uint32_t A[4];
-      a_frag_fp8(A, A1.x, A1.y); mma16816(t1, A, X.x, X.y);
-      a_frag_fp8(A, A3.x, A3.y); mma16816(t3, A, X.x, X.y);
-      a_frag_fp8(A, A1.z, A1.w); mma16816(t1, A, X.z, X.w);
-      a_frag_fp8(A, A3.z, A3.w); mma16816(t3, A, X.z, X.w);
-      if ((c & 3) == 3) {
-        const int h = c >> 2;  // 128-K block within the item
-        fma4s(acc1, t1, ldsf(stage + FSC13 + 4 * fp8_w13_scale_index(h, 0)));
-        fma4s(acc3, t3, ldsf(stage + FSC13 + 4 * fp8_w13_scale_index(h, 1)));
+    for (int blk = 0; blk < 2; ++blk) {  // two 128-K blocks, four chunks each
+      uint4 A1[4], A3[4], X[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int cc = 4 * blk + c;
+        A1[c] = lds16(stage + cc * 1024 + lane * 16);
+        A3[c] = lds16(stage + cc * 1024 + 512 + lane * 16);
+        X[c] = lds16(xrow + (p * FCH + cc) * 64 + tq * 16);
+      }
+      float u1[4][4], u3[4][4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) u1[c][q] = u3[c][q] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t A[4];
+          const uint32_t b0 = ks ? X[c].z : X[c].x, b1 = ks ? X[c].w : X[c].y;
+          a_frag_fp8(A, ks ? A1[c].z : A1[c].x, ks ? A1[c].w : A1[c].y);
+          mma16816(u1[c], A, b0, b1);
+          a_frag_fp8(A, ks ? A3[c].z : A3[c].x, ks ? A3[c].w : A3[c].y);
+          mma16816(u3[c], A, b0, b1);
+        }
+      }
+      const float s1 = ldsf(stage + FCH * 1024 + 4 * fp8_w13_scale_index(blk, 0));
+      const float s3 = ldsf(stage + FCH * 1024 + 4 * fp8_w13_scale_index(blk, 1));
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc1[q] = fmaf((u1[0][q] + u1[1][q]) + (u1[2][q] + u1[3][q]), s1, acc1[q]);
+        acc3[q] = fmaf((u3[0][q] + u3[1][q]) + (u3[2][q] + u3[3][q]), s3, acc3[q]);
       }
     }
   } else {
 #pragma unroll
-    for (int c = 0; c < FCH; ++c) {
-      const int gc = p * FCH + c;
-      const uint8_t* ch = stage + c * 1088;
-      const uint4 A1 = lds16(ch + lane * 16), A3 = lds16(ch + 512 + lane * 16);
-      const uint32_t S1 = lds32(ch + 1024 + 4 * g), S3 = lds32(ch + 1056 + 4 * g);
-      const uint4 X0 = lds16(xrow + (2 * gc) * 64 + tq * 16), X1 = lds16(xrow + (2 * gc + 1) * 64 + tq * 16);
-      uint32_t A[4];
-      a_frag_fp4(A, A1.x); mma16816(t1, A, X0.x, X0.y);
-      a_frag_fp4(A, A1.y); mma16816(t1, A, X0.z, X0.w);
-      a_frag_fp4(A, A3.x); mma16816(t3, A, X0.x, X0.y);
-      a_frag_fp4(A, A3.y); mma16816(t3, A, X0.z, X0.w);
-      fma4r(acc1, t1, e8m0_to_f32(S1), e8m0_to_f32(S1 >> 16));
-      fma4r(acc3, t3, e8m0_to_f32(S3), e8m0_to_f32(S3 >> 16));
-      a_frag_fp4(A, A1.z); mma16816(t1, A, X1.x, X1.y);
-      a_frag_fp4(A, A1.w); mma16816(t1, A, X1.z, X1.w);
-      a_frag_fp4(A, A3.z); mma16816(t3, A, X1.x, X1.y);
-      a_frag_fp4(A, A3.w); mma16816(t3, A, X1.z, X1.w);
-      fma4r(acc1, t1, e8m0_to_f32(S1 >> 8), e8m0_to_f32(S1 >> 24));
-      fma4r(acc3, t3, e8m0_to_f32(S3 >> 8), e8m0_to_f32(S3 >> 24));
+    for (int c0 = 0; c0 < FCH; c0 += 2) {  // two chunks (four 32-K groups) at a time
+      uint4 A1[2], A3[2], X[2][2];
+      uint32_t S1[2], S3[2];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const uint8_t* ch = stage + (c0 + c) * 1088;
+        const int gc = p * FCH + c0 + c;
+        A1[c] = lds16(ch + lane * 16);
+        A3[c] = lds16(ch + 512 + lane * 16);
+        S1[c] = lds32(ch + 1024 + 4 * g);
+        S3[c] = lds32(ch + 1056 + 4 * g);
+        X[c][0] = lds16(xrow + (2 * gc) * 64 + tq * 16);
+        X[c][1] = lds16(xrow + (2 * gc + 1) * 64 + tq * 16);
+      }
+      float u1[2][2][4], u3[2][2][4];  // [chunk][group][fragment]
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) u1[c][h][q] = u3[c][h][q] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t w1 = h ? (ks ? A1[c].w : A1[c].z) : (ks ? A1[c].y : A1[c].x);
+            const uint32_t w3 = h ? (ks ? A3[c].w : A3[c].z) : (ks ? A3[c].y : A3[c].x);
+            const uint32_t b0 = ks ? X[c][h].z : X[c][h].x, b1 = ks ? X[c][h].w : X[c][h].y;
+            uint32_t A[4];
+            a_frag_fp4(A, w1);
+            mma16816(u1[c][h], A, b0, b1);
+            a_frag_fp4(A, w3);
+            mma16816(u3[c][h], A, b0, b1);
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          fma4r(acc1, u1[c][h], e8m0_to_f32(S1[c] >> (8 * h)), e8m0_to_f32(S1[c] >> (8 * h + 16)));
+          fma4r(acc3, u3[c][h], e8m0_to_f32(S3[c] >> (8 * h)), e8m0_to_f32(S3[c] >> (8 * h + 16)));
+        }
+      }
     }
   }
 }
@@ -369,42 +414,79 @@ __device__ void w13_flush(const FusedArgs& a, const Geo& G, const FPlan& pl, int
 
 // ------------------------------------------------------------------ w2
 // One w2 item of slot s (weights, FP8 scales and the slot's h rows all in the stage) accumulated
-// into out[] in token columns: rows g, g+8 x tokens 2tq, 2tq+1.
+// into out[] in token columns: rows g, g+8 x tokens 2tq, 2tq+1. One accumulator per chunk / group.
 template <int FMT>
 __device__ __forceinline__ void w2_accum(const FusedArgs& a, const FPlan& pl, const uint8_t* stage, int s, int p,
                                          int lane, float (&out)[4]) {
   const int g = lane >> 2, tq = lane & 3;
   const uint8_t* hrow = stage + FH2 + min(g, pl.ntok[s] - 1) * 512 + tq * 16;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f}, tt[4] = {0.f, 0.f, 0.f, 0.f};
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float u[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) u[i][q] = 0.f;
   if (FMT == DSMOE_FMT_FP8) {
     const int nch = min(8, a.I_loc / 32 - p * 8);
+    uint4 A0[8], hb[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       if (i < nch) {
-        const uint4 A0 = lds16(stage + i * 512 + lane * 16);
-        const uint4 hb = lds16(hrow + i * 64);
-        uint32_t A[4];
-        a_frag_fp8(A, A0.x, A0.y); mma16816(tt, A, hb.x, hb.y);
-        a_frag_fp8(A, A0.z, A0.w); mma16816(tt, A, hb.z, hb.w);
-        fma4s(acc, tt, ldsf(stage + FSC2 + 4 * i));
+        A0[i] = lds16(stage + i * 512 + lane * 16);
+        hb[i] = lds16(hrow + i * 64);
       }
     }
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i < nch) {
+          uint32_t A[4];
+          a_frag_fp8(A, ks ? A0[i].z : A0[i].x, ks ? A0[i].w : A0[i].y);
+          mma16816(u[i], A, ks ? hb[i].z : hb[i].x, ks ? hb[i].w : hb[i].y);
+        }
+      }
+    }
+    const uint8_t* sc = stage + nch * 512;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < nch) fma4s(acc, u[i], ldsf(sc + 4 * i));
   } else {
     const int nch = min(4, a.I_loc / 64 - p * 4);
+    uint4 A0[4], hb[8];
+    uint32_t S[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       if (i < nch) {
         const uint8_t* ch = stage + i * 544;
-        const uint4 A0 = lds16(ch + lane * 16);
-        const uint32_t S = lds32(ch + 512 + 4 * g);
-        const uint4 h0 = lds16(hrow + (2 * i) * 64), h1 = lds16(hrow + (2 * i + 1) * 64);
-        uint32_t A[4];
-        a_frag_fp4(A, A0.x); mma16816(tt, A, h0.x, h0.y);
-        a_frag_fp4(A, A0.y); mma16816(tt, A, h0.z, h0.w);
-        fma4r(acc, tt, e8m0_to_f32(S), e8m0_to_f32(S >> 16));
-        a_frag_fp4(A, A0.z); mma16816(tt, A, h1.x, h1.y);
-        a_frag_fp4(A, A0.w); mma16816(tt, A, h1.z, h1.w);
-        fma4r(acc, tt, e8m0_to_f32(S >> 8), e8m0_to_f32(S >> 24));
+        A0[i] = lds16(ch + lane * 16);
+        S[i] = lds32(ch + 512 + 4 * g);
+        hb[2 * i] = lds16(hrow + (2 * i) * 64);
+        hb[2 * i + 1] = lds16(hrow + (2 * i + 1) * 64);
+      }
+    }
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (i < nch) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t w = h ? (ks ? A0[i].w : A0[i].z) : (ks ? A0[i].y : A0[i].x);
+            const uint4 hv = hb[2 * i + h];
+            uint32_t A[4];
+            a_frag_fp4(A, w);
+            mma16816(u[2 * i + h], A, ks ? hv.z : hv.x, ks ? hv.w : hv.y);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (i < nch) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          fma4r(acc, u[2 * i + h], e8m0_to_f32(S[i] >> (8 * h)), e8m0_to_f32(S[i] >> (8 * h + 16)));
       }
     }
   }
@@ -467,7 +549,7 @@ __device__ void w2_flush(const FusedArgs& a, int n, int Q, int nt, int seg_first
 
 // ------------------------------------------------------------------ the kernel
 template <int RFMT>
-__global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
+__global__ void __maxnreg__(224) moe_fused_kernel(FusedArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
   uint8_t* xf = ring + (size_t)a.nstage * FSTAGE;
@@ -498,20 +580,23 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   __syncthreads();
 
   // ================================================================ producer warp
+  // Lane w (< 8) feeds consumer warp w: it walks the same runs in the same order and fills the
+  // warp's own stages (w * spw .. w * spw + spw - 1), so every stage has one issuer and one reader.
+  const int spw = a.nstage / FW;  // stages per consumer warp
   if (warp == FW) {
-    if (lane != 0) return;
-    int j = 0;
+    if (lane >= FW) return;
+    const int w = lane;
+    int kw = 0;  // items issued for warp w
     bool ok = true;
-    // w2 items issued before grid barrier B get their h rows later: (stage, slot, part)
-    int def_n = 0, def_stage[16], def_slot[16], def_p[16];
+    int def_n = 0, def_stage[2], def_slot[2], def_p[2];  // w2 items waiting for their h rows
     bool h_open = false;
-    int j2 = 0x7FFFFFFF;  // sequence number of the first w2 item
-    auto copy_h = [&](int s, int slot, int p) {
+    int kw2 = 0x7FFFFFFF;  // item number of warp w's first w2 item
+    auto copy_h = [&](int st, int slot, int p) {
       const int sidx = slot < pl.n_routed ? slot : a.sh_idx;
       const uint32_t hb = (uint32_t)(min(FK2, a.I_loc - p * FK2) * 2);
       for (int c = 0; c < pl.ntok[slot]; ++c)
-        bulk_g2s(ring + (size_t)s * FSTAGE + FH2 + c * 512,
-                 a.hf + (long long)(sidx * 8 + c) * a.I_loc + (long long)p * FK2, hb, &full[s]);
+        bulk_g2s(ring + (size_t)st * FSTAGE + FH2 + c * 512,
+                 a.hf + (long long)(sidx * 8 + c) * a.I_loc + (long long)p * FK2, hb, &full[st]);
     };
     auto open_h = [&]() {  // grid barrier B passed: h is complete; send the deferred h rows
       if (h_open || !ok) return;
@@ -524,13 +609,13 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       for (int d = 0; d < def_n; ++d) copy_h(def_stage[d], def_slot[d], def_p[d]);
       h_open = true;
     };
-    auto acquire = [&](int& s) -> bool {  // the next stage, free
-      s = j % a.nstage;
-      const int k = j / a.nstage;
-      if (k > 0) {
-        if (j - a.nstage >= j2) open_h();  // that stage's last occupant was a w2 item
+    auto acquire = [&](int& st) -> bool {  // warp w's next stage, free
+      st = w * spw + kw % spw;
+      const int f = kw / spw;
+      if (f > 0) {
+        if (kw - spw >= kw2) open_h();  // its last occupant was a w2 item: it needs its h rows first
         if (!ok) return false;
-        if (!mbar_wait(&empty[s], (k - 1) & 1, kWaitNs)) {
+        if (!mbar_wait(&empty[st], (f - 1) & 1, kWaitNs)) {
           atomicOr(a.status, ST_EMPTY);
           ok = false;
           return false;
@@ -538,32 +623,26 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       }
       return true;
     };
-    auto issue = [&](const void* src, uint32_t bytes, const void* src2, uint32_t bytes2) {
-      int s;
-      if (!ok || !acquire(s)) return;
-      mbar_expect_tx(&full[s], bytes + bytes2);
-      bulk_g2s(ring + (size_t)s * FSTAGE, src, bytes, &full[s]);
-      if (bytes2) bulk_g2s(ring + (size_t)s * FSTAGE + (bytes == FSC13 ? FSC13 : FSC2), src2, bytes2, &full[s]);
-      ++j;
+    auto issue = [&](const void* src, uint32_t bytes) {
+      int st;
+      if (!ok || !acquire(st)) return;
+      mbar_expect_tx(&full[st], bytes);
+      bulk_g2s(ring + (size_t)st * FSTAGE, src, bytes, &full[st]);
+      ++kw;
     };
-    auto issue_span = [&](Span cs, auto&& item) {
-      const int L = (cs.e - cs.s + FW - 1) / FW;
-      for (int k = 0; k < L && ok; ++k)
-        for (int w = 0; w < FW && ok; ++w) {
-          const Span r = warp_run(cs, w);
-          if (r.s + k < r.e) item(r.s + k);
+    // phase R
+    {
+      const Span run = warp_run(localR, w);
+      for (int li = run.s; li < run.e && ok; ++li) {
+        if (li < my_router) {
+          const int i = rspan.s + li;
+          issue(a.wg + (long long)(i >> 2) * a.H + (i & 3) * (a.H / 4), (uint32_t)a.H);
+        } else {
+          const int i = sspan.s + li - my_router, t = i / geo.P13s, p = i % geo.P13s;
+          issue(a.s_w13 + t * geo.tile13s + (long long)p * kFp8W13Item, kFp8W13Item);
         }
-    };
-    issue_span(localR, [&](int li) {
-      if (li < my_router) {
-        const int i = rspan.s + li;
-        issue(a.wg + (long long)(i >> 2) * a.H + (i & 3) * (a.H / 4), (uint32_t)a.H, nullptr, 0);
-      } else {
-        const int i = sspan.s + li - my_router, t = i / geo.P13s, p = i % geo.P13s;
-        const uint8_t* tile = a.s_w13 + t * geo.tile13s;
-        issue(tile + (long long)p * FSC13, FSC13, tile + (long long)(a.H / 32) * 1024 + 16 * p, 16);
       }
-    });
+    }
     if (ok && !mbar_wait(&planbar[0], 0, 4 * kWaitNs)) {
       atomicOr(a.status, ST_PLAN);
       ok = false;
@@ -571,54 +650,63 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     if (ok) {
       const int nr = pl.n_routed;
       const int N1 = nr * geo.T * geo.P13r;
-      issue_span(cta_span(N1, cta, G), [&](int i) {
-        const int tile = i / geo.P13r, p = i % geo.P13r, s = tile / geo.T, t = tile % geo.T;
-        const uint8_t* base = a.r_w13 + (long long)pl.expert[s] * a.r_w13_eb + t * geo.tile13r;
-        if (RFMT == DSMOE_FMT_FP8)
-          issue(base + (long long)p * FSC13, FSC13, base + (long long)(a.H / 32) * 1024 + 16 * p, 16);
-        else
-          issue(base + (long long)p * FCH * 1088, FCH * 1088, nullptr, 0);
-      });
-      const int Q = (nr + 1) * geo.P2;
-      const int N2 = geo.NT * Q;
-      j2 = j;
-      issue_span(cta_span(N2, cta, G), [&](int i) {
-        const int nt = i / Q, jq = i % Q, s = jq / geo.P2, p = jq % geo.P2;
-        int st;
-        if (!ok || !acquire(st)) return;
-        const uint32_t hbytes = (uint32_t)(pl.ntok[s] * min(FK2, a.I_loc - p * FK2) * 2);
-        uint32_t wbytes, sbytes = 0;
-        const uint8_t *wsrc, *ssrc = nullptr;
-        if (s < nr && RFMT == DSMOE_FMT_FP4) {
-          const int nch = min(4, a.I_loc / 64 - p * 4);
-          wsrc = a.r_w2 + (long long)pl.expert[s] * a.r_w2_eb + nt * geo.tile2r + (long long)p * 4 * 544;
-          wbytes = (uint32_t)(nch * 544);
-        } else {
-          const uint8_t* tile = s < nr ? a.r_w2 + (long long)pl.expert[s] * a.r_w2_eb + nt * geo.tile2r
-                                       : a.s_w2 + nt * geo.tile2s;
-          const int kc = a.I_loc / 32, nch = min(8, kc - p * 8);
-          wsrc = tile + (long long)p * 8 * 512;
-          wbytes = (uint32_t)(nch * 512);
-          ssrc = tile + (long long)kc * 512 + p * 32;
-          sbytes = (uint32_t)(((nch + 3) / 4) * 16);
+      {  // phase 1: walk the run incrementally (tile, part)
+        const Span run = warp_run(cta_span(N1, cta, G), w);
+        int tile = run.s / geo.P13r, p = run.s % geo.P13r;
+        const uint32_t ib = RFMT == DSMOE_FMT_FP8 ? kFp8W13Item : FCH * 1088;
+        for (int i = run.s; i < run.e && ok; ++i) {
+          const int sl = tile / geo.T, t = tile - sl * geo.T;
+          issue(a.r_w13 + (long long)pl.expert[sl] * a.r_w13_eb + t * geo.tile13r + (long long)p * ib, ib);
+          if (++p == geo.P13r) {
+            p = 0;
+            ++tile;
+          }
         }
-        mbar_expect_tx(&full[st], wbytes + sbytes + hbytes);
-        bulk_g2s(ring + (size_t)st * FSTAGE, wsrc, wbytes, &full[st]);
-        if (sbytes) bulk_g2s(ring + (size_t)st * FSTAGE + FSC2, ssrc, sbytes, &full[st]);
-        if (h_open) {
-          copy_h(st, s, p);
-        } else {
-          def_stage[def_n] = st;
-          def_slot[def_n] = s;
-          def_p[def_n] = p;
-          ++def_n;
+      }
+      {  // phase 2: (n-tile, slot, part), h rows deferred until grid barrier B
+        const int Q = (nr + 1) * geo.P2;
+        const Span run = warp_run(cta_span(geo.NT * Q, cta, G), w);
+        kw2 = kw;
+        int nt = run.s / Q, jq = run.s % Q;
+        for (int i = run.s; i < run.e && ok; ++i) {
+          const int sl = jq / geo.P2, p = jq - sl * geo.P2;
+          int st;
+          if (!acquire(st)) break;
+          const uint32_t hbytes = (uint32_t)(pl.ntok[sl] * min(FK2, a.I_loc - p * FK2) * 2);
+          const uint8_t* src;
+          uint32_t bytes;
+          if (sl < nr && RFMT == DSMOE_FMT_FP4) {
+            const int nch = min(4, a.I_loc / 64 - p * 4);
+            src = a.r_w2 + (long long)pl.expert[sl] * a.r_w2_eb + nt * geo.tile2r + (long long)p * 4 * 544;
+            bytes = (uint32_t)(nch * 544);
+          } else {
+            const uint8_t* tile = sl < nr ? a.r_w2 + (long long)pl.expert[sl] * a.r_w2_eb + nt * geo.tile2r
+                                          : a.s_w2 + nt * geo.tile2s;
+            const int nch = min(8, a.I_loc / 32 - p * 8);
+            src = tile + (long long)p * kFp8W2Item;
+            bytes = (uint32_t)(nch * 512 + 32);
+          }
+          mbar_expect_tx(&full[st], bytes + hbytes);
+          bulk_g2s(ring + (size_t)st * FSTAGE, src, bytes, &full[st]);
+          if (h_open) {
+            copy_h(st, sl, p);
+          } else {
+            def_stage[def_n] = st;
+            def_slot[def_n] = sl;
+            def_p[def_n] = p;
+            ++def_n;
+          }
+          ++kw;
+          if (++jq == Q) {
+            jq = 0;
+            ++nt;
+          }
         }
-        ++j;
-      });
+      }
       open_h();
     }
-    // let every copy this thread issued land before the CTA may exit
-    for (int jj = max(0, j - a.nstage); jj < j; ++jj) mbar_wait(&full[jj % a.nstage], (jj / a.nstage) & 1, kWaitNs);
+    // let every copy this lane issued land before the CTA may exit
+    for (int q = max(0, kw - spw); q < kw; ++q) mbar_wait(&full[w * spw + q % spw], (q / spw) & 1, kWaitNs);
     return;
   }
 
@@ -708,9 +796,11 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     shared_wts[b] = 1.0f;
   }
 
-  auto wait_full = [&](int jj) -> bool {
+  int kw = 0;  // this warp's items so far: stage warp * spw + kw % spw, fill kw / spw
+  auto stage_of = [&]() { return ring + (size_t)(warp * spw + kw % spw) * FSTAGE; };
+  auto wait_full = [&]() -> bool {
     if (*(volatile int*)&pl.abort) return false;
-    if (!mbar_wait(&full[jj % a.nstage], (jj / a.nstage) & 1, kWaitNs)) {
+    if (!mbar_wait(&full[warp * spw + kw % spw], (kw / spw) & 1, kWaitNs)) {
       if (lane == 0) {
         atomicOr(a.status, ST_FULL);
         pl.abort = 1;
@@ -719,12 +809,11 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     }
     return true;
   };
-  auto release = [&](int jj) {
+  auto release = [&]() {
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[jj % a.nstage]);
+    if (lane == 0) mbar_arrive(&empty[warp * spw + kw % spw]);
+    ++kw;
   };
-
-  int jbase = 0;  // sequence number of the phase's first item in this CTA (the producer's order)
 
   // ---- phase R: router quarter-rows, then the shared expert's w1|w3 parts
   {
@@ -739,9 +828,8 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
                 });
     };
     for (int li = run.s; li < run.e; ++li) {
-      const int jj = jbase + 8 * (li - run.s) + warp;
-      if (!wait_full(jj)) break;
-      const uint8_t* stage = ring + (size_t)(jj % a.nstage) * FSTAGE;
+      if (!wait_full()) break;
+      const uint8_t* stage = stage_of();
       if (li < my_router) {
         const int i = rspan.s + li;
         router_item(a, stage, i >> 2, i & 3, lane);
@@ -759,7 +847,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
         w13_accum<DSMOE_FMT_FP8>(stage, xrow, p, lane, acc1, acc3);
         ++seg_np;
       }
-      release(jj);
+      release();
       if (li + 1 == min(run.e, my_router)) {  // this warp's last router row: count its rows toward barrier A
         __threadfence();
         __syncwarp();
@@ -771,7 +859,6 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     }
     if (cur >= 0 && !pl.abort) flush();
   }
-  jbase += localR.e;
   __threadfence();
   named_bar_sync(1, FW * 32);
   if (tid == 0 && !pl.abort) {
@@ -954,9 +1041,8 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
                 [&](auto&& f) { for_segments(N1, G, cur * geo.P13r, (cur + 1) * geo.P13r, f); });
     };
     for (int i = run.s; i < run.e; ++i) {
-      const int jj = jbase + 8 * (i - run.s) + warp;
-      if (!wait_full(jj)) break;
-      const uint8_t* stage = ring + (size_t)(jj % a.nstage) * FSTAGE;
+      if (!wait_full()) break;
+      const uint8_t* stage = stage_of();
       const int tile = i / geo.P13r, p = i % geo.P13r, s = tile / geo.T;
       if (tile != cur) {
         if (cur >= 0) flush();
@@ -969,10 +1055,9 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       const uint8_t* xrow = xf + (long long)pl.tok[s][min(lane >> 2, pl.ntok[s] - 1)] * a.xrow;
       w13_accum<RFMT>(stage, xrow, p, lane, acc1, acc3);
       ++seg_np;
-      release(jj);
+      release();
     }
     if (cur >= 0 && !pl.abort) flush();
-    jbase += span.e - span.s;
   }
   __threadfence();
   named_bar_sync(1, FW * 32);
@@ -996,9 +1081,8 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     int cur = -1, seg_first = 0, seg_np = 0;
     float out[4] = {0.f, 0.f, 0.f, 0.f};
     for (int i = run.s; i < run.e; ++i) {
-      const int jj = jbase + 8 * (i - run.s) + warp;
-      if (!wait_full(jj)) break;
-      const uint8_t* stage = ring + (size_t)(jj % a.nstage) * FSTAGE;
+      if (!wait_full()) break;
+      const uint8_t* stage = stage_of();
       const int nt = i / Q, jq = i % Q, s = jq / geo.P2, p = jq % geo.P2;
       if (nt != cur) {
         if (cur >= 0) w2_flush(a, N2, Q, cur, seg_first, seg_np, out, lane);
@@ -1012,7 +1096,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       else
         w2_accum<DSMOE_FMT_FP8>(a, pl, stage, s, p, lane, out);
       ++seg_np;
-      release(jj);
+      release();
     }
     if (cur >= 0 && !pl.abort) w2_flush(a, N2, Q, cur, seg_first, seg_np, out, lane);
   }
@@ -1085,8 +1169,8 @@ int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* im
                  int64_t* idx, float* wt, float* scores, uint8_t* ws, cudaStream_t st, void* const* events) {
   DevInfo& d = dev_info();
   const int optin = d.optin, sms = d.sms;
-  int nstage = 16;
-  while (nstage > 8 && fused_smem_bytes(L->hidden, B, L->n_experts, nstage) > (size_t)optin) --nstage;
+  int nstage = 2 * FW;  // two stages per consumer warp, or one when shared memory is short
+  if (fused_smem_bytes(L->hidden, B, L->n_experts, nstage) > (size_t)optin) nstage = FW;
   const size_t smem = fused_smem_bytes(L->hidden, B, L->n_experts, nstage);
   DSMOE_REQUIRE(smem <= (size_t)optin, DSMOE_ERR_UNSUPPORTED, "fused: %zu bytes of shared memory needed", smem);
   const FusedScratch f = fused_scratch(L->hidden, L->inter_local, L->n_experts, B, L->topk, L->routed.fmt);

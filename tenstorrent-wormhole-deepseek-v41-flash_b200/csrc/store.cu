@@ -15,7 +15,7 @@
 //    j: 0 (g, 2t)   1 (g+8, 2t)   2 (g, 2t+8)   3 (g+8, 2t+8)
 //  FP4 chunk scales, 32 bytes: byte 4g + q: q 0 (g, group 2c), 1 (g, 2c+1), 2 (g+8, 2c), 3 (g+8, 2c+1)
 // These are the register orders of the A operand of mma.m16n8k16 (two f16 per 32-bit register).
-// FP8 w1|w3 tile scales: 16 bytes per 256 K (one fused-kernel work item): s1[2p] s1[2p+1] s3[2p] s3[2p+1].
+// FP8 chunks are grouped 8 to an item with the item's scales right after (common.cuh).
 #include "common.cuh"
 
 namespace dsmoe {
@@ -53,7 +53,7 @@ __global__ void pack_w13_kernel(PackArgs a) {
     const int rbase = a.row0 + 16 * t;
     uint8_t v[16];
     if (a.fmt == DSMOE_FMT_FP8) {
-      uint8_t* dst = a.w13 + t * tile_b + (long long)c * 1024 + m * 512 + l * 16;
+      uint8_t* dst = a.w13 + t * tile_b + fp8_w13_chunk_off(c) + m * 512 + l * 16;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         int row, k;
@@ -61,12 +61,14 @@ __global__ void pack_w13_kernel(PackArgs a) {
         v[j] = src[(long long)(rbase + row) * a.H + 32 * c + k];
       }
       *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<uint4*>(v);
-      if (c == 0 && l == 0) {  // this tile's scales after its data, 16 B per 256 K: s1 s1 s3 s3
+      if ((c & 7) == 0 && l == 0) {  // the item's scales after its chunks: s1 s1 s3 s3
         const float* s = (const float*)(m ? a.s3 : a.s1);
-        float* sd = reinterpret_cast<float*>(a.w13 + t * tile_b + (long long)KC * 1024);
-        const int KB = a.H / 128;
-        for (int kb = 0; kb < 2 * ((KB + 1) / 2); ++kb)
+        const int p = c >> 3, KB = a.H / 128;
+        float* sd = reinterpret_cast<float*>(a.w13 + t * tile_b + fp8_w13_scale_off(p, KC));
+        for (int h = 0; h < 2; ++h) {
+          const int kb = 2 * p + h;
           sd[fp8_w13_scale_index(kb, m)] = kb < KB ? s[(long long)(rbase / 128) * KB + kb] : 0.f;
+        }
       }
     } else {
       uint8_t* dst = a.w13 + t * tile_b + (long long)c * 1088 + m * 512 + l * 16;
@@ -104,7 +106,7 @@ __global__ void pack_w2_kernel(PackArgs a) {
     const int nbase = 16 * nt;
     uint8_t v[16];
     if (a.fmt == DSMOE_FMT_FP8) {
-      uint8_t* dst = a.w2d + nt * tile_b + (long long)c * 512 + l * 16;
+      uint8_t* dst = a.w2d + nt * tile_b + fp8_w2_chunk_off(c) + l * 16;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         int row, k;
@@ -112,10 +114,12 @@ __global__ void pack_w2_kernel(PackArgs a) {
         v[j] = a.w2[(long long)(nbase + row) * a.I + a.row0 + 32 * c + k];
       }
       *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<uint4*>(v);
-      if (l == 0) {
+      if (l == 0) {  // one scale per chunk, after the item's chunks; the item's 8 slots padded with 0
         const int KBI = (a.I + 127) / 128;
-        float* sd = reinterpret_cast<float*>(a.w2d + nt * tile_b + (long long)KC2 * 512) + c;
-        *sd = ((const float*)a.s2)[(long long)(nbase / 128) * KBI + (a.row0 + 32 * c) / 128];
+        float* sd = reinterpret_cast<float*>(a.w2d + nt * tile_b + fp8_w2_scale_off(c >> 3, KC2));
+        sd[c & 7] = ((const float*)a.s2)[(long long)(nbase / 128) * KBI + (a.row0 + 32 * c) / 128];
+        if (c == KC2 - 1)
+          for (int q = (c & 7) + 1; q < 8; ++q) sd[q] = 0.f;
       }
     } else {
       uint8_t* dst = a.w2d + nt * tile_b + (long long)c * 544 + l * 16;
@@ -159,9 +163,9 @@ __global__ void unpack_w13_kernel(UnpackArgs a) {
     float* dst = m ? a.w3 : a.w1;
     const uint8_t* tile = a.w13 + t * tile_b;
     if (a.fmt == DSMOE_FMT_FP8) {
-      const uint4 q = ld16(tile + (long long)c * 1024 + m * 512 + l * 16);
+      const uint4 q = ld16(tile + fp8_w13_chunk_off(c) + m * 512 + l * 16);
       const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-      const float s = reinterpret_cast<const float*>(tile + (long long)KC * 1024)[fp8_w13_scale_index((32 * c) / 128, m)];
+      const float s = reinterpret_cast<const float*>(tile + fp8_w13_scale_off(c >> 3, KC))[fp8_w13_scale_index((32 * c) / 128, m)];
 #pragma unroll
       for (int p = 0; p < 8; ++p) {  // p-th byte pair
         const uint32_t h = e4m3x2_to_f16x2((w[p >> 1] >> (16 * (p & 1))) & 0xFFFF);
@@ -202,9 +206,9 @@ __global__ void unpack_w2_kernel(UnpackArgs a) {
     const int c = (int)(nc % KC2), nt = (int)(nc / KC2);
     const uint8_t* tile = a.w2s + nt * tile_b;
     if (a.fmt == DSMOE_FMT_FP8) {
-      const uint4 q = ld16(tile + (long long)c * 512 + l * 16);
+      const uint4 q = ld16(tile + fp8_w2_chunk_off(c) + l * 16);
       const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-      const float s = reinterpret_cast<const float*>(tile + (long long)KC2 * 512)[c];
+      const float s = reinterpret_cast<const float*>(tile + fp8_w2_scale_off(c >> 3, KC2))[c & 7];
 #pragma unroll
       for (int p = 0; p < 8; ++p) {
         const uint32_t h = e4m3x2_to_f16x2((w[p >> 1] >> (16 * (p & 1))) & 0xFFFF);
