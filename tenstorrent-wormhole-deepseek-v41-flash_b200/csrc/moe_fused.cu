@@ -5,10 +5,10 @@
 // (dsv41/tt/model.py:400-442; dsv41/tt/moe.py:108-180; dsv41/kernels/slot_cat.cpp) -- with one
 // launch that streams every weight byte the step needs exactly once.
 //
-// Shape: one CTA per SM (cooperative launch), 8 consumer warps + 1 producer warp.
+// Shape: one CTA per SM (cooperative launch), 7 consumer warps + 1 producer warp.
 //   producer   one thread issues 1-D bulk copies (cp.async.bulk, the TMA engine) of everything a
 //              work item reads -- its packed weights, their FP8 scales and, for w2 items, the h
-//              rows of its slot -- into a ring of up to 16 x 8.5 KB shared-memory stages, counted
+//              rows of its slot -- into a ring of 14 x 8.5 KB shared-memory stages, counted
 //              on one mbarrier per stage. It runs ahead across phase boundaries: w2 weights stream
 //              in while the grid still waits for the last w1|w3 tiles; their h rows follow as soon
 //              as grid barrier B has passed.
@@ -32,7 +32,7 @@
 
 namespace dsmoe {
 
-constexpr int FW = 8;                  // consumer warps
+constexpr int FW = 7;                  // consumer warps (+1 producer: two warps per SM sub-partition)
 constexpr int FT = (FW + 1) * 32;      // + producer warp
 constexpr int FCH = 8;                 // packed chunks per w1|w3 item
 constexpr int FSTAGE = FCH * 1088;     // bytes per ring stage (8 FP4 w1|w3 chunks, the largest item)
@@ -549,7 +549,7 @@ __device__ void w2_flush(const FusedArgs& a, int n, int Q, int nt, int seg_first
 
 // ------------------------------------------------------------------ the kernel
 template <int RFMT>
-__global__ void __maxnreg__(224) moe_fused_kernel(FusedArgs a) {
+__global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
   uint8_t* xf = ring + (size_t)a.nstage * FSTAGE;
@@ -580,7 +580,7 @@ __global__ void __maxnreg__(224) moe_fused_kernel(FusedArgs a) {
   __syncthreads();
 
   // ================================================================ producer warp
-  // Lane w (< 8) feeds consumer warp w: it walks the same runs in the same order and fills the
+  // Lane w (< FW) feeds consumer warp w: it walks the same runs in the same order and fills the
   // warp's own stages (w * spw .. w * spw + spw - 1), so every stage has one issuer and one reader.
   const int spw = a.nstage / FW;  // stages per consumer warp
   if (warp == FW) {
@@ -713,8 +713,8 @@ __global__ void __maxnreg__(224) moe_fused_kernel(FusedArgs a) {
   // ================================================================ consumer warps
   // token fragments: amax -> power-of-2 pre-scale -> f16 fragments in shared memory (one pass,
   // every load of the row in flight at once)
-  if (warp < a.B) {
-    const __nv_bfloat16* xr = a.x + (long long)warp * a.H;
+  for (int b = warp; b < a.B; b += FW) {
+    const __nv_bfloat16* xr = a.x + (long long)b * a.H;
     const int nchunk = a.H / 32;  // <= 256: at most 8 chunks of 32 values per lane
     float m = 0.f;
 #pragma unroll
@@ -748,7 +748,7 @@ __global__ void __maxnreg__(224) moe_fused_kernel(FusedArgs a) {
       frexpf(m, &e2);
       p = e2 - 15;  // m * 2^-p in [2^14, 2^15): inside f16 range with room to spare
     }
-    if (lane == 0) pl.xscale[warp] = ldexpf(1.0f, p);
+    if (lane == 0) pl.xscale[b] = ldexpf(1.0f, p);
     const float inv = ldexpf(1.0f, -p);
 #pragma unroll
     for (int k0 = 0; k0 < 8; k0 += 4) {  // second pass over the (now cached) row: convert
@@ -777,7 +777,7 @@ __global__ void __maxnreg__(224) moe_fused_kernel(FusedArgs a) {
           }
 #pragma unroll
           for (int tq = 0; tq < 4; ++tq)
-            *reinterpret_cast<uint4*>(xf + (long long)warp * a.xrow + c * 64 + tq * 16) =
+            *reinterpret_cast<uint4*>(xf + (long long)b * a.xrow + c * 64 + tq * 16) =
                 make_uint4(pack_f16x2(v[2 * tq], v[2 * tq + 1]), pack_f16x2(v[2 * tq + 8], v[2 * tq + 9]),
                            pack_f16x2(v[2 * tq + 16], v[2 * tq + 17]), pack_f16x2(v[2 * tq + 24], v[2 * tq + 25]));
         }
@@ -905,8 +905,7 @@ __global__ void __maxnreg__(224) moe_fused_kernel(FusedArgs a) {
     named_bar_sync(1, FW * 32);
     if (cta == 0 && a.scores)
       for (int i = tid; i < n; i += FW * 32) a.scores[i] = sc_s[i];
-    if (warp < a.B) {  // top-k of token `warp`: lane-local top-k lists, then k rounds of warp argmax
-      const int b = warp;
+    for (int b = warp; b < a.B; b += FW) {  // top-k of token b: lane-local top-k lists, then k warp argmaxes
       float tv[FMAXK];
       int ti[FMAXK];
 #pragma unroll
