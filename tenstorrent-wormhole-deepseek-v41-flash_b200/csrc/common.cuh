@@ -5,10 +5,13 @@
 //   FP4  e2m1 codes, two per byte, LOW nibble first, bit 3 = sign,
 //        one e8m0 scale (2^(b-127)) per 32 consecutive K values      (dsv41/ref/kernel.py:91-98,
 //                                                                      dsv41/ref/fp4lib.c:12-30)
-// Weights are widened on the fly to f16 (exact for every e4m3 and e2m1 value) and fed to the
-// tensor cores with mma.sync m16n8k16 (f16 x f16 -> fp32). The fragment order of the packed store
+// Weights enter the tensor cores in their own 8-bit form: mma.sync m16n8k32 with e4m3 operands and
+// fp32 accumulation. FP8 bytes are used as they are; an FP4 word becomes two e4m3 words with four
+// integer operations (the e2m1 value times 2^-6, exact). The fragment order of the packed store
 // (store.cu) is the A-operand register order of that instruction, so one 16-byte load per lane
-// yields the whole A fragment of 2 (FP8) or 4 (FP4) k16 steps.
+// yields the A fragments of one (FP8) or two (FP4) MMAs. Activations are split into two e4m3
+// terms, hi + lo / 16, that occupy adjacent B columns (about 8 significant bits, exact for bf16
+// values in the normal e4m3 range after a power-of-2 pre-scale).
 #pragma once
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
@@ -90,35 +93,84 @@ __device__ __forceinline__ float e8m0_to_f32(uint32_t b) {
 __device__ __forceinline__ float f16_lo(uint32_t h2) { return __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFF))); }
 __device__ __forceinline__ float f16_hi(uint32_t h2) { return __half2float(__ushort_as_half((unsigned short)(h2 >> 16))); }
 
-__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
-  __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
-// ------------------------------------------------------------------ tensor-core fragment op
-// D = A(16x16, f16, row) * B(16x8, f16, col) + C, fp32 accumulate.
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+// ------------------------------------------------------------------ 8-bit tensor-core path
+// D += A(16x32, e4m3, row) * B(32x8, e4m3, col), fp32 accumulate. A registers: a0 = row g, K 4t..4t+3;
+// a1 = row g+8; a2 = row g, K 16+4t..; a3 = row g+8, K 16+4t.. (g = lane/4, t = lane%4).
+// B registers: b0 = K 4t..4t+3 of column g, b1 = K 16+4t.. of column g.
+__device__ __forceinline__ void mma_e4m3(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// A fragment of one k16 step from 8 FP8 bytes (two 32-bit words of a lane's packed chunk).
-__device__ __forceinline__ void a_frag_fp8(uint32_t (&a)[4], uint32_t w_lo, uint32_t w_hi) {
-  a[0] = e4m3x2_to_f16x2(w_lo & 0xFFFF);
-  a[1] = e4m3x2_to_f16x2(w_lo >> 16);
-  a[2] = e4m3x2_to_f16x2(w_hi & 0xFFFF);
-  a[3] = e4m3x2_to_f16x2(w_hi >> 16);
+// D = A * B with C = 0 (a fresh partial that the caller scales).
+__device__ __forceinline__ void mma_e4m3_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
 }
 
-// A fragment of one k16 step from 4 FP4 bytes (one 32-bit word of a lane's packed chunk).
-__device__ __forceinline__ void a_frag_fp4(uint32_t (&a)[4], uint32_t w) {
-  a[0] = e2m1x2_to_f16x2(w & 0xFF);
-  a[1] = e2m1x2_to_f16x2((w >> 8) & 0xFF);
-  a[2] = e2m1x2_to_f16x2((w >> 16) & 0xFF);
-  a[3] = e2m1x2_to_f16x2(w >> 24);
+// One 32-bit word of packed FP4 (four bytes, two e2m1 codes each, bit 3 of a code = sign) ->
+// two words of e4m3: `lo` from the low nibbles, `hi` from the high nibbles. The e4m3 byte
+// ((code & 7) << 2) | ((code & 8) << 4) equals the e2m1 value times 2^-6 for all 16 codes (the
+// 2^6 is applied with the group scale), so this is exact and needs no conversion instruction.
+__device__ __forceinline__ void fp4w_to_e4m3(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  lo = ((w << 2) & 0x1C1C1C1Cu) | ((w << 4) & 0x80808080u);
+  hi = ((w >> 2) & 0x1C1C1C1Cu) | (w & 0x80808080u);
+}
+constexpr float kFp4E4m3Scale = 64.0f;  // undoes the 2^-6 of fp4w_to_e4m3
+
+// Two fp32 -> two e4m3 (low byte = v0), round to nearest even, saturating at +-448.
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float v0, float v1) {
+  unsigned short r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(v1), "f"(v0));
+  return r;
+}
+// Activation split for the 8-bit MMA: v ~= hi + lo / kLoScale, two values at a time (low byte =
+// v0). hi keeps 4 significant bits, lo the next 4 (|v| <= 448).
+constexpr float kLoScale = 16.0f;
+constexpr float kLoInv = 1.0f / 16.0f;
+__device__ __forceinline__ void split2_e4m3(float v0, float v1, uint32_t& hi2, uint32_t& lo2) {
+  hi2 = f32x2_to_e4m3x2(v0, v1);
+  const uint32_t b = e4m3x2_to_f16x2(hi2);  // exact
+  lo2 = f32x2_to_e4m3x2((v0 - f16_lo(b)) * kLoScale, (v1 - f16_hi(b)) * kLoScale);
+}
+
+// One FP4 chunk (64 K: two k32 MMAs, each with its own per-row 32-K group scales) of one matrix
+// against NTL n-tiles of activations; fp32 partials scaled and added to acc (times 2^-6, see
+// fp4w_to_e4m3). Scale word bytes: (row g, group 0), (g, 1), (g + 8, 0), (g + 8, 1).
+template <int NTL>
+__device__ __forceinline__ void fp4_chunk_mma(const uint4& w, uint32_t sv, const uint4* xv, float (*acc)[4]) {
+  uint32_t l0, h0, l1, h1, l2, h2, l3, h3;
+  fp4w_to_e4m3(w.x, l0, h0);
+  fp4w_to_e4m3(w.y, l1, h1);
+  fp4w_to_e4m3(w.z, l2, h2);
+  fp4w_to_e4m3(w.w, l3, h3);
+  const float sa0 = e8m0_to_f32(sv), sa1 = e8m0_to_f32(sv >> 16);
+  const float sb0 = e8m0_to_f32(sv >> 8), sb1 = e8m0_to_f32(sv >> 24);
+#pragma unroll
+  for (int j = 0; j < NTL; ++j) {
+    float d[4], e[4];
+    mma_e4m3_z(d, l0, l1, h0, h1, xv[j].x, xv[j].y);
+    mma_e4m3_z(e, l2, l3, h2, h3, xv[j].z, xv[j].w);
+    acc[j][0] = fmaf(e[0], sb0, fmaf(d[0], sa0, acc[j][0]));
+    acc[j][1] = fmaf(e[1], sb0, fmaf(d[1], sa0, acc[j][1]));
+    acc[j][2] = fmaf(e[2], sb1, fmaf(d[2], sa1, acc[j][2]));
+    acc[j][3] = fmaf(e[3], sb1, fmaf(d[3], sa1, acc[j][3]));
+  }
+}
+
+// Activation rows (one row per token and term) hold K in the B-operand order of m16n8k32, in blocks
+// of 64 K: lane t's 16 bytes at 64 * block + 16 * t are
+//   [K 4t..4t+3 | K 16+4t.. | K 32+4t.. | K 48+4t..]   (b0 / b1 of the block's two k32 steps).
+__host__ __device__ __forceinline__ int qk_off(int k) {
+  return (k >> 6) * 64 + ((k >> 2) & 3) * 16 + ((k >> 5) & 1) * 8 + ((k >> 4) & 1) * 4 + (k & 3);
 }
 
 // Streaming 16-byte load of weight data: read once per step, keep it out of L1.

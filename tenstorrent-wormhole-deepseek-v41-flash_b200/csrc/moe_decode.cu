@@ -7,12 +7,14 @@
 //
 // Per step (after the router kernels, router.cu):
 //   moe_w13_kernel  grid (inter_local/16 tiles, slots): one CTA streams one 16-row tile of w1 and
-//                   of w3 for one slot (expert + up to 8 tokens), 8 warps split K, mma.sync f16
-//                   with fp32 accumulation, per-block (FP8) or per-32 (FP4) scales applied to the
-//                   fp32 partials; epilogue: clamp, SiLU(g)*u, routing weight, write h (f16) in the
-//                   fragment order w2 reads.
+//                   of w3 for one slot (expert + up to 8 tokens), 8 warps split K, mma.sync
+//                   m16n8k32 on the e4m3 weights (FP4 expanded to e4m3 in registers) against the
+//                   tokens' e4m3 hi / lo terms, fp32 accumulation, per-block (FP8) or per-32 (FP4)
+//                   scales applied to the fp32 partials; epilogue: clamp, SiLU(g)*u -> h as e4m3
+//                   hi / lo rows in the order w2 reads.
 //   moe_w2_kernel   grid hidden/16: one CTA owns 16 output rows for all slots and all tokens;
-//                   warps split the (slot, K-chunk) items evenly; deterministic combine in smem.
+//                   warps split the (slot, K-chunk) items evenly; routing weight on the fp32
+//                   partials; deterministic combine in smem.
 // Both kernels are HBM-bound: every weight byte of the touched experts is read exactly once per
 // step, with 16-byte streaming loads, 4 independent chunks in flight per warp.
 #include "router.cuh"
@@ -21,7 +23,7 @@ namespace dsmoe {
 
 // fused persistent path (moe_fused.cu)
 struct FusedScratch {
-  size_t rl, p13, p2, hf, cnt13, cnt2, gbar, status, total;
+  size_t rl, p13, p2, hq, cnt13, cnt2, gbar, status, total;
   int p13max, qmax, slots;
 };
 FusedScratch fused_scratch(int H, int I_loc, int E, int B, int topk, int r_fmt);
@@ -42,9 +44,9 @@ struct DecodeArgs {
   const int* slot_ntok;
   const int* slot_tok;
   const float* slot_wt;
-  const uint32_t* xf;
-  const float* xscale;
-  uint16_t* hf;  // [slots * 8 rows][I_loc] f16, fragment order
+  const uint8_t* xq;     // [B][2][H] e4m3 hi / lo token rows
+  const float* xscale;   // [B]
+  uint8_t* hq;           // [slots] h rows (hq_off)
   void* y;
   int y_f32;
 };
@@ -54,68 +56,68 @@ constexpr float kLimit = 10.0f;  // SwiGLU clamp (dsv41/tt/moe.py:15, 134-135)
 
 __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
 
-// position of intermediate row j inside a fragment-ordered f16 row (see router.cu, xf layout)
-__device__ __forceinline__ int frag_pos(int j) {
-  const int k = j & 31, s = k >> 4, kk = k & 15;
-  return (j >> 5) * 32 + ((kk & 7) >> 1) * 8 + (2 * s + (kk >> 3)) * 2 + (kk & 1);
-}
-
-__device__ __forceinline__ void fma4(float (&acc)[4], const float (&t)[4], float s) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) acc[j] = fmaf(t[j], s, acc[j]);
-}
-// FP4: rows g (c0, c1) and g+8 (c2, c3) carry their own scales
-__device__ __forceinline__ void fma4_rows(float (&acc)[4], const float (&t)[4], float s_lo, float s_hi) {
-  acc[0] = fmaf(t[0], s_lo, acc[0]);
-  acc[1] = fmaf(t[1], s_lo, acc[1]);
-  acc[2] = fmaf(t[2], s_hi, acc[2]);
-  acc[3] = fmaf(t[3], s_hi, acc[3]);
-}
-
-template <int RFMT>
-__global__ void __launch_bounds__(256, 2) moe_w13_kernel(DecodeArgs a) {
-  const int slot = blockIdx.y;
-  if (slot >= a.plan[0]) return;
-  const int t = blockIdx.x;
+// w1|w3 of one 16-row tile for one slot: warps split K; C columns 2u, 2u+1 = (hi, lo) of slot
+// token nt * 4 + u.
+template <int RFMT, int NTL>
+__device__ __forceinline__ void w13_tile(const DecodeArgs& a, int slot, int t, float (*red)[16][32]) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
   const int e = a.slot_expert[slot];
   const bool shared = e >= a.E;
   const int ntok = a.slot_ntok[slot];
-  const int mytok = a.slot_tok[slot * DSMOE_SLOT_TOKENS + min(g, ntok - 1)];
-  const uint4* xrow = reinterpret_cast<const uint4*>(a.xf) + (long long)mytok * (a.H / 32) * 4 + tq;
+  const uint8_t* xr[NTL];
+#pragma unroll
+  for (int j = 0; j < NTL; ++j) {
+    const int tok = a.slot_tok[slot * DSMOE_SLOT_TOKENS + min(4 * j + (g >> 1), ntok - 1)];
+    xr[j] = a.xq + ((long long)tok * 2 + (g & 1)) * a.H + tq * 16;
+  }
+  float acc1[NTL][4], acc3[NTL][4];
+#pragma unroll
+  for (int j = 0; j < NTL; ++j)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc1[j][q] = acc3[j][q] = 0.f;
 
-  float acc1[4] = {0.f, 0.f, 0.f, 0.f}, acc3[4] = {0.f, 0.f, 0.f, 0.f};
   if (RFMT == DSMOE_FMT_FP8 || shared) {
     const uint8_t* tile =
         (shared ? a.s_w13 : a.r_w13 + (long long)e * a.r_w13_eb) + (long long)t * fp8_w13_tile_bytes(a.H);
     const int KB = a.H / 128, KC = a.H / 32;
     const int kb0 = warp * KB / kWarps, kb1 = (warp + 1) * KB / kWarps;
     for (int kb = kb0; kb < kb1; ++kb) {
-      uint4 w1v[4], w3v[4], xv[4];
+      uint4 w1v[4], w3v[4], xv[NTL][2];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const uint8_t* ch = tile + fp8_w13_chunk_off(4 * kb + i) + lane * 16;
         w1v[i] = ld_stream16(ch);
         w3v[i] = ld_stream16(ch + 512);
-        xv[i] = xrow[(4 * kb + i) * 4];
+      }
+#pragma unroll
+      for (int j = 0; j < NTL; ++j) {
+        xv[j][0] = ld16(xr[j] + (2 * kb) * 64);
+        xv[j][1] = ld16(xr[j] + (2 * kb + 1) * 64);
       }
       const float* sc = reinterpret_cast<const float*>(tile + fp8_w13_scale_off(kb >> 1, KC));
       const float s1 = __ldg(sc + fp8_w13_scale_index(kb, 0)), s3 = __ldg(sc + fp8_w13_scale_index(kb, 1));
-      float t1[4] = {0.f, 0.f, 0.f, 0.f}, t3[4] = {0.f, 0.f, 0.f, 0.f};
+      float u1[NTL][4], u3[NTL][4];
+#pragma unroll
+      for (int j = 0; j < NTL; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) u1[j][q] = u3[j][q] = 0.f;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        uint32_t A[4];
-        a_frag_fp8(A, w1v[i].x, w1v[i].y);
-        mma16816(t1, A, xv[i].x, xv[i].y);
-        a_frag_fp8(A, w3v[i].x, w3v[i].y);
-        mma16816(t3, A, xv[i].x, xv[i].y);
-        a_frag_fp8(A, w1v[i].z, w1v[i].w);
-        mma16816(t1, A, xv[i].z, xv[i].w);
-        a_frag_fp8(A, w3v[i].z, w3v[i].w);
-        mma16816(t3, A, xv[i].z, xv[i].w);
+#pragma unroll
+        for (int j = 0; j < NTL; ++j) {
+          const uint4 xb = xv[j][i >> 1];
+          const uint32_t b0 = (i & 1) ? xb.z : xb.x, b1 = (i & 1) ? xb.w : xb.y;
+          mma_e4m3(u1[j], w1v[i].x, w1v[i].y, w1v[i].z, w1v[i].w, b0, b1);
+          mma_e4m3(u3[j], w3v[i].x, w3v[i].y, w3v[i].z, w3v[i].w, b0, b1);
+        }
       }
-      fma4(acc1, t1, s1);
-      fma4(acc3, t3, s3);
+#pragma unroll
+      for (int j = 0; j < NTL; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc1[j][q] = fmaf(u1[j][q], s1, acc1[j][q]);
+          acc3[j][q] = fmaf(u3[j][q], s3, acc3[j][q]);
+        }
     }
   } else {
     const uint8_t* tile = a.r_w13 + (long long)e * a.r_w13_eb + (long long)t * fp4_w13_tile_bytes(a.H);
@@ -123,7 +125,7 @@ __global__ void __launch_bounds__(256, 2) moe_w13_kernel(DecodeArgs a) {
     const int c0 = warp * KC / kWarps, c1 = (warp + 1) * KC / kWarps;
     for (int c = c0; c < c1; c += 2) {
       const int nch = min(2, c1 - c);
-      uint4 w1v[2], w3v[2], xv[4];
+      uint4 w1v[2], w3v[2], xv[2][NTL];
       uint32_t s1v[2], s3v[2];
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
@@ -133,75 +135,154 @@ __global__ void __launch_bounds__(256, 2) moe_w13_kernel(DecodeArgs a) {
           w3v[i] = ld_stream16(ch + 512 + lane * 16);
           s1v[i] = __ldg(reinterpret_cast<const uint32_t*>(ch + 1024) + g);
           s3v[i] = __ldg(reinterpret_cast<const uint32_t*>(ch + 1056) + g);
-          xv[2 * i] = xrow[(2 * (c + i)) * 4];
-          xv[2 * i + 1] = xrow[(2 * (c + i) + 1) * 4];
+#pragma unroll
+          for (int j = 0; j < NTL; ++j) xv[i][j] = ld16(xr[j] + (c + i) * 64);
         }
       }
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         if (i < nch) {
-#pragma unroll
-          for (int grp = 0; grp < 2; ++grp) {
-            const uint4 xb = xv[2 * i + grp];
-            const uint32_t wa1 = grp ? w1v[i].z : w1v[i].x, wb1 = grp ? w1v[i].w : w1v[i].y;
-            const uint32_t wa3 = grp ? w3v[i].z : w3v[i].x, wb3 = grp ? w3v[i].w : w3v[i].y;
-            float t1[4] = {0.f, 0.f, 0.f, 0.f}, t3[4] = {0.f, 0.f, 0.f, 0.f};
-            uint32_t A[4];
-            a_frag_fp4(A, wa1);
-            mma16816(t1, A, xb.x, xb.y);
-            a_frag_fp4(A, wb1);
-            mma16816(t1, A, xb.z, xb.w);
-            a_frag_fp4(A, wa3);
-            mma16816(t3, A, xb.x, xb.y);
-            a_frag_fp4(A, wb3);
-            mma16816(t3, A, xb.z, xb.w);
-            fma4_rows(acc1, t1, e8m0_to_f32(s1v[i] >> (8 * grp)), e8m0_to_f32(s1v[i] >> (8 * grp + 16)));
-            fma4_rows(acc3, t3, e8m0_to_f32(s3v[i] >> (8 * grp)), e8m0_to_f32(s3v[i] >> (8 * grp + 16)));
-          }
+          fp4_chunk_mma<NTL>(w1v[i], s1v[i], xv[i], acc1);
+          fp4_chunk_mma<NTL>(w3v[i], s3v[i], xv[i], acc3);
         }
       }
     }
   }
 
-  __shared__ float red[kWarps][8][32];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    red[warp][j][lane] = acc1[j];
-    red[warp][4 + j][lane] = acc3[j];
-  }
-  __syncthreads();
-  if (warp == 0) {
+  for (int j = 0; j < NTL; ++j)
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      float gs = 0.f, us = 0.f;
+      red[warp][8 * j + q][lane] = acc1[j][q];
+      red[warp][8 * j + 4 + q][lane] = acc3[j][q];
+    }
+  __syncthreads();
+  if (warp < NTL) {  // warp j finishes n-tile j
+    const int j = warp;
+    float s[8];
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        gs += red[w][q][lane];
-        us += red[w][4 + q][lane];
+    for (int q = 0; q < 8; ++q) {
+      s[q] = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) s[q] += red[w][8 * j + q][lane];
+    }
+    const int q = 4 * j + tq;
+    if (q < ntok) {
+      const int tok = a.slot_tok[slot * DSMOE_SLOT_TOKENS + q];
+      const float f = a.xscale[tok] * (RFMT == DSMOE_FMT_FP4 && !shared ? kFp4E4m3Scale : 1.0f);
+      float h[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const float gv = fminf((s[2 * r] + s[2 * r + 1] * kLoInv) * f, kLimit);
+        const float uv = fminf(fmaxf((s[4 + 2 * r] + s[5 + 2 * r] * kLoInv) * f, -kLimit), kLimit);
+        h[r] = silu_f(gv) * uv * kHScale;
       }
-      const int row = q >= 2 ? g + 8 : g, col = 2 * tq + (q & 1);
-      if (col < ntok) {
-        const int tok = a.slot_tok[slot * DSMOE_SLOT_TOKENS + col];
-        const float xs = a.xscale[tok];
-        const float gv = fminf(gs * xs, kLimit);
-        const float uv = fminf(fmaxf(us * xs, -kLimit), kLimit);
-        const float h = silu_f(gv) * uv * a.slot_wt[slot * DSMOE_SLOT_TOKENS + col];
-        const int j = 16 * t + row;
-        a.hf[(long long)(slot * DSMOE_SLOT_TOKENS + col) * a.I_loc + frag_pos(j)] =
-            __half_as_ushort(__float2half_rn(h));
-      }
+      uint32_t hi2, lo2;
+      split2_e4m3(h[0], h[1], hi2, lo2);
+      const int k = 16 * t + g;
+      a.hq[hq_off(a.I_loc, slot, q, 0, k)] = (uint8_t)hi2;
+      a.hq[hq_off(a.I_loc, slot, q, 0, k + 8)] = (uint8_t)(hi2 >> 8);
+      a.hq[hq_off(a.I_loc, slot, q, 1, k)] = (uint8_t)lo2;
+      a.hq[hq_off(a.I_loc, slot, q, 1, k + 8)] = (uint8_t)(lo2 >> 8);
     }
   }
 }
 
-// Per-warp accumulation of one slot's 16 x 8 partial into the CTA's [16][B] tile of this warp.
-__device__ __forceinline__ void flush_slot(const DecodeArgs& a, float* yw, int slot, const float (&acc)[4],
-                                           int g, int tq) {
+template <int RFMT>
+__global__ void __launch_bounds__(256, 2) moe_w13_kernel(DecodeArgs a) {
+  const int slot = blockIdx.y;
+  if (slot >= a.plan[0]) return;
+  __shared__ float red[kWarps][16][32];  // [warp][n-tile * 8 + matrix * 4 + c][lane]
+  if (a.slot_ntok[slot] <= 4)
+    w13_tile<RFMT, 1>(a, slot, blockIdx.x, red);
+  else
+    w13_tile<RFMT, 2>(a, slot, blockIdx.x, red);
+}
+
+// A warp's run of n consecutive w2 chunks of one slot, from chunk c, for the CTA's 16 output rows;
+// added to the warp's [16][B] tile in token columns with the routing weight.
+template <int RFMT, int NTL>
+__device__ __forceinline__ void w2_run(const DecodeArgs& a, float* yw, int nt, int slot, int c, int n) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int e = a.slot_expert[slot];
+  const bool shared = e >= a.E;
   const int ntok = a.slot_ntok[slot];
+  const uint8_t* hr[NTL];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const int row = q >= 2 ? g + 8 : g, col = 2 * tq + (q & 1);
-    if (col < ntok) yw[row * a.B + a.slot_tok[slot * DSMOE_SLOT_TOKENS + col]] += acc[q];
+  for (int j = 0; j < NTL; ++j)
+    hr[j] = a.hq + slot * hq_slot_bytes(a.I_loc) + (g & 1) * (DSMOE_SLOT_TOKENS * kHPartK) +
+            min(4 * j + (g >> 1), ntok - 1) * kHPartK + tq * 16;
+  float acc[NTL][4];
+#pragma unroll
+  for (int j = 0; j < NTL; ++j)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[j][q] = 0.f;
+  if (RFMT == DSMOE_FMT_FP8 || shared) {
+    const int KC8 = a.I_loc / 32;
+    const uint8_t* tile =
+        (shared ? a.s_w2 : a.r_w2 + (long long)e * a.r_w2_eb) + (long long)nt * fp8_w2_tile_bytes(a.I_loc);
+    for (int cc = c; cc < c + n; cc += 4) {
+      const int m = min(4, c + n - cc);
+      uint4 wv[4];
+      uint2 hv[4][NTL];
+      float s[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (i < m) {
+          const int k = cc + i;
+          wv[i] = ld_stream16(tile + fp8_w2_chunk_off(k) + lane * 16);
+          s[i] = __ldg(reinterpret_cast<const float*>(tile + fp8_w2_scale_off(k >> 3, KC8)) + (k & 7));
+#pragma unroll
+          for (int j = 0; j < NTL; ++j)
+            hv[i][j] = *reinterpret_cast<const uint2*>(hr[j] + (k >> 3) * kHPartBytes + ((k & 7) >> 1) * 64 + (k & 1) * 8);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (i < m) {
+#pragma unroll
+          for (int j = 0; j < NTL; ++j) {
+            float d[4];
+            mma_e4m3_z(d, wv[i].x, wv[i].y, wv[i].z, wv[i].w, hv[i][j].x, hv[i][j].y);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[j][q] = fmaf(d[q], s[i], acc[j][q]);
+          }
+        }
+      }
+    }
+  } else {
+    const uint8_t* tile = a.r_w2 + (long long)e * a.r_w2_eb + (long long)nt * fp4_w2_tile_bytes(a.I_loc);
+    constexpr int NB = 1;  // chunks per step (register budget of 2 CTAs per SM)
+    for (int cc = c; cc < c + n; cc += NB) {
+      const int m = min(NB, c + n - cc);
+      uint4 wv[NB], hv[NB][NTL];
+      uint32_t sv[NB];
+#pragma unroll
+      for (int i = 0; i < NB; ++i) {
+        if (i < m) {
+          const int k = cc + i;
+          const uint8_t* ch = tile + (long long)k * 544;
+          wv[i] = ld_stream16(ch + lane * 16);
+          sv[i] = __ldg(reinterpret_cast<const uint32_t*>(ch + 512) + g);
+#pragma unroll
+          for (int j = 0; j < NTL; ++j) hv[i][j] = ld16(hr[j] + (k >> 2) * kHPartBytes + (k & 3) * 64);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < NB; ++i)
+        if (i < m) fp4_chunk_mma<NTL>(wv[i], sv[i], hv[i], acc);
+    }
+  }
+  const float fs = (RFMT == DSMOE_FMT_FP4 && !shared ? kFp4E4m3Scale : 1.0f) / kHScale;
+#pragma unroll
+  for (int j = 0; j < NTL; ++j) {
+    const int q = 4 * j + tq;
+    if (q < ntok) {
+      const int tok = a.slot_tok[slot * DSMOE_SLOT_TOKENS + q];
+      const float f = a.slot_wt[slot * DSMOE_SLOT_TOKENS + q] * fs;
+      yw[g * a.B + tok] += (acc[j][0] + acc[j][1] * kLoInv) * f;
+      yw[(g + 8) * a.B + tok] += (acc[j][2] + acc[j][3] * kLoInv) * f;
+    }
   }
   __syncwarp();
 }
@@ -210,7 +291,7 @@ template <int RFMT>
 __global__ void __launch_bounds__(256, 2) moe_w2_kernel(DecodeArgs a) {
   extern __shared__ float ysm[];  // [kWarps][16][B]
   const int nt = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int warp = threadIdx.x >> 5;
   for (int i = threadIdx.x; i < kWarps * 16 * a.B; i += blockDim.x) ysm[i] = 0.f;
   __syncthreads();
   const int nslots = a.plan[0], nrouted = a.plan[1];
@@ -235,74 +316,10 @@ __global__ void __launch_bounds__(256, 2) moe_w2_kernel(DecodeArgs a) {
       nch_slot = KC8;
     }
     const int n = (int)min((long long)(nch_slot - c), i1 - it);
-    const int e = a.slot_expert[slot];
-    const bool shared = e >= a.E;
-    const uint4* hrow =
-        reinterpret_cast<const uint4*>(a.hf + (long long)(slot * DSMOE_SLOT_TOKENS + g) * a.I_loc) + tq;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    if (RFMT == DSMOE_FMT_FP8 || shared) {
-      const uint8_t* tile =
-          (shared ? a.s_w2 : a.r_w2 + (long long)e * a.r_w2_eb) + (long long)nt * fp8_w2_tile_bytes(a.I_loc);
-      for (int cc = c; cc < c + n; cc += 4) {
-        const int m = min(4, c + n - cc);
-        uint4 wv[4], hv[4];
-        float s[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          if (i < m) {
-            wv[i] = ld_stream16(tile + fp8_w2_chunk_off(cc + i) + lane * 16);
-            hv[i] = hrow[(cc + i) * 4];
-            s[i] = __ldg(reinterpret_cast<const float*>(tile + fp8_w2_scale_off((cc + i) >> 3, KC8)) + ((cc + i) & 7));
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          if (i < m) {
-            float tt[4] = {0.f, 0.f, 0.f, 0.f};
-            uint32_t A[4];
-            a_frag_fp8(A, wv[i].x, wv[i].y);
-            mma16816(tt, A, hv[i].x, hv[i].y);
-            a_frag_fp8(A, wv[i].z, wv[i].w);
-            mma16816(tt, A, hv[i].z, hv[i].w);
-            fma4(acc, tt, s[i]);
-          }
-        }
-      }
-    } else {
-      const uint8_t* tile = a.r_w2 + (long long)e * a.r_w2_eb + (long long)nt * fp4_w2_tile_bytes(a.I_loc);
-      for (int cc = c; cc < c + n; cc += 2) {
-        const int m = min(2, c + n - cc);
-        uint4 wv[2], hv[4];
-        uint32_t sv[2];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          if (i < m) {
-            const uint8_t* ch = tile + (long long)(cc + i) * 544;
-            wv[i] = ld_stream16(ch + lane * 16);
-            sv[i] = __ldg(reinterpret_cast<const uint32_t*>(ch + 512) + g);
-            hv[2 * i] = hrow[(2 * (cc + i)) * 4];
-            hv[2 * i + 1] = hrow[(2 * (cc + i) + 1) * 4];
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          if (i < m) {
-#pragma unroll
-            for (int grp = 0; grp < 2; ++grp) {
-              const uint4 hb = hv[2 * i + grp];
-              float tt[4] = {0.f, 0.f, 0.f, 0.f};
-              uint32_t A[4];
-              a_frag_fp4(A, grp ? wv[i].z : wv[i].x);
-              mma16816(tt, A, hb.x, hb.y);
-              a_frag_fp4(A, grp ? wv[i].w : wv[i].y);
-              mma16816(tt, A, hb.z, hb.w);
-              fma4_rows(acc, tt, e8m0_to_f32(sv[i] >> (8 * grp)), e8m0_to_f32(sv[i] >> (8 * grp + 16)));
-            }
-          }
-        }
-      }
-    }
-    flush_slot(a, yw, slot, acc, g, tq);
+    if (a.slot_ntok[slot] <= 4)
+      w2_run<RFMT, 1>(a, yw, nt, slot, c, n);
+    else
+      w2_run<RFMT, 2>(a, yw, nt, slot, c, n);
     it += n;
   }
   __syncthreads();
@@ -326,7 +343,7 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ s, __nv_bfloat16* _
 
 // ------------------------------------------------------------------ workspace and validation
 struct WsLayout {
-  size_t logits, idx32, wt32, xf, xscale, plan, slot_expert, slot_ntok, slot_tok, slot_wt, hf, total;
+  size_t logits, idx32, wt32, xq, xscale, plan, slot_expert, slot_ntok, slot_tok, slot_wt, hq, total;
 };
 
 static size_t al(size_t v) { return (v + 255) & ~size_t(255); }
@@ -338,14 +355,14 @@ static WsLayout ws_layout(int B, int H, int E, int topk, int I_loc, size_t base)
   w.logits = o; o += al((size_t)B * E * 4);
   w.idx32 = o; o += al((size_t)B * topk * 4);
   w.wt32 = o; o += al((size_t)B * topk * 4);
-  w.xf = o; o += al((size_t)B * H * 2);
+  w.xq = o; o += al((size_t)B * 2 * H);
   w.xscale = o; o += al((size_t)B * 4);
   w.plan = o; o += al(16);
   w.slot_expert = o; o += al((size_t)S * 4);
   w.slot_ntok = o; o += al((size_t)S * 4);
   w.slot_tok = o; o += al((size_t)S * DSMOE_SLOT_TOKENS * 4);
   w.slot_wt = o; o += al((size_t)S * DSMOE_SLOT_TOKENS * 4);
-  w.hf = o; o += al((size_t)S * DSMOE_SLOT_TOKENS * I_loc * 2);
+  w.hq = o; o += al((size_t)S * hq_slot_bytes(I_loc));
   w.total = o;
   return w;
 }
@@ -416,7 +433,7 @@ static RouterArgs router_args(const dsmoe_layer_t* L, const void* x, int B, cons
   a.logits = (float*)(ws + w.logits);
   a.idx32 = (int*)(ws + w.idx32);
   a.wt32 = (float*)(ws + w.wt32);
-  a.xf = (uint32_t*)(ws + w.xf);
+  a.xq = ws + w.xq;
   a.xscale = (float*)(ws + w.xscale);
   a.plan = (int*)(ws + w.plan);
   a.slot_expert = (int*)(ws + w.slot_expert);
@@ -490,9 +507,9 @@ static int moe_decode_impl(const dsmoe_layer_t* L, const void* x, int B, const u
   a.slot_ntok = ra.slot_ntok;
   a.slot_tok = ra.slot_tok;
   a.slot_wt = ra.slot_wt;
-  a.xf = ra.xf;
+  a.xq = ra.xq;
   a.xscale = ra.xscale;
-  a.hf = (uint16_t*)(ws + w.hf);
+  a.hq = ws + w.hq;
   a.y = y;
   a.y_f32 = y_dtype == DSMOE_DTYPE_F32;
   const dim3 g13(L->inter_local / 16, max_slots(B, L->topk));

@@ -12,9 +12,10 @@
 //              on one mbarrier per stage. It runs ahead across phase boundaries: w2 weights stream
 //              in while the grid still waits for the last w1|w3 tiles; their h rows follow as soon
 //              as grid barrier B has passed.
-//   consumers  read nothing from global memory on the streaming path: dequantize A fragments from
-//              the stage, mma.sync m16n8k16 (f16 x f16 -> fp32) against the tokens' f16 fragments
-//              (shared memory) or the stage's h rows, block scales on the fp32 partials.
+//   consumers  read nothing from global memory on the streaming path: A fragments straight from
+//              the stage (FP8 bytes as they are, FP4 expanded to e4m3 with integer operations),
+//              mma.sync m16n8k32 e4m3 x e4m3 -> fp32 against the tokens' e4m3 hi / lo rows (shared
+//              memory) or the stage's h rows, block scales on the fp32 partials.
 // Work distribution: every phase is a flat list of items (2-8.5 KB each); each CTA takes a
 // contiguous span and each consumer warp a contiguous run of it, so a warp accumulates the
 // consecutive parts of a 16-row tile in registers and publishes one partial per tile it shares.
@@ -24,8 +25,9 @@
 //   R  router quarter-rows (fp64) and the shared expert's w1|w3 parts (no routing needed), both
 //      spread over all CTAs; a CTA arrives at grid barrier A when its router rows are done.
 //   P  every CTA computes the same scores, top-k and slot plan (shared memory scratch).
-//   1  routed w1|w3 parts; tile epilogue: clamp / SiLU / up / routing weight -> h (f16).
-//   2  after grid barrier B: w2 parts (16 output rows x slot x 256 K); tile epilogue -> y.
+//   1  routed w1|w3 parts; tile epilogue: clamp / SiLU / up -> h (e4m3 hi / lo rows).
+//   2  after grid barrier B: w2 parts (16 output rows x slot x 256 K), routing weight on the fp32
+//      partials; tile epilogue -> y.
 // Every wait (mbarrier, grid barrier) is bounded by %globaltimer; on expiry the kernel records a
 // status bit in the workspace, stops issuing work, lets its own copies land and returns.
 #include "router.cuh"
@@ -37,8 +39,10 @@ constexpr int FT = (FW + 1) * 32;      // + producer warp
 constexpr int FCH = 8;                 // packed chunks per w1|w3 item
 constexpr int FSTAGE = FCH * 1088;     // bytes per ring stage (8 FP4 w1|w3 chunks, the largest item)
 constexpr int FK2 = 256;               // K values per w2 item (8 FP8 chunks or 4 FP4 chunks)
-constexpr int FH2 = kFp8W2Item;        // w2 item: h rows of the slot's tokens (512 B each) after
-                                       // the packed item (<= 4128 B)
+constexpr int FH2 = kFp8W2Item;        // w2 stage: the packed item (<= 4128 B), then the slot's h
+constexpr int FH2T = 8 * kHPartK + 64; // rows: hi rows at FH2, lo rows FH2T further (the 64-byte
+                                       // offset puts the two terms in opposite bank halves)
+static_assert(FH2 + FH2T + 8 * kHPartK <= FSTAGE, "w2 stage overflow");
 constexpr int FMAXB = 8;               // tokens per call
 constexpr int FMAXK = DSMOE_MAX_TOPK;
 constexpr int FMAXS = FMAXB * FMAXK + 1;
@@ -70,13 +74,13 @@ struct FusedArgs {
   double* rl;        // [8][E][4] router quarter-row partial logits
   float* p13;        // [slots][T][p13max][32][8] w1|w3 tile-segment partials
   float* p2;         // [NT][qmax][32][4] w2 tile-segment partials (token columns)
-  uint16_t* hf;      // [slots * 8][I_loc] h, f16, fragment order
+  uint8_t* hq;       // [slots] h rows, e4m3 hi / lo (hq_off)
   unsigned* cnt13;   // [slots][T]
   unsigned* cnt2;    // [NT]
   unsigned* gbar;    // [0] arrivals, [1] generation
   unsigned* status;  // [0]
   int sh_idx;        // scratch slot index of the shared expert
-  int nstage, xrow, p13max, qmax;
+  int nstage, xrs, p13max, qmax;   // xrs: bytes per token row (hi or lo) in shared memory
 };
 
 struct FPlan {
@@ -186,27 +190,6 @@ __device__ __forceinline__ float ldsf(const uint8_t* p) { return *reinterpret_ca
 
 __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
 
-__device__ __forceinline__ int frag_pos(int j) {
-  const int k = j & 31, s = k >> 4, kk = k & 15;
-  return (j >> 5) * 32 + ((kk & 7) >> 1) * 8 + (2 * s + (kk >> 3)) * 2 + (kk & 1);
-}
-
-__device__ __forceinline__ void fma4s(float (&acc)[4], float (&t)[4], float s) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    acc[j] = fmaf(t[j], s, acc[j]);
-    t[j] = 0.f;
-  }
-}
-__device__ __forceinline__ void fma4r(float (&acc)[4], float (&t)[4], float s_lo, float s_hi) {
-  acc[0] = fmaf(t[0], s_lo, acc[0]);
-  acc[1] = fmaf(t[1], s_lo, acc[1]);
-  acc[2] = fmaf(t[2], s_hi, acc[2]);
-  acc[3] = fmaf(t[3], s_hi, acc[3]);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) t[j] = 0.f;
-}
-
 // ------------------------------------------------------------------ grid barrier (bounded)
 __device__ __forceinline__ unsigned grid_arrive(unsigned* gbar, int G) {
   const unsigned g0 = ld_acquire_u32(gbar + 1);
@@ -262,115 +245,99 @@ __device__ void router_item(const FusedArgs& a, const uint8_t* stage, int r, int
 }
 
 // ------------------------------------------------------------------ w1|w3
-// One item (8 chunks of a 16-row tile, part p) accumulated into acc1 / acc3. Scales come with the
-// weights (FP8: 16 bytes after the 8 chunks; FP4: inside each chunk). Every chunk (and FP4 32-K
-// group) accumulates into its own registers and the MMAs are issued k-step by k-step across
-// chunks, so no MMA waits on the one before it.
-template <int FMT>
-__device__ __forceinline__ void w13_accum(const uint8_t* stage, const uint8_t* xrow, int p, int lane, float (&acc1)[4],
-                                          float (&acc3)[4]) {
-  const int g = lane >> 2, tq = lane & 3;
+// One item (8 chunks of a 16-row tile, part p) accumulated into acc1 / acc3 for NTL n-tiles of
+// slot tokens: C columns 2u, 2u + 1 of n-tile j hold the hi and lo terms of slot token 4j + u.
+// xr[j] is the lane's token row in shared memory (B column g of n-tile j). Scales come with the
+// weights (FP8: 16 bytes after the 8 chunks; FP4: inside each chunk).
+template <int FMT, int NTL>
+__device__ __forceinline__ void w13_accum(const uint8_t* stage, const uint8_t* const* xr, int p, int lane,
+                                          float (&acc1)[2][4], float (&acc3)[2][4]) {
+  const int g = lane >> 2;
   if (FMT == DSMOE_FMT_FP8) {
 #pragma unroll
-    for (int blk = 0; blk < 2; ++blk) {  // two 128-K blocks, four chunks each
-      uint4 A1[4], A3[4], X[4];
+    for (int blk = 0; blk < 2; ++blk) {  // two 128-K blocks, four chunks each, one MMA chain per
+      uint4 X[NTL][2];                   // matrix and n-tile (seven warps hide its latency)
+#pragma unroll
+      for (int j = 0; j < NTL; ++j) {
+        X[j][0] = lds16(xr[j] + (4 * p + 2 * blk) * 64);
+        X[j][1] = lds16(xr[j] + (4 * p + 2 * blk + 1) * 64);
+      }
+      float u1[NTL][4], u3[NTL][4];
+#pragma unroll
+      for (int j = 0; j < NTL; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) u1[j][q] = u3[j][q] = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const int cc = 4 * blk + c;
-        A1[c] = lds16(stage + cc * 1024 + lane * 16);
-        A3[c] = lds16(stage + cc * 1024 + 512 + lane * 16);
-        X[c] = lds16(xrow + (p * FCH + cc) * 64 + tq * 16);
-      }
-      float u1[4][4], u3[4][4];
+        const uint4 A1 = lds16(stage + (4 * blk + c) * 1024 + lane * 16);
+        const uint4 A3 = lds16(stage + (4 * blk + c) * 1024 + 512 + lane * 16);
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) u1[c][q] = u3[c][q] = 0.f;
-#pragma unroll
-      for (int ks = 0; ks < 2; ++ks) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t A[4];
-          const uint32_t b0 = ks ? X[c].z : X[c].x, b1 = ks ? X[c].w : X[c].y;
-          a_frag_fp8(A, ks ? A1[c].z : A1[c].x, ks ? A1[c].w : A1[c].y);
-          mma16816(u1[c], A, b0, b1);
-          a_frag_fp8(A, ks ? A3[c].z : A3[c].x, ks ? A3[c].w : A3[c].y);
-          mma16816(u3[c], A, b0, b1);
+        for (int j = 0; j < NTL; ++j) {
+          const uint4 xb = X[j][c >> 1];
+          const uint32_t b0 = (c & 1) ? xb.z : xb.x, b1 = (c & 1) ? xb.w : xb.y;
+          mma_e4m3(u1[j], A1.x, A1.y, A1.z, A1.w, b0, b1);
+          mma_e4m3(u3[j], A3.x, A3.y, A3.z, A3.w, b0, b1);
         }
       }
       const float s1 = ldsf(stage + FCH * 1024 + 4 * fp8_w13_scale_index(blk, 0));
       const float s3 = ldsf(stage + FCH * 1024 + 4 * fp8_w13_scale_index(blk, 1));
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        acc1[q] = fmaf((u1[0][q] + u1[1][q]) + (u1[2][q] + u1[3][q]), s1, acc1[q]);
-        acc3[q] = fmaf((u3[0][q] + u3[1][q]) + (u3[2][q] + u3[3][q]), s3, acc3[q]);
-      }
+      for (int j = 0; j < NTL; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc1[j][q] = fmaf(u1[j][q], s1, acc1[j][q]);
+          acc3[j][q] = fmaf(u3[j][q], s3, acc3[j][q]);
+        }
     }
   } else {
 #pragma unroll
-    for (int c0 = 0; c0 < FCH; c0 += 2) {  // two chunks (four 32-K groups) at a time
-      uint4 A1[2], A3[2], X[2][2];
+    for (int c0 = 0; c0 < FCH; c0 += 2) {  // two chunks (four k32 MMAs per matrix and n-tile) at a time
+      uint4 A1[2], A3[2], X[2][NTL];
       uint32_t S1[2], S3[2];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const uint8_t* ch = stage + (c0 + c) * 1088;
-        const int gc = p * FCH + c0 + c;
         A1[c] = lds16(ch + lane * 16);
         A3[c] = lds16(ch + 512 + lane * 16);
         S1[c] = lds32(ch + 1024 + 4 * g);
         S3[c] = lds32(ch + 1056 + 4 * g);
-        X[c][0] = lds16(xrow + (2 * gc) * 64 + tq * 16);
-        X[c][1] = lds16(xrow + (2 * gc + 1) * 64 + tq * 16);
-      }
-      float u1[2][2][4], u3[2][2][4];  // [chunk][group][fragment]
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-          for (int q = 0; q < 4; ++q) u1[c][h][q] = u3[c][h][q] = 0.f;
-#pragma unroll
-      for (int ks = 0; ks < 2; ++ks) {
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t w1 = h ? (ks ? A1[c].w : A1[c].z) : (ks ? A1[c].y : A1[c].x);
-            const uint32_t w3 = h ? (ks ? A3[c].w : A3[c].z) : (ks ? A3[c].y : A3[c].x);
-            const uint32_t b0 = ks ? X[c][h].z : X[c][h].x, b1 = ks ? X[c][h].w : X[c][h].y;
-            uint32_t A[4];
-            a_frag_fp4(A, w1);
-            mma16816(u1[c][h], A, b0, b1);
-            a_frag_fp4(A, w3);
-            mma16816(u3[c][h], A, b0, b1);
-          }
-        }
+        for (int j = 0; j < NTL; ++j) X[c][j] = lds16(xr[j] + (FCH * p + c0 + c) * 64);
       }
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          fma4r(acc1, u1[c][h], e8m0_to_f32(S1[c] >> (8 * h)), e8m0_to_f32(S1[c] >> (8 * h + 16)));
-          fma4r(acc3, u3[c][h], e8m0_to_f32(S3[c] >> (8 * h)), e8m0_to_f32(S3[c] >> (8 * h + 16)));
-        }
+        fp4_chunk_mma<NTL>(A1[c], S1[c], X[c], acc1);
+        fp4_chunk_mma<NTL>(A3[c], S3[c], X[c], acc3);
       }
     }
   }
 }
 
-// Tile epilogue: clamp, SiLU(gate) * up * routing weight -> h (f16, w2's fragment order).
-__device__ __forceinline__ void w13_epilogue(const FusedArgs& a, const FPlan& pl, int sidx, int t, const float (&s)[8],
-                                             int ntok, const int* toks, const float* wts, int lane) {
+// Tile epilogue. v[4j + 0..3] = gate row g, gate row g + 8, up row g, up row g + 8 of slot token
+// 4j + tq, before the token's pre-scale and the weight-format factor fmtf. Clamp, SiLU(gate) * up
+// -> h, written as e4m3 hi / lo bytes (times kHScale) where w2 reads them.
+__device__ __forceinline__ void w13_epilogue(const FusedArgs& a, const FPlan& pl, int sidx, int t, const float (&v)[8],
+                                             int ntok, const int* toks, float fmtf, int lane) {
   const int g = lane >> 2, tq = lane & 3;
 #pragma unroll
-  for (int q4 = 0; q4 < 4; ++q4) {
-    const int row = q4 >= 2 ? g + 8 : g, col = 2 * tq + (q4 & 1);
-    if (col < ntok) {
-      const float xs = pl.xscale[toks[col]];
-      const float gv = fminf(s[q4] * xs, 10.0f);
-      const float uv = fminf(fmaxf(s[4 + q4] * xs, -10.0f), 10.0f);
-      const float h = silu_f(gv) * uv * wts[col];
-      a.hf[(long long)(sidx * 8 + col) * a.I_loc + frag_pos(16 * t + row)] = __half_as_ushort(__float2half_rn(h));
+  for (int j = 0; j < 2; ++j) {
+    const int q = 4 * j + tq;
+    if (q < ntok) {
+      const float f = pl.xscale[toks[q]] * fmtf;
+      float h[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const float gv = fminf(v[4 * j + r] * f, 10.0f);
+        const float uv = fminf(fmaxf(v[4 * j + 2 + r] * f, -10.0f), 10.0f);
+        h[r] = silu_f(gv) * uv * kHScale;
+      }
+      uint32_t hi2, lo2;
+      split2_e4m3(h[0], h[1], hi2, lo2);
+      const int k = 16 * t + g;
+      a.hq[hq_off(a.I_loc, sidx, q, 0, k)] = (uint8_t)hi2;
+      a.hq[hq_off(a.I_loc, sidx, q, 0, k + 8)] = (uint8_t)(hi2 >> 8);
+      a.hq[hq_off(a.I_loc, sidx, q, 1, k)] = (uint8_t)lo2;
+      a.hq[hq_off(a.I_loc, sidx, q, 1, k + 8)] = (uint8_t)(lo2 >> 8);
     }
   }
 }
@@ -380,11 +347,18 @@ __device__ __forceinline__ void w13_epilogue(const FusedArgs& a, const FPlan& pl
 // tile's segments (same order everywhere) for the last contributor.
 template <class Segs>
 __device__ void w13_flush(const FusedArgs& a, const Geo& G, const FPlan& pl, int P, int seg_rel, int seg_np, int sidx,
-                          int t, const float (&acc1)[4], const float (&acc3)[4], int ntok, const int* toks,
-                          const float* wts, int lane, Segs&& segs) {
-  float s[8] = {acc1[0], acc1[1], acc1[2], acc1[3], acc3[0], acc3[1], acc3[2], acc3[3]};
+                          int t, const float (&acc1)[2][4], const float (&acc3)[2][4], int ntok, const int* toks,
+                          float fmtf, int lane, Segs&& segs) {
+  float s[8];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {  // hi + lo / 16 per row
+    s[4 * j] = acc1[j][0] + acc1[j][1] * kLoInv;
+    s[4 * j + 1] = acc1[j][2] + acc1[j][3] * kLoInv;
+    s[4 * j + 2] = acc3[j][0] + acc3[j][1] * kLoInv;
+    s[4 * j + 3] = acc3[j][2] + acc3[j][3] * kLoInv;
+  }
   if (seg_np == P) {
-    w13_epilogue(a, pl, sidx, t, s, ntok, toks, wts, lane);
+    w13_epilogue(a, pl, sidx, t, s, ntok, toks, fmtf, lane);
     return;
   }
   float* base = a.p13 + (((long long)sidx * G.T + t) * a.p13max) * 32 * 8;
@@ -408,52 +382,55 @@ __device__ void w13_flush(const FusedArgs& a, const Geo& G, const FPlan& pl, int
     s[4] += __uint_as_float(v1.x); s[5] += __uint_as_float(v1.y);
     s[6] += __uint_as_float(v1.z); s[7] += __uint_as_float(v1.w);
   });
-  w13_epilogue(a, pl, sidx, t, s, ntok, toks, wts, lane);
+  w13_epilogue(a, pl, sidx, t, s, ntok, toks, fmtf, lane);
   if (lane == 0) a.cnt13[sidx * G.T + t] = 0u;
 }
 
 // ------------------------------------------------------------------ w2
 // One w2 item of slot s (weights, FP8 scales and the slot's h rows all in the stage) accumulated
-// into out[] in token columns: rows g, g+8 x tokens 2tq, 2tq+1. One accumulator per chunk / group.
-template <int FMT>
+// into out[] in token columns: rows g, g+8 x tokens 2tq, 2tq+1, with the routing weight.
+template <int FMT, int NTL>
 __device__ __forceinline__ void w2_accum(const FusedArgs& a, const FPlan& pl, const uint8_t* stage, int s, int p,
                                          int lane, float (&out)[4]) {
   const int g = lane >> 2, tq = lane & 3;
-  const uint8_t* hrow = stage + FH2 + min(g, pl.ntok[s] - 1) * 512 + tq * 16;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  float u[8][4];
+  const int ntok = pl.ntok[s];
+  const uint8_t* hr[NTL];
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int j = 0; j < NTL; ++j) hr[j] = stage + FH2 + (g & 1) * FH2T + min(4 * j + (g >> 1), ntok - 1) * kHPartK + tq * 16;
+  float tot[NTL][4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) u[i][q] = 0.f;
+  for (int j = 0; j < NTL; ++j)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) tot[j][q] = 0.f;
   if (FMT == DSMOE_FMT_FP8) {
     const int nch = min(8, a.I_loc / 32 - p * 8);
-    uint4 A0[8], hb[8];
+    const uint8_t* sc = stage + nch * 512;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (i < nch) {
-        A0[i] = lds16(stage + i * 512 + lane * 16);
-        hb[i] = lds16(hrow + i * 64);
-      }
-    }
+    for (int b = 0; b < 4; ++b) {  // 64-K blocks: two chunks each
+      if (2 * b < nch) {
+        uint4 Hb[NTL];
 #pragma unroll
-    for (int ks = 0; ks < 2; ++ks) {
+        for (int j = 0; j < NTL; ++j) Hb[j] = lds16(hr[j] + b * 64);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (i < nch) {
-          uint32_t A[4];
-          a_frag_fp8(A, ks ? A0[i].z : A0[i].x, ks ? A0[i].w : A0[i].y);
-          mma16816(u[i], A, ks ? hb[i].z : hb[i].x, ks ? hb[i].w : hb[i].y);
+        for (int h = 0; h < 2; ++h) {
+          const int i = 2 * b + h;
+          if (i < nch) {
+            const uint4 A0 = lds16(stage + i * 512 + lane * 16);
+            const float si = ldsf(sc + 4 * i);
+#pragma unroll
+            for (int j = 0; j < NTL; ++j) {
+              float d[4];
+              mma_e4m3_z(d, A0.x, A0.y, A0.z, A0.w, h ? Hb[j].z : Hb[j].x, h ? Hb[j].w : Hb[j].y);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) tot[j][q] = fmaf(d[q], si, tot[j][q]);
+            }
+          }
         }
       }
     }
-    const uint8_t* sc = stage + nch * 512;
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (i < nch) fma4s(acc, u[i], ldsf(sc + 4 * i));
   } else {
     const int nch = min(4, a.I_loc / 64 - p * 4);
-    uint4 A0[4], hb[8];
+    uint4 A0[4], Hb[4][NTL];
     uint32_t S[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -461,46 +438,36 @@ __device__ __forceinline__ void w2_accum(const FusedArgs& a, const FPlan& pl, co
         const uint8_t* ch = stage + i * 544;
         A0[i] = lds16(ch + lane * 16);
         S[i] = lds32(ch + 512 + 4 * g);
-        hb[2 * i] = lds16(hrow + (2 * i) * 64);
-        hb[2 * i + 1] = lds16(hrow + (2 * i + 1) * 64);
+#pragma unroll
+        for (int j = 0; j < NTL; ++j) Hb[i][j] = lds16(hr[j] + i * 64);
       }
     }
 #pragma unroll
-    for (int ks = 0; ks < 2; ++ks) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (i < nch) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t w = h ? (ks ? A0[i].w : A0[i].z) : (ks ? A0[i].y : A0[i].x);
-            const uint4 hv = hb[2 * i + h];
-            uint32_t A[4];
-            a_frag_fp4(A, w);
-            mma16816(u[2 * i + h], A, ks ? hv.z : hv.x, ks ? hv.w : hv.y);
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (i < nch) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-          fma4r(acc, u[2 * i + h], e8m0_to_f32(S[i] >> (8 * h)), e8m0_to_f32(S[i] >> (8 * h + 16)));
-      }
-    }
+    for (int i = 0; i < 4; ++i)
+      if (i < nch) fp4_chunk_mma<NTL>(A0[i], S[i], Hb[i], tot);
   }
-  // slot columns -> token columns
+  // hi + lo / 16, routing weight and the h pre-scale; then slot columns -> token columns
+  const float fs = (FMT == DSMOE_FMT_FP4 ? kFp4E4m3Scale : 1.0f) / kHScale;
+  float vg[NTL], vh[NTL];
+#pragma unroll
+  for (int j = 0; j < NTL; ++j) {
+    const int q = 4 * j + tq;
+    const float f = q < ntok ? pl.wt[s][q] * fs : 0.f;
+    vg[j] = (tot[j][0] + tot[j][1] * kLoInv) * f;
+    vh[j] = (tot[j][2] + tot[j][3] * kLoInv) * f;
+  }
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int tok = 2 * tq + h;
     const int col = tok < a.B ? pl.col_of[s][tok] : -1;
-    const int src = g * 4 + (col < 0 ? 0 : col >> 1);
-    const float v0 = __shfl_sync(0xffffffffu, acc[0], src), v1 = __shfl_sync(0xffffffffu, acc[1], src);
-    const float v2 = __shfl_sync(0xffffffffu, acc[2], src), v3 = __shfl_sync(0xffffffffu, acc[3], src);
-    if (col >= 0) {
-      out[h] += (col & 1) ? v1 : v0;
-      out[2 + h] += (col & 1) ? v3 : v2;
+    const int src = g * 4 + (col < 0 ? 0 : (col & 3));
+#pragma unroll
+    for (int j = 0; j < NTL; ++j) {
+      const float x0 = __shfl_sync(0xffffffffu, vg[j], src), x1 = __shfl_sync(0xffffffffu, vh[j], src);
+      if (col >= 0 && (col >> 2) == j) {
+        out[h] += x0;
+        out[2 + h] += x1;
+      }
     }
   }
 }
@@ -552,8 +519,8 @@ template <int RFMT>
 __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
-  uint8_t* xf = ring + (size_t)a.nstage * FSTAGE;
-  uint64_t* full = reinterpret_cast<uint64_t*>(xf + (size_t)a.B * a.xrow);
+  uint8_t* xq = ring + (size_t)a.nstage * FSTAGE;  // [B][2 terms] rows of xrs bytes
+  uint64_t* full = reinterpret_cast<uint64_t*>(xq + (size_t)a.B * 2 * a.xrs);
   uint64_t* empty = full + a.nstage;
   uint64_t* planbar = empty + a.nstage;  // [0] plan ready, [1] grid barrier B passed
   FPlan& pl = *reinterpret_cast<FPlan*>(planbar + 2);
@@ -591,12 +558,13 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     int def_n = 0, def_stage[2], def_slot[2], def_p[2];  // w2 items waiting for their h rows
     bool h_open = false;
     int kw2 = 0x7FFFFFFF;  // item number of warp w's first w2 item
-    auto copy_h = [&](int st, int slot, int p) {
+    auto copy_h = [&](int st, int slot, int p) {  // the slot's hi rows and lo rows of part p
       const int sidx = slot < pl.n_routed ? slot : a.sh_idx;
-      const uint32_t hb = (uint32_t)(min(FK2, a.I_loc - p * FK2) * 2);
-      for (int c = 0; c < pl.ntok[slot]; ++c)
-        bulk_g2s(ring + (size_t)st * FSTAGE + FH2 + c * 512,
-                 a.hf + (long long)(sidx * 8 + c) * a.I_loc + (long long)p * FK2, hb, &full[st]);
+      const uint32_t nb = (uint32_t)(pl.ntok[slot] * kHPartK);
+      const uint8_t* src = a.hq + (long long)sidx * hq_slot_bytes(a.I_loc) + (long long)p * kHPartBytes;
+      uint8_t* dst = ring + (size_t)st * FSTAGE + FH2;
+      bulk_g2s(dst, src, nb, &full[st]);
+      bulk_g2s(dst + FH2T, src + 8 * kHPartK, nb, &full[st]);
     };
     auto open_h = [&]() {  // grid barrier B passed: h is complete; send the deferred h rows
       if (h_open || !ok) return;
@@ -672,7 +640,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
           const int sl = jq / geo.P2, p = jq - sl * geo.P2;
           int st;
           if (!acquire(st)) break;
-          const uint32_t hbytes = (uint32_t)(pl.ntok[sl] * min(FK2, a.I_loc - p * FK2) * 2);
+          const uint32_t hbytes = (uint32_t)(2 * pl.ntok[sl] * kHPartK);
           const uint8_t* src;
           uint32_t bytes;
           if (sl < nr && RFMT == DSMOE_FMT_FP4) {
@@ -711,8 +679,8 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   }
 
   // ================================================================ consumer warps
-  // token fragments: amax -> power-of-2 pre-scale -> f16 fragments in shared memory (one pass,
-  // every load of the row in flight at once)
+  // token rows: amax -> power-of-2 pre-scale (amax * 2^-p in [128, 256)) -> e4m3 hi / lo rows in
+  // shared memory, K in B-operand order (qk_off); one pass of loads, all in flight at once
   for (int b = warp; b < a.B; b += FW) {
     const __nv_bfloat16* xr = a.x + (long long)b * a.H;
     const int nchunk = a.H / 32;  // <= 256: at most 8 chunks of 32 values per lane
@@ -746,10 +714,12 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     if (m > 0.f && m <= 3.0e38f) {
       int e2;
       frexpf(m, &e2);
-      p = e2 - 15;  // m * 2^-p in [2^14, 2^15): inside f16 range with room to spare
+      p = e2 - 8;
     }
     if (lane == 0) pl.xscale[b] = ldexpf(1.0f, p);
     const float inv = ldexpf(1.0f, -p);
+    uint8_t* rh = xq + (size_t)(2 * b) * a.xrs;
+    uint8_t* rl = rh + a.xrs;
 #pragma unroll
     for (int k0 = 0; k0 < 8; k0 += 4) {  // second pass over the (now cached) row: convert
       uint4 u[4][4];
@@ -776,10 +746,16 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
             }
           }
 #pragma unroll
-          for (int tq = 0; tq < 4; ++tq)
-            *reinterpret_cast<uint4*>(xf + (long long)b * a.xrow + c * 64 + tq * 16) =
-                make_uint4(pack_f16x2(v[2 * tq], v[2 * tq + 1]), pack_f16x2(v[2 * tq + 8], v[2 * tq + 9]),
-                           pack_f16x2(v[2 * tq + 16], v[2 * tq + 17]), pack_f16x2(v[2 * tq + 24], v[2 * tq + 25]));
+          for (int tt = 0; tt < 4; ++tt) {  // lane tt's 8 bytes of this 32-K chunk, per term
+            uint32_t h0, l0, h1, l1, h2, l2, h3, l3;
+            split2_e4m3(v[4 * tt], v[4 * tt + 1], h0, l0);
+            split2_e4m3(v[4 * tt + 2], v[4 * tt + 3], h1, l1);
+            split2_e4m3(v[16 + 4 * tt], v[16 + 4 * tt + 1], h2, l2);
+            split2_e4m3(v[16 + 4 * tt + 2], v[16 + 4 * tt + 3], h3, l3);
+            const int off = (c >> 1) * 64 + tt * 16 + (c & 1) * 8;
+            *reinterpret_cast<uint2*>(rh + off) = make_uint2(h0 | (h1 << 16), h2 | (h3 << 16));
+            *reinterpret_cast<uint2*>(rl + off) = make_uint2(l0 | (l1 << 16), l2 | (l3 << 16));
+          }
         }
       }
     }
@@ -789,12 +765,15 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   named_bar_sync(1, FW * 32);
 
   int shared_toks[FMAXB];
-  float shared_wts[FMAXB];
 #pragma unroll
-  for (int b = 0; b < FMAXB; ++b) {
-    shared_toks[b] = min(b, a.B - 1);
-    shared_wts[b] = 1.0f;
-  }
+  for (int b = 0; b < FMAXB; ++b) shared_toks[b] = min(b, a.B - 1);
+  // the lane's token row (B column g) of n-tile j, for a slot's token list
+  auto token_rows = [&](const uint8_t** xr, const int* toks, int ntok) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+      xr[j] = xq + (size_t)(2 * toks[min(4 * j + (lane >> 3), ntok - 1)] + ((lane >> 2) & 1)) * a.xrs +
+              (lane & 3) * 16;
+  };
 
   int kw = 0;  // this warp's items so far: stage warp * spw + kw % spw, fill kw / spw
   auto stage_of = [&]() { return ring + (size_t)(warp * spw + kw % spw) * FSTAGE; };
@@ -819,11 +798,12 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   {
     const Span run = warp_run(localR, warp);
     int cur = -1, seg_first = 0, seg_np = 0, n_router = 0;
-    float acc1[4] = {0.f, 0.f, 0.f, 0.f}, acc3[4] = {0.f, 0.f, 0.f, 0.f};
-    const uint8_t* xrow = xf + (long long)shared_toks[min(lane >> 2, a.B - 1)] * a.xrow;
+    float acc1[2][4], acc3[2][4];
+    const uint8_t* xr[2];
+    token_rows(xr, shared_toks, a.B);
     auto flush = [&]() {
       w13_flush(a, geo, pl, geo.P13s, seg_first - cur * geo.P13s, seg_np, a.sh_idx, cur, acc1, acc3, a.B, shared_toks,
-                shared_wts, lane, [&](auto&& f) {
+                1.0f, lane, [&](auto&& f) {
                   for_segments_R(geo.NR, geo.NS, G, cur * geo.P13s, (cur + 1) * geo.P13s, f);
                 });
     };
@@ -842,9 +822,14 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
           seg_first = i;
           seg_np = 0;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) acc1[q] = acc3[q] = 0.f;
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc1[j][q] = acc3[j][q] = 0.f;
         }
-        w13_accum<DSMOE_FMT_FP8>(stage, xrow, p, lane, acc1, acc3);
+        if (a.B > 4)
+          w13_accum<DSMOE_FMT_FP8, 2>(stage, xr, p, lane, acc1, acc3);
+        else
+          w13_accum<DSMOE_FMT_FP8, 1>(stage, xr, p, lane, acc1, acc3);
         ++seg_np;
       }
       release();
@@ -1032,11 +1017,13 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     const Span span = cta_span(N1, cta, G);
     const Span run = warp_run(span, warp);
     int cur = -1, seg_first = 0, seg_np = 0;
-    float acc1[4] = {0.f, 0.f, 0.f, 0.f}, acc3[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc1[2][4], acc3[2][4];
+    const uint8_t* xr[2];
+    constexpr float fmtf = RFMT == DSMOE_FMT_FP4 ? kFp4E4m3Scale : 1.0f;
     auto flush = [&]() {
       const int cs = cur / geo.T;
       w13_flush(a, geo, pl, geo.P13r, seg_first - cur * geo.P13r, seg_np, cs, cur % geo.T, acc1, acc3, pl.ntok[cs],
-                pl.tok[cs], pl.wt[cs], lane,
+                pl.tok[cs], fmtf, lane,
                 [&](auto&& f) { for_segments(N1, G, cur * geo.P13r, (cur + 1) * geo.P13r, f); });
     };
     for (int i = run.s; i < run.e; ++i) {
@@ -1049,10 +1036,15 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
         seg_first = i;
         seg_np = 0;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) acc1[q] = acc3[q] = 0.f;
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc1[j][q] = acc3[j][q] = 0.f;
+        token_rows(xr, pl.tok[s], pl.ntok[s]);
       }
-      const uint8_t* xrow = xf + (long long)pl.tok[s][min(lane >> 2, pl.ntok[s] - 1)] * a.xrow;
-      w13_accum<RFMT>(stage, xrow, p, lane, acc1, acc3);
+      if (pl.ntok[s] > 4)
+        w13_accum<RFMT, 2>(stage, xr, p, lane, acc1, acc3);
+      else
+        w13_accum<RFMT, 1>(stage, xr, p, lane, acc1, acc3);
       ++seg_np;
       release();
     }
@@ -1090,10 +1082,18 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
         seg_np = 0;
         out[0] = out[1] = out[2] = out[3] = 0.f;
       }
-      if (s < nr)
-        w2_accum<RFMT>(a, pl, stage, s, p, lane, out);
-      else
-        w2_accum<DSMOE_FMT_FP8>(a, pl, stage, s, p, lane, out);
+      const bool two = pl.ntok[s] > 4;
+      if (s < nr) {
+        if (two)
+          w2_accum<RFMT, 2>(a, pl, stage, s, p, lane, out);
+        else
+          w2_accum<RFMT, 1>(a, pl, stage, s, p, lane, out);
+      } else {
+        if (two)
+          w2_accum<DSMOE_FMT_FP8, 2>(a, pl, stage, s, p, lane, out);
+        else
+          w2_accum<DSMOE_FMT_FP8, 1>(a, pl, stage, s, p, lane, out);
+      }
       ++seg_np;
       release();
     }
@@ -1103,13 +1103,13 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
 
 // ------------------------------------------------------------------ host side
 size_t fused_smem_bytes(int H, int B, int E, int nstage) {
-  const size_t xrow = (size_t)H * 2 + 64;
-  return (size_t)nstage * FSTAGE + (size_t)B * xrow + (2 * (size_t)nstage + 2) * 8 + sizeof(FPlan) +
+  const size_t xrs = (size_t)H + 64;
+  return (size_t)nstage * FSTAGE + (size_t)B * 2 * xrs + (2 * (size_t)nstage + 2) * 8 + sizeof(FPlan) +
          (size_t)E * 4 + 16;
 }
 
 struct FusedScratch {
-  size_t rl, p13, p2, hf, cnt13, cnt2, gbar, status, total;
+  size_t rl, p13, p2, hq, cnt13, cnt2, gbar, status, total;
   int p13max, qmax, slots;
 };
 
@@ -1136,7 +1136,7 @@ FusedScratch fused_scratch(int H, int I_loc, int E, int B, int topk, int r_fmt) 
   f.rl = o; o += al2((size_t)B * E * 4 * 8);
   f.p13 = o; o += al2((size_t)f.slots * T * f.p13max * 32 * 8 * 4);
   f.p2 = o; o += al2((size_t)NT * f.qmax * 32 * 4 * 4);
-  f.hf = o; o += al2((size_t)f.slots * 8 * I_loc * 2);
+  f.hq = o; o += al2((size_t)f.slots * hq_slot_bytes(I_loc));
   f.total = o;
   return f;
 }
@@ -1202,14 +1202,14 @@ int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* im
   a.rl = (double*)(ws + f.rl);
   a.p13 = (float*)(ws + f.p13);
   a.p2 = (float*)(ws + f.p2);
-  a.hf = (uint16_t*)(ws + f.hf);
+  a.hq = ws + f.hq;
   a.cnt13 = (unsigned*)(ws + f.cnt13);
   a.cnt2 = (unsigned*)(ws + f.cnt2);
   a.gbar = (unsigned*)(ws + f.gbar);
   a.status = (unsigned*)(ws + f.status);
   a.sh_idx = FMAXB * L->topk;
   a.nstage = nstage;
-  a.xrow = L->hidden * 2 + 64;
+  a.xrs = L->hidden + 64;
   a.p13max = f.p13max;
   a.qmax = f.qmax;
 

@@ -5,7 +5,7 @@
 // all of it stays on the GPU:
 //   router_logits_kernel  logits[b, e] = x[b] . gate_w[e]   (fp64 accumulation, rounded to fp32)
 //   router_select_kernel  score function, bias, top-k, normalized weights; also writes the token
-//                         in the f16 fragment order the expert kernels read (power-of-2 pre-scale)
+//                         as the two e4m3 terms the expert kernels read (power-of-2 pre-scale)
 //   route_plan_kernel     groups the picks by expert into slots of <= 8 tokens (the virtual
 //                         buckets of dsv41/tt/moe.py:184-187) plus the shared expert's slots
 #include <float.h>
@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(256) router_select_kernel(RouterArgs a) {
   const int tok = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const __nv_bfloat16* xr = a.x + (long long)tok * a.H;
 
-  // (a) token -> f16 fragments with a power-of-2 pre-scale that keeps it inside f16 range
+  // (a) token -> e4m3 hi / lo rows with a power-of-2 pre-scale: amax * 2^-p in [128, 256)
   float amax = 0.f;
   for (int i = tid; i < a.H; i += blockDim.x) amax = fmaxf(amax, fabsf(__bfloat162float(xr[i])));
   amax = warp_max(amax);
@@ -97,17 +97,17 @@ __global__ void __launch_bounds__(256) router_select_kernel(RouterArgs a) {
   int p = 0;
   if (amax > 0.f && amax <= FLT_MAX) {
     int e2;
-    frexpf(amax, &e2);        // amax in [2^(e2-1), 2^e2)
-    p = (e2 - 1) - 14;        // amax * 2^-p in [2^14, 2^15)
+    frexpf(amax, &e2);  // amax in [2^(e2-1), 2^e2)
+    p = e2 - 8;
   }
   const float inv = ldexpf(1.0f, -p);
   if (tid == 0) a.xscale[tok] = ldexpf(1.0f, p);
-  uint4* xf = reinterpret_cast<uint4*>(a.xf) + (long long)tok * (a.H / 32) * 4;
-  for (int i = tid; i < (a.H / 32) * 4; i += blockDim.x) {
-    const int c = i >> 2, t = i & 3;
-    const int k0 = 32 * c + 2 * t;
-    auto pr = [&](int k) { return pack_f16x2(__bfloat162float(xr[k]) * inv, __bfloat162float(xr[k + 1]) * inv); };
-    xf[i] = make_uint4(pr(k0), pr(k0 + 8), pr(k0 + 16), pr(k0 + 24));
+  uint8_t* xh = a.xq + (long long)tok * 2 * a.H;
+  for (int k = 2 * tid; k < a.H; k += 2 * blockDim.x) {
+    uint32_t hi2, lo2;
+    split2_e4m3(__bfloat162float(xr[k]) * inv, __bfloat162float(xr[k + 1]) * inv, hi2, lo2);
+    *reinterpret_cast<uint16_t*>(xh + qk_off(k)) = (uint16_t)hi2;
+    *reinterpret_cast<uint16_t*>(xh + a.H + qk_off(k)) = (uint16_t)lo2;
   }
 
   // (b) scores and selection values

@@ -18,8 +18,8 @@ struct RouterArgs {
   float* logits;           // [B, E]
   int* idx32;              // [B, k]
   float* wt32;             // [B, k]
-  uint32_t* xf;            // [B][H/32][4 lanes-in-group][4 words] f16 fragments
-  float* xscale;           // [B] power of 2 undoing the fragment pre-scale
+  uint8_t* xq;             // [B][2 terms][H] e4m3 hi / lo rows in B-operand order (qk_off)
+  float* xscale;           // [B] power of 2 undoing the pre-scale of xq
   int* plan;               // [0] = slots, [1] = routed slots
   int* slot_expert;        // [MAXS] expert id, E = the shared expert
   int* slot_ntok;          // [MAXS]
@@ -30,6 +30,21 @@ struct RouterArgs {
   float* wt;               // [B, k]
   float* scores;           // [B, E]
 };
+
+// SwiGLU output h of one slot for w2, the B operand of its 8-bit MMAs: per 256-K part of the
+// intermediate dimension, [term 0 (hi): 8 slot tokens x 256 B][term 1 (lo): 8 x 256 B], K within a
+// row in qk_off order. h is stored times kHScale (|SiLU(min(g, 10)) * clamp(u, +-10)| <= 100, so
+// 400 stays inside e4m3's 448); the routing weight and 1/kHScale are applied to w2's fp32 output.
+constexpr float kHScale = 4.0f;
+constexpr int kHPartK = 256;
+constexpr int kHPartBytes = 2 * DSMOE_SLOT_TOKENS * kHPartK;
+__host__ __device__ inline long long hq_slot_bytes(int I_loc) {
+  return (long long)((I_loc + kHPartK - 1) / kHPartK) * kHPartBytes;
+}
+__host__ __device__ inline long long hq_off(int I_loc, int slot, int q, int term, int k) {
+  return slot * hq_slot_bytes(I_loc) + (long long)(k >> 8) * kHPartBytes + term * (DSMOE_SLOT_TOKENS * kHPartK) +
+         q * kHPartK + qk_off(k & 255);
+}
 
 // Upper bound on slots in one step: every pick its own slot, plus the shared expert's.
 inline int max_slots(int B, int topk) {

@@ -7,14 +7,16 @@
 // the device, so there is no paging and no per-token gather (the reference's SlotCat gather,
 // dsv41/kernels/slot_cat.cpp:194-365, has no counterpart).
 //
-// Lane chunk layout (lane l: g = l / 4, t = l % 4; rows relative to a 16-row tile):
-//  FP8, 32 K values per chunk, 16 bytes per lane, byte 8*s + j (k16 step s = 0, 1):
-//    j: 0 (g, 2t)   1 (g, 2t+1)   2 (g+8, 2t)   3 (g+8, 2t+1)
-//       4 (g, 2t+8) 5 (g, 2t+9)   6 (g+8, 2t+8) 7 (g+8, 2t+9)      (k offsets within step s)
-//  FP4, 64 K values per chunk, byte 4*s + j (s = 0..3), each byte = two codes (k, k+1), low first:
-//    j: 0 (g, 2t)   1 (g+8, 2t)   2 (g, 2t+8)   3 (g+8, 2t+8)
+// Lane chunk layout (lane l: g = l / 4, t = l % 4; rows relative to a 16-row tile), built around
+// the A operand of mma.m16n8k32 with 8-bit inputs (four 32-bit registers, 4 consecutive K each:
+// a0 = row g, K 4t..4t+3; a1 = row g+8, same K; a2 = row g, K 16+4t..; a3 = row g+8, K 16+4t..):
+//  FP8, 32 K per chunk, 16 bytes per lane: byte 4r + i (r = register 0..3, i = 0..3) holds
+//      row g + 8*(r & 1), K = 4t + i + 16*(r >> 1)          -- the A fragment itself
+//  FP4, 64 K per chunk (two MMAs), 16 bytes per lane = words w = 0..3, byte i of word w holds two
+//      codes of row g + 8*(w & 1): low nibble K = 32*(w >> 1) + 4t + i, high nibble that K + 16.
+//      A word expands to two A registers of e4m3 (low nibbles -> a0 / a1, high -> a2 / a3) with
+//      four integer operations (fp4x8_to_e4m3).
 //  FP4 chunk scales, 32 bytes: byte 4g + q: q 0 (g, group 2c), 1 (g, 2c+1), 2 (g+8, 2c), 3 (g+8, 2c+1)
-// These are the register orders of the A operand of mma.m16n8k16 (two f16 per 32-bit register).
 // FP8 chunks are grouped 8 to an item with the item's scales right after (common.cuh).
 #include "common.cuh"
 
@@ -28,14 +30,19 @@ struct PackArgs {
 };
 
 __device__ __forceinline__ void lane_rows_fp8(int l, int j, int& row, int& k) {
-  const int g = l >> 2, t = l & 3, s = j >> 3, jj = j & 7;
-  row = (jj & 2) ? g + 8 : g;
-  k = 16 * s + 2 * t + (jj & 1) + ((jj & 4) ? 8 : 0);
+  const int g = l >> 2, t = l & 3, r = j >> 2, i = j & 3;
+  row = g + 8 * (r & 1);
+  k = 4 * t + i + 16 * (r >> 1);
 }
+// FP4: the low-nibble code's K; the high nibble holds K + 16 of the same row
 __device__ __forceinline__ void lane_rows_fp4(int l, int j, int& row, int& k) {
-  const int g = l >> 2, t = l & 3, s = j >> 2, jj = j & 3;
-  row = (jj & 1) ? g + 8 : g;
-  k = 16 * s + 2 * t + ((jj & 2) ? 8 : 0);  // even k: one source byte holds (k, k+1)
+  const int g = l >> 2, t = l & 3, w = j >> 2, i = j & 3;
+  row = g + 8 * (w & 1);
+  k = 32 * (w >> 1) + 4 * t + i;
+}
+// e2m1 code of (row, k) from a checkpoint-layout FP4 row (low nibble = even k)
+__device__ __forceinline__ uint32_t fp4_code(const uint8_t* rowp, int k) {
+  return (rowp[k >> 1] >> (4 * (k & 1))) & 0xF;
 }
 
 // One thread per (tile, chunk, matrix, lane) 16-byte output.
@@ -76,7 +83,8 @@ __global__ void pack_w13_kernel(PackArgs a) {
       for (int j = 0; j < 16; ++j) {
         int row, k;
         lane_rows_fp4(l, j, row, k);
-        v[j] = src[(long long)(rbase + row) * (a.H / 2) + (64 * c + k) / 2];
+        const uint8_t* rp = src + (long long)(rbase + row) * (a.H / 2);
+        v[j] = (uint8_t)(fp4_code(rp, 64 * c + k) | (fp4_code(rp, 64 * c + k + 16) << 4));
       }
       *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<uint4*>(v);
       if (l < 8) {  // lanes 0..7 write the 4 scale bytes of row pair (g = l, g + 8)
@@ -127,7 +135,9 @@ __global__ void pack_w2_kernel(PackArgs a) {
       for (int j = 0; j < 16; ++j) {
         int row, k;
         lane_rows_fp4(l, j, row, k);
-        v[j] = a.w2[(long long)(nbase + row) * (a.I / 2) + (a.row0 + 64 * c + k) / 2];
+        const uint8_t* rp = a.w2 + (long long)(nbase + row) * (a.I / 2);
+        const int kk = a.row0 + 64 * c + k;
+        v[j] = (uint8_t)(fp4_code(rp, kk) | (fp4_code(rp, kk + 16) << 4));
       }
       *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<uint4*>(v);
       if (l < 8) {
@@ -187,8 +197,8 @@ __global__ void unpack_w13_kernel(UnpackArgs a) {
         const int g = row & 7, hi_row = row >> 3, grp = k >> 5;  // group within chunk (0/1)
         const float s = e8m0_to_f32(sc[4 * g + 2 * hi_row + grp]);
         float* o = dst + (long long)(16 * t + row) * a.H + 64 * c + k;
-        o[0] = f16_lo(h) * s;
-        o[1] = f16_hi(h) * s;
+        o[0] = f16_lo(h) * s;   // low nibble: K
+        o[16] = f16_hi(h) * s;  // high nibble: K + 16 (same 32-K scale group)
       }
     }
   }
@@ -231,7 +241,7 @@ __global__ void unpack_w2_kernel(UnpackArgs a) {
         const float s = e8m0_to_f32(sc[4 * g + 2 * hi_row + grp]);
         float* o = a.w2 + (long long)(16 * nt + row) * a.I_loc + 64 * c + k;
         o[0] = f16_lo(h) * s;
-        o[1] = f16_hi(h) * s;
+        o[16] = f16_hi(h) * s;
       }
     }
   }
