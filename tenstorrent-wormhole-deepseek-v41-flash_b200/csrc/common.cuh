@@ -90,6 +90,22 @@ __device__ __forceinline__ float e8m0_to_f32(uint32_t b) {
   return __uint_as_float(bits);
 }
 
+// Four e8m0 bytes -> 2^(b-127) each. Byte shifts into the fp32 exponent field; the two codes
+// that are not plain powers of two (0 -> 2^-127, 0xFF -> NaN) take the exact per-byte path.
+__device__ __forceinline__ void e8m0x4_to_f32(uint32_t sv, float& s0, float& s1, float& s2, float& s3) {
+  s0 = __uint_as_float((sv & 0xFFu) << 23);
+  s1 = __uint_as_float((sv & 0xFF00u) << 15);
+  s2 = __uint_as_float((sv & 0xFF0000u) << 7);
+  s3 = __uint_as_float((sv >> 1) & 0x7F800000u);
+  const uint32_t zero_or_ff = (((sv - 0x01010101u) & ~sv) | ((~sv - 0x01010101u) & sv)) & 0x80808080u;
+  if (zero_or_ff) {
+    s0 = e8m0_to_f32(sv);
+    s1 = e8m0_to_f32(sv >> 8);
+    s2 = e8m0_to_f32(sv >> 16);
+    s3 = e8m0_to_f32(sv >> 24);
+  }
+}
+
 __device__ __forceinline__ float f16_lo(uint32_t h2) { return __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFF))); }
 __device__ __forceinline__ float f16_hi(uint32_t h2) { return __half2float(__ushort_as_half((unsigned short)(h2 >> 16))); }
 
@@ -99,8 +115,7 @@ __device__ __forceinline__ float f16_hi(uint32_t h2) { return __half2float(__ush
 // B registers: b0 = K 4t..4t+3 of column g, b1 = K 16+4t.. of column g.
 __device__ __forceinline__ void mma_e4m3(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 "
+  asm("mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -109,8 +124,7 @@ __device__ __forceinline__ void mma_e4m3(float (&d)[4], uint32_t a0, uint32_t a1
 // D = A * B with C = 0 (a fresh partial that the caller scales).
 __device__ __forceinline__ void mma_e4m3_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                            uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 "
+  asm("mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
@@ -152,8 +166,8 @@ __device__ __forceinline__ void fp4_chunk_mma(const uint4& w, uint32_t sv, const
   fp4w_to_e4m3(w.y, l1, h1);
   fp4w_to_e4m3(w.z, l2, h2);
   fp4w_to_e4m3(w.w, l3, h3);
-  const float sa0 = e8m0_to_f32(sv), sa1 = e8m0_to_f32(sv >> 16);
-  const float sb0 = e8m0_to_f32(sv >> 8), sb1 = e8m0_to_f32(sv >> 24);
+  float sa0, sb0, sa1, sb1;
+  e8m0x4_to_f32(sv, sa0, sb0, sa1, sb1);
 #pragma unroll
   for (int j = 0; j < NTL; ++j) {
     float d[4], e[4];
@@ -244,6 +258,19 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
       ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
+// L2 policy for bytes read once per step (expert and router weights): first to be evicted, so the
+// kernel's code, tokens and scratch stay resident in L2 across the stream.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 __device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

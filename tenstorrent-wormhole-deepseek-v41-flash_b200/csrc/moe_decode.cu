@@ -21,16 +21,6 @@
 
 namespace dsmoe {
 
-// fused persistent path (moe_fused.cu)
-struct FusedScratch {
-  size_t rl, p13, p2, hq, cnt13, cnt2, gbar, status, total;
-  int p13max, qmax, slots;
-};
-FusedScratch fused_scratch(int H, int I_loc, int E, int B, int topk, int r_fmt);
-bool fused_supported(const dsmoe_layer_t* L, int B);
-int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image_mask, void* y, int y_dtype,
-                 int64_t* idx, float* wt, float* scores, uint8_t* ws, cudaStream_t st, void* const* events);
-
 struct DecodeArgs {
   int H, I_loc, E, B;
   int r_fmt;
@@ -210,8 +200,7 @@ __device__ __forceinline__ void w2_run(const DecodeArgs& a, float* yw, int nt, i
   const uint8_t* hr[NTL];
 #pragma unroll
   for (int j = 0; j < NTL; ++j)
-    hr[j] = a.hq + slot * hq_slot_bytes(a.I_loc) + (g & 1) * (DSMOE_SLOT_TOKENS * kHPartK) +
-            min(4 * j + (g >> 1), ntok - 1) * kHPartK + tq * 16;
+    hr[j] = a.hq + hq_row(a.I_loc, slot, g & 1, min(4 * j + (g >> 1), ntok - 1)) + tq * 16;
   float acc[NTL][4];
 #pragma unroll
   for (int j = 0; j < NTL; ++j)
@@ -234,7 +223,7 @@ __device__ __forceinline__ void w2_run(const DecodeArgs& a, float* yw, int nt, i
           s[i] = __ldg(reinterpret_cast<const float*>(tile + fp8_w2_scale_off(k >> 3, KC8)) + (k & 7));
 #pragma unroll
           for (int j = 0; j < NTL; ++j)
-            hv[i][j] = *reinterpret_cast<const uint2*>(hr[j] + (k >> 3) * kHPartBytes + ((k & 7) >> 1) * 64 + (k & 1) * 8);
+            hv[i][j] = *reinterpret_cast<const uint2*>(hr[j] + (k >> 1) * 64 + (k & 1) * 8);
         }
       }
 #pragma unroll
@@ -265,7 +254,7 @@ __device__ __forceinline__ void w2_run(const DecodeArgs& a, float* yw, int nt, i
           wv[i] = ld_stream16(ch + lane * 16);
           sv[i] = __ldg(reinterpret_cast<const uint32_t*>(ch + 512) + g);
 #pragma unroll
-          for (int j = 0; j < NTL; ++j) hv[i][j] = ld16(hr[j] + (k >> 2) * kHPartBytes + (k & 3) * 64);
+          for (int j = 0; j < NTL; ++j) hv[i][j] = ld16(hr[j] + k * 64);
         }
       }
 #pragma unroll
@@ -482,7 +471,7 @@ static int moe_decode_impl(const dsmoe_layer_t* L, const void* x, int B, const u
                 w.total);
   uint8_t* ws = (uint8_t*)workspace;
   cudaStream_t st = (cudaStream_t)stream;
-  if (fused_region(L) > 0 && fused_supported(L, B))
+  if (fused_region(L) > 0 && fused_supported(L, B) && ((uintptr_t)x & 15) == 0)  // 16-byte token loads
     return launch_fused(L, x, B, image_mask, y, y_dtype, idx, wt, scores, ws, st, events);
   RouterArgs ra = router_args(L, x, B, image_mask, idx, wt, scores, ws, w);
   if (events) cudaEventRecord((cudaEvent_t)events[0], st);

@@ -5,51 +5,54 @@
 // (dsv41/tt/model.py:400-442; dsv41/tt/moe.py:108-180; dsv41/kernels/slot_cat.cpp) -- with one
 // launch that streams every weight byte the step needs exactly once.
 //
-// Shape: one CTA per SM (cooperative launch), 7 consumer warps + 1 producer warp.
-//   producer   one thread issues 1-D bulk copies (cp.async.bulk, the TMA engine) of everything a
-//              work item reads -- its packed weights, their FP8 scales and, for w2 items, the h
-//              rows of its slot -- into a ring of 14 x 8.5 KB shared-memory stages, counted
-//              on one mbarrier per stage. It runs ahead across phase boundaries: w2 weights stream
-//              in while the grid still waits for the last w1|w3 tiles; their h rows follow as soon
-//              as grid barrier B has passed.
-//   consumers  read nothing from global memory on the streaming path: A fragments straight from
-//              the stage (FP8 bytes as they are, FP4 expanded to e4m3 with integer operations),
-//              mma.sync m16n8k32 e4m3 x e4m3 -> fp32 against the tokens' e4m3 hi / lo rows (shared
-//              memory) or the stage's h rows, block scales on the fp32 partials.
-// Work distribution: every phase is a flat list of items (2-8.5 KB each); each CTA takes a
-// contiguous span and each consumer warp a contiguous run of it, so a warp accumulates the
-// consecutive parts of a 16-row tile in registers and publishes one partial per tile it shares.
-// The last contributor of a tile (counter in the workspace) re-derives the tile's segments from
-// the same deterministic distribution and sums them in order: results do not depend on timing.
+// Shape: one CTA per SM (cooperative launch), 8 warps. Every warp walks its own list of work items
+// and keeps two of them in flight: lane 0 issues a 1-D bulk copy (cp.async.bulk, the TMA engine,
+// L2 evict-first) of an item's packed weights and scales into one of the warp's two 8.5 KB
+// shared-memory stages, counted on that stage's mbarrier, while the warp computes on the other. A
+// stage is refilled by the warp that just read it. Compute reads nothing from global memory on
+// the streaming path: A fragments straight from the stage (FP8 bytes as they are, FP4 expanded to
+// e4m3 with integer operations), mma.sync m16n8k32 e4m3 x e4m3 -> fp32 against e4m3 hi / lo
+// activation rows held in shared memory, block scales on the fp32 partials.
+// A warp accumulates consecutive items of one output tile in registers and writes one partial per
+// tile it shares with other warps; every sum over partials runs in a fixed order derived from the
+// deterministic distribution, so results do not depend on timing.
 // Phases:
-//   R  router quarter-rows (fp64) and the shared expert's w1|w3 parts (no routing needed), both
-//      spread over all CTAs; a CTA arrives at grid barrier A when its router rows are done.
-//   P  every CTA computes the same scores, top-k and slot plan (shared memory scratch).
-//   1  routed w1|w3 parts; tile epilogue: clamp / SiLU / up -> h (e4m3 hi / lo rows).
-//   2  after grid barrier B: w2 parts (16 output rows x slot x 256 K), routing weight on the fp32
-//      partials; tile epilogue -> y.
-// Every wait (mbarrier, grid barrier) is bounded by %globaltimer; on expiry the kernel records a
-// status bit in the workspace, stops issuing work, lets its own copies land and returns.
+//   R  router quarter-rows (fp64 accumulation), spread round-robin over the warps, while the shared
+//      expert's weights (routing-independent) are prefetched into L2; then grid barrier A.
+//   P  every CTA computes the same scores, top-k and slot plan (shared memory).
+//   1  w1|w3 items (slot, 16-row tile, part) of the routed slots and of the shared expert (the last
+//      slot). A tile split between warps is published (one fence per batch, one counter per tile)
+//      and finished by its last contributor: clamp / SiLU / up -> h as e4m3 hi / lo rows in the
+//      workspace, and a per-slot count of finished tiles.
+//   2  w2 items (slot, 16 output rows, 512 K of FP8 or 1024 K of FP4), slot-major, so a CTA touches
+//      at most two slots: once their tiles are counted it copies their h rows into shared memory.
+//      Routing weight on the fp32 partials; after grid barrier C every warp of the grid sums the
+//      slots' partials of (at most a few) 16-row output tiles into y.
+// Every wait (mbarrier, grid barrier, slot count) is bounded by %globaltimer; on expiry the kernel
+// records a status bit in the workspace, stops consuming, lets its own copies land and returns.
 #include "router.cuh"
 
 namespace dsmoe {
 
-constexpr int FW = 7;                  // consumer warps (+1 producer: two warps per SM sub-partition)
-constexpr int FT = (FW + 1) * 32;      // + producer warp
+constexpr int FW = 8;                  // warps per CTA
+constexpr int FT = FW * 32;
+constexpr int SPW = 2;                 // stages per warp
+constexpr int NST = FW * SPW;
 constexpr int FCH = 8;                 // packed chunks per w1|w3 item
-constexpr int FSTAGE = FCH * 1088;     // bytes per ring stage (8 FP4 w1|w3 chunks, the largest item)
-constexpr int FK2 = 256;               // K values per w2 item (8 FP8 chunks or 4 FP4 chunks)
-constexpr int FH2 = kFp8W2Item;        // w2 stage: the packed item (<= 4128 B), then the slot's h
-constexpr int FH2T = 8 * kHPartK + 64; // rows: hi rows at FH2, lo rows FH2T further (the 64-byte
-                                       // offset puts the two terms in opposite bank halves)
-static_assert(FH2 + FH2T + 8 * kHPartK <= FSTAGE, "w2 stage overflow");
+constexpr int FSTAGE = FCH * 1088;     // bytes per stage (8 FP4 w1|w3 chunks, the largest item)
+constexpr int FK2_8 = 512;             // K per FP8 w2 item: two 8-chunk store items (8256 B)
+constexpr int FK2_4 = 1024;            // K per FP4 w2 item: 16 chunks of 544 B (8704 B)
+static_assert(2 * kFp8W2Item <= FSTAGE && 16 * 544 <= FSTAGE, "w2 item exceeds a stage");
 constexpr int FMAXB = 8;               // tokens per call
+constexpr int FXB = 4;                 // up to this many tokens keep bf16 x in shared memory (router)
 constexpr int FMAXK = DSMOE_MAX_TOPK;
 constexpr int FMAXS = FMAXB * FMAXK + 1;
 constexpr int FEMAX = 1024;            // routed experts
+constexpr int FHSLOTS = 2;             // slots whose h rows a CTA stages for phase 2
+constexpr int NPEND = 8;               // segments a warp holds before publishing them
 constexpr uint64_t kWaitNs = 1000000000ull;
 
-enum : unsigned { ST_FULL = 1u, ST_EMPTY = 2u, ST_PLAN = 4u, ST_GRID = 8u };
+enum : unsigned { ST_FULL = 1u, ST_SLOT = 2u, ST_GRID = 8u };
 
 struct FusedArgs {
   int H, I_loc, E, B, topk, score_func;
@@ -71,16 +74,17 @@ struct FusedArgs {
   float* wt;
   float* scores;
   // scratch (workspace)
-  double* rl;        // [8][E][4] router quarter-row partial logits
-  float* p13;        // [slots][T][p13max][32][8] w1|w3 tile-segment partials
-  float* p2;         // [NT][qmax][32][4] w2 tile-segment partials (token columns)
-  uint8_t* hq;       // [slots] h rows, e4m3 hi / lo (hq_off)
-  unsigned* cnt13;   // [slots][T]
-  unsigned* cnt2;    // [NT]
-  unsigned* gbar;    // [0] arrivals, [1] generation
-  unsigned* status;  // [0]
-  int sh_idx;        // scratch slot index of the shared expert
-  int nstage, xrs, p13max, qmax;   // xrs: bytes per token row (hi or lo) in shared memory
+  double* rl;          // [8][E][4] router quarter-row partial logits
+  float* p13;          // [slots][T][p13max][32][8] w1|w3 tile-segment partials
+  float* p2;           // [NT][slots][p2max][32][4] w2 segment partials (token columns)
+  uint8_t* hq;         // [slots] h rows, e4m3 hi / lo (hq_row)
+  unsigned* cnt13;     // [slots][T]
+  unsigned* cnt2;      // [NT]
+  unsigned* slot_done; // [slots] finished w1|w3 tiles per routed slot
+  unsigned* gbar;      // [0] arrivals, [1] generation
+  unsigned* status;    // [0]
+  int sh_idx;          // scratch slot index of the shared expert
+  int slots, p13max, p2max;
 };
 
 struct FPlan {
@@ -91,17 +95,43 @@ struct FPlan {
   float wt[FMAXS][8];
   signed char col_of[FMAXS][8];
   float xscale[FMAXB];
+  float xinv[FMAXB];
+  float red[FW][FMAXB];
   int sel[FMAXB][FMAXK];
   float selw[FMAXB][FMAXK];
   int wcnt[FW];
-  unsigned router_done;
-  unsigned gen_a;
   int abort;
 };
 
+// Shared-memory carve-up (host and device agree): stage ring; token rows (e4m3 hi rows [B][H], lo
+// rows [B][H] 64 bytes further) and bf16 token rows for the router (B <= FXB), a region that phase 2
+// reuses for the h rows of up to FHSLOTS slots; stage mbarriers + the h mbarrier; plan; per-expert
+// token masks.
+struct SmemLayout {
+  size_t xq, xs, hs_stride, bars, plan, emask, total;
+};
+__host__ __device__ inline SmemLayout smem_layout(int H, int I_loc, int B, int E) {
+  SmemLayout L;
+  size_t o = (size_t)NST * FSTAGE;
+  L.xq = o;
+  const size_t xbytes = 2 * (size_t)B * H + 64 + (B <= FXB ? (size_t)B * H * 2 : 0);
+  L.xs = o + 2 * (size_t)B * H + 64;
+  L.hs_stride = 2 * (size_t)B * hq_row_bytes(I_loc) + 64;
+  const size_t hbytes = FHSLOTS * L.hs_stride;
+  o += xbytes > hbytes ? xbytes : hbytes;
+  o = (o + 15) & ~size_t(15);
+  L.bars = o;
+  o += (size_t)(NST + 1) * 8;
+  L.plan = o;
+  o += (sizeof(FPlan) + 15) & ~size_t(15);
+  L.emask = o;
+  o += (size_t)E * 4;
+  L.total = o;
+  return L;
+}
+
 struct Geo {
-  int T, NT, KB, NR, NS, P13s, P13r, P2;
-  int chunk13r, chunk2r, nch2r;
+  int T, NT, NR, NS, P13s, P13r, P2r, P2s;
   long long tile13r, tile13s, tile2r, tile2s;
 };
 
@@ -109,15 +139,12 @@ __device__ __forceinline__ Geo make_geo(const FusedArgs& a) {
   Geo g;
   g.T = a.I_loc / 16;
   g.NT = a.H / 16;
-  g.KB = a.H / 128;
   g.NR = 4 * a.E;
   g.P13s = (a.H / 32) / FCH;
   g.P13r = a.r_fmt == DSMOE_FMT_FP8 ? (a.H / 32) / FCH : (a.H / 64) / FCH;
   g.NS = g.T * g.P13s;
-  g.P2 = (a.I_loc + FK2 - 1) / FK2;
-  g.chunk13r = a.r_fmt == DSMOE_FMT_FP8 ? 1024 : 1088;
-  g.chunk2r = a.r_fmt == DSMOE_FMT_FP8 ? 512 : 544;
-  g.nch2r = a.r_fmt == DSMOE_FMT_FP8 ? FK2 / 32 : FK2 / 64;
+  g.P2r = a.r_fmt == DSMOE_FMT_FP8 ? (a.I_loc + FK2_8 - 1) / FK2_8 : (a.I_loc + FK2_4 - 1) / FK2_4;
+  g.P2s = (a.I_loc + FK2_8 - 1) / FK2_8;
   g.tile13r = w13_tile_bytes(a.r_fmt, a.H);
   g.tile13s = fp8_w13_tile_bytes(a.H);
   g.tile2r = w2_tile_bytes(a.r_fmt, a.I_loc);
@@ -129,7 +156,7 @@ __device__ __forceinline__ Geo make_geo(const FusedArgs& a) {
 struct Span {
   int s, e;
 };
-__device__ __forceinline__ Span cta_span(int n, int c, int G) {
+__host__ __device__ __forceinline__ Span cta_span(int n, int c, int G) {
   return {(int)((long long)n * c / G), (int)((long long)n * (c + 1) / G)};
 }
 __device__ __forceinline__ Span warp_run(Span cs, int w) {
@@ -137,8 +164,8 @@ __device__ __forceinline__ Span warp_run(Span cs, int w) {
   const int rs = cs.s + w * L + min(w, r);
   return {rs, rs + L + (w < r ? 1 : 0)};
 }
-// Phases 1 and 2: item i of n belongs to CTA span / warp run as above. Calls f(first item of the
-// segment - a) for every warp run that intersects [a, b), in order.
+// Item i of n belongs to CTA span / warp run as above. Calls f(first item of the segment - a) for
+// every warp run that intersects [a, b), in order.
 template <class F>
 __device__ __forceinline__ void for_segments(int n, int G, int a, int b, F&& f) {
   int c = (int)(((long long)a * G) / n);
@@ -155,27 +182,65 @@ __device__ __forceinline__ void for_segments(int n, int G, int a, int b, F&& f) 
     }
   }
 }
-// Phase R: CTA c's local list is its router span (over NR) followed by its shared-expert span
-// (over NS); warp runs split the local list. Same contract as for_segments, over the NS items.
-template <class F>
-__device__ __forceinline__ void for_segments_R(int NR, int NS, int G, int a, int b, F&& f) {
-  int c = (int)(((long long)a * G) / NS);
-  while (c + 1 < G && cta_span(NS, c + 1, G).s <= a) ++c;
-  while (c > 0 && cta_span(NS, c, G).s > a) --c;
-  for (; c < G; ++c) {
-    const Span ss = cta_span(NS, c, G);
-    if (ss.s >= b) break;
-    const Span rs = cta_span(NR, c, G);
-    const int rc = rs.e - rs.s;
-    const Span local = {0, rc + ss.e - ss.s};
-    for (int w = 0; w < FW; ++w) {
-      const Span r = warp_run(local, w);
-      const int s0 = max(r.s, rc) - rc + ss.s, s1 = r.e - rc + ss.s;  // the run's shared items
-      if (r.e <= rc || s1 <= a || s0 >= s1) continue;
-      if (s0 >= b) break;
-      f(max(s0, a) - a);
+
+// Phase-2 item space: routed slots first (NT x P2r items each), then the shared slot (NT x P2s),
+// (slot, 16-row n-tile, part) with the part fastest.
+struct W2Item {
+  int s, nt, p;
+};
+__device__ __forceinline__ W2Item w2_item(const Geo& g, int nr, int i) {
+  W2Item w;
+  const int NR2 = nr * g.NT * g.P2r;
+  if (i < NR2) {
+    w.s = i / (g.NT * g.P2r);
+    const int r = i - w.s * g.NT * g.P2r;
+    w.nt = r / g.P2r;
+    w.p = r - w.nt * g.P2r;
+  } else {
+    w.s = nr;
+    const int r = i - NR2;
+    w.nt = r / g.P2s;
+    w.p = r - w.nt * g.P2s;
+  }
+  return w;
+}
+__device__ __forceinline__ int w2_range_start(const Geo& g, int nr, int s, int nt) {
+  return s < nr ? (s * g.NT + nt) * g.P2r : nr * g.NT * g.P2r + nt * g.P2s;
+}
+
+// Position of a warp's item in the phase-1 or phase-2 item space, advanced without divisions:
+// phase 1 (slot s, 16-row tile t, part p), phase 2 (slot s, n-tile t, part p). Routed slots come
+// first; slot nr is the shared expert, with its own part count.
+struct Cursor {
+  int s, t, p;
+  __device__ __forceinline__ void next(int nr, int n_t, int pr, int ps) {
+    if (++p == (s < nr ? pr : ps)) {
+      p = 0;
+      if (++t == n_t) {
+        t = 0;
+        ++s;
+      }
     }
   }
+};
+__device__ __forceinline__ Cursor cursor1(const Geo& g, int nr, int NR1, int i) {
+  Cursor c;
+  if (i < NR1) {
+    const int tile = i / g.P13r;
+    c.p = i - tile * g.P13r;
+    c.s = tile / g.T;
+    c.t = tile - c.s * g.T;
+  } else {
+    const int j = i - NR1;
+    c.t = j / g.P13s;
+    c.p = j - c.t * g.P13s;
+    c.s = nr;
+  }
+  return c;
+}
+__device__ __forceinline__ Cursor cursor2(const Geo& g, int nr, int i) {
+  const W2Item w = w2_item(g, nr, i);
+  return {w.s, w.nt, w.p};
 }
 
 __device__ __forceinline__ float fscore(float l, int func) {
@@ -190,58 +255,151 @@ __device__ __forceinline__ float ldsf(const uint8_t* p) { return *reinterpret_ca
 
 __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
 
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const unsigned* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // ------------------------------------------------------------------ grid barrier (bounded)
+// Arrive: the CTA's writes are ordered before it by the caller's __syncthreads and this thread's
+// fence; the last arrival resets the count and bumps the generation with release semantics.
+// Wait: relaxed polling, one acquire fence once the generation moved.
 __device__ __forceinline__ unsigned grid_arrive(unsigned* gbar, int G) {
   const unsigned g0 = ld_acquire_u32(gbar + 1);
-  __threadfence();
-  const unsigned old = atomicAdd(gbar, 1u);
+  fence_acq_rel_gpu();
+  unsigned old;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(gbar) : "memory");
   if (old == (unsigned)G - 1) {
-    atomicExch(gbar, 0u);
-    __threadfence();
-    atomicAdd(gbar + 1, 1u);
+    asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(gbar) : "memory");
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(gbar + 1) : "memory");
   }
   return g0;
 }
 __device__ __forceinline__ bool grid_wait(unsigned* gbar, unsigned g0, const unsigned* status) {
   const uint64_t t0 = globaltimer_ns();
-  while (ld_acquire_u32(gbar + 1) == g0) {
-    if (ld_acquire_u32(status) != 0u) return false;
+  while (ld_relaxed_u32(gbar + 1) == g0) {
+    if (ld_relaxed_u32(status) != 0u) return false;
     if (globaltimer_ns() - t0 > kWaitNs) return false;
-    __nanosleep(32);
   }
+  fence_acq_rel_gpu();
   return true;
 }
 
 // ------------------------------------------------------------------ router
-// Router quarter-row: 1/4 of gate_w[r] (H/4 fp32, in the stage) . x[b] for every token, fp64.
-// The token's values come from global memory (L1-resident after the first row); each token's
-// loads are all issued before its multiply-adds.
-__device__ void router_item(const FusedArgs& a, const uint8_t* stage, int r, int q, int lane) {
+// Router quarter-row: 1/4 of gate_w[r] (H/4 fp32, in the stage) . x[b] for every token, each
+// product exact in fp64 and accumulated there (rounded to fp32 once, after the four quarters).
+// x comes from shared memory (B <= FXB) or global memory; both through one generic pointer.
+__device__ void router_item(const FusedArgs& a, const uint8_t* stage, const __nv_bfloat16* xsrc, int r, int q,
+                            int lane) {
   const float4* wv = reinterpret_cast<const float4*>(stage);
-  const int n4 = a.H / 16;  // float4 per quarter (<= 512 for H <= 8192)
-  for (int b = 0; b < a.B; ++b) {
-    const __nv_bfloat16* xr = a.x + (long long)b * a.H + q * (a.H / 4);
-    uint2 xv[16];
-#pragma unroll
-    for (int it = 0; it < 16; ++it) {
-      const int f = lane + 32 * it;
-      if (f < n4) xv[it] = __ldg(reinterpret_cast<const uint2*>(xr + 4 * f));
-    }
-    double acc = 0.0;
-#pragma unroll
-    for (int it = 0; it < 16; ++it) {
-      const int f = lane + 32 * it;
-      if (f < n4) {
+  const int n4 = a.H / 16;  // float4 per quarter
+  for (int b0 = 0; b0 < a.B; b0 += 2) {  // two tokens at a time (one for an odd last), four chains each
+    const __nv_bfloat16* x0 = xsrc + (long long)b0 * a.H + q * (a.H / 4);
+    if (b0 + 1 < a.B) {
+      const __nv_bfloat16* x1 = x0 + a.H;
+      double acc[2][4] = {{0.0, 0.0, 0.0, 0.0}, {0.0, 0.0, 0.0, 0.0}};
+#pragma unroll 2
+      for (int f = lane; f < n4; f += 32) {
         const float4 w = wv[f];
-        acc = fma((double)__uint_as_float(xv[it].x << 16), (double)w.x, acc);
-        acc = fma((double)__uint_as_float(xv[it].x & 0xFFFF0000u), (double)w.y, acc);
-        acc = fma((double)__uint_as_float(xv[it].y << 16), (double)w.z, acc);
-        acc = fma((double)__uint_as_float(xv[it].y & 0xFFFF0000u), (double)w.w, acc);
+        const double w0 = w.x, w1 = w.y, w2 = w.z, w3 = w.w;
+        const uint2 u0 = *reinterpret_cast<const uint2*>(x0 + 4 * f);
+        const uint2 u1 = *reinterpret_cast<const uint2*>(x1 + 4 * f);
+        acc[0][0] = fma((double)__uint_as_float(u0.x << 16), w0, acc[0][0]);
+        acc[0][1] = fma((double)__uint_as_float(u0.x & 0xFFFF0000u), w1, acc[0][1]);
+        acc[0][2] = fma((double)__uint_as_float(u0.y << 16), w2, acc[0][2]);
+        acc[0][3] = fma((double)__uint_as_float(u0.y & 0xFFFF0000u), w3, acc[0][3]);
+        acc[1][0] = fma((double)__uint_as_float(u1.x << 16), w0, acc[1][0]);
+        acc[1][1] = fma((double)__uint_as_float(u1.x & 0xFFFF0000u), w1, acc[1][1]);
+        acc[1][2] = fma((double)__uint_as_float(u1.y << 16), w2, acc[1][2]);
+        acc[1][3] = fma((double)__uint_as_float(u1.y & 0xFFFF0000u), w3, acc[1][3]);
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const double v = warp_sum_d((acc[j][0] + acc[j][1]) + (acc[j][2] + acc[j][3]));
+        if (lane == 0) a.rl[((long long)(b0 + j) * a.E + r) * 4 + q] = v;
+      }
+    } else {
+      double acc[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll 2
+      for (int f = lane; f < n4; f += 32) {
+        const float4 w = wv[f];
+        const uint2 u0 = *reinterpret_cast<const uint2*>(x0 + 4 * f);
+        acc[0] = fma((double)__uint_as_float(u0.x << 16), (double)w.x, acc[0]);
+        acc[1] = fma((double)__uint_as_float(u0.x & 0xFFFF0000u), (double)w.y, acc[1]);
+        acc[2] = fma((double)__uint_as_float(u0.y << 16), (double)w.z, acc[2]);
+        acc[3] = fma((double)__uint_as_float(u0.y & 0xFFFF0000u), (double)w.w, acc[3]);
+      }
+      const double v = warp_sum_d((acc[0] + acc[1]) + (acc[2] + acc[3]));
+      if (lane == 0) a.rl[((long long)b0 * a.E + r) * 4 + q] = v;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ token rows
+// bf16 x -> shared memory (router copy for B <= FXB), per-token power-of-2 pre-scale (amax * 2^-p in
+// [128, 256)), e4m3 hi / lo rows in B-operand order (qk_off). All threads; ends with __syncthreads.
+__device__ void setup_tokens(const FusedArgs& a, uint8_t* xq, __nv_bfloat16* xs, FPlan& pl, int lo_off) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nv = a.H / 8;  // uint4 per row
+  for (int b = 0; b < a.B; ++b) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.x + (long long)b * a.H);
+    uint4* dst = reinterpret_cast<uint4*>(xs + (long long)b * a.H);
+    float m = 0.f;
+    for (int v = tid; v < nv; v += FT) {
+      const uint4 u = __ldg(src + v);
+      if (a.B <= FXB) dst[v] = u;
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h)
+        m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w[h] << 16)), fabsf(__uint_as_float(w[h] & 0xFFFF0000u))));
+    }
+    m = warp_max(m);
+    if (lane == 0) pl.red[warp][b] = m;
+  }
+  __syncthreads();
+  if (tid < a.B) {
+    float m = 0.f;
+    for (int w = 0; w < FW; ++w) m = fmaxf(m, pl.red[w][tid]);
+    int p = 0;
+    if (m > 0.f && m <= 3.0e38f) {
+      int e2;
+      frexpf(m, &e2);
+      p = e2 - 8;
+    }
+    pl.xscale[tid] = ldexpf(1.0f, p);
+    pl.xinv[tid] = ldexpf(1.0f, -p);
+  }
+  __syncthreads();
+  const int nch = a.H / 32;
+  for (int i = tid; i < a.B * nch; i += FT) {
+    const int b = i / nch, c = i - b * nch;
+    const uint4* src = reinterpret_cast<const uint4*>((a.B <= FXB ? xs : a.x) + (long long)b * a.H + 32 * c);
+    const float inv = pl.xinv[b];
+    float v[32];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 u = src[q];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        v[8 * q + 2 * h] = __uint_as_float(w[h] << 16) * inv;
+        v[8 * q + 2 * h + 1] = __uint_as_float(w[h] & 0xFFFF0000u) * inv;
       }
     }
-    acc = warp_sum_d(acc);
-    if (lane == 0) a.rl[((long long)b * a.E + r) * 4 + q] = acc;
+    uint8_t* rh = xq + (long long)b * a.H + (c >> 1) * 64 + (c & 1) * 8;
+#pragma unroll
+    for (int tt = 0; tt < 4; ++tt) {  // lane-group tt's 8 bytes of this 32-K chunk, per term
+      uint32_t h0, l0, h1, l1, h2, l2, h3, l3;
+      split2_e4m3(v[4 * tt], v[4 * tt + 1], h0, l0);
+      split2_e4m3(v[4 * tt + 2], v[4 * tt + 3], h1, l1);
+      split2_e4m3(v[16 + 4 * tt], v[16 + 4 * tt + 1], h2, l2);
+      split2_e4m3(v[16 + 4 * tt + 2], v[16 + 4 * tt + 3], h3, l3);
+      *reinterpret_cast<uint2*>(rh + tt * 16) = make_uint2(h0 | (h1 << 16), h2 | (h3 << 16));
+      *reinterpret_cast<uint2*>(rh + lo_off + tt * 16) = make_uint2(l0 | (l1 << 16), l2 | (l3 << 16));
+    }
   }
+  __syncthreads();
 }
 
 // ------------------------------------------------------------------ w1|w3
@@ -255,18 +413,14 @@ __device__ __forceinline__ void w13_accum(const uint8_t* stage, const uint8_t* c
   const int g = lane >> 2;
   if (FMT == DSMOE_FMT_FP8) {
 #pragma unroll
-    for (int blk = 0; blk < 2; ++blk) {  // two 128-K blocks, four chunks each, one MMA chain per
-      uint4 X[NTL][2];                   // matrix and n-tile (seven warps hide its latency)
+    for (int blk = 0; blk < 2; ++blk) {  // two 128-K blocks, four chunks each
+      uint4 X[NTL][2];
 #pragma unroll
       for (int j = 0; j < NTL; ++j) {
         X[j][0] = lds16(xr[j] + (4 * p + 2 * blk) * 64);
         X[j][1] = lds16(xr[j] + (4 * p + 2 * blk + 1) * 64);
       }
-      float u1[NTL][4], u3[NTL][4];
-#pragma unroll
-      for (int j = 0; j < NTL; ++j)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) u1[j][q] = u3[j][q] = 0.f;
+      float u1[4][NTL][4], u3[4][NTL][4];  // every MMA of the block independent
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const uint4 A1 = lds16(stage + (4 * blk + c) * 1024 + lane * 16);
@@ -275,8 +429,8 @@ __device__ __forceinline__ void w13_accum(const uint8_t* stage, const uint8_t* c
         for (int j = 0; j < NTL; ++j) {
           const uint4 xb = X[j][c >> 1];
           const uint32_t b0 = (c & 1) ? xb.z : xb.x, b1 = (c & 1) ? xb.w : xb.y;
-          mma_e4m3(u1[j], A1.x, A1.y, A1.z, A1.w, b0, b1);
-          mma_e4m3(u3[j], A3.x, A3.y, A3.z, A3.w, b0, b1);
+          mma_e4m3_z(u1[c][j], A1.x, A1.y, A1.z, A1.w, b0, b1);
+          mma_e4m3_z(u3[c][j], A3.x, A3.y, A3.z, A3.w, b0, b1);
         }
       }
       const float s1 = ldsf(stage + FCH * 1024 + 4 * fp8_w13_scale_index(blk, 0));
@@ -285,12 +439,12 @@ __device__ __forceinline__ void w13_accum(const uint8_t* stage, const uint8_t* c
       for (int j = 0; j < NTL; ++j)
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          acc1[j][q] = fmaf(u1[j][q], s1, acc1[j][q]);
-          acc3[j][q] = fmaf(u3[j][q], s3, acc3[j][q]);
+          acc1[j][q] = fmaf((u1[0][j][q] + u1[1][j][q]) + (u1[2][j][q] + u1[3][j][q]), s1, acc1[j][q]);
+          acc3[j][q] = fmaf((u3[0][j][q] + u3[1][j][q]) + (u3[2][j][q] + u3[3][j][q]), s3, acc3[j][q]);
         }
     }
   } else {
-#pragma unroll
+#pragma unroll 1
     for (int c0 = 0; c0 < FCH; c0 += 2) {  // two chunks (four k32 MMAs per matrix and n-tile) at a time
       uint4 A1[2], A3[2], X[2][NTL];
       uint32_t S1[2], S3[2];
@@ -342,119 +496,167 @@ __device__ __forceinline__ void w13_epilogue(const FusedArgs& a, const FPlan& pl
   }
 }
 
-// A warp's contribution to one tile ends: publish it, or finish the tile if the warp covered all
-// of it. seg_rel = the segment's first item minus the tile's first item. `segs` enumerates the
-// tile's segments (same order everywhere) for the last contributor.
-template <class Segs>
-__device__ void w13_flush(const FusedArgs& a, const Geo& G, const FPlan& pl, int P, int seg_rel, int seg_np, int sidx,
-                          int t, const float (&acc1)[2][4], const float (&acc3)[2][4], int ntok, const int* toks,
-                          float fmtf, int lane, Segs&& segs) {
-  float s[8];
+// hi + lo / 16 per row: the 8 per-lane values of a w1|w3 tile segment.
+__device__ __forceinline__ void w13_combine(const float (&acc1)[2][4], const float (&acc3)[2][4], float (&s)[8]) {
 #pragma unroll
-  for (int j = 0; j < 2; ++j) {  // hi + lo / 16 per row
+  for (int j = 0; j < 2; ++j) {
     s[4 * j] = acc1[j][0] + acc1[j][1] * kLoInv;
     s[4 * j + 1] = acc1[j][2] + acc1[j][3] * kLoInv;
     s[4 * j + 2] = acc3[j][0] + acc3[j][1] * kLoInv;
     s[4 * j + 3] = acc3[j][2] + acc3[j][3] * kLoInv;
   }
-  if (seg_np == P) {
-    w13_epilogue(a, pl, sidx, t, s, ntok, toks, fmtf, lane);
-    return;
-  }
-  float* base = a.p13 + (((long long)sidx * G.T + t) * a.p13max) * 32 * 8;
-  float* dst = base + ((long long)seg_rel * 32 + lane) * 8;
-  *reinterpret_cast<float4*>(dst) = make_float4(s[0], s[1], s[2], s[3]);
-  *reinterpret_cast<float4*>(dst + 4) = make_float4(s[4], s[5], s[6], s[7]);
-  __threadfence();
-  __syncwarp();
-  unsigned old = 0;
-  if (lane == 0) old = atomicAdd(a.cnt13 + sidx * G.T + t, (unsigned)seg_np);
-  old = __shfl_sync(0xffffffffu, old, 0);
-  if ((int)old + seg_np != P) return;
-  __threadfence();
+}
+
+// Ordered sum of published partials (nv floats per lane, nv = 4 or 8): the offsets (in floats, from
+// base) come in distribution order; up to 8 loads are in flight at a time, added in that order.
+template <int NV>
+struct SegSum {
+  const float* base;
+  float s[NV];
+  int off[8];
+  int n = 0;
+  __device__ explicit SegSum(const float* b) : base(b) {
 #pragma unroll
-  for (int j = 0; j < 8; ++j) s[j] = 0.f;
-  segs([&](int q) {
-    const float* src = base + ((long long)q * 32 + lane) * 8;
-    const uint4 v0 = ld_cg16(src), v1 = ld_cg16(src + 4);
-    s[0] += __uint_as_float(v0.x); s[1] += __uint_as_float(v0.y);
-    s[2] += __uint_as_float(v0.z); s[3] += __uint_as_float(v0.w);
-    s[4] += __uint_as_float(v1.x); s[5] += __uint_as_float(v1.y);
-    s[6] += __uint_as_float(v1.z); s[7] += __uint_as_float(v1.w);
-  });
-  w13_epilogue(a, pl, sidx, t, s, ntok, toks, fmtf, lane);
-  if (lane == 0) a.cnt13[sidx * G.T + t] = 0u;
+    for (int j = 0; j < NV; ++j) s[j] = 0.f;
+  }
+  __device__ void flush() {
+    uint4 v[8][NV / 4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < n)
+#pragma unroll
+        for (int h = 0; h < NV / 4; ++h) v[i][h] = ld_cg16(base + off[i] + 4 * h);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < n)
+#pragma unroll
+        for (int h = 0; h < NV / 4; ++h) {
+          s[4 * h] += __uint_as_float(v[i][h].x);
+          s[4 * h + 1] += __uint_as_float(v[i][h].y);
+          s[4 * h + 2] += __uint_as_float(v[i][h].z);
+          s[4 * h + 3] += __uint_as_float(v[i][h].w);
+        }
+    n = 0;
+  }
+  __device__ void add(int o) {
+    off[n++] = o;
+    if (n == 8) flush();
+  }
+};
+
+__device__ __forceinline__ float* p13_slot(const FusedArgs& a, const Geo& G, int sidx, int t, int rel, int lane) {
+  return a.p13 + ((((long long)sidx * G.T + t) * a.p13max + rel) * 32 + lane) * 8;
+}
+
+// Sum of a w1|w3 tile's published segments, in distribution order: the tile's items are
+// [a0, a0 + P) of the phase-1 item space (N1 items).
+__device__ __noinline__ void w13_reduce(const FusedArgs& a, const Geo& G, int sidx, int t, int a0, int P, int N1,
+                                        int lane, float* s) {
+  const float* base = p13_slot(a, G, sidx, t, 0, lane);
+  SegSum<8> sum(base);
+  for_segments(N1, gridDim.x, a0, a0 + P, [&](int q) { sum.add(q * 32 * 8); });
+  sum.flush();
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s[j] = sum.s[j];
 }
 
 // ------------------------------------------------------------------ w2
-// One w2 item of slot s (weights, FP8 scales and the slot's h rows all in the stage) accumulated
-// into out[] in token columns: rows g, g+8 x tokens 2tq, 2tq+1, with the routing weight.
+// One w2 item of a slot (packed weights and scales in the stage; the slot's h rows in shared memory
+// at hbase: hi rows of its ntok tokens, lo rows ntok * rp + 64 bytes further) added to tot[] in
+// slot columns (per n-tile j: rows g, g+8 x hi / lo terms of slot token 4j + tq).
+// FP8: the item is up to two 8-chunk store items, each followed by its 32 B of chunk scales.
 template <int FMT, int NTL>
-__device__ __forceinline__ void w2_accum(const FusedArgs& a, const FPlan& pl, const uint8_t* stage, int s, int p,
-                                         int lane, float (&out)[4]) {
+__device__ __forceinline__ void w2_accum(const FusedArgs& a, const uint8_t* stage, const uint8_t* hbase, int rp,
+                                         int ntok, int p, int lane, float (&tot)[2][4]) {
   const int g = lane >> 2, tq = lane & 3;
-  const int ntok = pl.ntok[s];
   const uint8_t* hr[NTL];
 #pragma unroll
-  for (int j = 0; j < NTL; ++j) hr[j] = stage + FH2 + (g & 1) * FH2T + min(4 * j + (g >> 1), ntok - 1) * kHPartK + tq * 16;
-  float tot[NTL][4];
-#pragma unroll
   for (int j = 0; j < NTL; ++j)
-#pragma unroll
-    for (int q = 0; q < 4; ++q) tot[j][q] = 0.f;
+    hr[j] = hbase + (g & 1) * (ntok * rp + 64) + min(4 * j + (g >> 1), ntok - 1) * rp + tq * 16;
   if (FMT == DSMOE_FMT_FP8) {
-    const int nch = min(8, a.I_loc / 32 - p * 8);
-    const uint8_t* sc = stage + nch * 512;
+    const int KC = a.I_loc / 32;
+#pragma unroll 1
+    for (int u = 0; u < 2; ++u) {
+      const int c0 = 16 * p + 8 * u;  // first chunk of this store item
+      const int nch = min(8, KC - c0);
+      if (nch <= 0) break;
+      const uint8_t* sub = stage + u * kFp8W2Item;
+      const uint8_t* sc = sub + nch * 512;
+      if (nch == 8) {  // full store item: every MMA independent, then the per-chunk scales
+        float d[8][NTL][4];
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {  // 64-K blocks: two chunks each
-      if (2 * b < nch) {
-        uint4 Hb[NTL];
+        for (int b = 0; b < 4; ++b) {
+          uint4 Hb[NTL];
 #pragma unroll
-        for (int j = 0; j < NTL; ++j) Hb[j] = lds16(hr[j] + b * 64);
+          for (int j = 0; j < NTL; ++j) Hb[j] = lds16(hr[j] + ((c0 >> 1) + b) * 64);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int i = 2 * b + h;
-          if (i < nch) {
-            const uint4 A0 = lds16(stage + i * 512 + lane * 16);
-            const float si = ldsf(sc + 4 * i);
+          for (int h = 0; h < 2; ++h) {
+            const uint4 A0 = lds16(sub + (2 * b + h) * 512 + lane * 16);
 #pragma unroll
-            for (int j = 0; j < NTL; ++j) {
-              float d[4];
-              mma_e4m3_z(d, A0.x, A0.y, A0.z, A0.w, h ? Hb[j].z : Hb[j].x, h ? Hb[j].w : Hb[j].y);
+            for (int j = 0; j < NTL; ++j)
+              mma_e4m3_z(d[2 * b + h][j], A0.x, A0.y, A0.z, A0.w, h ? Hb[j].z : Hb[j].x, h ? Hb[j].w : Hb[j].y);
+          }
+        }
 #pragma unroll
-              for (int q = 0; q < 4; ++q) tot[j][q] = fmaf(d[q], si, tot[j][q]);
-            }
+        for (int i = 0; i < 8; ++i) {
+          const float si = ldsf(sc + 4 * i);
+#pragma unroll
+          for (int j = 0; j < NTL; ++j)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) tot[j][q] = fmaf(d[i][j][q], si, tot[j][q]);
+        }
+      } else {
+#pragma unroll 1
+        for (int i = 0; i < nch; ++i) {  // short last store item
+          const int kc = c0 + i;
+          const uint4 A0 = lds16(sub + i * 512 + lane * 16);
+          const float si = ldsf(sc + 4 * i);
+#pragma unroll
+          for (int j = 0; j < NTL; ++j) {
+            const uint2 hb = *reinterpret_cast<const uint2*>(hr[j] + (kc >> 1) * 64 + (kc & 1) * 8);
+            float d[4];
+            mma_e4m3_z(d, A0.x, A0.y, A0.z, A0.w, hb.x, hb.y);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) tot[j][q] = fmaf(d[q], si, tot[j][q]);
           }
         }
       }
     }
   } else {
-    const int nch = min(4, a.I_loc / 64 - p * 4);
-    uint4 A0[4], Hb[4][NTL];
-    uint32_t S[4];
+    const int c0 = 16 * p, nch = min(16, a.I_loc / 64 - c0);
+#pragma unroll 1
+    for (int i0 = 0; i0 < nch; i0 += 4) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (i < nch) {
-        const uint8_t* ch = stage + i * 544;
-        A0[i] = lds16(ch + lane * 16);
-        S[i] = lds32(ch + 512 + 4 * g);
+      for (int i = i0; i < i0 + 4; ++i) {
+        if (i < nch) {
+          const uint8_t* ch = stage + i * 544;
+          const uint4 A0 = lds16(ch + lane * 16);
+          const uint32_t S = lds32(ch + 512 + 4 * g);
+          uint4 Hb[NTL];
 #pragma unroll
-        for (int j = 0; j < NTL; ++j) Hb[i][j] = lds16(hr[j] + i * 64);
+          for (int j = 0; j < NTL; ++j) Hb[j] = lds16(hr[j] + (c0 + i) * 64);
+          fp4_chunk_mma<NTL>(A0, S, Hb, tot);
+        }
       }
     }
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (i < nch) fp4_chunk_mma<NTL>(A0[i], S[i], Hb[i], tot);
   }
-  // hi + lo / 16, routing weight and the h pre-scale; then slot columns -> token columns
-  const float fs = (FMT == DSMOE_FMT_FP4 ? kFp4E4m3Scale : 1.0f) / kHScale;
-  float vg[NTL], vh[NTL];
+}
+
+// A slot's accumulated w2 partial -> token columns: hi + lo / 16, routing weight, 1 / kHScale and the
+// weight-format factor; out[h] / out[2 + h] = rows g / g + 8 of token 2tq + h. Clears tot.
+__device__ __forceinline__ void w2_fold(const FusedArgs& a, const FPlan& pl, int s, float fs, float (&tot)[2][4],
+                                        int lane, float (&out)[4]) {
+  const int g = lane >> 2, tq = lane & 3;
+  const int ntok = pl.ntok[s];
+  float vg[2], vh[2];
 #pragma unroll
-  for (int j = 0; j < NTL; ++j) {
+  for (int j = 0; j < 2; ++j) {
     const int q = 4 * j + tq;
     const float f = q < ntok ? pl.wt[s][q] * fs : 0.f;
     vg[j] = (tot[j][0] + tot[j][1] * kLoInv) * f;
     vh[j] = (tot[j][2] + tot[j][3] * kLoInv) * f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) tot[j][k] = 0.f;
   }
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -462,7 +664,7 @@ __device__ __forceinline__ void w2_accum(const FusedArgs& a, const FPlan& pl, co
     const int col = tok < a.B ? pl.col_of[s][tok] : -1;
     const int src = g * 4 + (col < 0 ? 0 : (col & 3));
 #pragma unroll
-    for (int j = 0; j < NTL; ++j) {
+    for (int j = 0; j < 2; ++j) {
       const float x0 = __shfl_sync(0xffffffffu, vg[j], src), x1 = __shfl_sync(0xffffffffu, vh[j], src);
       if (col >= 0 && (col >> 2) == j) {
         out[h] += x0;
@@ -472,7 +674,19 @@ __device__ __forceinline__ void w2_accum(const FusedArgs& a, const FPlan& pl, co
   }
 }
 
-__device__ __forceinline__ void w2_epilogue(const FusedArgs& a, int nt, const float (&s)[4], int lane) {
+__device__ __forceinline__ float* p2_slot(const FusedArgs& a, int nt, int s, int rel, int lane) {
+  return a.p2 + ((((long long)nt * a.slots + s) * a.p2max + rel) * 32 + lane) * 4;
+}
+
+// Sum over every slot's published segments of n-tile nt, in distribution order, -> y.
+__device__ __noinline__ void w2_finish(const FusedArgs& a, const Geo& G, int nr, int N2, int nt, int lane) {
+  SegSum<4> sum(p2_slot(a, nt, 0, 0, lane));
+  for (int s = 0; s <= nr; ++s) {
+    const int a0 = w2_range_start(G, nr, s, nt), len = s < nr ? G.P2r : G.P2s;
+    for_segments(N2, gridDim.x, a0, a0 + len, [&](int q) { sum.add((s * a.p2max + q) * 32 * 4); });
+  }
+  sum.flush();
+  const float* s4 = sum.s;
   const int g = lane >> 2, tq = lane & 3;
 #pragma unroll
   for (int q4 = 0; q4 < 4; ++q4) {
@@ -480,306 +694,109 @@ __device__ __forceinline__ void w2_epilogue(const FusedArgs& a, int nt, const fl
     if (tok < a.B) {
       const long long o = (long long)tok * a.H + row;
       if (a.y_f32)
-        reinterpret_cast<float*>(a.y)[o] = s[q4];
+        reinterpret_cast<float*>(a.y)[o] = s4[q4];
       else
-        reinterpret_cast<__nv_bfloat16*>(a.y)[o] = __float2bfloat16_rn(s[q4]);
+        reinterpret_cast<__nv_bfloat16*>(a.y)[o] = __float2bfloat16_rn(s4[q4]);
     }
   }
 }
 
-__device__ void w2_flush(const FusedArgs& a, int n, int Q, int nt, int seg_first, int seg_np, const float (&out)[4],
-                         int lane) {
-  float s[4] = {out[0], out[1], out[2], out[3]};
-  const int a0 = nt * Q;
-  if (seg_np == Q) {
-    w2_epilogue(a, nt, s, lane);
-    return;
-  }
-  float* base = a.p2 + ((long long)nt * a.qmax) * 32 * 4;
-  *reinterpret_cast<float4*>(base + ((long long)(seg_first - a0) * 32 + lane) * 4) = make_float4(s[0], s[1], s[2], s[3]);
-  __threadfence();
-  __syncwarp();
-  unsigned old = 0;
-  if (lane == 0) old = atomicAdd(a.cnt2 + nt, (unsigned)seg_np);
-  old = __shfl_sync(0xffffffffu, old, 0);
-  if ((int)old + seg_np != Q) return;
-  __threadfence();
-  s[0] = s[1] = s[2] = s[3] = 0.f;
-  for_segments(n, gridDim.x, a0, a0 + Q, [&](int q) {
-    const uint4 v = ld_cg16(base + ((long long)q * 32 + lane) * 4);
-    s[0] += __uint_as_float(v.x); s[1] += __uint_as_float(v.y);
-    s[2] += __uint_as_float(v.z); s[3] += __uint_as_float(v.w);
-  });
-  w2_epilogue(a, nt, s, lane);
-  if (lane == 0) a.cnt2[nt] = 0u;
-}
-
 // ------------------------------------------------------------------ the kernel
+// A published w1|w3 segment: kind 1 = tile t of slot s (np items), kind 3 = tile of slot s finished
+// by this warp alone (only the slot's count is due).
+struct Pend {
+  int kind, s, t, np;
+};
+
 template <int RFMT>
 __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
+  const SmemLayout SL = smem_layout(a.H, a.I_loc, a.B, a.E);
   uint8_t* ring = smem;
-  uint8_t* xq = ring + (size_t)a.nstage * FSTAGE;  // [B][2 terms] rows of xrs bytes
-  uint64_t* full = reinterpret_cast<uint64_t*>(xq + (size_t)a.B * 2 * a.xrs);
-  uint64_t* empty = full + a.nstage;
-  uint64_t* planbar = empty + a.nstage;  // [0] plan ready, [1] grid barrier B passed
-  FPlan& pl = *reinterpret_cast<FPlan*>(planbar + 2);
-  unsigned* emask = reinterpret_cast<unsigned*>(&pl + 1);
+  uint8_t* xq = smem + SL.xq;
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem + SL.xs);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SL.bars);
+  uint64_t* hbar = full + NST;
+  FPlan& pl = *reinterpret_cast<FPlan*>(smem + SL.plan);
+  unsigned* emask = reinterpret_cast<unsigned*>(smem + SL.emask);
+  const int lo_off = a.B * a.H + 64;  // lo token rows after the hi rows (opposite bank half)
+  const int rp = hq_row_bytes(a.I_loc);
+  constexpr float fmtf = RFMT == DSMOE_FMT_FP4 ? kFp4E4m3Scale : 1.0f;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int G = gridDim.x, cta = blockIdx.x;
   const Geo geo = make_geo(a);
-  const Span rspan = cta_span(geo.NR, cta, G), sspan = cta_span(geo.NS, cta, G);
+  const Span rspan = cta_span(geo.NR, cta, G);
   const int my_router = rspan.e - rspan.s;
-  const Span localR = {0, my_router + sspan.e - sspan.s};  // phase R: router part, then shared part
+  const int nR = my_router > warp ? (my_router - warp + FW - 1) / FW : 0;  // rows rspan.s + warp + FW * k
 
   if (tid == 0) {
-    for (int s = 0; s < a.nstage; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    mbar_init(&planbar[0], 1);
-    mbar_init(&planbar[1], 1);
-    pl.router_done = 0;
+    for (int s = 0; s <= NST; ++s) mbar_init(&full[s], 1);  // NST stage barriers + the h barrier
     pl.abort = 0;
     fence_mbar_init();
   }
   __syncthreads();
 
-  // ================================================================ producer warp
-  // Lane w (< FW) feeds consumer warp w: it walks the same runs in the same order and fills the
-  // warp's own stages (w * spw .. w * spw + spw - 1), so every stage has one issuer and one reader.
-  const int spw = a.nstage / FW;  // stages per consumer warp
-  if (warp == FW) {
-    if (lane >= FW) return;
-    const int w = lane;
-    int kw = 0;  // items issued for warp w
-    bool ok = true;
-    int def_n = 0, def_stage[2], def_slot[2], def_p[2];  // w2 items waiting for their h rows
-    bool h_open = false;
-    int kw2 = 0x7FFFFFFF;  // item number of warp w's first w2 item
-    auto copy_h = [&](int st, int slot, int p) {  // the slot's hi rows and lo rows of part p
-      const int sidx = slot < pl.n_routed ? slot : a.sh_idx;
-      const uint32_t nb = (uint32_t)(pl.ntok[slot] * kHPartK);
-      const uint8_t* src = a.hq + (long long)sidx * hq_slot_bytes(a.I_loc) + (long long)p * kHPartBytes;
-      uint8_t* dst = ring + (size_t)st * FSTAGE + FH2;
-      bulk_g2s(dst, src, nb, &full[st]);
-      bulk_g2s(dst + FH2T, src + 8 * kHPartK, nb, &full[st]);
-    };
-    auto open_h = [&]() {  // grid barrier B passed: h is complete; send the deferred h rows
-      if (h_open || !ok) return;
-      if (!mbar_wait(&planbar[1], 0, 4 * kWaitNs)) {
-        atomicOr(a.status, ST_PLAN);
-        ok = false;
-        return;
-      }
-      asm volatile("fence.proxy.async.global;" ::: "memory");
-      for (int d = 0; d < def_n; ++d) copy_h(def_stage[d], def_slot[d], def_p[d]);
-      h_open = true;
-    };
-    auto acquire = [&](int& st) -> bool {  // warp w's next stage, free
-      st = w * spw + kw % spw;
-      const int f = kw / spw;
-      if (f > 0) {
-        if (kw - spw >= kw2) open_h();  // its last occupant was a w2 item: it needs its h rows first
-        if (!ok) return false;
-        if (!mbar_wait(&empty[st], (f - 1) & 1, kWaitNs)) {
-          atomicOr(a.status, ST_EMPTY);
-          ok = false;
-          return false;
-        }
-      }
-      return true;
-    };
-    auto issue = [&](const void* src, uint32_t bytes) {
-      int st;
-      if (!ok || !acquire(st)) return;
-      mbar_expect_tx(&full[st], bytes);
-      bulk_g2s(ring + (size_t)st * FSTAGE, src, bytes, &full[st]);
-      ++kw;
-    };
-    // phase R
-    {
-      const Span run = warp_run(localR, w);
-      for (int li = run.s; li < run.e && ok; ++li) {
-        if (li < my_router) {
-          const int i = rspan.s + li;
-          issue(a.wg + (long long)(i >> 2) * a.H + (i & 3) * (a.H / 4), (uint32_t)a.H);
-        } else {
-          const int i = sspan.s + li - my_router, t = i / geo.P13s, p = i % geo.P13s;
-          issue(a.s_w13 + t * geo.tile13s + (long long)p * kFp8W13Item, kFp8W13Item);
-        }
-      }
-    }
-    if (ok && !mbar_wait(&planbar[0], 0, 4 * kWaitNs)) {
-      atomicOr(a.status, ST_PLAN);
-      ok = false;
-    }
-    if (ok) {
-      const int nr = pl.n_routed;
-      const int N1 = nr * geo.T * geo.P13r;
-      {  // phase 1: walk the run incrementally (tile, part)
-        const Span run = warp_run(cta_span(N1, cta, G), w);
-        int tile = run.s / geo.P13r, p = run.s % geo.P13r;
+  // ---- the warp's item stream: items k < nR are router rows (phase R), the next n1 belong to phase
+  // 1 and the last n2 to phase 2 (both known once the plan is). Item k lives in stage (k & 1).
+  int kc = 0, ki = 0;  // next item to consume / to issue (warp-uniform)
+  int nr = 0, n1 = 0, n2 = 0, N1 = 0, NR1 = 0, N2 = 0;
+  Span run1{0, 0}, run2{0, 0};
+  bool planned = false;
+  const uint64_t pol_stream = l2_evict_first();
+  auto stage_of = [&](int k) { return ring + (size_t)(warp * SPW + (k & 1)) * FSTAGE; };
+  auto bar_of = [&](int k) { return &full[warp * SPW + (k & 1)]; };
+  Cursor ic1{0, 0, 0}, ic2{0, 0, 0};  // issue-side positions of the next phase-1 / phase-2 item
+  auto issue = [&](int k) {  // lane 0: item k's bytes into its stage
+    const uint8_t* src;
+    uint32_t bytes;
+    if (k < nR) {
+      const int i = rspan.s + warp + FW * k;
+      src = reinterpret_cast<const uint8_t*>(a.wg + (long long)(i >> 2) * a.H + (i & 3) * (a.H / 4));
+      bytes = (uint32_t)a.H;
+    } else if (k < nR + n1) {
+      if (ic1.s < nr) {
         const uint32_t ib = RFMT == DSMOE_FMT_FP8 ? kFp8W13Item : FCH * 1088;
-        for (int i = run.s; i < run.e && ok; ++i) {
-          const int sl = tile / geo.T, t = tile - sl * geo.T;
-          issue(a.r_w13 + (long long)pl.expert[sl] * a.r_w13_eb + t * geo.tile13r + (long long)p * ib, ib);
-          if (++p == geo.P13r) {
-            p = 0;
-            ++tile;
-          }
-        }
+        src = a.r_w13 + (long long)pl.expert[ic1.s] * a.r_w13_eb + ic1.t * geo.tile13r + (long long)ic1.p * ib;
+        bytes = ib;
+      } else {
+        src = a.s_w13 + ic1.t * geo.tile13s + (long long)ic1.p * kFp8W13Item;
+        bytes = kFp8W13Item;
       }
-      {  // phase 2: (n-tile, slot, part), h rows deferred until grid barrier B
-        const int Q = (nr + 1) * geo.P2;
-        const Span run = warp_run(cta_span(geo.NT * Q, cta, G), w);
-        kw2 = kw;
-        int nt = run.s / Q, jq = run.s % Q;
-        for (int i = run.s; i < run.e && ok; ++i) {
-          const int sl = jq / geo.P2, p = jq - sl * geo.P2;
-          int st;
-          if (!acquire(st)) break;
-          const uint32_t hbytes = (uint32_t)(2 * pl.ntok[sl] * kHPartK);
-          const uint8_t* src;
-          uint32_t bytes;
-          if (sl < nr && RFMT == DSMOE_FMT_FP4) {
-            const int nch = min(4, a.I_loc / 64 - p * 4);
-            src = a.r_w2 + (long long)pl.expert[sl] * a.r_w2_eb + nt * geo.tile2r + (long long)p * 4 * 544;
-            bytes = (uint32_t)(nch * 544);
-          } else {
-            const uint8_t* tile = sl < nr ? a.r_w2 + (long long)pl.expert[sl] * a.r_w2_eb + nt * geo.tile2r
-                                          : a.s_w2 + nt * geo.tile2s;
-            const int nch = min(8, a.I_loc / 32 - p * 8);
-            src = tile + (long long)p * kFp8W2Item;
-            bytes = (uint32_t)(nch * 512 + 32);
-          }
-          mbar_expect_tx(&full[st], bytes + hbytes);
-          bulk_g2s(ring + (size_t)st * FSTAGE, src, bytes, &full[st]);
-          if (h_open) {
-            copy_h(st, sl, p);
-          } else {
-            def_stage[def_n] = st;
-            def_slot[def_n] = sl;
-            def_p[def_n] = p;
-            ++def_n;
-          }
-          ++kw;
-          if (++jq == Q) {
-            jq = 0;
-            ++nt;
-          }
-        }
-      }
-      open_h();
-    }
-    // let every copy this lane issued land before the CTA may exit
-    for (int q = max(0, kw - spw); q < kw; ++q) mbar_wait(&full[w * spw + q % spw], (q / spw) & 1, kWaitNs);
-    return;
-  }
-
-  // ================================================================ consumer warps
-  // token rows: amax -> power-of-2 pre-scale (amax * 2^-p in [128, 256)) -> e4m3 hi / lo rows in
-  // shared memory, K in B-operand order (qk_off); one pass of loads, all in flight at once
-  for (int b = warp; b < a.B; b += FW) {
-    const __nv_bfloat16* xr = a.x + (long long)b * a.H;
-    const int nchunk = a.H / 32;  // <= 256: at most 8 chunks of 32 values per lane
-    float m = 0.f;
-#pragma unroll
-    for (int k0 = 0; k0 < 8; k0 += 4) {  // 4 chunks (16 loads) in flight per batch
-      uint4 u[4][4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int c = lane + 32 * (k0 + k);
-        if (c < nchunk) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) u[k][q] = __ldg(reinterpret_cast<const uint4*>(xr + 32 * c + 8 * q));
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        if (lane + 32 * (k0 + k) < nchunk) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t w[4] = {u[k][q].x, u[k][q].y, u[k][q].z, u[k][q].w};
-#pragma unroll
-            for (int h = 0; h < 4; ++h)
-              m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w[h] << 16)), fabsf(__uint_as_float(w[h] & 0xFFFF0000u))));
-          }
-        }
+    } else {
+      const W2Item w = {ic2.s, ic2.t, ic2.p};
+      if (w.s < nr && RFMT == DSMOE_FMT_FP4) {
+        const int c0 = 16 * w.p;
+        src = a.r_w2 + (long long)pl.expert[w.s] * a.r_w2_eb + w.nt * geo.tile2r + (long long)c0 * 544;
+        bytes = (uint32_t)(min(16, a.I_loc / 64 - c0) * 544);
+      } else {
+        const uint8_t* tile = w.s < nr ? a.r_w2 + (long long)pl.expert[w.s] * a.r_w2_eb + w.nt * geo.tile2r
+                                       : a.s_w2 + w.nt * geo.tile2s;
+        const int KC = a.I_loc / 32, c0 = 16 * w.p;
+        const int n0 = min(8, KC - c0), n1c = min(8, KC - c0 - 8);
+        src = tile + (long long)(2 * w.p) * kFp8W2Item;
+        bytes = (uint32_t)(n0 * 512 + 32 + (n0 == 8 && n1c > 0 ? n1c * 512 + 32 : 0));
       }
     }
-    m = warp_max(m);
-    int p = 0;
-    if (m > 0.f && m <= 3.0e38f) {
-      int e2;
-      frexpf(m, &e2);
-      p = e2 - 8;
-    }
-    if (lane == 0) pl.xscale[b] = ldexpf(1.0f, p);
-    const float inv = ldexpf(1.0f, -p);
-    uint8_t* rh = xq + (size_t)(2 * b) * a.xrs;
-    uint8_t* rl = rh + a.xrs;
-#pragma unroll
-    for (int k0 = 0; k0 < 8; k0 += 4) {  // second pass over the (now cached) row: convert
-      uint4 u[4][4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int c = lane + 32 * (k0 + k);
-        if (c < nchunk) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) u[k][q] = __ldg(reinterpret_cast<const uint4*>(xr + 32 * c + 8 * q));
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int c = lane + 32 * (k0 + k);
-        if (c < nchunk) {
-          float v[32];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t w[4] = {u[k][q].x, u[k][q].y, u[k][q].z, u[k][q].w};
-#pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              v[8 * q + 2 * h] = __uint_as_float(w[h] << 16) * inv;
-              v[8 * q + 2 * h + 1] = __uint_as_float(w[h] & 0xFFFF0000u) * inv;
-            }
-          }
-#pragma unroll
-          for (int tt = 0; tt < 4; ++tt) {  // lane tt's 8 bytes of this 32-K chunk, per term
-            uint32_t h0, l0, h1, l1, h2, l2, h3, l3;
-            split2_e4m3(v[4 * tt], v[4 * tt + 1], h0, l0);
-            split2_e4m3(v[4 * tt + 2], v[4 * tt + 3], h1, l1);
-            split2_e4m3(v[16 + 4 * tt], v[16 + 4 * tt + 1], h2, l2);
-            split2_e4m3(v[16 + 4 * tt + 2], v[16 + 4 * tt + 3], h3, l3);
-            const int off = (c >> 1) * 64 + tt * 16 + (c & 1) * 8;
-            *reinterpret_cast<uint2*>(rh + off) = make_uint2(h0 | (h1 << 16), h2 | (h3 << 16));
-            *reinterpret_cast<uint2*>(rl + off) = make_uint2(l0 | (l1 << 16), l2 | (l3 << 16));
-          }
-        }
-      }
-    }
-  }
-  for (int e = tid; e < a.E; e += FW * 32) emask[e] = 0u;
-  if (my_router == 0 && tid == 0) pl.gen_a = grid_arrive(a.gbar, G);
-  named_bar_sync(1, FW * 32);
-
-  int shared_toks[FMAXB];
-#pragma unroll
-  for (int b = 0; b < FMAXB; ++b) shared_toks[b] = min(b, a.B - 1);
-  // the lane's token row (B column g) of n-tile j, for a slot's token list
-  auto token_rows = [&](const uint8_t** xr, const int* toks, int ntok) {
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-      xr[j] = xq + (size_t)(2 * toks[min(4 * j + (lane >> 3), ntok - 1)] + ((lane >> 2) & 1)) * a.xrs +
-              (lane & 3) * 16;
+    // The warp's reads of this stage (its previous item) have all completed: each fed an MMA whose
+    // result was consumed before this refill, so the copy cannot overtake them.
+    mbar_expect_tx(bar_of(k), bytes);
+    bulk_g2s_hint(stage_of(k), src, bytes, bar_of(k), pol_stream);
   };
-
-  int kw = 0;  // this warp's items so far: stage warp * spw + kw % spw, fill kw / spw
-  auto stage_of = [&]() { return ring + (size_t)(warp * spw + kw % spw) * FSTAGE; };
-  auto wait_full = [&]() -> bool {
+  auto refill = [&]() {  // keep SPW items of the known stream in flight
+    const int known = planned ? nR + n1 + n2 : nR;
+    while (ki < kc + SPW && ki < known) {
+      if (lane == 0) issue(ki);
+      if (ki >= nR + n1)
+        ic2.next(nr, geo.NT, geo.P2r, geo.P2s);
+      else if (ki >= nR)
+        ic1.next(nr, geo.T, geo.P13r, geo.P13s);
+      ++ki;
+    }
+  };
+  auto wait_full = [&](int k) -> bool {
     if (*(volatile int*)&pl.abort) return false;
-    if (!mbar_wait(&full[warp * spw + kw % spw], (kw / spw) & 1, kWaitNs)) {
+    if (!mbar_wait(bar_of(k), (k >> 1) & 1, kWaitNs)) {
       if (lane == 0) {
         atomicOr(a.status, ST_FULL);
         pl.abort = 1;
@@ -788,135 +805,90 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     }
     return true;
   };
-  auto release = [&]() {
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[warp * spw + kw % spw]);
-    ++kw;
+  auto drain = [&]() {  // every copy this warp issued lands before the CTA exits
+    for (int k = kc; k < ki; ++k) mbar_wait(bar_of(k), (k >> 1) & 1, kWaitNs);
+  };
+  // bounded grid barrier by thread 0, with the CTA's __syncthreads around it; false = abandon the call
+  auto grid_sync = [&]() -> bool {
+    __syncthreads();
+    if (tid == 0 && !pl.abort) {
+      const unsigned g0 = grid_arrive(a.gbar, G);
+      if (!grid_wait(a.gbar, g0, a.status)) {
+        atomicOr(a.status, ST_GRID);
+        pl.abort = 1;
+      }
+    }
+    __syncthreads();
+    return !pl.abort;
   };
 
-  // ---- phase R: router quarter-rows, then the shared expert's w1|w3 parts
+  refill();  // router rows stream in while the token rows are prepared
+  // the shared expert's weights do not depend on routing: pull them into L2 now (each warp a slice)
+  if (lane == 0) {
+    const long long b13 = (long long)geo.T * geo.tile13s, b2 = (long long)geo.NT * geo.tile2s;
+    const long long piece = 16384, n13 = (b13 + piece - 1) / piece, n2p = (b2 + piece - 1) / piece;
+    for (long long q = (long long)cta * FW + warp; q < n13 + n2p; q += (long long)G * FW) {
+      const bool w2p = q >= n13;
+      const long long off = (w2p ? q - n13 : q) * piece, tot = w2p ? b2 : b13;
+      const uint32_t len = (uint32_t)min(piece, tot - off);
+      const uint8_t* src = (w2p ? a.s_w2 : a.s_w13) + off;
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(len) : "memory");
+    }
+  }
+  setup_tokens(a, xq, xs, pl, lo_off);
+  for (int e = tid; e < a.E; e += FT) emask[e] = 0u;
+  if (tid == 0)  // finished-tile counts per slot start from zero after grid barrier A
+    for (int i = cta; i < a.slots; i += G) a.slot_done[i] = 0u;
+
+  // ---- phase R: router quarter-rows
   {
-    const Span run = warp_run(localR, warp);
-    int cur = -1, seg_first = 0, seg_np = 0, n_router = 0;
-    float acc1[2][4], acc3[2][4];
-    const uint8_t* xr[2];
-    token_rows(xr, shared_toks, a.B);
-    auto flush = [&]() {
-      w13_flush(a, geo, pl, geo.P13s, seg_first - cur * geo.P13s, seg_np, a.sh_idx, cur, acc1, acc3, a.B, shared_toks,
-                1.0f, lane, [&](auto&& f) {
-                  for_segments_R(geo.NR, geo.NS, G, cur * geo.P13s, (cur + 1) * geo.P13s, f);
-                });
-    };
-    for (int li = run.s; li < run.e; ++li) {
-      if (!wait_full()) break;
-      const uint8_t* stage = stage_of();
-      if (li < my_router) {
-        const int i = rspan.s + li;
-        router_item(a, stage, i >> 2, i & 3, lane);
-        ++n_router;
-      } else {
-        const int i = sspan.s + li - my_router, t = i / geo.P13s, p = i % geo.P13s;
-        if (t != cur) {
-          if (cur >= 0) flush();
-          cur = t;
-          seg_first = i;
-          seg_np = 0;
-#pragma unroll
-          for (int j = 0; j < 2; ++j)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) acc1[j][q] = acc3[j][q] = 0.f;
-        }
-        if (a.B > 4)
-          w13_accum<DSMOE_FMT_FP8, 2>(stage, xr, p, lane, acc1, acc3);
-        else
-          w13_accum<DSMOE_FMT_FP8, 1>(stage, xr, p, lane, acc1, acc3);
-        ++seg_np;
-      }
-      release();
-      if (li + 1 == min(run.e, my_router)) {  // this warp's last router row: count its rows toward barrier A
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) {
-          const unsigned done = atomicAdd(&pl.router_done, (unsigned)n_router) + n_router;
-          if ((int)done == my_router) pl.gen_a = grid_arrive(a.gbar, G);
-        }
-      }
-    }
-    if (cur >= 0 && !pl.abort) flush();
-  }
-  __threadfence();
-  named_bar_sync(1, FW * 32);
-  if (tid == 0 && !pl.abort) {
-    if (!grid_wait(a.gbar, pl.gen_a, a.status)) {
-      atomicOr(a.status, ST_GRID);
-      pl.abort = 1;
+    const __nv_bfloat16* xsrc = a.B <= FXB ? xs : a.x;
+    while (kc < nR) {
+      if (!wait_full(kc)) break;
+      const int i = rspan.s + warp + FW * kc;
+      router_item(a, stage_of(kc), xsrc, i >> 2, i & 3, lane);
+      __syncwarp();
+      ++kc;
+      refill();
     }
   }
-  named_bar_sync(1, FW * 32);
-  if (pl.abort) return;
-  __threadfence();
+  if (!grid_sync()) {  // grid barrier A: every router row of the step is done
+    drain();
+    return;
+  }
 
   // ---- plan: identical in every CTA. The ring is idle here (phase R consumed, phase 1 not yet
   // issued), so its first bytes hold the scores.
   {
-    float* sc_s = reinterpret_cast<float*>(ring);    // [B][E] scores
-    float* bi_s = sc_s + a.B * a.E;                  // [B][E] scores + selection bias
+    float* sc_s = reinterpret_cast<float*>(ring);  // [B][E] scores
+    float* bi_s = sc_s + a.B * a.E;                // [B][E] scores + selection bias
     const int n = a.B * a.E;
-    for (int i0 = tid; i0 < n; i0 += 4 * FW * 32) {
-      double l4[4][4];
-      float bs[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int i = i0 + u * FW * 32;
-        if (i < n) {
-          const int b = i / a.E, e = i % a.E;
-          const double* r4 = a.rl + (long long)i * 4;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) l4[u][q] = ld_cg_f64(r4 + q);
-          const bool vl = a.bias_vl != nullptr && a.image_mask != nullptr && a.image_mask[b] != 0;
-          bs[u] = (vl ? a.bias_vl : a.bias)[e];
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int i = i0 + u * FW * 32;
-        if (i < n) {
-          const float sc = fscore(__double2float_rn(((l4[u][0] + l4[u][1]) + l4[u][2]) + l4[u][3]), a.score_func);
-          sc_s[i] = sc;
-          bi_s[i] = sc + bs[u];
-        }
-      }
+    for (int i = tid; i < n; i += FT) {
+      const double* r4 = a.rl + (long long)i * 4;
+      const double l = ((ld_cg_f64(r4) + ld_cg_f64(r4 + 1)) + ld_cg_f64(r4 + 2)) + ld_cg_f64(r4 + 3);
+      const int b = i / a.E, e = i - b * a.E;
+      const bool vl = a.bias_vl != nullptr && a.image_mask != nullptr && a.image_mask[b] != 0;
+      const float s = fscore(__double2float_rn(l), a.score_func);
+      sc_s[i] = s;
+      bi_s[i] = s + (vl ? a.bias_vl : a.bias)[e];
     }
-    named_bar_sync(1, FW * 32);
+    __syncthreads();
     if (cta == 0 && a.scores)
-      for (int i = tid; i < n; i += FW * 32) a.scores[i] = sc_s[i];
-    for (int b = warp; b < a.B; b += FW) {  // top-k of token b: lane-local top-k lists, then k warp argmaxes
-      float tv[FMAXK];
-      int ti[FMAXK];
-#pragma unroll
-      for (int r = 0; r < FMAXK; ++r) {
-        tv[r] = -INFINITY;
-        ti[r] = 0x7FFFFFFF;
-      }
-      for (int e = lane; e < a.E; e += 32) {
-        float v = bi_s[b * a.E + e];
-        int vi = e;
-#pragma unroll
-        for (int r = 0; r < FMAXK; ++r) {  // insertion: larger value first, lower index on ties
-          if (v > tv[r] || (v == tv[r] && vi < ti[r])) {
-            const float ov = tv[r];
-            const int oi = ti[r];
-            tv[r] = v;
-            ti[r] = vi;
-            v = ov;
-            vi = oi;
-          }
-        }
-      }
+      for (int i = tid; i < n; i += FT) a.scores[i] = sc_s[i];
+    // top-k of token b (warp b): k rounds of (lane-local best, warp argmax); ties -> lower index
+    for (int b = warp; b < a.B; b += FW) {
+      float* v = bi_s + b * a.E;
       float tot = 0.f;
       for (int r = 0; r < a.topk; ++r) {
-        float best = tv[0];
-        int bi = ti[0];
+        float best = -INFINITY;
+        int bi = 0x7FFFFFFF;
+        for (int e = lane; e < a.E; e += 32) {
+          const float x = v[e];
+          if (x > best) {
+            best = x;
+            bi = e;
+          }
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
           const float ov = __shfl_xor_sync(0xffffffffu, best, o);
@@ -927,23 +899,16 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
           }
         }
         if (bi == 0x7FFFFFFF) bi = 0;
-        if (ti[0] == bi) {  // the winning lane pops its head
-#pragma unroll
-          for (int q = 0; q < FMAXK - 1; ++q) {
-            tv[q] = tv[q + 1];
-            ti[q] = ti[q + 1];
-          }
-          tv[FMAXK - 1] = -INFINITY;
-          ti[FMAXK - 1] = 0x7FFFFFFF;
-        }
         const float w = sc_s[b * a.E + bi];
+        __syncwarp();
         if (lane == 0) {
           pl.sel[b][r] = bi;
           pl.selw[b][r] = w;
+          v[bi] = -INFINITY;
         }
+        __syncwarp();
         tot += w;
       }
-      __syncwarp();
       if (lane < a.topk) {
         const float w = pl.selw[b][lane] / (tot + 1e-20f) * a.route_scale;
         pl.selw[b][lane] = w;
@@ -953,18 +918,17 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
         }
       }
     }
-  }
-  named_bar_sync(1, FW * 32);
-  for (int i = tid; i < a.B * a.topk; i += FW * 32) atomicOr(&emask[pl.sel[i / a.topk][i % a.topk]], 1u << (i / a.topk));
-  named_bar_sync(1, FW * 32);
-  {
+    __syncthreads();
+    for (int i = tid; i < a.B * a.topk; i += FT) atomicOr(&emask[pl.sel[i / a.topk][i % a.topk]], 1u << (i / a.topk));
+    __syncthreads();
+    // slots in expert order: block-wide compaction of the experts with picks
     int base = 0;
-    for (int e0 = 0; e0 < a.E; e0 += FW * 32) {
+    for (int e0 = 0; e0 < a.E; e0 += FT) {
       const int e = e0 + tid;
       const unsigned m = e < a.E ? emask[e] : 0u;
       const unsigned bal = __ballot_sync(0xffffffffu, m != 0u);
       if (lane == 0) pl.wcnt[warp] = __popc(bal);
-      named_bar_sync(1, FW * 32);
+      __syncthreads();
       int off = base, total = 0;
       for (int w = 0; w < FW; ++w) {
         if (w < warp) off += pl.wcnt[w];
@@ -974,26 +938,26 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       if (m != 0u) {
         pl.expert[off] = e;
         pl.ntok[off] = __popc(m);
-        int n = 0;
+        int cnt = 0;
         for (int b = 0; b < FMAXB; ++b) pl.col_of[off][b] = -1;
         for (int b = 0; b < a.B; ++b) {
           if (m & (1u << b)) {
             float w = 0.f;
             for (int r = 0; r < a.topk; ++r)
               if (pl.sel[b][r] == e) w = pl.selw[b][r];
-            pl.tok[off][n] = b;
-            pl.wt[off][n] = w;
-            pl.col_of[off][b] = (signed char)n;
-            ++n;
+            pl.tok[off][cnt] = b;
+            pl.wt[off][cnt] = w;
+            pl.col_of[off][b] = (signed char)cnt;
+            ++cnt;
           }
         }
-        for (; n < 8; ++n) {
-          pl.tok[off][n] = pl.tok[off][0];
-          pl.wt[off][n] = 0.f;
+        for (; cnt < 8; ++cnt) {
+          pl.tok[off][cnt] = pl.tok[off][0];
+          pl.wt[off][cnt] = 0.f;
         }
       }
       base += total;
-      named_bar_sync(1, FW * 32);
+      __syncthreads();
     }
     if (tid == 0) {
       const int s = base;  // the shared expert's slot
@@ -1006,33 +970,109 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
         pl.col_of[s][b] = b < a.B ? (signed char)b : (signed char)-1;
       }
     }
+    __syncthreads();
   }
-  named_bar_sync(1, FW * 32);
-  if (tid == 0) mbar_arrive(&planbar[0]);
 
-  // ---- phase 1: routed w1|w3
-  const int nr = pl.n_routed;
-  const int N1 = nr * geo.T * geo.P13r;
+
+
+  // ---- the rest of the stream is known. Phase-1 items: routed slots (tiles of P13r items), then
+  // the shared expert as slot nr (tiles of P13s FP8 items).
+  nr = pl.n_routed;
+  NR1 = nr * geo.T * geo.P13r;
+  N1 = NR1 + geo.T * geo.P13s;
+  run1 = warp_run(cta_span(N1, cta, G), warp);
+  n1 = run1.e - run1.s;
+  N2 = nr * geo.NT * geo.P2r + geo.NT * geo.P2s;
+  run2 = warp_run(cta_span(N2, cta, G), warp);
+  n2 = run2.e - run2.s;
+  ic1 = cursor1(geo, nr, NR1, run1.s);
+  ic2 = cursor2(geo, nr, run2.s);
+  planned = true;
+  refill();
+
+  // the lane's token row (B column g = lane / 4) of n-tiles 0 and 1, for a slot's token list
+  auto token_rows = [&](const uint8_t** xr, const int* toks, int ntok) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+      xr[j] = xq + (size_t)toks[min(4 * j + (lane >> 3), ntok - 1)] * a.H + ((lane >> 2) & 1) * lo_off + (lane & 3) * 16;
+  };
+  // phase-1 tile (slot s, tile t): its first item and its part count
+  auto tile_first = [&](int s, int t) { return s < nr ? (s * geo.T + t) * geo.P13r : NR1 + t * geo.P13s; };
+  auto tile_parts = [&](int s) { return s < nr ? geo.P13r : geo.P13s; };
+
+  // ---- published segments: one fence for the batch, one counter per tile, one acquire fence if
+  // this warp finished any; the last contributor applies the epilogue and counts the slot's tile
+  Pend pend[NPEND];
+  int npend = 0;
+  auto publish = [&]() {
+    if (npend == 0) return;
+    fence_acq_rel_gpu();
+    __syncwarp();
+    unsigned last = 0;  // bit i: this warp completed pending segment i's tile
+    for (int i = 0; i < npend; ++i) {
+      const Pend e = pend[i];
+      if (e.kind == 3) continue;
+      const int sidx = e.s < nr ? e.s : a.sh_idx;
+      unsigned* cnt = a.cnt13 + sidx * geo.T + e.t;
+      unsigned old = 0;
+      if (lane == 0) old = atomicAdd(cnt, (unsigned)e.np);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if ((int)old + e.np == tile_parts(e.s)) last |= 1u << i;
+    }
+    if (last) fence_acq_rel_gpu();
+    for (int i = 0; i < npend; ++i) {
+      if (!((last >> i) & 1u)) continue;
+      const Pend e = pend[i];
+      const int sidx = e.s < nr ? e.s : a.sh_idx;
+      float s8[8];
+      w13_reduce(a, geo, sidx, e.t, tile_first(e.s, e.t), tile_parts(e.s), N1, lane, s8);
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = s8[j];
+      w13_epilogue(a, pl, sidx, e.t, v, pl.ntok[e.s], pl.tok[e.s], e.s < nr ? fmtf : 1.0f, lane);
+      if (lane == 0) a.cnt13[sidx * geo.T + e.t] = 0u;
+    }
+    fence_acq_rel_gpu();
+    __syncwarp();
+    if (lane == 0)
+      for (int i = 0; i < npend; ++i)
+        if (pend[i].kind == 3 || ((last >> i) & 1u)) atomicAdd(a.slot_done + (pend[i].s < nr ? pend[i].s : a.sh_idx), 1u);
+    npend = 0;
+  };
+  auto add_pend = [&](int kind, int s, int t, int np) {
+    pend[npend++] = {kind, s, t, np};
+    if (npend == NPEND) publish();
+  };
+
+  // ---- phase 1: w1|w3 of every slot
   {
-    const Span span = cta_span(N1, cta, G);
-    const Span run = warp_run(span, warp);
-    int cur = -1, seg_first = 0, seg_np = 0;
+    int cur_s = -1, cur_t = -1, seg_first = 0, seg_np = 0;
     float acc1[2][4], acc3[2][4];
-    const uint8_t* xr[2];
-    constexpr float fmtf = RFMT == DSMOE_FMT_FP4 ? kFp4E4m3Scale : 1.0f;
-    auto flush = [&]() {
-      const int cs = cur / geo.T;
-      w13_flush(a, geo, pl, geo.P13r, seg_first - cur * geo.P13r, seg_np, cs, cur % geo.T, acc1, acc3, pl.ntok[cs],
-                pl.tok[cs], fmtf, lane,
-                [&](auto&& f) { for_segments(N1, G, cur * geo.P13r, (cur + 1) * geo.P13r, f); });
+    const uint8_t* xr[2] = {xq, xq};
+    auto end_seg = [&]() {
+      const int sidx = cur_s < nr ? cur_s : a.sh_idx;
+      float s8[8];
+      w13_combine(acc1, acc3, s8);
+      if (seg_np == tile_parts(cur_s)) {
+        w13_epilogue(a, pl, sidx, cur_t, s8, pl.ntok[cur_s], pl.tok[cur_s], cur_s < nr ? fmtf : 1.0f, lane);
+        add_pend(3, cur_s, cur_t, 0);
+      } else {
+        float* dst = p13_slot(a, geo, sidx, cur_t, seg_first - tile_first(cur_s, cur_t), lane);
+        *reinterpret_cast<float4*>(dst) = make_float4(s8[0], s8[1], s8[2], s8[3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(s8[4], s8[5], s8[6], s8[7]);
+        add_pend(1, cur_s, cur_t, seg_np);
+      }
     };
-    for (int i = run.s; i < run.e; ++i) {
-      if (!wait_full()) break;
-      const uint8_t* stage = stage_of();
-      const int tile = i / geo.P13r, p = i % geo.P13r, s = tile / geo.T;
-      if (tile != cur) {
-        if (cur >= 0) flush();
-        cur = tile;
+    Cursor cc = cursor1(geo, nr, NR1, run1.s);
+    while (kc < nR + n1) {
+      if (!wait_full(kc)) break;
+      const int i = run1.s + (kc - nR);
+      const int s = cc.s, t = cc.t, p = cc.p;
+      cc.next(nr, geo.T, geo.P13r, geo.P13s);
+      if (s != cur_s || t != cur_t) {
+        if (cur_s >= 0) end_seg();
+        cur_s = s;
+        cur_t = t;
         seg_first = i;
         seg_np = 0;
 #pragma unroll
@@ -1041,78 +1081,136 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
           for (int q = 0; q < 4; ++q) acc1[j][q] = acc3[j][q] = 0.f;
         token_rows(xr, pl.tok[s], pl.ntok[s]);
       }
-      if (pl.ntok[s] > 4)
-        w13_accum<RFMT, 2>(stage, xr, p, lane, acc1, acc3);
-      else
-        w13_accum<RFMT, 1>(stage, xr, p, lane, acc1, acc3);
-      ++seg_np;
-      release();
-    }
-    if (cur >= 0 && !pl.abort) flush();
-  }
-  __threadfence();
-  named_bar_sync(1, FW * 32);
-  if (tid == 0 && !pl.abort) {
-    const unsigned g0 = grid_arrive(a.gbar, G);
-    if (!grid_wait(a.gbar, g0, a.status)) {
-      atomicOr(a.status, ST_GRID);
-      pl.abort = 1;
-    }
-  }
-  named_bar_sync(1, FW * 32);
-  if (tid == 0 && !pl.abort) mbar_arrive(&planbar[1]);  // the producer may now copy h rows
-  if (pl.abort) return;
-
-  // ---- phase 2: w2
-  {
-    const int Q = (nr + 1) * geo.P2;
-    const int N2 = geo.NT * Q;
-    const Span span = cta_span(N2, cta, G);
-    const Span run = warp_run(span, warp);
-    int cur = -1, seg_first = 0, seg_np = 0;
-    float out[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int i = run.s; i < run.e; ++i) {
-      if (!wait_full()) break;
-      const uint8_t* stage = stage_of();
-      const int nt = i / Q, jq = i % Q, s = jq / geo.P2, p = jq % geo.P2;
-      if (nt != cur) {
-        if (cur >= 0) w2_flush(a, N2, Q, cur, seg_first, seg_np, out, lane);
-        cur = nt;
-        seg_first = i;
-        seg_np = 0;
-        out[0] = out[1] = out[2] = out[3] = 0.f;
-      }
+      const uint8_t* stage = stage_of(kc);
       const bool two = pl.ntok[s] > 4;
       if (s < nr) {
         if (two)
-          w2_accum<RFMT, 2>(a, pl, stage, s, p, lane, out);
+          w13_accum<RFMT, 2>(stage, xr, p, lane, acc1, acc3);
         else
-          w2_accum<RFMT, 1>(a, pl, stage, s, p, lane, out);
+          w13_accum<RFMT, 1>(stage, xr, p, lane, acc1, acc3);
       } else {
         if (two)
-          w2_accum<DSMOE_FMT_FP8, 2>(a, pl, stage, s, p, lane, out);
+          w13_accum<DSMOE_FMT_FP8, 2>(stage, xr, p, lane, acc1, acc3);
         else
-          w2_accum<DSMOE_FMT_FP8, 1>(a, pl, stage, s, p, lane, out);
+          w13_accum<DSMOE_FMT_FP8, 1>(stage, xr, p, lane, acc1, acc3);
       }
       ++seg_np;
-      release();
+      __syncwarp();
+      ++kc;
+      refill();
     }
-    if (cur >= 0 && !pl.abort) w2_flush(a, N2, Q, cur, seg_first, seg_np, out, lane);
+    if (cur_s >= 0 && !pl.abort) end_seg();
+    if (!pl.abort) publish();
   }
+
+  // ---- phase 2 set-up: the h rows of the (at most FHSLOTS) slots of this CTA's span, once their
+  // w1|w3 tiles are all finished, into the token-row region (free after phase 1)
+  const Span span2 = cta_span(N2, cta, G);
+  int sA = 0, sB = -1;
+  if (span2.e > span2.s) {
+    sA = w2_item(geo, nr, span2.s).s;
+    sB = w2_item(geo, nr, span2.e - 1).s;
+  }
+  __syncthreads();
+  if (tid == 0 && sB >= sA && !pl.abort) {
+    bool ok = sB - sA + 1 <= FHSLOTS;
+    if (!ok) atomicOr(a.status, ST_SLOT);
+    const uint64_t t0 = globaltimer_ns();
+    for (int s = sA; s <= sB && ok; ++s) {
+      const unsigned* cnt = a.slot_done + (s < nr ? s : a.sh_idx);
+      while (ld_relaxed_u32(cnt) < (unsigned)geo.T) {
+        if (ld_relaxed_u32(a.status) != 0u || globaltimer_ns() - t0 > kWaitNs) {
+          atomicOr(a.status, ST_SLOT);
+          ok = false;
+          break;
+        }
+      }
+    }
+    if (ok) {
+      fence_acq_rel_gpu();
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      uint32_t total = 0;
+      for (int s = sA; s <= sB; ++s) total += 2u * pl.ntok[s] * rp;
+      mbar_expect_tx(hbar, total);
+      for (int s = sA; s <= sB; ++s) {
+        const int sidx = s < nr ? s : a.sh_idx, nt = pl.ntok[s];
+        uint8_t* dst = xq + (size_t)(s - sA) * SL.hs_stride;
+        bulk_g2s(dst, a.hq + hq_row(a.I_loc, sidx, 0, 0), (uint32_t)(nt * rp), hbar);
+        bulk_g2s(dst + nt * rp + 64, a.hq + hq_row(a.I_loc, sidx, 1, 0), (uint32_t)(nt * rp), hbar);
+      }
+    } else {
+      pl.abort = 1;
+    }
+  }
+  __syncthreads();
+  if (pl.abort) {
+    drain();
+    return;
+  }
+  if (sB >= sA && !mbar_wait(hbar, 0, kWaitNs)) {
+    if (lane == 0) {
+      atomicOr(a.status, ST_SLOT);
+      pl.abort = 1;
+    }
+  }
+
+  // ---- phase 2: w2; each (slot, n-tile) segment folded into token columns and written as a partial
+  {
+    int cur_s = -1, cur_nt = -1, seg_first = 0;
+    const uint8_t* hbase = xq;
+    float tot[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tot[j][q] = 0.f;
+    auto end_seg = [&]() {
+      float out[4] = {0.f, 0.f, 0.f, 0.f};
+      const float fs = (cur_s < nr && RFMT == DSMOE_FMT_FP4 ? kFp4E4m3Scale : 1.0f) / kHScale;
+      w2_fold(a, pl, cur_s, fs, tot, lane, out);
+      const int rel = seg_first - w2_range_start(geo, nr, cur_s, cur_nt);
+      *reinterpret_cast<float4*>(p2_slot(a, cur_nt, cur_s, rel, lane)) = make_float4(out[0], out[1], out[2], out[3]);
+    };
+    Cursor cc = cursor2(geo, nr, run2.s);
+    while (kc < nR + n1 + n2) {
+      if (!wait_full(kc)) break;
+      const int i = run2.s + (kc - nR - n1);
+      const W2Item w = {cc.s, cc.t, cc.p};
+      cc.next(nr, geo.NT, geo.P2r, geo.P2s);
+      if (w.s != cur_s || w.nt != cur_nt) {
+        if (cur_s >= 0) end_seg();
+        cur_s = w.s;
+        cur_nt = w.nt;
+        seg_first = i;
+        hbase = xq + (size_t)(w.s - sA) * SL.hs_stride;
+      }
+      const uint8_t* stage = stage_of(kc);
+      const int ntok = pl.ntok[w.s];
+      if (w.s < nr) {
+        if (ntok > 4)
+          w2_accum<RFMT, 2>(a, stage, hbase, rp, ntok, w.p, lane, tot);
+        else
+          w2_accum<RFMT, 1>(a, stage, hbase, rp, ntok, w.p, lane, tot);
+      } else {
+        if (ntok > 4)
+          w2_accum<DSMOE_FMT_FP8, 2>(a, stage, hbase, rp, ntok, w.p, lane, tot);
+        else
+          w2_accum<DSMOE_FMT_FP8, 1>(a, stage, hbase, rp, ntok, w.p, lane, tot);
+      }
+      __syncwarp();
+      ++kc;
+      refill();
+    }
+    if (cur_s >= 0 && !pl.abort) end_seg();
+  }
+  drain();
+  // ---- grid barrier C, then every warp of the grid finishes at most a few 16-row output tiles:
+  // the ordered sum over all slots' segments -> y
+  if (!grid_sync()) return;
+  for (int nt = cta * FW + warp; nt < geo.NT; nt += G * FW) w2_finish(a, geo, nr, N2, nt, lane);
 }
 
 // ------------------------------------------------------------------ host side
-size_t fused_smem_bytes(int H, int B, int E, int nstage) {
-  const size_t xrs = (size_t)H + 64;
-  return (size_t)nstage * FSTAGE + (size_t)B * 2 * xrs + (2 * (size_t)nstage + 2) * 8 + sizeof(FPlan) +
-         (size_t)E * 4 + 16;
-}
-
-struct FusedScratch {
-  size_t rl, p13, p2, hq, cnt13, cnt2, gbar, status, total;
-  int p13max, qmax, slots;
-};
-
 static size_t al2(size_t v) { return (v + 255) & ~size_t(255); }
 
 // Scratch of the persistent path, always laid out for 8 tokens so that its position in the
@@ -1126,16 +1224,17 @@ FusedScratch fused_scratch(int H, int I_loc, int E, int B, int topk, int r_fmt) 
   FusedScratch f{};
   const int T = I_loc / 16, NT = H / 16;
   f.slots = B * topk + 1;
-  f.p13max = (H / 32) / FCH;                        // FP8 parts per tile bound both formats
-  f.qmax = f.slots * ((I_loc + FK2 - 1) / FK2);     // w2 items per 16 output rows
+  f.p13max = (H / 32) / FCH;                // FP8 parts per tile bound both formats
+  f.p2max = (I_loc + FK2_8 - 1) / FK2_8;    // FP8 w2 items per (slot, n-tile) bound both formats
   size_t o = 0;
   f.gbar = o; o += al2(8);
   f.status = o; o += al2(4);
   f.cnt2 = o; o += al2((size_t)NT * 4);
   f.cnt13 = o; o += al2((size_t)f.slots * T * 4);
+  f.slot_done = o; o += al2((size_t)f.slots * 4);
   f.rl = o; o += al2((size_t)B * E * 4 * 8);
   f.p13 = o; o += al2((size_t)f.slots * T * f.p13max * 32 * 8 * 4);
-  f.p2 = o; o += al2((size_t)NT * f.qmax * 32 * 4 * 4);
+  f.p2 = o; o += al2((size_t)NT * f.slots * f.p2max * 32 * 4 * 4);
   f.hq = o; o += al2((size_t)f.slots * hq_slot_bytes(I_loc));
   f.total = o;
   return f;
@@ -1159,18 +1258,27 @@ static DevInfo& dev_info() {
   return d;
 }
 
+size_t fused_smem_bytes(int H, int I_loc, int B, int E) { return smem_layout(H, I_loc, B, E).total; }
+
+// Geometry the persistent kernel takes: at most 8 tokens and 1024 experts, whole 256-K w1|w3 items,
+// a router quarter-row that fits a stage, and phase-2 CTA spans that touch at most FHSLOTS slots.
 bool fused_supported(const dsmoe_layer_t* L, int B) {
   if (B < 1 || B > FMAXB || L->n_experts > FEMAX || L->hidden % 512 != 0 || L->hidden > FSTAGE) return false;
-  return fused_smem_bytes(L->hidden, B, L->n_experts, 8) <= (size_t)dev_info().optin;
+  const DevInfo& d = dev_info();
+  if (fused_smem_bytes(L->hidden, L->inter_local, B, L->n_experts) > (size_t)d.optin) return false;
+  const int NT = L->hidden / 16, I = L->inter_local;
+  const int P2s = (I + FK2_8 - 1) / FK2_8;
+  const int P2r = L->routed.fmt == DSMOE_FMT_FP8 ? P2s : (I + FK2_4 - 1) / FK2_4;
+  const long long n2max = (long long)B * L->topk * NT * P2r + (long long)NT * P2s;
+  const long long span = (n2max + d.sms - 1) / d.sms;
+  return span <= (long long)NT * (P2r < P2s ? P2r : P2s) + 1;
 }
 
 int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image_mask, void* y, int y_dtype,
                  int64_t* idx, float* wt, float* scores, uint8_t* ws, cudaStream_t st, void* const* events) {
   DevInfo& d = dev_info();
   const int optin = d.optin, sms = d.sms;
-  int nstage = 2 * FW;  // two stages per consumer warp, or one when shared memory is short
-  if (fused_smem_bytes(L->hidden, B, L->n_experts, nstage) > (size_t)optin) nstage = FW;
-  const size_t smem = fused_smem_bytes(L->hidden, B, L->n_experts, nstage);
+  const size_t smem = fused_smem_bytes(L->hidden, L->inter_local, B, L->n_experts);
   DSMOE_REQUIRE(smem <= (size_t)optin, DSMOE_ERR_UNSUPPORTED, "fused: %zu bytes of shared memory needed", smem);
   const FusedScratch f = fused_scratch(L->hidden, L->inter_local, L->n_experts, B, L->topk, L->routed.fmt);
 
@@ -1205,13 +1313,13 @@ int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* im
   a.hq = ws + f.hq;
   a.cnt13 = (unsigned*)(ws + f.cnt13);
   a.cnt2 = (unsigned*)(ws + f.cnt2);
+  a.slot_done = (unsigned*)(ws + f.slot_done);
   a.gbar = (unsigned*)(ws + f.gbar);
   a.status = (unsigned*)(ws + f.status);
   a.sh_idx = FMAXB * L->topk;
-  a.nstage = nstage;
-  a.xrs = L->hidden + 64;
+  a.slots = f.slots;
   a.p13max = f.p13max;
-  a.qmax = f.qmax;
+  a.p2max = f.p2max;
 
   const int fi = L->routed.fmt == DSMOE_FMT_FP8 ? 0 : 1;
   void (*kern)(FusedArgs) = fi == 0 ? moe_fused_kernel<DSMOE_FMT_FP8> : moe_fused_kernel<DSMOE_FMT_FP4>;

@@ -31,19 +31,20 @@ struct RouterArgs {
   float* scores;           // [B, E]
 };
 
-// SwiGLU output h of one slot for w2, the B operand of its 8-bit MMAs: per 256-K part of the
-// intermediate dimension, [term 0 (hi): 8 slot tokens x 256 B][term 1 (lo): 8 x 256 B], K within a
-// row in qk_off order. h is stored times kHScale (|SiLU(min(g, 10)) * clamp(u, +-10)| <= 100, so
-// 400 stays inside e4m3's 448); the routing weight and 1/kHScale are applied to w2's fp32 output.
+// SwiGLU output h of one slot for w2, the B operand of its 8-bit MMAs: rows of hq_row_bytes, hi
+// rows of the 8 slot tokens then lo rows of the 8 slot tokens, K within a row in qk_off order. h
+// is stored times kHScale (|SiLU(min(g, 10)) * clamp(u, +-10)| <= 100, so 400 stays inside e4m3's
+// 448); the routing weight and 1/kHScale are applied to w2's fp32 output.
 constexpr float kHScale = 4.0f;
-constexpr int kHPartK = 256;
-constexpr int kHPartBytes = 2 * DSMOE_SLOT_TOKENS * kHPartK;
+__host__ __device__ inline int hq_row_bytes(int I_loc) { return (I_loc + 63) / 64 * 64; }
 __host__ __device__ inline long long hq_slot_bytes(int I_loc) {
-  return (long long)((I_loc + kHPartK - 1) / kHPartK) * kHPartBytes;
+  return 2LL * DSMOE_SLOT_TOKENS * hq_row_bytes(I_loc);
+}
+__host__ __device__ inline long long hq_row(int I_loc, int slot, int term, int q) {
+  return slot * hq_slot_bytes(I_loc) + (long long)(term * DSMOE_SLOT_TOKENS + q) * hq_row_bytes(I_loc);
 }
 __host__ __device__ inline long long hq_off(int I_loc, int slot, int q, int term, int k) {
-  return slot * hq_slot_bytes(I_loc) + (long long)(k >> 8) * kHPartBytes + term * (DSMOE_SLOT_TOKENS * kHPartK) +
-         q * kHPartK + qk_off(k & 255);
+  return hq_row(I_loc, slot, term, q) + qk_off(k);
 }
 
 // Upper bound on slots in one step: every pick its own slot, plus the shared expert's.
@@ -52,5 +53,15 @@ inline int max_slots(int B, int topk) {
 }
 
 int launch_router(const RouterArgs& a, bool with_plan, cudaStream_t st);
+
+// Workspace scratch of the persistent decode kernel (moe_fused.cu); counters first.
+struct FusedScratch {
+  size_t rl, p13, p2, hq, cnt13, cnt2, slot_done, gbar, status, total;
+  int p13max, p2max, slots;
+};
+FusedScratch fused_scratch(int H, int I_loc, int E, int B, int topk, int r_fmt);
+bool fused_supported(const dsmoe_layer_t* L, int B);
+int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image_mask, void* y, int y_dtype,
+                 int64_t* idx, float* wt, float* scores, uint8_t* ws, cudaStream_t st, void* const* events);
 
 }  // namespace dsmoe
