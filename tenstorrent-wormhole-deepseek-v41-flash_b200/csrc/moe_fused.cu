@@ -156,8 +156,10 @@ __device__ __forceinline__ Geo make_geo(const FusedArgs& a) {
 struct Span {
   int s, e;
 };
+// n * G stays below 2^31 for every item space of a supported layer (checked on the host), so the
+// split uses 32-bit unsigned division.
 __host__ __device__ __forceinline__ Span cta_span(int n, int c, int G) {
-  return {(int)((long long)n * c / G), (int)((long long)n * (c + 1) / G)};
+  return {(int)((unsigned)n * (unsigned)c / (unsigned)G), (int)((unsigned)n * (unsigned)(c + 1) / (unsigned)G)};
 }
 __device__ __forceinline__ Span warp_run(Span cs, int w) {
   const int nc = cs.e - cs.s, L = nc / FW, r = nc % FW;
@@ -168,7 +170,7 @@ __device__ __forceinline__ Span warp_run(Span cs, int w) {
 // every warp run that intersects [a, b), in order.
 template <class F>
 __device__ __forceinline__ void for_segments(int n, int G, int a, int b, F&& f) {
-  int c = (int)(((long long)a * G) / n);
+  int c = (int)(((unsigned)a * (unsigned)G) / (unsigned)n);
   while (c + 1 < G && cta_span(n, c + 1, G).s <= a) ++c;
   while (c > 0 && cta_span(n, c, G).s > a) --c;
   for (; c < G; ++c) {
@@ -678,25 +680,48 @@ __device__ __forceinline__ float* p2_slot(const FusedArgs& a, int nt, int s, int
   return a.p2 + ((((long long)nt * a.slots + s) * a.p2max + rel) * 32 + lane) * 4;
 }
 
-// Sum over every slot's published segments of n-tile nt, in distribution order, -> y.
-__device__ __noinline__ void w2_finish(const FusedArgs& a, const Geo& G, int nr, int N2, int nt, int lane) {
-  SegSum<4> sum(p2_slot(a, nt, 0, 0, lane));
-  for (int s = 0; s <= nr; ++s) {
-    const int a0 = w2_range_start(G, nr, s, nt), len = s < nr ? G.P2r : G.P2s;
-    for_segments(N2, gridDim.x, a0, a0 + len, [&](int q) { sum.add((s * a.p2max + q) * 32 * 4); });
+// Ordered sum of positions [q0, q1) of n-tile nt's w2 partials. Positions run slot-major over the
+// n-tile's items (nr routed slots of P2r parts, then the shared slot's P2s); every position holds a
+// partial (first item of a segment) or zero (any other item), so no segment bookkeeping is needed.
+__device__ __noinline__ float4 w2_chunk_sum(const FusedArgs& a, const Geo& G, int nr, int nt, int q0, int q1,
+                                            int lane) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int NRP = nr * G.P2r;
+  for (int qb = q0; qb < q1; qb += 8) {
+    uint4 v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int q = qb + i;
+      if (q < q1) {
+        const int s = q < NRP ? q / G.P2r : nr, rel = q < NRP ? q - s * G.P2r : q - NRP;
+        v[i] = ld_cg16(p2_slot(a, nt, s, rel, lane));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (qb + i < q1) {
+        acc.x += __uint_as_float(v[i].x);
+        acc.y += __uint_as_float(v[i].y);
+        acc.z += __uint_as_float(v[i].z);
+        acc.w += __uint_as_float(v[i].w);
+      }
+    }
   }
-  sum.flush();
-  const float* s4 = sum.s;
+  return acc;
+}
+
+__device__ __forceinline__ void w2_store_y(const FusedArgs& a, int nt, float4 s4, int lane) {
   const int g = lane >> 2, tq = lane & 3;
+  const float v[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
   for (int q4 = 0; q4 < 4; ++q4) {
     const int row = nt * 16 + (q4 >= 2 ? g + 8 : g), tok = 2 * tq + (q4 & 1);
     if (tok < a.B) {
       const long long o = (long long)tok * a.H + row;
       if (a.y_f32)
-        reinterpret_cast<float*>(a.y)[o] = s4[q4];
+        reinterpret_cast<float*>(a.y)[o] = v[q4];
       else
-        reinterpret_cast<__nv_bfloat16*>(a.y)[o] = __float2bfloat16_rn(s4[q4]);
+        reinterpret_cast<__nv_bfloat16*>(a.y)[o] = __float2bfloat16_rn(v[q4]);
     }
   }
 }
@@ -1157,7 +1182,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
 
   // ---- phase 2: w2; each (slot, n-tile) segment folded into token columns and written as a partial
   {
-    int cur_s = -1, cur_nt = -1, seg_first = 0;
+    int cur_s = -1, cur_nt = -1, seg_first = 0, seg_np = 0;
     const uint8_t* hbase = xq;
     float tot[2][4];
 #pragma unroll
@@ -1170,6 +1195,8 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       w2_fold(a, pl, cur_s, fs, tot, lane, out);
       const int rel = seg_first - w2_range_start(geo, nr, cur_s, cur_nt);
       *reinterpret_cast<float4*>(p2_slot(a, cur_nt, cur_s, rel, lane)) = make_float4(out[0], out[1], out[2], out[3]);
+      for (int q = 1; q < seg_np; ++q)
+        *reinterpret_cast<float4*>(p2_slot(a, cur_nt, cur_s, rel + q, lane)) = make_float4(0.f, 0.f, 0.f, 0.f);
     };
     Cursor cc = cursor2(geo, nr, run2.s);
     while (kc < nR + n1 + n2) {
@@ -1182,8 +1209,10 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
         cur_s = w.s;
         cur_nt = w.nt;
         seg_first = i;
+        seg_np = 0;
         hbase = xq + (size_t)(w.s - sA) * SL.hs_stride;
       }
+      ++seg_np;
       const uint8_t* stage = stage_of(kc);
       const int ntok = pl.ntok[w.s];
       if (w.s < nr) {
@@ -1204,10 +1233,30 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     if (cur_s >= 0 && !pl.abort) end_seg();
   }
   drain();
-  // ---- grid barrier C, then every warp of the grid finishes at most a few 16-row output tiles:
-  // the ordered sum over all slots' segments -> y
+  // ---- grid barrier C, then each CTA finishes its 16-row output tiles nt = cta + G * j: the warps
+  // split each tile's positions into fixed chunks summed in order, and the chunk sums are added in
+  // chunk order -> y (deterministic)
   if (!grid_sync()) return;
-  for (int nt = cta * FW + warp; nt < geo.NT; nt += G * FW) w2_finish(a, geo, nr, N2, nt, lane);
+  const int nn = cta < geo.NT ? (geo.NT - 1 - cta) / G + 1 : 0;
+  if (nn > 0) {
+    const int P = nr * geo.P2r + geo.P2s;
+    const int j = warp % nn, ci = warp / nn, nw = (FW - j + nn - 1) / nn;
+    const float4 part = w2_chunk_sum(a, geo, nr, cta + G * j, P * ci / nw, P * (ci + 1) / nw, lane);
+    float4* red = reinterpret_cast<float4*>(ring);  // idle after phase 2
+    red[warp * 32 + lane] = part;
+    __syncthreads();
+    if (warp < nn) {
+      float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c = 0; c < nw; ++c) {
+        const float4 v = red[(c * nn + warp) * 32 + lane];
+        s4.x += v.x;
+        s4.y += v.y;
+        s4.z += v.z;
+        s4.w += v.w;
+      }
+      w2_store_y(a, cta + G * warp, s4, lane);
+    }
+  }
 }
 
 // ------------------------------------------------------------------ host side
@@ -1271,6 +1320,9 @@ bool fused_supported(const dsmoe_layer_t* L, int B) {
   const int P2r = L->routed.fmt == DSMOE_FMT_FP8 ? P2s : (I + FK2_4 - 1) / FK2_4;
   const long long n2max = (long long)B * L->topk * NT * P2r + (long long)NT * P2s;
   const long long span = (n2max + d.sms - 1) / d.sms;
+  const long long T = I / 16, n1max = (long long)(B * L->topk + 1) * T * ((L->hidden / 32) / FCH);
+  const long long nmax = n1max > n2max ? n1max : n2max;
+  if (nmax * d.sms >= (1LL << 31) || 4LL * L->n_experts * d.sms >= (1LL << 31)) return false;
   return span <= (long long)NT * (P2r < P2s ? P2r : P2s) + 1;
 }
 
