@@ -56,17 +56,24 @@ def parse():
     ap.add_argument("--experts", type=int, default=E,
                     help="routed experts kept resident per layer (default 384; smaller only for profiler runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", choices=["both", "fp8", "fp4"], default="both",
+                    help="layer formats per step (default both; one format only for profiler runs)")
     ap.add_argument("--l2-flush", action="store_true",
                     help="write 256 MiB between steps (default: off; each step already streams more than L2)")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline sampling")
     return ap.parse_args()
 
 
+def layer_formats(args):
+    lay = getattr(args, "layers", "both")
+    return ["fp8", "fp4"] if lay == "both" else [lay]
+
+
 def workload_config(args, world):
     flush_l2 = getattr(args, "l2_flush", False)
     return {"workload": "one FP8 + one FP4 MoE decode layer per step (experts resident, TP over GPUs)",
             "hidden": H, "inter": I, "experts": getattr(args, "experts", E), "topk": TOPK, "shared_experts": 1, "batch": args.batch,
-            "score_func": "sigmoid", "route_scale": ROUTE_SCALE, "layers_per_step": ["fp8-block128", "fp4-e2m1-e8m0"],
+            "score_func": "sigmoid", "route_scale": ROUTE_SCALE, "layers_per_step": [{"fp8": "fp8-block128", "fp4": "fp4-e2m1-e8m0"}[f] for f in layer_formats(args)],
             "parallelism": f"tp{world}",
             "l2": ("flushed between steps (256 MiB write, outside the timed events)" if flush_l2 else
                    "not flushed: every step streams more weight bytes than the 126 MB L2 (read with an L2 "
@@ -211,7 +218,7 @@ def ours(args):
     t_setup = time.time()
     gen = torch.Generator(device=dev).manual_seed(args.seed)
     layers = []
-    for fmt in ("fp8", "fp4"):
+    for fmt in layer_formats(args):
         NE = args.experts
         m = dsmoe.MoE(H, I, NE, TOPK, fmt, "sigmoid", ROUTE_SCALE, rank=rank, world=world, device=dev, max_tokens=B)
         m.load_router(dsmoe.make_router(NE, H, gen, device=dev))
@@ -314,7 +321,7 @@ def ours(args):
 
     # unique experts per step -> algorithmic bytes
     uniq = [[len(set(idx_log[s, li].flatten().tolist())) for li in range(n_layers)] for s in range(W, W + K)]
-    names = ["fp8", "fp4"]
+    names = layer_formats(args)
     w13_b = {"fp8": FP8_W13, "fp4": FP4_W13}
     w2_b = {"fp8": FP8_W2, "fp4": FP4_W2}
     kern = {}
