@@ -159,6 +159,15 @@ DSMOE_API int dsmoe_router(const dsmoe_layer_t* layer, const void* x, int B, con
                  int64_t* idx, float* wt, float* scores, void* workspace, size_t workspace_bytes,
                  void* stream);
 
+/* dsmoe_router with no caller workspace and no allocation: the scratch is a 1,315,072-byte array in
+ * the library's own device image (limits B <= 64, n_experts <= 1024, hidden <= 8192, topk <= 8;
+ * larger calls return DSMOE_ERR_ARG). For callers that cannot provide device scratch memory.
+ * The first call on a device (with that device current) resolves the array's address and must
+ * come before any stream capture; calls on one device must not overlap (they share the array).
+ * Same outputs as dsmoe_router. No counterpart in the reference. */
+DSMOE_API int dsmoe_router_noalloc(const dsmoe_layer_t* layer, const void* x, int B, const uint8_t* image_mask,
+                                   int64_t* idx, float* wt, float* scores, void* stream);
+
 /* Whole MoE layer for B <= DSMOE_MAX_DECODE_TOKENS tokens: router, routed experts (each weight
  * tile read once per step for all tokens that chose it), shared expert, routing-weighted combine.
  * Replaces MoE.decode / verify_batched (dsv41/tt/moe.py:148-180, 202-241).

@@ -55,6 +55,7 @@ _SIGS = {
     "dsmoe_store_unpack_expert": ([_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P], _I),
     "dsmoe_moe_workspace_bytes": ([ctypes.POINTER(Layer), _I], ctypes.c_size_t),
     "dsmoe_router": ([ctypes.POINTER(Layer), _P, _I, _P, _P, _P, _P, _P, ctypes.c_size_t, _P], _I),
+    "dsmoe_router_noalloc": ([ctypes.POINTER(Layer), _P, _I, _P, _P, _P, _P, _P], _I),
     "dsmoe_moe_decode": ([ctypes.POINTER(Layer), _P, _I, _P, _P, _I, _P, _P, _P, _P, ctypes.c_size_t, _P], _I),
     "dsmoe_moe_decode_profiled": ([ctypes.POINTER(Layer), _P, _I, _P, _P, _I, _P, _P, _P, _P, ctypes.c_size_t, _P,
                                    ctypes.POINTER(_P)], _I),
