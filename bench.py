@@ -209,7 +209,7 @@ def ours(args):
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     B = args.batch
     if not 1 <= B <= L.MAX_DECODE_TOKENS:
         raise SystemExit(f"--batch must be in 1..{L.MAX_DECODE_TOKENS}")
@@ -253,35 +253,47 @@ def ours(args):
             dist.all_reduce(part[li])
             L.call("dsmoe_f32_to_bf16", L.ptr(part[li]), L.ptr(yout[li]), part[li].numel(), st_)
 
-    # eager warm-up (first-call set-up, NCCL communicators), then one CUDA graph per (layer, variant):
-    # the timed steps replay graphs, so host-side launch work does not sit between the kernels
+    # eager warm-up (first-call set-up, NCCL communicators), then one CUDA graph per token variant
+    # holding the whole step (every layer) with timestamp nodes before, between and after the layers:
+    # the timed steps replay graphs, so no host-side launch work sits between the kernels
     for v in range(NV):
         for li in range(n_layers):
             layer_launch(li, v)
     torch.cuda.synchronize()
-    graphs, timing_mode = None, "cuda-graph replay per layer"
+    gev = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_layers + 1)] for _ in range(NV)]
+    graphs, timing_mode = None, "cuda-graph replay per step (timestamp nodes between layers)"
     try:
-        graphs = [[torch.cuda.CUDAGraph() for _ in range(NV)] for _ in range(n_layers)]
-        for li in range(n_layers):
-            for v in range(NV):
-                with torch.cuda.graph(graphs[li][v]):
+        graphs = [torch.cuda.CUDAGraph() for _ in range(NV)]
+        for v in range(NV):
+            with torch.cuda.graph(graphs[v]):
+                for li in range(n_layers):
+                    gev[v][li].record()
                     layer_launch(li, v)
+                gev[v][n_layers].record()
         torch.cuda.synchronize()
     except Exception as ex:  # pragma: no cover - depends on the driver
         graphs, timing_mode = None, f"eager launches (graph capture failed: {type(ex).__name__})"
         torch.cuda.synchronize()
-    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_layers)]
-          for _ in range(K + W)]
+    eev = [[torch.cuda.Event(enable_timing=True) for _ in range(n_layers + 1)] for _ in range(NV)]
+    layer_t = [[] for _ in range(n_layers)]
+    step_t = []
 
-    def step(s):
+    def step(s, timed):
         v = s % NV
-        for li in range(n_layers):
-            ev[s][li][0].record(stream)
-            if graphs is not None:
-                graphs[li][v].replay()
-            else:
+        if graphs is not None:
+            graphs[v].replay()
+            e_ = gev[v]
+        else:
+            e_ = eev[v]
+            for li in range(n_layers):
+                e_[li].record(stream)
                 layer_launch(li, v)
-            ev[s][li][1].record(stream)
+            e_[n_layers].record(stream)
+        torch.cuda.synchronize()  # the variant's timestamps are re-written by its next replay
+        if timed:
+            for li in range(n_layers):
+                layer_t[li].append(e_[li].elapsed_time(e_[li + 1]))
+            step_t.append(e_[0].elapsed_time(e_[n_layers]))
         for li in range(n_layers):
             idx_log[s, li].copy_(idx_st[li][v])
         if args.l2_flush:
@@ -297,14 +309,14 @@ def ours(args):
     if world > 1:
         dist.barrier()
     for s in range(W):
-        step(s)
+        step(s, False)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(uuid) as clk:
         for s in range(W, W + K):
-            step(s)
+            step(s, True)
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -314,8 +326,8 @@ def ours(args):
     graphs = None  # released before the process group goes away
 
     # ---- per-step and per-layer device times
-    step_ms = [ev[s][0][0].elapsed_time(ev[s][n_layers - 1][1]) for s in range(W, W + K)]
-    layer_ms = {li: [ev[s][li][0].elapsed_time(ev[s][li][1]) for s in range(W, W + K)] for li in range(n_layers)}
+    step_ms = step_t
+    layer_ms = {li: layer_t[li] for li in range(n_layers)}
     ms_per_step = max_over_ranks(sum(step_ms) / K, dev)
     value = ms_per_step * 1e3 / (n_layers * B)
 

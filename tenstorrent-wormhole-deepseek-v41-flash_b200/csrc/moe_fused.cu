@@ -121,7 +121,7 @@ __host__ __device__ inline SmemLayout smem_layout(int H, int I_loc, int B, int E
   o += xbytes > hbytes ? xbytes : hbytes;
   o = (o + 15) & ~size_t(15);
   L.bars = o;
-  o += (size_t)(NST + 1) * 8;
+  o += (size_t)(NST + 2) * 8;  // stage barriers, the h barrier, the token-row barrier
   L.plan = o;
   o += (sizeof(FPlan) + 15) & ~size_t(15);
   L.emask = o;
@@ -339,18 +339,17 @@ __device__ void router_item(const FusedArgs& a, const uint8_t* stage, const __nv
 }
 
 // ------------------------------------------------------------------ token rows
-// bf16 x -> shared memory (router copy for B <= FXB), per-token power-of-2 pre-scale (amax * 2^-p in
-// [128, 256)), e4m3 hi / lo rows in B-operand order (qk_off). All threads; ends with __syncthreads.
+// Token rows (bf16 in shared memory for B <= FXB, else global) -> per-token power-of-2 pre-scale
+// (amax * 2^-p in [128, 256)) -> e4m3 hi / lo rows in B-operand order (qk_off). All threads; ends
+// with __syncthreads.
 __device__ void setup_tokens(const FusedArgs& a, uint8_t* xq, __nv_bfloat16* xs, FPlan& pl, int lo_off) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nv = a.H / 8;  // uint4 per row
   for (int b = 0; b < a.B; ++b) {
-    const uint4* src = reinterpret_cast<const uint4*>(a.x + (long long)b * a.H);
-    uint4* dst = reinterpret_cast<uint4*>(xs + (long long)b * a.H);
+    const uint4* src = reinterpret_cast<const uint4*>((a.B <= FXB ? xs : a.x) + (long long)b * a.H);
     float m = 0.f;
     for (int v = tid; v < nv; v += FT) {
-      const uint4 u = __ldg(src + v);
-      if (a.B <= FXB) dst[v] = u;
+      const uint4 u = src[v];
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
       for (int h = 0; h < 4; ++h)
@@ -742,6 +741,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem + SL.xs);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + SL.bars);
   uint64_t* hbar = full + NST;
+  uint64_t* xbar = full + NST + 1;
   FPlan& pl = *reinterpret_cast<FPlan*>(smem + SL.plan);
   unsigned* emask = reinterpret_cast<unsigned*>(smem + SL.emask);
   const int lo_off = a.B * a.H + 64;  // lo token rows after the hi rows (opposite bank half)
@@ -756,7 +756,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   const int nR = my_router > warp ? (my_router - warp + FW - 1) / FW : 0;  // rows rspan.s + warp + FW * k
 
   if (tid == 0) {
-    for (int s = 0; s <= NST; ++s) mbar_init(&full[s], 1);  // NST stage barriers + the h barrier
+    for (int s = 0; s < NST + 2; ++s) mbar_init(&full[s], 1);  // stage barriers, h barrier, token-row barrier
     pl.abort = 0;
     fence_mbar_init();
   }
@@ -847,7 +847,11 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     return !pl.abort;
   };
 
-  refill();  // router rows stream in while the token rows are prepared
+  refill();  // router rows stream in while the token rows arrive
+  if (tid == 0 && a.B <= FXB) {  // bf16 token rows for the router, one bulk copy
+    mbar_expect_tx(xbar, (uint32_t)(a.B * a.H * 2));
+    bulk_g2s(xs, a.x, (uint32_t)(a.B * a.H * 2), xbar);
+  }
   // the shared expert's weights do not depend on routing: pull them into L2 now (each warp a slice)
   if (lane == 0) {
     const long long b13 = (long long)geo.T * geo.tile13s, b2 = (long long)geo.NT * geo.tile2s;
@@ -860,10 +864,16 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(len) : "memory");
     }
   }
-  setup_tokens(a, xq, xs, pl, lo_off);
   for (int e = tid; e < a.E; e += FT) emask[e] = 0u;
   if (tid == 0)  // finished-tile counts per slot start from zero after grid barrier A
     for (int i = cta; i < a.slots; i += G) a.slot_done[i] = 0u;
+
+  if (a.B <= FXB && !mbar_wait(xbar, 0, kWaitNs)) {
+    if (tid == 0) {
+      atomicOr(a.status, ST_FULL);
+      pl.abort = 1;
+    }
+  }
 
   // ---- phase R: router quarter-rows
   {
@@ -877,7 +887,18 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       refill();
     }
   }
-  if (!grid_sync()) {  // grid barrier A: every router row of the step is done
+  // ---- grid barrier A (every router row of the step is done); the token rows are converted to
+  // e4m3 hi / lo while the other CTAs arrive
+  __syncthreads();
+  unsigned genA = 0;
+  if (tid == 0 && !pl.abort) genA = grid_arrive(a.gbar, G);
+  setup_tokens(a, xq, xs, pl, lo_off);
+  if (tid == 0 && !pl.abort && !grid_wait(a.gbar, genA, a.status)) {
+    atomicOr(a.status, ST_GRID);
+    pl.abort = 1;
+  }
+  __syncthreads();
+  if (pl.abort) {
     drain();
     return;
   }
