@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--l2-flush", action="store_true",
                     help="write 256 MiB between steps (default: off; each step already streams more than L2)")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline sampling")
+    ap.add_argument("--allreduce", choices=["p2p", "nccl"], default="p2p",
+                    help="N > 1: sum the partials inside the layer kernel over NVLink peers (default) or with NCCL")
     return ap.parse_args()
 
 
@@ -75,6 +77,8 @@ def workload_config(args, world):
             "hidden": H, "inter": I, "experts": getattr(args, "experts", E), "topk": TOPK, "shared_experts": 1, "batch": args.batch,
             "score_func": "sigmoid", "route_scale": ROUTE_SCALE, "layers_per_step": [{"fp8": "fp8-block128", "fp4": "fp4-e2m1-e8m0"}[f] for f in layer_formats(args)],
             "parallelism": f"tp{world}",
+            "allreduce": (None if world == 1 else "in-kernel NVLink peer exchange (one launch per layer)"
+                          if getattr(args, "allreduce", "p2p") == "p2p" else "NCCL all-reduce of fp32 partials"),
             "l2": ("flushed between steps (256 MiB write, outside the timed events)" if flush_l2 else
                    "not flushed: every step streams more weight bytes than the 126 MB L2 (read with an L2 "
                    "evict-first policy); tokens rotate through a 256-row pool")}
@@ -229,6 +233,12 @@ def ours(args):
     pool = 256
     toks = dsmoe.make_tokens(pool + B, H, gen, device=dev)
     torch.cuda.synchronize()
+    comm = None
+    if world > 1 and args.allreduce == "p2p":
+        from dsmoe.tp import PeerComm
+        comm = PeerComm(H, device=dev)
+        for m in layers:
+            m.use_comm(comm)
     setup_s = time.time() - t_setup
 
     flush = torch.empty(256 * 1024 * 1024 if args.l2_flush else 1, dtype=torch.uint8, device=dev)
@@ -241,11 +251,18 @@ def ours(args):
     idx_log = torch.zeros((K + W, n_layers, B, TOPK), dtype=torch.int64, device=dev)
     part = [torch.empty((B, H), dtype=torch.float32, device=dev) for _ in range(n_layers)]
     yout = [torch.empty((B, H), dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
-    launches_per_layer = (1 if B <= 8 else 5) + (1 if world > 1 else 0)
+    p2p = comm is not None and all(
+        L.lib.dsmoe_moe_allreduce_supported(m._layer, comm.handle, L.ptr(xin[0][0]), B) for m in layers)
+    launches_per_layer = (1 if B <= 8 else 5) + (1 if world > 1 and not p2p else 0)
 
     def layer_launch(li, v):
         m = layers[li]
         st_ = torch.cuda.current_stream(dev).cuda_stream
+        if p2p:  # the layer kernel sums the ranks' partials itself
+            L.call("dsmoe_moe_decode_allreduce", m._layer, comm.handle, L.ptr(xin[li][v]), B, None,
+                   L.ptr(yout[li]), L.DTYPE_BF16, L.ptr(idx_st[li][v]), None, None, L.ptr(m.workspace),
+                   m.workspace.numel(), st_)
+            return
         y_t, y_dt = (part[li], L.DTYPE_F32) if world > 1 else (yout[li], L.DTYPE_BF16)
         L.call("dsmoe_moe_decode", m._layer, L.ptr(xin[li][v]), B, None, L.ptr(y_t), y_dt,
                L.ptr(idx_st[li][v]), None, None, L.ptr(m.workspace), m.workspace.numel(), st_)
@@ -253,6 +270,9 @@ def ours(args):
             dist.all_reduce(part[li])
             L.call("dsmoe_f32_to_bf16", L.ptr(part[li]), L.ptr(yout[li]), part[li].numel(), st_)
 
+    if world > 1:  # ranks enter the first layer together (the in-kernel exchange's waits are bounded)
+        dist.barrier()
+        torch.cuda.synchronize()
     # eager warm-up (first-call set-up, NCCL communicators), then one CUDA graph per token variant
     # holding the whole step (every layer) with timestamp nodes before, between and after the layers:
     # the timed steps replay graphs, so no host-side launch work sits between the kernels
@@ -412,6 +432,8 @@ def ours(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        if comm is not None:
+            comm.close()
         dist.destroy_process_group()
 
 

@@ -200,6 +200,39 @@ DSMOE_API int dsmoe_moe_decode_profiled(const dsmoe_layer_t* layer, const void* 
 /* fp32 [n] -> bf16 [n] (the last step after an fp32 all-reduce of the partial sums). */
 DSMOE_API int dsmoe_f32_to_bf16(const float* src, void* dst, long long n, void* stream);
 
+/* ---- all-reduce inside the decode kernel (tensor parallelism over NVLink peers) ----------- */
+
+/* One rank's end of a tensor-parallel group for dsmoe_moe_decode_allreduce: an exchange buffer in
+ * this GPU's memory that the other ranks map with CUDA IPC. Replaces the reference's per-layer
+ * all_reduce_sum (dsv41/tt/attn.py:19-21, called at dsv41/tt/moe.py:162, 180).
+ * Set-up: every rank calls dsmoe_comm_create (with its device current), the ranks exchange the
+ * DSMOE_COMM_HANDLE_BYTES-byte handles (any host channel), then every rank calls dsmoe_comm_open
+ * with all handles concatenated in rank order. world 2..8; hidden must match the layers'. */
+#define DSMOE_COMM_HANDLE_BYTES 64
+typedef struct dsmoe_comm dsmoe_comm_t;
+DSMOE_API int dsmoe_comm_create(int rank, int world, int hidden, dsmoe_comm_t** comm, void* handle_out);
+DSMOE_API int dsmoe_comm_open(dsmoe_comm_t* comm, const void* handles);
+/* Synchronizes the device, unmaps the peers' buffers and frees this rank's. */
+DSMOE_API int dsmoe_comm_destroy(dsmoe_comm_t* comm);
+
+/* 1 when dsmoe_moe_decode_allreduce takes this call (the persistent path: B <= 8 tokens, hidden a
+ * multiple of 512, <= 1024 experts, x 16-byte aligned), else 0. */
+DSMOE_API int dsmoe_moe_allreduce_supported(const dsmoe_layer_t* layer, const dsmoe_comm_t* comm, const void* x,
+                                            int B);
+
+/* dsmoe_moe_decode whose output y is the sum of every rank's partial: each rank's persistent
+ * kernel stores its output tiles into the peers' exchange buffers over NVLink and sums the tiles
+ * it receives in rank order, so y is bit-identical on every rank and the layer is one launch per
+ * rank. All ranks must make the same sequence of calls on one comm (layers may share it); calls on
+ * one comm must not overlap. A peer that has not delivered a tile within 5 s sets a status bit
+ * that dsmoe_moe_check reports; the comm must then be destroyed and re-created on every rank.
+ * Returns DSMOE_ERR_UNSUPPORTED when dsmoe_moe_allreduce_supported is 0 (use dsmoe_moe_decode with
+ * y_dtype F32 and a collective library then). */
+DSMOE_API int dsmoe_moe_decode_allreduce(const dsmoe_layer_t* layer, const dsmoe_comm_t* comm, const void* x,
+                                         int B, const uint8_t* image_mask, void* y, int y_dtype, int64_t* idx,
+                                         float* wt, float* scores, void* workspace, size_t workspace_bytes,
+                                         void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -457,9 +457,14 @@ extern "C" int dsmoe_router(const dsmoe_layer_t* L, const void* x, int B, const 
   return launch_router(a, false, (cudaStream_t)stream);
 }
 
+static bool takes_fused(const dsmoe_layer_t* L, const void* x, int B) {
+  return fused_region(L) > 0 && fused_supported(L, B) && ((uintptr_t)x & 15) == 0;  // 16-byte token loads
+}
+
 static int moe_decode_impl(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image_mask, void* y,
                            int y_dtype, int64_t* idx, float* wt, float* scores, void* workspace,
-                           size_t workspace_bytes, void* stream, void* const* events) {
+                           size_t workspace_bytes, void* stream, void* const* events,
+                           const PeerExchange* px = nullptr) {
   int rc = validate(L, B, true);
   if (rc) return rc;
   DSMOE_REQUIRE(x && y && workspace, DSMOE_ERR_ARG, "moe_decode: x / y / workspace null");
@@ -471,8 +476,8 @@ static int moe_decode_impl(const dsmoe_layer_t* L, const void* x, int B, const u
                 w.total);
   uint8_t* ws = (uint8_t*)workspace;
   cudaStream_t st = (cudaStream_t)stream;
-  if (fused_region(L) > 0 && fused_supported(L, B) && ((uintptr_t)x & 15) == 0)  // 16-byte token loads
-    return launch_fused(L, x, B, image_mask, y, y_dtype, idx, wt, scores, ws, st, events);
+  if (takes_fused(L, x, B)) return launch_fused(L, x, B, image_mask, y, y_dtype, idx, wt, scores, ws, st, events, px);
+  DSMOE_REQUIRE(!px, DSMOE_ERR_UNSUPPORTED, "moe_decode_allreduce: batch %d / layer shape not on the persistent path", B);
   RouterArgs ra = router_args(L, x, B, image_mask, idx, wt, scores, ws, w);
   if (events) cudaEventRecord((cudaEvent_t)events[0], st);
   rc = launch_router(ra, true, st);
@@ -531,6 +536,22 @@ extern "C" int dsmoe_moe_decode_profiled(const dsmoe_layer_t* L, const void* x, 
                 "moe_decode_profiled: four events required");
   return moe_decode_impl(L, x, B, image_mask, y, y_dtype, idx, wt, scores, workspace, workspace_bytes, stream,
                          events);
+}
+
+extern "C" int dsmoe_moe_allreduce_supported(const dsmoe_layer_t* L, const dsmoe_comm_t* comm, const void* x,
+                                             int B) {
+  const PeerExchange* px = comm_exchange(comm);
+  if (!px || !L || !x || validate(L, B, true) != DSMOE_OK || px->hidden != L->hidden) return 0;
+  return takes_fused(L, x, B) ? 1 : 0;
+}
+
+extern "C" int dsmoe_moe_decode_allreduce(const dsmoe_layer_t* L, const dsmoe_comm_t* comm, const void* x, int B,
+                                          const uint8_t* image_mask, void* y, int y_dtype, int64_t* idx, float* wt,
+                                          float* scores, void* workspace, size_t workspace_bytes, void* stream) {
+  const PeerExchange* px = comm_exchange(comm);
+  DSMOE_REQUIRE(px, DSMOE_ERR_ARG, "moe_decode_allreduce: comm is null or not opened");
+  return moe_decode_impl(L, x, B, image_mask, y, y_dtype, idx, wt, scores, workspace, workspace_bytes, stream,
+                         nullptr, px);
 }
 
 extern "C" int dsmoe_moe_check(const dsmoe_layer_t* L, int B, void* workspace, size_t workspace_bytes,

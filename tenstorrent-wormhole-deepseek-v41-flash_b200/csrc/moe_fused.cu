@@ -51,8 +51,9 @@ constexpr int FEMAX = 1024;            // routed experts
 constexpr int FHSLOTS = 2;             // slots whose h rows a CTA stages for phase 2
 constexpr int NPEND = 8;               // segments a warp holds before publishing them
 constexpr uint64_t kWaitNs = 1000000000ull;
+constexpr uint64_t kPeerWaitNs = 5000000000ull;  // a peer GPU's tile: ranks may start seconds apart
 
-enum : unsigned { ST_FULL = 1u, ST_SLOT = 2u, ST_GRID = 8u };
+enum : unsigned { ST_FULL = 1u, ST_SLOT = 2u, ST_GRID = 8u, ST_PEER = 16u };
 
 struct FusedArgs {
   int H, I_loc, E, B, topk, score_func;
@@ -85,6 +86,10 @@ struct FusedArgs {
   unsigned* status;    // [0]
   int sh_idx;          // scratch slot index of the shared expert
   int slots, p13max, p2max;
+  // peer all-reduce of y (ar_world > 1): see ar_tile
+  int ar_world, ar_rank;
+  unsigned* ar_ctl;
+  unsigned long long* ar_slots[kMaxWorld];
 };
 
 struct FPlan {
@@ -101,6 +106,7 @@ struct FPlan {
   float selw[FMAXB][FMAXK];
   int wcnt[FW];
   int abort;
+  unsigned ar_epoch;
 };
 
 // Shared-memory carve-up (host and device agree): stage ring; token rows (e4m3 hi rows [B][H], lo
@@ -267,12 +273,16 @@ __device__ __forceinline__ uint32_t ld_relaxed_u32(const unsigned* p) {
 // Arrive: the CTA's writes are ordered before it by the caller's __syncthreads and this thread's
 // fence; the last arrival resets the count and bumps the generation with release semantics.
 // Wait: relaxed polling, one acquire fence once the generation moved.
-__device__ __forceinline__ unsigned grid_arrive(unsigned* gbar, int G) {
+// With `ep_ctl`, the last arrival also stores `ep` there (the peer exchange's epoch: every CTA read
+// the previous one before it arrived).
+__device__ __forceinline__ unsigned grid_arrive(unsigned* gbar, int G, unsigned* ep_ctl = nullptr,
+                                                unsigned ep = 0u) {
   const unsigned g0 = ld_acquire_u32(gbar + 1);
   fence_acq_rel_gpu();
   unsigned old;
   asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(gbar) : "memory");
   if (old == (unsigned)G - 1) {
+    if (ep_ctl) asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(ep_ctl), "r"(ep) : "memory");
     asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(gbar) : "memory");
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(gbar + 1) : "memory");
   }
@@ -725,6 +735,70 @@ __device__ __forceinline__ void w2_store_y(const FusedArgs& a, int nt, float4 s4
   }
 }
 
+// ------------------------------------------------------------------ peer all-reduce
+// One-shot all-reduce of an output tile over the tensor-parallel ranks, on NVLink peer memory.
+// Each rank pushes its tile partial (32 lanes x 4 fp32) into slot (parity, its rank, tile) of every
+// peer's exchange buffer, then reads the peers' partials of the same tile from its own buffer and
+// sums all ranks' partials in rank order, so every rank computes the same bits.
+// Words are LL pairs: the value's bits in the low half and the call's epoch in the high half. An
+// aligned 8-byte store is single-copy atomic, so a reader that sees this call's epoch in a word
+// sees the value written with it; no fence or flag is needed. Epochs grow by one per call (the
+// control word), and slots alternate between two parities: a peer can be at most one call ahead
+// (it cannot finish call e + 1 without this rank's tiles of call e + 1), so it never overwrites a
+// slot this rank still reads.
+__device__ __forceinline__ unsigned long long ll_word(float v, unsigned ep) {
+  return ((unsigned long long)ep << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ void st_ll2(unsigned long long* p, unsigned long long w0, unsigned long long w1) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(w0), "l"(w1) : "memory");
+}
+__device__ __forceinline__ void ld_ll2(const unsigned long long* p, unsigned long long& w0, unsigned long long& w1) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(p) : "memory");
+}
+__device__ __forceinline__ size_t ar_slot(int par, int q, int W, int NT, int nt, int lane) {
+  return ((((size_t)par * W + q) * NT + nt) * 32 + lane) * 4;
+}
+// s4: this rank's partial of tile nt in, the sum over ranks out. False if a peer's words did not
+// arrive within kPeerWaitNs (s4 is then incomplete).
+__device__ __noinline__ bool ar_tile(const FusedArgs& a, int nt, unsigned ep, float4& s4, int lane) {
+  const int W = a.ar_world, r = a.ar_rank, NT = a.H / 16, par = (int)(ep & 1u);
+  const unsigned long long w0 = ll_word(s4.x, ep), w1 = ll_word(s4.y, ep), w2 = ll_word(s4.z, ep),
+                           w3 = ll_word(s4.w, ep);
+  const size_t mine = ar_slot(par, r, W, NT, nt, lane);
+  for (int d = 1; d < W; ++d) {  // peers in the order r+1, r+2, ... (spreads the first stores)
+    const int q = r + d < W ? r + d : r + d - W;
+    unsigned long long* p = a.ar_slots[q] + mine;
+    st_ll2(p, w0, w1);
+    st_ll2(p + 2, w2, w3);
+  }
+  float4 tot = make_float4(0.f, 0.f, 0.f, 0.f);
+  bool ok = true;
+  for (int q = 0; q < W; ++q) {
+    float4 v = s4;
+    if (q != r) {
+      const unsigned long long* p = a.ar_slots[r] + ar_slot(par, q, W, NT, nt, lane);
+      unsigned long long x0 = 0, x1 = 0, x2 = 0, x3 = 0;
+      const uint64_t t0 = globaltimer_ns();
+      while (ok) {
+        ld_ll2(p, x0, x1);
+        ld_ll2(p + 2, x2, x3);
+        if ((unsigned)(x0 >> 32) == ep && (unsigned)(x1 >> 32) == ep && (unsigned)(x2 >> 32) == ep &&
+            (unsigned)(x3 >> 32) == ep)
+          break;
+        if (globaltimer_ns() - t0 > kPeerWaitNs) ok = false;
+      }
+      v = make_float4(__uint_as_float((unsigned)x0), __uint_as_float((unsigned)x1), __uint_as_float((unsigned)x2),
+                      __uint_as_float((unsigned)x3));
+    }
+    tot.x += v.x;
+    tot.y += v.y;
+    tot.z += v.z;
+    tot.w += v.w;
+  }
+  s4 = tot;
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ------------------------------------------------------------------ the kernel
 // A published w1|w3 segment: kind 1 = tile t of slot s (np items), kind 3 = tile of slot s finished
 // by this warp alone (only the slot's count is due).
@@ -758,6 +832,9 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   if (tid == 0) {
     for (int s = 0; s < NST + 2; ++s) mbar_init(&full[s], 1);  // stage barriers, h barrier, token-row barrier
     pl.abort = 0;
+    // the peer exchange's epoch of this call: one past the last call's (read before barrier A,
+    // whose last arrival stores it back)
+    pl.ar_epoch = a.ar_world > 1 ? *(volatile unsigned*)a.ar_ctl + 1u : 0u;
     fence_mbar_init();
   }
   __syncthreads();
@@ -891,7 +968,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   // e4m3 hi / lo while the other CTAs arrive
   __syncthreads();
   unsigned genA = 0;
-  if (tid == 0 && !pl.abort) genA = grid_arrive(a.gbar, G);
+  if (tid == 0 && !pl.abort) genA = grid_arrive(a.gbar, G, a.ar_world > 1 ? a.ar_ctl : nullptr, pl.ar_epoch);
   setup_tokens(a, xq, xs, pl, lo_off);
   if (tid == 0 && !pl.abort && !grid_wait(a.gbar, genA, a.status)) {
     atomicOr(a.status, ST_GRID);
@@ -1275,6 +1352,9 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
         s4.z += v.z;
         s4.w += v.w;
       }
+      if (a.ar_world > 1 && !ar_tile(a, cta + G * warp, pl.ar_epoch, s4, lane)) {
+        if (lane == 0) atomicOr(a.status, ST_PEER);
+      }
       w2_store_y(a, cta + G * warp, s4, lane);
     }
   }
@@ -1348,7 +1428,8 @@ bool fused_supported(const dsmoe_layer_t* L, int B) {
 }
 
 int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image_mask, void* y, int y_dtype,
-                 int64_t* idx, float* wt, float* scores, uint8_t* ws, cudaStream_t st, void* const* events) {
+                 int64_t* idx, float* wt, float* scores, uint8_t* ws, cudaStream_t st, void* const* events,
+                 const PeerExchange* px) {
   DevInfo& d = dev_info();
   const int optin = d.optin, sms = d.sms;
   const size_t smem = fused_smem_bytes(L->hidden, L->inter_local, B, L->n_experts);
@@ -1393,6 +1474,17 @@ int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* im
   a.slots = f.slots;
   a.p13max = f.p13max;
   a.p2max = f.p2max;
+  if (px && px->world > 1) {
+    DSMOE_REQUIRE(px->hidden == L->hidden && px->world <= kMaxWorld && px->rank >= 0 && px->rank < px->world,
+                  DSMOE_ERR_ARG, "fused: exchange for hidden %d, world %d, rank %d", px->hidden, px->world, px->rank);
+    a.ar_world = px->world;
+    a.ar_rank = px->rank;
+    a.ar_ctl = px->ctl;
+    for (int q = 0; q < px->world; ++q) {
+      DSMOE_REQUIRE(px->slots[q], DSMOE_ERR_ARG, "fused: exchange slots of rank %d not mapped", q);
+      a.ar_slots[q] = px->slots[q];
+    }
+  }
 
   const int fi = L->routed.fmt == DSMOE_FMT_FP8 ? 0 : 1;
   void (*kern)(FusedArgs) = fi == 0 ? moe_fused_kernel<DSMOE_FMT_FP8> : moe_fused_kernel<DSMOE_FMT_FP4>;

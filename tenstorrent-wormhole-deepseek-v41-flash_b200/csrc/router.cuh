@@ -61,7 +61,23 @@ struct FusedScratch {
 };
 FusedScratch fused_scratch(int H, int I_loc, int E, int B, int topk, int r_fmt);
 bool fused_supported(const dsmoe_layer_t* L, int B);
+
+// Peer exchange of the persistent kernel's all-reduce (comm.cu owns the memory). Every rank has one
+// exchange buffer: a control word (the epoch of its last call) and the slots its peers write,
+// [2 parities][world source ranks][hidden / 16 output tiles][32 lanes][4 words]; slots[q] is rank
+// q's buffer as this GPU addresses it (its own for q == rank, an IPC mapping otherwise).
+constexpr int kMaxWorld = 8;
+struct PeerExchange {
+  int rank, world, hidden;
+  unsigned* ctl;
+  unsigned long long* slots[kMaxWorld];
+};
+inline size_t exchange_slot_words(int world, int hidden) { return 2ull * world * (hidden / 16) * 128; }
+// The exchange of an opened comm (comm.cu), or nullptr.
+const PeerExchange* comm_exchange(const dsmoe_comm_t* c);
+
 int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image_mask, void* y, int y_dtype,
-                 int64_t* idx, float* wt, float* scores, uint8_t* ws, cudaStream_t st, void* const* events);
+                 int64_t* idx, float* wt, float* scores, uint8_t* ws, cudaStream_t st, void* const* events,
+                 const PeerExchange* px = nullptr);
 
 }  // namespace dsmoe

@@ -17,6 +17,7 @@ FMT_FP8, FMT_FP4 = 0, 1
 SCORE_SIGMOID, SCORE_SQRTSOFTPLUS = 0, 1
 DTYPE_F32, DTYPE_BF16, DTYPE_E4M3 = 0, 1, 2
 MAX_DECODE_TOKENS = 64
+COMM_HANDLE_BYTES = 64
 SLOT_TOKENS = 8
 
 FMT_NAMES = {"fp8": FMT_FP8, "fp4": FMT_FP4}
@@ -61,6 +62,12 @@ _SIGS = {
                                    ctypes.POINTER(_P)], _I),
     "dsmoe_moe_check": ([ctypes.POINTER(Layer), _I, _P, ctypes.c_size_t, _P], _I),
     "dsmoe_f32_to_bf16": ([_P, _P, _LL, _P], _I),
+    "dsmoe_comm_create": ([_I, _I, _I, ctypes.POINTER(_P), _P], _I),
+    "dsmoe_comm_open": ([_P, _P], _I),
+    "dsmoe_comm_destroy": ([_P], _I),
+    "dsmoe_moe_allreduce_supported": ([ctypes.POINTER(Layer), _P, _P, _I], _I),
+    "dsmoe_moe_decode_allreduce": ([ctypes.POINTER(Layer), _P, _P, _I, _P, _P, _I, _P, _P, _P, _P, ctypes.c_size_t,
+                                    _P], _I),
 }
 
 

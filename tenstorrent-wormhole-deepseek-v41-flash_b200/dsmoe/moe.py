@@ -61,6 +61,7 @@ class MoE:
         nbytes = L.lib.dsmoe_moe_workspace_bytes(self._layer, self.max_tokens)
         # zero-filled once: the persistent kernel keeps counters and a grid barrier here
         self.workspace = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        self.comm = None  # tp.PeerComm: all-reduce inside the decode kernel
 
     # ---------------------------------------------------------------- loading
     def _make_layer(self) -> L.Layer:
@@ -119,10 +120,29 @@ class MoE:
         """This rank's fp32 partial sum [B, H] (routed + shared over its intermediate slice)."""
         return self._run(x, image_mask, out, L.DTYPE_F32, idx, wt)
 
+    def use_comm(self, comm) -> None:
+        """Sum the tensor-parallel partials inside the decode kernel over ``comm`` (a tp.PeerComm of
+        this layer's group) whenever the call takes the persistent path; None = the collective
+        library's all-reduce always."""
+        if comm is not None and (comm.world != self.world or comm.rank != self.rank or comm.hidden != self.hidden):
+            raise ValueError("comm does not match this layer's rank, world or hidden size")
+        self.comm = comm
+
     def forward(self, x: torch.Tensor, image_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         """y [B, H] bf16: the full layer output (partials all-reduced when world > 1)."""
         if self.world == 1:
             return self._run(x, image_mask, None, L.DTYPE_BF16)
+        if self.comm is not None and self.comm.handle is not None:
+            x = _check_x(x, self.hidden, self.device)
+            B = x.shape[0]
+            if B <= self.max_tokens and L.lib.dsmoe_moe_allreduce_supported(self._layer, self.comm.handle,
+                                                                             L.ptr(x), B):
+                y = torch.empty((B, self.hidden), dtype=torch.bfloat16, device=self.device)
+                mask = self._mask(image_mask, B)
+                L.call("dsmoe_moe_decode_allreduce", self._layer, self.comm.handle, L.ptr(x), B, L.ptr(mask),
+                       L.ptr(y), L.DTYPE_BF16, None, None, None, L.ptr(self.workspace), self.workspace.numel(),
+                       L.stream_of(x))
+                return y
         part = self._run(x, image_mask, None, L.DTYPE_F32)
         torch.distributed.all_reduce(part, group=self.group)
         y = torch.empty(part.shape, dtype=torch.bfloat16, device=self.device)

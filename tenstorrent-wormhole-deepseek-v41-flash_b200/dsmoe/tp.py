@@ -44,3 +44,51 @@ def env_rank_world():
     """(rank, local_rank, world) from torchrun's environment (1 process when absent)."""
     return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
             int(os.environ.get("WORLD_SIZE", 1)))
+
+
+class PeerComm:
+    """One rank's end of the all-reduce inside the decode kernel (``dsmoe_comm`` of libdsmoe.so).
+
+    An exchange buffer on this GPU that every other rank of ``group`` maps with CUDA IPC; a layer
+    called through it (``MoE.forward`` once ``MoE.use_comm`` is set) stores its output tiles into the
+    peers' buffers over NVLink and sums what it receives, in one launch per rank -- the role of the
+    reference's ``all_reduce_sum`` after each MoE layer (dsv41/tt/attn.py:19-21). Collective: every
+    rank of ``group`` constructs it, with its own GPU current. One comm serves any number of layers
+    of the same hidden size, provided every rank calls them in the same order.
+    """
+
+    def __init__(self, hidden: int, group=None, device=None):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _lib as L
+        self.rank, self.world, self.hidden = dist.get_rank(group), dist.get_world_size(group), hidden
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        handle = (ctypes.c_uint8 * L.COMM_HANDLE_BYTES)()
+        p = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            L.call("dsmoe_comm_create", self.rank, self.world, hidden, ctypes.byref(p), handle)
+            self.handle = p.value
+            try:
+                handles = [None] * self.world
+                dist.all_gather_object(handles, bytes(handle), group=group)
+                L.call("dsmoe_comm_open", self.handle, b"".join(handles))
+            except Exception:
+                L.lib.dsmoe_comm_destroy(self.handle)
+                self.handle = None
+                raise
+
+    def close(self) -> None:
+        """Free this rank's buffer and unmap the peers' (synchronizes the device)."""
+        from . import _lib as L
+        if self.handle is not None:
+            with torch.cuda.device(self.device):
+                L.call("dsmoe_comm_destroy", self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()

@@ -1,7 +1,9 @@
-"""Tensor parallelism across real GPUs: one process per GPU over NCCL, each rank holding I/world rows
-of every expert. Each rank's fused decode writes its fp32 partial, MoE.forward all-reduces them, and
-the bf16 result must match the oracle's whole layer on every rank (the all-reduce in
-dsv41/tt/attn.py:19-21 sums the same partials). Needs at least two GPUs; skipped otherwise."""
+"""Tensor parallelism across real GPUs: one process per GPU, each rank holding I/world rows of every
+expert. Two all-reduce paths sum the ranks' partials (the role of dsv41/tt/attn.py:19-21):
+NCCL over the fp32 partials, and the peer exchange inside the decode kernel (tp.PeerComm). Both
+must match the oracle's whole layer on every rank; the in-kernel sum must also be bit-identical
+across ranks, stay right over many calls sharing one comm (epochs, slot parities) and under CUDA
+graph replay. Needs at least two GPUs; skipped otherwise."""
 import datetime
 import os
 import socket
@@ -32,24 +34,65 @@ def _worker(rank, world, port, root, out_q):
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
-    res = []
+    res, extra = [], {}
     try:
         from oracle import moe as OM
         from _util import make_layer_cpu, to_gpu_moe, to_oracle_layer
+        from dsmoe.tp import PeerComm
+        comm = PeerComm(1024, device=dev)
+        layers = []
         for fmt, B in (("fp8", 1), ("fp4", 3), ("fp8", 8), ("fp4", 13)):
             spec = make_layer_cpu(fmt, 1024, 512, 32, seed=4000 + B)
             m = to_gpu_moe(spec, rank=rank, world=world, device=dev)
             x = torch.randn((B, 1024), generator=torch.Generator().manual_seed(B)).to(torch.bfloat16)
-            y = m.forward(x.to(dev)).float().cpu().numpy()
-            idx, _, _ = m.route(x.to(dev))
-            m.check(B)
             yr, ridx, _ = OM.moe_forward(to_oracle_layer(spec), x.float().numpy())
-            mar, cos = OM.compare(y, yr)
-            res.append((fmt, B, bool(np.array_equal(idx.cpu().numpy(), ridx)), float(mar), float(cos)))
+            idx, _, _ = m.route(x.to(dev))
+            for path in ("nccl", "p2p"):
+                m.use_comm(comm if path == "p2p" else None)
+                torch.cuda.synchronize(dev)
+                dist.barrier()  # ranks enter the in-kernel exchange together (its waits are bounded)
+                y = m.forward(x.to(dev))
+                m.check(B)
+                mar, cos = OM.compare(y.float().cpu().numpy(), yr)
+                res.append((path, fmt, B, bool(np.array_equal(idx.cpu().numpy(), ridx)), float(mar), float(cos)))
+                if path == "p2p" and B <= 8:  # in-kernel sum: every rank holds the same bits
+                    allv = [torch.empty_like(y) for _ in range(world)]
+                    dist.all_gather(allv, y)
+                    res.append(("same-bits", fmt, B, all(torch.equal(allv[0], v) for v in allv), 0.0, 1.0))
+            layers.append((m, x.to(dev), y))
+        # many calls on one comm, layers interleaved: each output stays exactly the first one's
+        seq_ok = True
+        for it in range(24):
+            m, xd, y0 = layers[it % 3]
+            seq_ok &= bool(torch.equal(m.forward(xd), y0))
+        for m, _, _ in layers:
+            m.check(8)
+        extra["sequence"] = seq_ok
+        # the same under CUDA graph replay (the epoch lives in device memory)
+        m, xd, y0 = layers[0]
+        st = torch.cuda.Stream(dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(st):
+            m.forward(xd)
+        torch.cuda.current_stream(dev).wait_stream(st)
+        torch.cuda.synchronize(dev)
         dist.barrier()
-        out_q.put((rank, res, None))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            yg = m.forward(xd)
+        graph_ok = True
+        for _ in range(6):
+            g.replay()
+            torch.cuda.synchronize(dev)
+            graph_ok &= bool(torch.equal(yg, y0))
+        m.check(1)
+        extra["graph"] = graph_ok
+        del g
+        comm.close()
+        dist.barrier()
+        out_q.put((rank, res, extra, None))
     except Exception as ex:  # reported to the parent, which fails the test
-        out_q.put((rank, res, repr(ex)))
+        out_q.put((rank, res, extra, repr(ex)))
     finally:
         dist.destroy_process_group()
 
@@ -72,11 +115,12 @@ def test_tp_forward_nccl(world):
             p.join(timeout=60)
             if p.is_alive():
                 p.kill()
-    for rank, res, err in got:
+    for rank, res, extra, err in got:
         assert err is None, (rank, err)
-        assert len(res) == 4
-        for fmt, B, idx_ok, mar, cos in res:
-            assert idx_ok, (rank, fmt, B)
-            assert mar < MAR_TOL and cos > COS_TOL, (rank, fmt, B, mar, cos)
+        assert len(res) == 11
+        for path, fmt, B, ok, mar, cos in res:
+            assert ok, (rank, path, fmt, B)
+            assert mar < MAR_TOL and cos > COS_TOL, (rank, path, fmt, B, mar, cos)
+        assert extra == {"sequence": True, "graph": True}, (rank, extra)
     for p in procs:
         assert p.exitcode == 0
