@@ -200,6 +200,31 @@ DSMOE_API int dsmoe_moe_decode_profiled(const dsmoe_layer_t* layer, const void* 
 /* fp32 [n] -> bf16 [n] (the last step after an fp32 all-reduce of the partial sums). */
 DSMOE_API int dsmoe_f32_to_bf16(const float* src, void* dst, long long n, void* stream);
 
+/* ---- prefill / batched layer on the 5th-generation tensor cores --------------------------- */
+
+/* Workspace bytes for dsmoe_moe_prefill with P tokens (0 if the layer or P is unsupported). */
+DSMOE_API size_t dsmoe_moe_prefill_workspace_bytes(const dsmoe_layer_t* layer, int P);
+
+/* Whole MoE layer for P = 1..4096 tokens with given routing: idx [P, k] int64 and wt [P, k] fp32
+ * (from dsmoe_router, or forced), x [P, H] bf16 (16-byte aligned), y [P, H] bf16 or fp32 (this
+ * GPU's partial with y_dtype F32). The (token, expert) pairs are grouped by expert (counting sort,
+ * chunks of <= 64 tokens), then two grouped GEMMs on tcgen05 with TMEM accumulators: w1|w3 per
+ * chunk, SwiGLU, w2 per chunk, and a routing-weighted combine in k order plus the shared expert.
+ * FP8 experts use kind::f8f6f4 with their 128 x 128 fp32 scales applied per 128-K block to the
+ * accumulator; FP4 experts use kind::mxf8f6f4.block_scale with their e8m0 scales. Requires
+ * hidden and inter_local multiples of 128 and P * k <= 8192. Every device wait is bounded;
+ * dsmoe_moe_prefill_check reports an expired wait or an out-of-range expert index.
+ * Replaces MoE.prefill_batched / _batched (dsv41/tt/moe.py:182-200, 263-288) and MoE.prefill
+ * (dsv41/tt/moe.py:290-303). */
+DSMOE_API int dsmoe_moe_prefill(const dsmoe_layer_t* layer, const void* x, int P, const int64_t* idx,
+                                const float* wt, void* y, int y_dtype, void* workspace, size_t workspace_bytes,
+                                void* stream);
+
+/* Synchronizes `stream` and reads the prefill status word: DSMOE_OK, DSMOE_ERR_TIMEOUT (a bounded
+ * wait expired) or DSMOE_ERR_ARG (an expert index outside 0..n_experts-1); clears it. */
+DSMOE_API int dsmoe_moe_prefill_check(const dsmoe_layer_t* layer, int P, void* workspace, size_t workspace_bytes,
+                                      void* stream);
+
 /* ---- all-reduce inside the decode kernel (tensor parallelism over NVLink peers) ----------- */
 
 /* One rank's end of a tensor-parallel group for dsmoe_moe_decode_allreduce: an exchange buffer in

@@ -178,6 +178,22 @@ def moe_forward(layer: MoELayer, x: np.ndarray, rank: int = 0, world: int = 1,
     return bf16_round(y.astype(np.float32)).astype(np.float64), idx, wt
 
 
+def moe_forward_routed(layer: MoELayer, x: np.ndarray, idx: np.ndarray, wt: np.ndarray, rank: int = 0,
+                       world: int = 1, return_partial: bool = False) -> np.ndarray:
+    """The layer for tokens x [P, H] with routing given (idx [P, k], wt [P, k]): the batched prefill
+    of dsv41/tt/moe.py:182-200, 263-288 (bincount, per-expert buckets, gather, FFN, weighted
+    scatter-add) computes exactly this sum; the shared expert takes every token."""
+    inter = layer.shared.dense("w1").shape[0]
+    sl = slice(rank * inter // world, (rank + 1) * inter // world)
+    y = expert_ffn(x, layer.shared, None, sl)
+    for e in np.unique(idx):
+        tok, kk = np.nonzero(idx == e)
+        y[tok] += expert_ffn(x[tok], layer.experts[int(e)], wt[tok, kk], sl)
+    if return_partial:
+        return y
+    return bf16_round(y.astype(np.float32)).astype(np.float64)
+
+
 def compare(y: np.ndarray, y_ref: np.ndarray):
     """(max-abs-rel, cosine): max|y - ref| / max|ref| and the cosine similarity of the flattened rows."""
     y = np.asarray(y, np.float64).ravel()

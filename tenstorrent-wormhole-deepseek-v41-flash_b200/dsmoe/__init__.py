@@ -8,7 +8,7 @@ Gate / Expert / MoE surface (``moe``). Synthetic seeded weights for tests and be
 from . import _lib
 from .moe import MoE, Gate, Expert
 from .store import ExpertStore, expert_bytes
-from .synth import ExpertWeights, RouterWeights, make_expert, make_router, make_tokens
+from .synth import ExpertWeights, RouterWeights, make_expert, make_router, make_tokens, zipf_routing
 
 __all__ = ["MoE", "Gate", "Expert", "ExpertStore", "expert_bytes", "ExpertWeights", "RouterWeights",
-           "make_expert", "make_router", "make_tokens", "_lib"]
+           "make_expert", "make_router", "make_tokens", "zipf_routing", "_lib"]

@@ -62,6 +62,7 @@ class MoE:
         # zero-filled once: the persistent kernel keeps counters and a grid barrier here
         self.workspace = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
         self.comm = None  # tp.PeerComm: all-reduce inside the decode kernel
+        self._prefill_ws: Optional[torch.Tensor] = None  # grown on demand by prefill()
 
     # ---------------------------------------------------------------- loading
     def _make_layer(self) -> L.Layer:
@@ -119,6 +120,45 @@ class MoE:
                 idx=None, wt=None) -> torch.Tensor:
         """This rank's fp32 partial sum [B, H] (routed + shared over its intermediate slice)."""
         return self._run(x, image_mask, out, L.DTYPE_F32, idx, wt)
+
+    def prefill(self, x: torch.Tensor, idx: Optional[torch.Tensor] = None, wt: Optional[torch.Tensor] = None,
+                image_mask: Optional[torch.Tensor] = None, partial: bool = False) -> torch.Tensor:
+        """Batched layer for P tokens on the tcgen05 grouped GEMMs (dsv41/tt/moe.py:182-200, 263-288).
+
+        Routing comes from ``idx`` [P, k] int64 / ``wt`` [P, k] fp32 when given (e.g. forced), else
+        from this layer's router. Returns y [P, H] bf16 -- all-reduced over the tensor-parallel group
+        when world > 1 -- or this rank's fp32 partial with ``partial=True``."""
+        x = _check_x(x, self.hidden, self.device)
+        P = x.shape[0]
+        if idx is None:
+            idx, wt, _ = self.route(x, image_mask)
+        elif wt is None:
+            raise ValueError("wt is required with idx")
+        idx = idx.to(self.device, torch.int64).contiguous()
+        wt = wt.to(self.device, torch.float32).contiguous()
+        if idx.shape != (P, self.topk) or wt.shape != (P, self.topk):
+            raise ValueError(f"idx / wt must be [{P}, {self.topk}]")
+        nbytes = L.lib.dsmoe_moe_prefill_workspace_bytes(self._layer, P)
+        if nbytes == 0:
+            raise ValueError(f"prefill does not support this layer with {P} tokens")
+        if self._prefill_ws is None or self._prefill_ws.numel() < nbytes:
+            self._prefill_ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        f32 = partial or self.world > 1
+        y = torch.empty((P, self.hidden), dtype=torch.float32 if f32 else torch.bfloat16, device=self.device)
+        L.call("dsmoe_moe_prefill", self._layer, L.ptr(x), P, L.ptr(idx), L.ptr(wt), L.ptr(y),
+               L.DTYPE_F32 if f32 else L.DTYPE_BF16, L.ptr(self._prefill_ws), self._prefill_ws.numel(), L.stream_of(x))
+        if partial or self.world == 1:
+            return y
+        torch.distributed.all_reduce(y, group=self.group)
+        out = torch.empty((P, self.hidden), dtype=torch.bfloat16, device=self.device)
+        L.call("dsmoe_f32_to_bf16", L.ptr(y), L.ptr(out), y.numel(), L.stream_of(y))
+        return out
+
+    def prefill_check(self, P: int) -> None:
+        """Synchronize and raise if the last prefill call's bounded waits expired or an index was bad."""
+        if self._prefill_ws is not None:
+            L.call("dsmoe_moe_prefill_check", self._layer, P, L.ptr(self._prefill_ws), self._prefill_ws.numel(),
+                   L.stream_of(self._prefill_ws))
 
     def use_comm(self, comm) -> None:
         """Sum the tensor-parallel partials inside the decode kernel over ``comm`` (a tp.PeerComm of

@@ -94,3 +94,21 @@ def make_router(n_experts: int, hidden: int, gen: torch.Generator, device="cpu",
 
 def make_tokens(n: int, hidden: int, gen: torch.Generator, device="cpu") -> torch.Tensor:
     return torch.randn((n, hidden), generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+
+
+def zipf_routing(n_tokens: int, n_experts: int, topk: int, gen: torch.Generator, s: float = 1.1,
+                 route_scale: float = 2.5):
+    """Skewed routing for the prefill benchmark: expert popularity ~ Zipf(s) over a seeded random
+    permutation of the experts, each token drawing ``topk`` distinct experts without replacement;
+    weights uniform in [0.5, 1.5), normalised to sum to ``route_scale`` per token.
+    Returns (idx [n, k] int64, wt [n, k] float32) on the CPU."""
+    ranks = torch.arange(1, n_experts + 1, dtype=torch.float64)
+    p = ranks.pow(-s)
+    p = p / p.sum()
+    perm = torch.randperm(n_experts, generator=gen)
+    probs = torch.empty(n_experts, dtype=torch.float64)
+    probs[perm] = p
+    idx = torch.multinomial(probs.expand(n_tokens, -1).contiguous(), topk, replacement=False, generator=gen)
+    w = torch.rand((n_tokens, topk), generator=gen, dtype=torch.float32) + 0.5
+    wt = w / w.sum(dim=1, keepdim=True) * route_scale
+    return idx.to(torch.int64), wt.to(torch.float32)
