@@ -61,6 +61,12 @@ def parse():
     ap.add_argument("--l2-flush", action="store_true",
                     help="write 256 MiB between steps (default: off; each step already streams more than L2)")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline sampling")
+    ap.add_argument("--mode", choices=["decode", "prefill", "sweep", "stack"], default="decode",
+                    help="decode: the headline config (default); prefill: P tokens with Zipf routing through the "
+                         "tcgen05 grouped GEMMs; sweep: decode batch 1..64 and the batched path under uniform / Zipf routing")
+    ap.add_argument("--tokens", type=int, default=126, help="prefill mode: tokens per layer call")
+    ap.add_argument("--stack-layers", type=int, default=40,
+                    help="stack mode: layers (first half FP8, second half FP4); fewer if they do not fit in HBM")
     ap.add_argument("--allreduce", choices=["p2p", "nccl"], default="p2p",
                     help="N > 1: sum the partials inside the layer kernel over NVLink peers (default) or with NCCL")
     return ap.parse_args()
@@ -452,10 +458,271 @@ def read_traffic(kernel_name, B, world):
     return None
 
 
+def build_layers(args, dev, rank, world, fmts, max_tokens):
+    import torch
+    import dsmoe
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    layers = []
+    for fmt in fmts:
+        m = dsmoe.MoE(H, I, args.experts, TOPK, fmt, "sigmoid", ROUTE_SCALE, rank=rank, world=world, device=dev,
+                      max_tokens=max_tokens)
+        m.load_router(dsmoe.make_router(args.experts, H, gen, device=dev))
+        m.load_shared(dsmoe.make_expert("fp8", H, I, gen, device=dev))
+        for e in range(args.experts):
+            m.load_expert(e, dsmoe.make_expert(fmt, H, I, gen, device=dev))
+        layers.append(m)
+    return layers, gen
+
+
+def graph_times(fns, steps, warmup, dev):
+    """Capture fns (one per layer) into one CUDA graph with timestamp nodes between them; replay it
+    warmup + steps times (sync per replay); per-fn mean ms over the timed replays."""
+    import torch
+    for f in fns:
+        f()
+    torch.cuda.synchronize(dev)
+    ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(len(fns) + 1)]
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i, f in enumerate(fns):
+            ev[i].record()
+            f()
+        ev[-1].record()
+    torch.cuda.synchronize(dev)
+    t = [[] for _ in fns]
+    for s in range(warmup + steps):
+        g.replay()
+        torch.cuda.synchronize(dev)
+        if s >= warmup:
+            for i in range(len(fns)):
+                t[i].append(ev[i].elapsed_time(ev[i + 1]))
+    del g
+    return [statistics.mean(x) for x in t]
+
+
+def uniform_routing(P, E, k, gen, route_scale=ROUTE_SCALE):
+    import torch
+    idx = torch.stack([torch.randperm(E, generator=gen)[:k] for _ in range(P)]).to(torch.int64)
+    w = torch.rand((P, k), generator=gen) + 0.5
+    return idx, (w / w.sum(1, keepdim=True) * route_scale).to(torch.float32)
+
+
+def prefill_mode(args):
+    """Config: one FP8 and one FP4 layer (384 experts, full size) on P tokens with Zipf(1.1)
+    routing, through the tcgen05 grouped GEMMs (the reference's prefill_batched)."""
+    import torch
+    import dsmoe
+    from dsmoe.tp import env_rank_world
+    rank, local, world = env_rank_world()
+    if world != 1:
+        raise SystemExit("--mode prefill runs on one GPU")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    P = args.tokens
+    layers, _ = build_layers(args, dev, 0, 1, layer_formats(args), max_tokens=8)
+    gen = torch.Generator().manual_seed(args.seed + 1)
+    x = dsmoe.make_tokens(P, H, gen).to(dev)
+    idx, wt = dsmoe.zipf_routing(P, args.experts, TOPK, gen)
+    uniq = len(set(idx.flatten().tolist()))
+    idx_d, wt_d = idx.to(dev), wt.to(dev)
+    ms = graph_times([lambda m=m: m.prefill(x, idx_d, wt_d) for m in layers], args.steps, args.warmup, dev)
+    for m in layers:
+        m.prefill_check(P)
+    peak, peak_kind = measured_peak()
+    kern = {}
+    w13_b = {"fp8": FP8_W13, "fp4": FP4_W13}
+    w2_b = {"fp8": FP8_W2, "fp4": FP4_W2}
+    flops = 2.0 * 3 * H * I * (P * TOPK + P)
+    for nm, t in zip(layer_formats(args), ms):
+        byts = uniq * (w13_b[nm] + w2_b[nm]) + FP8_W13 + FP8_W2
+        kern[f"{nm}_prefill"] = {"us": round(t * 1e3, 1), "us_per_token": round(t * 1e3 / P, 3), "bytes": int(byts),
+                                 "gbs": round(byts / (t * 1e-3) / 1e9, 1),
+                                 "hbm_frac_of_measured": round(byts / (t * 1e-3) / 1e9 / peak, 3),
+                                 "tflops": round(flops / (t * 1e-3) / 1e12, 2)}
+    line = {"mode": "prefill", "metric": "prefill MoE layer us/token (tcgen05 grouped GEMMs)",
+            "value": round(statistics.mean(ms) * 1e3 / P, 3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": False,
+            "config": {"workload": f"prefill: {P} tokens, Zipf(1.1) routing over {args.experts} experts "
+                                   f"(seeded), one FP8 + one FP4 layer", "tokens": P, "pairs": P * TOPK,
+                       "unique_experts": uniq, "max_tokens_per_expert": int(idx.flatten().bincount().max())},
+            "kernels": kern, "peak_hbm_gbs": peak, "peak_source": peak_kind,
+            "timing": "cuda-graph replay per step (timestamp nodes between layers)"}
+    print(json.dumps(line), flush=True)
+
+
+def sweep_mode(args):
+    """Config: decode batch 1..64 on one FP8 and one FP4 layer (router routing, ~uniform), and the
+    batched tcgen05 path under forced uniform and Zipf(1.1) routing at the same batches."""
+    import torch
+    import dsmoe
+    from dsmoe import _lib as L
+    from dsmoe.tp import env_rank_world
+    rank, local, world = env_rank_world()
+    if world != 1:
+        raise SystemExit("--mode sweep runs on one GPU")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    layers, _ = build_layers(args, dev, 0, 1, layer_formats(args), max_tokens=64)
+    gen = torch.Generator().manual_seed(args.seed + 2)
+    pool = dsmoe.make_tokens(128, H, gen).to(dev)
+    peak, _ = measured_peak()
+    w13_b = {"fp8": FP8_W13, "fp4": FP4_W13}
+    w2_b = {"fp8": FP8_W2, "fp4": FP4_W2}
+    rows = []
+    for B in (1, 2, 4, 8, 16, 32, 64):
+        x = pool[:B].contiguous()
+        outs = [torch.empty((B, H), dtype=torch.bfloat16, device=dev) for _ in layers]
+        idxs = [torch.empty((B, TOPK), dtype=torch.int64, device=dev) for _ in layers]
+        fns = [lambda m=m, y=y, ix=ix: L.call("dsmoe_moe_decode", m._layer, L.ptr(x), B, None, L.ptr(y), L.DTYPE_BF16,
+                                                L.ptr(ix), None, None, L.ptr(m.workspace), m.workspace.numel(),
+                                                L.stream_of(x))
+               for m, y, ix in zip(layers, outs, idxs)]
+        ms = graph_times(fns, args.steps, args.warmup, dev)
+        for m in layers:
+            m.check(B)
+        for nm, t, ix in zip(layer_formats(args), ms, idxs):
+            u = len(set(ix.flatten().tolist()))
+            byts = args.experts * (H * 4 + 4) + u * (w13_b[nm] + w2_b[nm]) + FP8_W13 + FP8_W2
+            rows.append({"path": "decode", "routing": "router", "fmt": nm, "batch": B, "us": round(t * 1e3, 2),
+                         "us_per_token": round(t * 1e3 / B, 3), "unique_experts": u,
+                         "gbs": round(byts / (t * 1e-3) / 1e9, 1), "hbm_frac": round(byts / (t * 1e-3) / 1e9 / peak, 3)})
+        for rname, rfun in (("uniform", uniform_routing), ("zipf", dsmoe.zipf_routing)):
+            idx, wt = rfun(B, args.experts, TOPK, gen)
+            u = len(set(idx.flatten().tolist()))
+            idx_d, wt_d = idx.to(dev), wt.to(dev)
+            ms = graph_times([lambda m=m: m.prefill(x, idx_d, wt_d) for m in layers], args.steps, args.warmup, dev)
+            for nm, t in zip(layer_formats(args), ms):
+                byts = u * (w13_b[nm] + w2_b[nm]) + FP8_W13 + FP8_W2
+                flops = 2.0 * 3 * H * I * (B * TOPK + B)
+                rows.append({"path": "batched-tcgen05", "routing": rname, "fmt": nm, "batch": B,
+                             "us": round(t * 1e3, 2), "us_per_token": round(t * 1e3 / B, 3), "unique_experts": u,
+                             "gbs": round(byts / (t * 1e-3) / 1e9, 1),
+                             "hbm_frac": round(byts / (t * 1e-3) / 1e9 / peak, 3),
+                             "tflops": round(flops / (t * 1e-3) / 1e12, 2)})
+    print(json.dumps({"mode": "sweep", "metric": METRIC, "unit": "us/layer", "n_gpus": 1, "steps": args.steps,
+                      "warmup": args.warmup, "experts": args.experts, "peak_hbm_gbs": peak, "rows": rows}), flush=True)
+
+
+def stack_mode(args):
+    """Config: the 40-layer MoE stack (layers 0-19 FP8, 20-39 FP4), decode batch 1, every layer's
+    experts resident, each GPU holding 1/N of every expert, each layer ending in its all-reduce (in
+    the layer kernel at N > 1). One token step is one CUDA graph of all layers, y of layer l being
+    x of layer l + 1 (the MoE half of the reference's per-token DecodeTrace, dsv41/tt/model.py:262-446).
+    With fewer GPUs than the stack needs, as many FP8 / FP4 layer pairs as fit are built."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import dsmoe
+    from dsmoe import _lib as L
+    from dsmoe.tp import PeerComm, env_rank_world, max_over_ranks
+    rank, local, world = env_rank_world()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    per_pair = (E * (FP8_W13 + FP8_W2 + FP4_W13 + FP4_W2) + 2 * (FP8_W13 + FP8_W2)) / world + 2 * (E * H * 4 + 64e6)
+    free, _ = torch.cuda.mem_get_info(dev)
+    pairs = min(args.stack_layers // 2, int((free - 6e9) // per_pair))
+    if world > 1:  # every rank builds the same number of layers
+        t = torch.tensor([pairs], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        pairs = int(t.item())
+    if pairs < 1:
+        raise SystemExit("not enough device memory for one FP8 + FP4 layer pair")
+    fmts = ["fp8"] * pairs + ["fp4"] * pairs
+    t0 = time.time()
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    layers = []
+    for fmt in fmts:  # each layer its own uniform-random router and experts
+        m = dsmoe.MoE(H, I, E, TOPK, fmt, "sigmoid", ROUTE_SCALE, rank=rank, world=world, device=dev, max_tokens=8)
+        m.load_router(dsmoe.make_router(E, H, gen, device=dev))
+        m.load_shared(dsmoe.make_expert("fp8", H, I, gen, device=dev))
+        for e in range(E):
+            m.load_expert(e, dsmoe.make_expert(fmt, H, I, gen, device=dev))
+        layers.append(m)
+    comm = None
+    if world > 1:
+        comm = PeerComm(H, device=dev)
+        for m in layers:
+            m.use_comm(comm)
+    setup_s = time.time() - t0
+    B = 1
+    nl = len(layers)
+    xs = [torch.empty((B, H), dtype=torch.bfloat16, device=dev) for _ in range(nl + 1)]
+    idx = [torch.empty((B, TOPK), dtype=torch.int64, device=dev) for _ in range(nl)]
+    tokpool = dsmoe.make_tokens(64, H, torch.Generator(device=dev).manual_seed(args.seed + 3), device=dev)
+
+    def layer(li):
+        m = layers[li]
+        st_ = torch.cuda.current_stream(dev).cuda_stream
+        if comm is not None:
+            L.call("dsmoe_moe_decode_allreduce", m._layer, comm.handle, L.ptr(xs[li]), B, None, L.ptr(xs[li + 1]),
+                   L.DTYPE_BF16, L.ptr(idx[li]), None, None, L.ptr(m.workspace), m.workspace.numel(), st_)
+        else:
+            L.call("dsmoe_moe_decode", m._layer, L.ptr(xs[li]), B, None, L.ptr(xs[li + 1]), L.DTYPE_BF16,
+                   L.ptr(idx[li]), None, None, L.ptr(m.workspace), m.workspace.numel(), st_)
+
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+    xs[0].copy_(tokpool[:B])
+    for li in range(nl):
+        layer(li)
+    torch.cuda.synchronize(dev)
+    ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(nl + 1)]
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for li in range(nl):
+            ev[li].record()
+            layer(li)
+        ev[nl].record()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    lt = [[] for _ in range(nl)]
+    st = []
+    for s in range(args.warmup + args.steps):
+        xs[0].copy_(tokpool[s % 64:s % 64 + B])  # a new token each step
+        g.replay()
+        torch.cuda.synchronize(dev)
+        if s >= args.warmup:
+            st.append(ev[0].elapsed_time(ev[nl]))
+            for li in range(nl):
+                lt[li].append(ev[li].elapsed_time(ev[li + 1]))
+    for m in layers:
+        m.check(B)
+    del g
+    ms_tok = max_over_ranks(statistics.mean(st), dev)
+    fp8_us = max_over_ranks(statistics.mean(statistics.mean(lt[li]) for li in range(pairs)) * 1e3, dev)
+    fp4_us = max_over_ranks(statistics.mean(statistics.mean(lt[li]) for li in range(pairs, nl)) * 1e3, dev)
+    if rank == 0:
+        print(json.dumps({
+            "mode": "stack", "metric": "MoE stack ms/token (decode batch 1, all experts resident)",
+            "value": round(ms_tok, 4), "unit": "ms/token", "n_gpus": world, "layers": nl, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": False,
+            "ms_per_token_40_layers": round((20 * fp8_us + 20 * fp4_us) / 1e3, 4),
+            "layer_us": {"fp8": round(fp8_us, 2), "fp4": round(fp4_us, 2)},
+            "config": {"workload": f"{nl}-layer MoE stack ({pairs} FP8 + {pairs} FP4 layers), y of a layer feeding "
+                                   f"the next, one CUDA graph per token",
+                       "parallelism": f"tp{world}", "allreduce": "in-kernel NVLink peer exchange" if world > 1 else None,
+                       "experts": E, "hidden": H, "inter": I},
+            "setup_s": round(setup_s, 1)}), flush=True)
+    if world > 1:
+        dist.barrier()
+        comm.close()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
+    elif args.mode == "prefill":
+        prefill_mode(args)
+    elif args.mode == "sweep":
+        sweep_mode(args)
+    elif args.mode == "stack":
+        stack_mode(args)
     else:
         ours(args)
 
