@@ -12,10 +12,11 @@
 //   gemm 2   grouped w2: D[128 output rows][2 n], K = the intermediate slice.
 //   combine  y[t] = sum_k wt[t][k] * y_pair[t, k] + y_shared[t], in k order (deterministic).
 // GEMM kernel: one CTA per SM walks (chunk, M tile) units. Warp 0 lane 0 streams each 128-K step's
-// packed weight pieces and the chunk's token rows with 1-D bulk copies; warps 2-5 rearrange the
+// packed weight pieces and the chunk's token rows with 1-D bulk copies; warps 2-9 rearrange the
 // packed weights (the decode store's lane-fragment order) into the canonical K-major SW128 tile,
 // expanding FP4 to e4m3; warp 1 lane 0 issues tcgen05.mma (M 128, N = 2 x tokens, K 32 per
-// instruction) with the accumulator in TMEM; warps 2-5 read it back with tcgen05.ld.
+// instruction) with the accumulator in TMEM; warps 2-9 read it back with tcgen05.ld (two warps per
+// TMEM lane quadrant, splitting the columns).
 //   FP8 weights (fp32 scale per 128 x 128 block): kind::f8f6f4, one TMEM block accumulator per
 //     128-K step (two, alternating); the epilogue warps fold each block into a TMEM running sum
 //     with the block's scale (the non-MX scales applied per K block to the accumulator).
@@ -27,7 +28,8 @@
 
 namespace dsmoe {
 
-constexpr int PFW = 6, PFT = PFW * 32;  // warps: 0 producer, 1 MMA, 2-5 convert + epilogue
+constexpr int PFW = 10, PFT = PFW * 32;  // warps: 0 producer, 1 MMA, 2-9 convert + epilogue
+constexpr int PCW = PFW - 2, PCT = PCW * 32;  // convert + epilogue warps / threads (two per TMEM lane quadrant)
 constexpr int PST = 4;                   // pipeline stages (128-K steps)
 constexpr int PCHUNK = 64;               // tokens per chunk
 constexpr int PNMAX = 2 * PCHUNK;        // MMA N: hi and lo rows of every token
@@ -35,7 +37,7 @@ constexpr int PA_BYTES = 16384;          // A tile: 128 rows x 128 K e4m3, SW128
 constexpr int PB_BYTES = PNMAX * 128;    // B tile: up to 128 rows x 128 K
 constexpr int PRAW_BYTES = 16896;        // packed weight pieces of one step (<= 16416 used)
 constexpr int PSTAGE = PA_BYTES + PB_BYTES + PRAW_BYTES;
-constexpr int PSMEM = PST * PSTAGE + 1024;  // + barriers, flags
+constexpr int PSMEM = PST * PSTAGE + 2048;  // + 1024-byte alignment slack, barriers, flags
 constexpr uint64_t kPWaitNs = 1000000000ull;
 // TMEM columns: FP8 block accumulators 0 / 128, running sum 256; FP4 accumulator 0; A scale
 // factors 384 + 4 * stage; B scale factors 400.
@@ -337,14 +339,15 @@ __global__ void __launch_bounds__(PFT, 1) prefill_gemm_kernel(GemmArgs a) {
   uint8_t* sR = sB + PST * PB_BYTES;         // [PST][PRAW_BYTES]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sR + PST * PRAW_BYTES);
   uint64_t* full = bars;            // [PST] producer's copies landed
-  uint64_t* afull = full + PST;     // [PST] A tile converted (4 arrivals)
+  uint64_t* afull = full + PST;     // [PST] A tile converted (one arrival per converting warp)
   uint64_t* sfree = afull + PST;    // [PST] MMAs done with the stage
   uint64_t* bdone = sfree + PST;    // [2] FP8 block accumulator ready
-  uint64_t* bfree = bdone + 2;      // [2] FP8 block accumulator folded (4 arrivals)
+  uint64_t* bfree = bdone + 2;      // [2] FP8 block accumulator folded (one arrival per epilogue warp)
   uint64_t* udone = bfree + 2;      // [1] FP4 unit accumulator ready
-  uint64_t* ufree = udone + 1;      // [1] unit result read (4 arrivals)
+  uint64_t* ufree = udone + 1;      // [1] unit result read (one arrival per epilogue warp)
   uint64_t* endb = ufree + 1;       // [1] every MMA of this CTA done
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(endb + 1);
+  uint64_t* efin = endb + 1;        // [1] FP8 running sum complete (one arrival per epilogue warp)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(efin + 1);
   volatile int* abortf = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -353,16 +356,17 @@ __global__ void __launch_bounds__(PFT, 1) prefill_gemm_kernel(GemmArgs a) {
   if (tid == 0) {
     for (int s = 0; s < PST; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&afull[s], 4);
+      mbar_init(&afull[s], PCW);
       mbar_init(&sfree[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bdone[b], 1);
-      mbar_init(&bfree[b], 4);
+      mbar_init(&bfree[b], PCW);
     }
     mbar_init(udone, 1);
-    mbar_init(ufree, 4);
+    mbar_init(ufree, PCW);
     mbar_init(endb, 1);
+    mbar_init(efin, PCW);
     *abortf = 0;
     fence_mbar_init();
   }
@@ -485,20 +489,22 @@ __global__ void __launch_bounds__(PFT, 1) prefill_gemm_kernel(GemmArgs a) {
       mbar_wait(endb, 0, kPWaitNs);
     }
   } else {
-    // ---------------- convert + epilogue (warps 2-5: TMEM lane quadrant q = warp % 4)
-    const int q = warp & 3, c = tid - 64;
+    // ---------------- convert + epilogue (warps 2-9: TMEM lane quadrant q = warp % 4, column half hf)
+    const int q = warp & 3, c = tid - 64, hf = (warp - 2) >> 2;
     const uint32_t trow = tm + ((uint32_t)(32 * q) << 16);
-    tc_st4(trow + TM_SFB, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);  // B scale factors: 1.0
-    tc_wait_st();
+    if (hf == 0) {
+      tc_st4(trow + TM_SFB, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);  // B scale factors: 1.0
+      tc_wait_st();
+    }
     const int R = 32 * q + lane;  // this thread's accumulator row
-    int it = 0, nblk = 0, nmx = 0;
+    int it = 0, nblk = 0, nmx = 0, nfin = 0;
     float pend_scale = 0.f;
     // fold FP8 block accumulator (the step before) into the running sum with its scale
     auto epi_block = [&](int kb, float sc, int N) -> bool {
       const int bb = nblk & 1;
       if (!wait(&bdone[bb], (nblk >> 1) & 1)) return false;
       tc_fence_after();
-      for (int c0 = 0; c0 < N; c0 += 16) {
+      for (int c0 = 16 * hf; c0 < N; c0 += 32) {
         float blk[16], run[16];
         tc_ld16(trow + 128u * bb + c0, blk);
         if (kb > 0) tc_ld16(trow + TM_RUN + c0, run);
@@ -531,7 +537,7 @@ __global__ void __launch_bounds__(PFT, 1) prefill_gemm_kernel(GemmArgs a) {
         if (!mx) {
           // FP8 lane fragments -> K-major SW128 rows (4-byte pieces)
           const int nfr = 1024;
-          for (int f = c; f < nfr; f += 128) {
+          for (int f = c; f < nfr; f += PCT) {
             int l, R0, ch;
             const uint8_t* src;
             if (a.phase == 1) {
@@ -565,7 +571,7 @@ __global__ void __launch_bounds__(PFT, 1) prefill_gemm_kernel(GemmArgs a) {
         } else {
           // FP4 lane fragments -> e4m3 (x 2^-6) in K-major SW128 rows; e8m0 scales (+6) -> TMEM
           const int nfr = 512;
-          for (int f = c; f < nfr; f += 128) {
+          for (int f = c; f < nfr; f += PCT) {
             int l, R0, ch;
             const uint8_t* src;
             if (a.phase == 1) {
@@ -594,6 +600,7 @@ __global__ void __launch_bounds__(PFT, 1) prefill_gemm_kernel(GemmArgs a) {
               *reinterpret_cast<uint32_t*>(At + sw128(row, (kk + 16) >> 4) + ((kk + 16) & 15)) = hi;
             }
           }
+          if (hf == 0) {
           uint32_t sf[4];
 #pragma unroll
           for (int m1 = 0; m1 < 4; ++m1) {
@@ -618,6 +625,7 @@ __global__ void __launch_bounds__(PFT, 1) prefill_gemm_kernel(GemmArgs a) {
           }
           tc_st4(trow + TM_SFA + 4 * s, sf[0], sf[1], sf[2], sf[3]);
           tc_wait_st();
+          }
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         tc_fence_before();
@@ -635,6 +643,14 @@ __global__ void __launch_bounds__(PFT, 1) prefill_gemm_kernel(GemmArgs a) {
       uint32_t src_col;
       if (!mx) {
         if (!epi_block(a.katoms - 1, pend_scale, N)) break;
+        // the two warps of a quadrant wrote alternate 16-column chunks of the running sum; the hi /
+        // lo columns of a token can sit in chunks of different warps, so all folds finish first
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(efin);
+        if (!wait(efin, nfin & 1)) break;
+        ++nfin;
+        tc_fence_after();
         src_col = TM_RUN;
       } else {
         if (!wait(udone, nmx & 1)) break;
@@ -645,7 +661,7 @@ __global__ void __launch_bounds__(PFT, 1) prefill_gemm_kernel(GemmArgs a) {
       // unit result: row R, columns j (hi) and npad + j (lo) of token j
       // (16-column loads may read up to 8 columns past N; those values belong to no token)
       const int npad = p.c.npad;
-      for (int j0 = 0; j0 < npad; j0 += 16) {
+      for (int j0 = 16 * hf; j0 < npad; j0 += 32) {
         float hv[16], lv[16];
         tc_ld16(trow + src_col + j0, hv);
         tc_ld16(trow + src_col + npad + j0, lv);
