@@ -67,6 +67,9 @@ def parse():
     ap.add_argument("--tokens", type=int, default=126, help="prefill mode: tokens per layer call")
     ap.add_argument("--stack-layers", type=int, default=40,
                     help="stack mode: layers (first half FP8, second half FP4); fewer if they do not fit in HBM")
+    ap.add_argument("--emulate-tp", type=int, default=1,
+                    help="stack mode on one GPU: build rank 0's 1/N slice of every expert (the per-GPU kernel of "
+                         "an N-GPU run, without its all-reduce); the output is labelled as emulated")
     ap.add_argument("--allreduce", choices=["p2p", "nccl"], default="p2p",
                     help="N > 1: sum the partials inside the layer kernel over NVLink peers (default) or with NCCL")
     return ap.parse_args()
@@ -620,7 +623,9 @@ def stack_mode(args):
     torch.cuda.set_device(dev)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    per_pair = (E * (FP8_W13 + FP8_W2 + FP4_W13 + FP4_W2) + 2 * (FP8_W13 + FP8_W2)) / world + 2 * (E * H * 4 + 64e6)
+    emu = args.emulate_tp if world == 1 else 1
+    slices = world * emu  # expert slices: the layer is built as rank `rank` of `slices`
+    per_pair = (E * (FP8_W13 + FP8_W2 + FP4_W13 + FP4_W2) + 2 * (FP8_W13 + FP8_W2)) / slices + 2 * (E * H * 4 + 64e6)
     free, _ = torch.cuda.mem_get_info(dev)
     pairs = min(args.stack_layers // 2, int((free - 6e9) // per_pair))
     if world > 1:  # every rank builds the same number of layers
@@ -634,7 +639,7 @@ def stack_mode(args):
     gen = torch.Generator(device=dev).manual_seed(args.seed)
     layers = []
     for fmt in fmts:  # each layer its own uniform-random router and experts
-        m = dsmoe.MoE(H, I, E, TOPK, fmt, "sigmoid", ROUTE_SCALE, rank=rank, world=world, device=dev, max_tokens=8)
+        m = dsmoe.MoE(H, I, E, TOPK, fmt, "sigmoid", ROUTE_SCALE, rank=rank, world=slices, device=dev, max_tokens=8)
         m.load_router(dsmoe.make_router(E, H, gen, device=dev))
         m.load_shared(dsmoe.make_expert("fp8", H, I, gen, device=dev))
         for e in range(E):
@@ -704,7 +709,8 @@ def stack_mode(args):
             "layer_us": {"fp8": round(fp8_us, 2), "fp4": round(fp4_us, 2)},
             "config": {"workload": f"{nl}-layer MoE stack ({pairs} FP8 + {pairs} FP4 layers), y of a layer feeding "
                                    f"the next, one CUDA graph per token",
-                       "parallelism": f"tp{world}", "allreduce": "in-kernel NVLink peer exchange" if world > 1 else None,
+                       "parallelism": f"tp{world}" if emu == 1 else f"emulated tp{emu} on one GPU (rank 0's slice, no all-reduce)",
+                       "allreduce": "in-kernel NVLink peer exchange" if world > 1 else None,
                        "experts": E, "hidden": H, "inter": I},
             "setup_s": round(setup_s, 1)}), flush=True)
     if world > 1:
