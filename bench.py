@@ -152,27 +152,47 @@ def reference_arm(args):
 # ------------------------------------------------------------------ GPU arm
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the timed region runs."""
-    Q = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """SM clocks and throttle reasons of this rank's GPU during the timed region.
+
+    A background ``nvidia-smi -lms 200`` runs across the region; rows whose timestamp falls inside
+    [first step, last step] are kept. Timed regions are often shorter than the 200 ms period, so
+    ``mark()`` -- called between two timed steps, outside every step's events -- also takes one
+    synchronous sample, which is inside the region by construction."""
+    Q = ("index,uuid,timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, uuid):
         self.uuid, self.proc, self.path = uuid, None, None
+        self.marks, self.t0, self.t1 = [], None, None
+
+    def _cmd(self, loop):
+        c = ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits"]
+        if self.uuid:
+            c += ["-i", self.uuid]
+        return c + (["-lms", "200"] if loop else [])
 
     def __enter__(self):
         import tempfile
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            self.proc = subprocess.Popen(self._cmd(True), stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
         time.sleep(0.3)
+        self.t0 = time.time()
         return self
 
+    def mark(self):
+        try:
+            out = subprocess.run(self._cmd(False), capture_output=True, text=True, timeout=10).stdout
+            self.marks += [ln for ln in out.splitlines() if ln.strip()]
+        except (OSError, subprocess.SubprocessError):
+            pass
+
     def __exit__(self, *exc):
+        self.t1 = time.time()
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -180,24 +200,38 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
 
+    @staticmethod
+    def _parse(line):
+        f = [c.strip() for c in line.split(",")]
+        if len(f) < 11:
+            return None
+        try:
+            import datetime
+            ts = datetime.datetime.strptime(f[2], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            ts = None
+        return f, ts
+
     def summary(self):
         rows = []
         try:
             for line in open(self.path):
-                f = [c.strip() for c in line.split(",")]
-                if len(f) >= 10 and (self.uuid is None or f[1] == self.uuid):
-                    rows.append(f)
+                r = self._parse(line)
+                if r and r[1] is not None and self.t0 is not None and self.t0 <= r[1] <= (self.t1 or r[1]):
+                    rows.append(r[0])
             os.unlink(self.path)
         except OSError:
             pass
+        rows += [r[0] for r in map(self._parse, self.marks) if r]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
-        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        num = lambda v: float(v) if v.replace(".", "").isdigit() else None
+        sm = [num(r[3]) for r in rows if num(r[3]) is not None]
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({n for r in rows for n, v in zip(names, r[6:10]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": float(rows[0][3]) if rows[0][3].replace(".", "").isdigit() else None,
-                "reasons": reasons, "samples": len(rows)}
+        reasons = sorted({n for r in rows for n, v in zip(names, r[7:11]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(rows[0][4]),
+                "reasons": reasons, "samples": len(rows), "in_region": "timestamped background samples inside "
+                "the timed region plus one synchronous sample between two timed steps"}
 
 
 def measured_peak():
@@ -345,6 +379,8 @@ def ours(args):
     torch.cuda.synchronize()
     with ClockSampler(uuid) as clk:
         for s in range(W, W + K):
+            if s == W + K // 2 and rank == 0:
+                clk.mark()  # between two steps: outside every timed event pair
             step(s, True)
         torch.cuda.synchronize()
     if world > 1:
