@@ -324,28 +324,42 @@ def ours(args):
             layer_launch(li, v)
     torch.cuda.synchronize()
     gev = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_layers + 1)] for _ in range(NV)]
-    graphs, timing_mode = None, "cuda-graph replay per step (timestamp nodes between layers)"
+    pev = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)] for _ in range(NV)]
+    graphs, pgraphs = None, None
+    timing_mode = ("cuda-graph replay per step: the step time from graphs with timestamp nodes at their ends only, "
+                   "so consecutive layer kernels overlap (programmatic dependent launch); the per-layer split "
+                   "from a second pass of graphs with timestamp nodes between the layers")
     try:
         graphs = [torch.cuda.CUDAGraph() for _ in range(NV)]
+        pgraphs = [torch.cuda.CUDAGraph() for _ in range(NV)]
         for v in range(NV):
             with torch.cuda.graph(graphs[v]):
                 for li in range(n_layers):
                     gev[v][li].record()
                     layer_launch(li, v)
                 gev[v][n_layers].record()
+            with torch.cuda.graph(pgraphs[v]):
+                pev[v][0].record()
+                for li in range(n_layers):
+                    layer_launch(li, v)
+                pev[v][1].record()
         torch.cuda.synchronize()
     except Exception as ex:  # pragma: no cover - depends on the driver
-        graphs, timing_mode = None, f"eager launches (graph capture failed: {type(ex).__name__})"
+        graphs, pgraphs, timing_mode = None, None, f"eager launches (graph capture failed: {type(ex).__name__})"
         torch.cuda.synchronize()
     eev = [[torch.cuda.Event(enable_timing=True) for _ in range(n_layers + 1)] for _ in range(NV)]
     layer_t = [[] for _ in range(n_layers)]
     step_t = []
 
-    def step(s, timed):
+    def step(s, timed, split=False):
         v = s % NV
         if graphs is not None:
-            graphs[v].replay()
-            e_ = gev[v]
+            if split:
+                graphs[v].replay()
+                e_ = gev[v]
+            else:
+                pgraphs[v].replay()
+                e_ = pev[v]
         else:
             e_ = eev[v]
             for li in range(n_layers):
@@ -354,11 +368,14 @@ def ours(args):
             e_[n_layers].record(stream)
         torch.cuda.synchronize()  # the variant's timestamps are re-written by its next replay
         if timed:
+            if split or graphs is None:
+                for li in range(n_layers):
+                    layer_t[li].append(e_[li].elapsed_time(e_[li + 1]))
+            if not split:
+                step_t.append(e_[0].elapsed_time(e_[-1]))
+        if not split:
             for li in range(n_layers):
-                layer_t[li].append(e_[li].elapsed_time(e_[li + 1]))
-            step_t.append(e_[0].elapsed_time(e_[n_layers]))
-        for li in range(n_layers):
-            idx_log[s, li].copy_(idx_st[li][v])
+                idx_log[s, li].copy_(idx_st[li][v])
         if args.l2_flush:
             flush.zero_()
 
@@ -379,16 +396,25 @@ def ours(args):
     torch.cuda.synchronize()
     with ClockSampler(uuid) as clk:
         for s in range(W, W + K):
-            if s == W + K // 2 and rank == 0:
-                clk.mark()  # between two steps: outside every timed event pair
+            if s == W + K // 2:  # between two steps: outside every timed event pair
+                if rank == 0:
+                    clk.mark()
+                if world > 1:  # the ranks' kernels exchange tiles: all of them resume together
+                    dist.barrier()
+                    torch.cuda.synchronize()
             step(s, True)
         torch.cuda.synchronize()
+    if graphs is not None:  # second pass: the per-layer split (timestamp nodes between the layers)
+        for s in range(W):
+            step(s, False, split=True)
+        for s in range(W, W + K):
+            step(s, True, split=True)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     for m in layers:
         m.check(B)
-    graphs = None  # released before the process group goes away
+    graphs = pgraphs = None  # released before the process group goes away
 
     # ---- per-step and per-layer device times
     step_ms = step_t
@@ -710,29 +736,40 @@ def stack_mode(args):
     for li in range(nl):
         layer(li)
     torch.cuda.synchronize(dev)
+    # two graphs of the same step: timestamps at its ends only (consecutive layer kernels overlap,
+    # programmatic dependent launch) for the time per token; timestamps between layers for the split
     ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(nl + 1)]
-    g = torch.cuda.CUDAGraph()
+    pe = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)]
+    g, gp = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
         for li in range(nl):
             ev[li].record()
             layer(li)
         ev[nl].record()
+    with torch.cuda.graph(gp):
+        pe[0].record()
+        for li in range(nl):
+            layer(li)
+        pe[1].record()
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     lt = [[] for _ in range(nl)]
     st = []
-    for s in range(args.warmup + args.steps):
-        xs[0].copy_(tokpool[s % 64:s % 64 + B])  # a new token each step
-        g.replay()
-        torch.cuda.synchronize(dev)
-        if s >= args.warmup:
-            st.append(ev[0].elapsed_time(ev[nl]))
-            for li in range(nl):
-                lt[li].append(ev[li].elapsed_time(ev[li + 1]))
+    for split in (False, True):
+        for s in range(args.warmup + args.steps):
+            xs[0].copy_(tokpool[s % 64:s % 64 + B])  # a new token each step
+            (g if split else gp).replay()
+            torch.cuda.synchronize(dev)
+            if s >= args.warmup:
+                if split:
+                    for li in range(nl):
+                        lt[li].append(ev[li].elapsed_time(ev[li + 1]))
+                else:
+                    st.append(pe[0].elapsed_time(pe[1]))
     for m in layers:
         m.check(B)
-    del g
+    del g, gp
     ms_tok = max_over_ranks(statistics.mean(st), dev)
     fp8_us = max_over_ranks(statistics.mean(statistics.mean(lt[li]) for li in range(pairs)) * 1e3, dev)
     fp4_us = max_over_ranks(statistics.mean(statistics.mean(lt[li]) for li in range(pairs, nl)) * 1e3, dev)
@@ -741,7 +778,9 @@ def stack_mode(args):
             "mode": "stack", "metric": "MoE stack ms/token (decode batch 1, all experts resident)",
             "value": round(ms_tok, 4), "unit": "ms/token", "n_gpus": world, "layers": nl, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": False,
-            "ms_per_token_40_layers": round((20 * fp8_us + 20 * fp4_us) / 1e3, 4),
+            "ms_per_token_40_layers": round(ms_tok * 40 / nl, 4),
+            "timing": "CUDA events at the ends of one graph of all layers (per-layer split from a second graph "
+                      "with events between layers)",
             "layer_us": {"fp8": round(fp8_us, 2), "fp4": round(fp4_us, 2)},
             "config": {"workload": f"{nl}-layer MoE stack ({pairs} FP8 + {pairs} FP4 layers), y of a layer feeding "
                                    f"the next, one CUDA graph per token",

@@ -771,29 +771,42 @@ __device__ __noinline__ bool ar_tile(const FusedArgs& a, int nt, unsigned ep, fl
     st_ll2(p, w0, w1);
     st_ll2(p + 2, w2, w3);
   }
-  float4 tot = make_float4(0.f, 0.f, 0.f, 0.f);
+  // every peer's slot polled together: one round of loads per poll, not one per peer
+  float4 v[kMaxWorld];
+  unsigned got = 1u << r;  // ranks whose words have arrived
+  v[r] = s4;
+  const unsigned all = (1u << W) - 1u;
+  const uint64_t t0 = globaltimer_ns();
   bool ok = true;
-  for (int q = 0; q < W; ++q) {
-    float4 v = s4;
-    if (q != r) {
-      const unsigned long long* p = a.ar_slots[r] + ar_slot(par, q, W, NT, nt, lane);
-      unsigned long long x0 = 0, x1 = 0, x2 = 0, x3 = 0;
-      const uint64_t t0 = globaltimer_ns();
-      while (ok) {
-        ld_ll2(p, x0, x1);
-        ld_ll2(p + 2, x2, x3);
-        if ((unsigned)(x0 >> 32) == ep && (unsigned)(x1 >> 32) == ep && (unsigned)(x2 >> 32) == ep &&
-            (unsigned)(x3 >> 32) == ep)
-          break;
-        if (globaltimer_ns() - t0 > kPeerWaitNs) ok = false;
+  while (got != all) {
+    unsigned long long x[kMaxWorld][4];
+#pragma unroll
+    for (int q = 0; q < kMaxWorld; ++q)
+      if (q < W && !((got >> q) & 1u)) {
+        const unsigned long long* p = a.ar_slots[r] + ar_slot(par, q, W, NT, nt, lane);
+        ld_ll2(p, x[q][0], x[q][1]);
+        ld_ll2(p + 2, x[q][2], x[q][3]);
       }
-      v = make_float4(__uint_as_float((unsigned)x0), __uint_as_float((unsigned)x1), __uint_as_float((unsigned)x2),
-                      __uint_as_float((unsigned)x3));
+#pragma unroll
+    for (int q = 0; q < kMaxWorld; ++q)
+      if (q < W && !((got >> q) & 1u) && (unsigned)(x[q][0] >> 32) == ep && (unsigned)(x[q][1] >> 32) == ep &&
+          (unsigned)(x[q][2] >> 32) == ep && (unsigned)(x[q][3] >> 32) == ep) {
+        v[q] = make_float4(__uint_as_float((unsigned)x[q][0]), __uint_as_float((unsigned)x[q][1]),
+                           __uint_as_float((unsigned)x[q][2]), __uint_as_float((unsigned)x[q][3]));
+        got |= 1u << q;
+      }
+    if (got != all && globaltimer_ns() - t0 > kPeerWaitNs) {
+      ok = false;
+      break;
     }
-    tot.x += v.x;
-    tot.y += v.y;
-    tot.z += v.z;
-    tot.w += v.w;
+  }
+  float4 tot = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int q = 0; q < W; ++q) {  // rank order: the same bits on every rank
+    const float4 u = ((got >> q) & 1u) ? v[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+    tot.x += u.x;
+    tot.y += u.y;
+    tot.z += u.z;
+    tot.w += u.w;
   }
   s4 = tot;
   return __all_sync(0xffffffffu, ok);
@@ -832,9 +845,6 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   if (tid == 0) {
     for (int s = 0; s < NST + 2; ++s) mbar_init(&full[s], 1);  // stage barriers, h barrier, token-row barrier
     pl.abort = 0;
-    // the peer exchange's epoch of this call: one past the last call's (read before barrier A,
-    // whose last arrival stores it back)
-    pl.ar_epoch = a.ar_world > 1 ? *(volatile unsigned*)a.ar_ctl + 1u : 0u;
     fence_mbar_init();
   }
   __syncthreads();
@@ -924,11 +934,9 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     return !pl.abort;
   };
 
+  // Prologue on constant data only (router rows, shared expert weights). With a programmatic
+  // dependent launch it overlaps the previous kernel of the stream, which may still be running.
   refill();  // router rows stream in while the token rows arrive
-  if (tid == 0 && a.B <= FXB) {  // bf16 token rows for the router, one bulk copy
-    mbar_expect_tx(xbar, (uint32_t)(a.B * a.H * 2));
-    bulk_g2s(xs, a.x, (uint32_t)(a.B * a.H * 2), xbar);
-  }
   // the shared expert's weights do not depend on routing: pull them into L2 now (each warp a slice)
   if (lane == 0) {
     const long long b13 = (long long)geo.T * geo.tile13s, b2 = (long long)geo.NT * geo.tile2s;
@@ -939,6 +947,20 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       const uint32_t len = (uint32_t)min(piece, tot - off);
       const uint8_t* src = (w2p ? a.s_w2 : a.s_w13) + off;
       asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(len) : "memory");
+    }
+  }
+  // Past this point the previous kernel of the stream has completed and its writes are visible:
+  // this call's tokens (often that kernel's output), the workspace, the exchange epoch. The next
+  // kernel may be scheduled now; it cannot be resident on an SM before this grid's CTA there exits.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (tid == 0) {
+    // the peer exchange's epoch of this call: one past the last call's (read before barrier A,
+    // whose last arrival stores it back)
+    pl.ar_epoch = a.ar_world > 1 ? *(volatile unsigned*)a.ar_ctl + 1u : 0u;
+    if (a.B <= FXB) {  // bf16 token rows for the router, one bulk copy
+      mbar_expect_tx(xbar, (uint32_t)(a.B * a.H * 2));
+      bulk_g2s(xs, a.x, (uint32_t)(a.B * a.H * 2), xbar);
     }
   }
   for (int e = tid; e < a.E; e += FT) emask[e] = 0u;
@@ -1394,6 +1416,7 @@ FusedScratch fused_scratch(int H, int I_loc, int E, int B, int topk, int r_fmt) 
 struct DevInfo {
   int sms = 0, optin = 0;
   bool attr_set[2] = {false, false};
+  int pdl = -1;  // programmatic dependent launch with the cooperative attribute: -1 untested, 0 no, 1 yes
 };
 static DevInfo g_dev[64];
 
@@ -1499,17 +1522,34 @@ int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* im
   cfg.blockDim = dim3(FT);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  // Programmatic dependent launch: the kernel's prologue overlaps the tail of the previous kernel
+  // in the stream. Tried on the first call outside stream capture; a refusal turns it off.
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (d.pdl < 0) cudaStreamIsCapturing(st, &cap);
+  const bool try_pdl = d.pdl == 1 || (d.pdl < 0 && cap == cudaStreamCaptureStatusNone);
+  cfg.numAttrs = try_pdl ? 2 : 1;
   if (events) {
     cudaEventRecord((cudaEvent_t)events[0], st);
     cudaEventRecord((cudaEvent_t)events[1], st);
     cudaEventRecord((cudaEvent_t)events[2], st);
   }
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (try_pdl && d.pdl < 0) {
+    if (e == cudaSuccess) {
+      d.pdl = 1;
+    } else {  // not accepted with the cooperative attribute here: launch without it from now on
+      cudaGetLastError();
+      d.pdl = 0;
+      cfg.numAttrs = 1;
+      e = cudaLaunchKernelEx(&cfg, kern, a);
+    }
+  }
   if (events) cudaEventRecord((cudaEvent_t)events[3], st);
   if (e != cudaSuccess) {
     set_error("fused launch: %s", cudaGetErrorString(e));
