@@ -240,6 +240,18 @@ DSMOE_API int dsmoe_comm_open(dsmoe_comm_t* comm, const void* handles);
 /* Synchronizes the device, unmaps the peers' buffers and frees this rank's. */
 DSMOE_API int dsmoe_comm_destroy(dsmoe_comm_t* comm);
 
+/* y[b][:] = the sum over the group's ranks of x[b][:] for B = 1..8 rows of `hidden` values (bf16 or
+ * fp32 in and out), over the same NVLink peer exchange as dsmoe_moe_decode_allreduce: one launch,
+ * the sum in rank order (the same bits on every rank). Replaces the reference's all_reduce_sum of
+ * the attention output projection (dsv41/tt/attn.py:19-21, called at attn.py:229, 252). Every rank
+ * makes the same sequence of calls on one comm (this and the decode call share its epochs). */
+DSMOE_API int dsmoe_allreduce_rows(const dsmoe_comm_t* comm, const void* x, int x_dtype, int B, void* y,
+                                   int y_dtype, void* stream);
+/* Synchronizes `stream` and reads the comm's status word: DSMOE_OK, or DSMOE_ERR_TIMEOUT when a
+ * peer's tile did not arrive within the bound in dsmoe_allreduce_rows (the comm must then be
+ * re-created on every rank); clears it. */
+DSMOE_API int dsmoe_comm_check(const dsmoe_comm_t* comm, void* stream);
+
 /* 1 when dsmoe_moe_decode_allreduce takes this call (the persistent path: B <= 8 tokens, hidden a
  * multiple of 512, <= 1024 experts, x 16-byte aligned), else 0. */
 DSMOE_API int dsmoe_moe_allreduce_supported(const dsmoe_layer_t* layer, const dsmoe_comm_t* comm, const void* x,

@@ -12,7 +12,7 @@
 // every rank calls dsmoe_comm_open with all handles in rank order.
 #include <cstring>
 
-#include "router.cuh"
+#include "exchange.cuh"
 
 struct dsmoe_comm {
   dsmoe::PeerExchange px;
@@ -24,10 +24,58 @@ struct dsmoe_comm {
 };
 
 namespace dsmoe {
-// Control region: word 0 = the epoch of the last call; words 4..7 = an identity {magic, world, hidden,
+// Control region: word 0 = the epoch of the last call; word 1 = arrivals of the row all-reduce's
+// CTAs; word 2 = status bits of the row all-reduce; words 4..7 = an identity {magic, world, hidden,
 // bytes} that a peer checks before it maps the buffer; padded to keep the slots 256-byte aligned.
 constexpr size_t kCtlBytes = 256;
 constexpr unsigned kCommMagic = 0x64736D63u;  // "dsmc"
+constexpr uint64_t kRowWaitNs = 5000000000ull;
+constexpr unsigned CS_PEER = 1u;
+
+// y[b][:] = sum over ranks of x[b][:] for b < B <= 8 tokens of `hidden` values (the reference's
+// all_reduce_sum of the attention output projection, dsv41/tt/attn.py:19-21 at attn.py:229, 252).
+// One warp per 16-row tile, the same lane layout and exchange as the decode kernel's output.
+__global__ void allreduce_rows_kernel(PeerExchange px, const void* x, int x_f32, int B, void* y, int y_f32) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NT = px.hidden / 16, nt = blockIdx.x * (blockDim.x >> 5) + warp;
+  __shared__ unsigned ep_s;
+  if (threadIdx.x == 0) {
+    ep_s = *(volatile unsigned*)px.ctl + 1u;
+    __threadfence();  // the read of the old epoch precedes this CTA's arrival
+    const unsigned old = atomicAdd(px.ctl + 1, 1u);
+    if (old == gridDim.x - 1) {  // every CTA has read the old epoch: store the new one
+      px.ctl[1] = 0u;
+      __threadfence();
+      *(volatile unsigned*)px.ctl = ep_s;
+    }
+  }
+  __syncthreads();
+  if (nt >= NT) return;
+  const int g = lane >> 2, tq = lane & 3;
+  float v[4];
+#pragma unroll
+  for (int q4 = 0; q4 < 4; ++q4) {
+    const int row = nt * 16 + (q4 >= 2 ? g + 8 : g), tok = 2 * tq + (q4 & 1);
+    const long long o = (long long)tok * px.hidden + row;
+    v[q4] = tok >= B ? 0.f : x_f32 ? reinterpret_cast<const float*>(x)[o]
+                                   : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[o]);
+  }
+  float4 s4 = make_float4(v[0], v[1], v[2], v[3]);
+  if (!ll_allreduce_tile(px.slots, px.world, px.rank, NT, nt, ep_s, s4, lane, kRowWaitNs) && lane == 0)
+    atomicOr(px.ctl + 2, CS_PEER);
+  const float r[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+  for (int q4 = 0; q4 < 4; ++q4) {
+    const int row = nt * 16 + (q4 >= 2 ? g + 8 : g), tok = 2 * tq + (q4 & 1);
+    if (tok < B) {
+      const long long o = (long long)tok * px.hidden + row;
+      if (y_f32)
+        reinterpret_cast<float*>(y)[o] = r[q4];
+      else
+        reinterpret_cast<__nv_bfloat16*>(y)[o] = __float2bfloat16_rn(r[q4]);
+    }
+  }
+}
 }
 
 using namespace dsmoe;
@@ -144,3 +192,31 @@ extern "C" int dsmoe_comm_destroy(dsmoe_comm_t* c) {
 namespace dsmoe {
 const PeerExchange* comm_exchange(const dsmoe_comm_t* c) { return c && c->opened ? &c->px : nullptr; }
 }  // namespace dsmoe
+
+extern "C" int dsmoe_allreduce_rows(const dsmoe_comm_t* c, const void* x, int x_dtype, int B, void* y, int y_dtype,
+                                    void* stream) {
+  DSMOE_REQUIRE(c && c->opened, DSMOE_ERR_ARG, "allreduce_rows: comm is null or not opened");
+  DSMOE_REQUIRE(x && y, DSMOE_ERR_ARG, "allreduce_rows: x / y null");
+  DSMOE_REQUIRE(B >= 1 && B <= 8, DSMOE_ERR_ARG, "allreduce_rows: rows %d outside 1..8", B);
+  DSMOE_REQUIRE((x_dtype == DSMOE_DTYPE_BF16 || x_dtype == DSMOE_DTYPE_F32) &&
+                    (y_dtype == DSMOE_DTYPE_BF16 || y_dtype == DSMOE_DTYPE_F32),
+                DSMOE_ERR_ARG, "allreduce_rows: dtypes %d -> %d", x_dtype, y_dtype);
+  int dev = -1;
+  cudaGetDevice(&dev);
+  DSMOE_REQUIRE(dev == c->device, DSMOE_ERR_ARG, "allreduce_rows: device %d current, comm on %d", dev, c->device);
+  const int NT = c->px.hidden / 16, wpb = 8;
+  allreduce_rows_kernel<<<(NT + wpb - 1) / wpb, wpb * 32, 0, (cudaStream_t)stream>>>(
+      c->px, x, x_dtype == DSMOE_DTYPE_F32, B, y, y_dtype == DSMOE_DTYPE_F32);
+  return cuda_status("allreduce_rows");
+}
+
+extern "C" int dsmoe_comm_check(const dsmoe_comm_t* c, void* stream) {
+  DSMOE_REQUIRE(c, DSMOE_ERR_ARG, "comm_check: comm is null");
+  if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return cuda_status("comm_check: synchronize");
+  unsigned st = 0;
+  if (cudaMemcpy(&st, c->local + 8, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return cuda_status("comm_check: read");
+  if (st == 0) return DSMOE_OK;
+  cudaMemset(c->local + 8, 0, 4);
+  set_error("allreduce_rows: a peer's tile did not arrive within the bound (status 0x%x); re-create the comm", st);
+  return DSMOE_ERR_TIMEOUT;
+}

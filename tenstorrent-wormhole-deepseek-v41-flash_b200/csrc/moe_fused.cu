@@ -30,7 +30,7 @@
 //      slots' partials of (at most a few) 16-row output tiles into y.
 // Every wait (mbarrier, grid barrier, slot count) is bounded by %globaltimer; on expiry the kernel
 // records a status bit in the workspace, stops consuming, lets its own copies land and returns.
-#include "router.cuh"
+#include "exchange.cuh"
 
 namespace dsmoe {
 
@@ -736,80 +736,10 @@ __device__ __forceinline__ void w2_store_y(const FusedArgs& a, int nt, float4 s4
 }
 
 // ------------------------------------------------------------------ peer all-reduce
-// One-shot all-reduce of an output tile over the tensor-parallel ranks, on NVLink peer memory.
-// Each rank pushes its tile partial (32 lanes x 4 fp32) into slot (parity, its rank, tile) of every
-// peer's exchange buffer, then reads the peers' partials of the same tile from its own buffer and
-// sums all ranks' partials in rank order, so every rank computes the same bits.
-// Words are LL pairs: the value's bits in the low half and the call's epoch in the high half. An
-// aligned 8-byte store is single-copy atomic, so a reader that sees this call's epoch in a word
-// sees the value written with it; no fence or flag is needed. Epochs grow by one per call (the
-// control word), and slots alternate between two parities: a peer can be at most one call ahead
-// (it cannot finish call e + 1 without this rank's tiles of call e + 1), so it never overwrites a
-// slot this rank still reads.
-__device__ __forceinline__ unsigned long long ll_word(float v, unsigned ep) {
-  return ((unsigned long long)ep << 32) | __float_as_uint(v);
-}
-__device__ __forceinline__ void st_ll2(unsigned long long* p, unsigned long long w0, unsigned long long w1) {
-  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(w0), "l"(w1) : "memory");
-}
-__device__ __forceinline__ void ld_ll2(const unsigned long long* p, unsigned long long& w0, unsigned long long& w1) {
-  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(p) : "memory");
-}
-__device__ __forceinline__ size_t ar_slot(int par, int q, int W, int NT, int nt, int lane) {
-  return ((((size_t)par * W + q) * NT + nt) * 32 + lane) * 4;
-}
-// s4: this rank's partial of tile nt in, the sum over ranks out. False if a peer's words did not
-// arrive within kPeerWaitNs (s4 is then incomplete).
+// s4: this rank's partial of output tile nt in, the sum over ranks out (exchange.cuh). False if a
+// peer's words did not arrive within kPeerWaitNs (s4 is then incomplete).
 __device__ __noinline__ bool ar_tile(const FusedArgs& a, int nt, unsigned ep, float4& s4, int lane) {
-  const int W = a.ar_world, r = a.ar_rank, NT = a.H / 16, par = (int)(ep & 1u);
-  const unsigned long long w0 = ll_word(s4.x, ep), w1 = ll_word(s4.y, ep), w2 = ll_word(s4.z, ep),
-                           w3 = ll_word(s4.w, ep);
-  const size_t mine = ar_slot(par, r, W, NT, nt, lane);
-  for (int d = 1; d < W; ++d) {  // peers in the order r+1, r+2, ... (spreads the first stores)
-    const int q = r + d < W ? r + d : r + d - W;
-    unsigned long long* p = a.ar_slots[q] + mine;
-    st_ll2(p, w0, w1);
-    st_ll2(p + 2, w2, w3);
-  }
-  // every peer's slot polled together: one round of loads per poll, not one per peer
-  float4 v[kMaxWorld];
-  unsigned got = 1u << r;  // ranks whose words have arrived
-  v[r] = s4;
-  const unsigned all = (1u << W) - 1u;
-  const uint64_t t0 = globaltimer_ns();
-  bool ok = true;
-  while (got != all) {
-    unsigned long long x[kMaxWorld][4];
-#pragma unroll
-    for (int q = 0; q < kMaxWorld; ++q)
-      if (q < W && !((got >> q) & 1u)) {
-        const unsigned long long* p = a.ar_slots[r] + ar_slot(par, q, W, NT, nt, lane);
-        ld_ll2(p, x[q][0], x[q][1]);
-        ld_ll2(p + 2, x[q][2], x[q][3]);
-      }
-#pragma unroll
-    for (int q = 0; q < kMaxWorld; ++q)
-      if (q < W && !((got >> q) & 1u) && (unsigned)(x[q][0] >> 32) == ep && (unsigned)(x[q][1] >> 32) == ep &&
-          (unsigned)(x[q][2] >> 32) == ep && (unsigned)(x[q][3] >> 32) == ep) {
-        v[q] = make_float4(__uint_as_float((unsigned)x[q][0]), __uint_as_float((unsigned)x[q][1]),
-                           __uint_as_float((unsigned)x[q][2]), __uint_as_float((unsigned)x[q][3]));
-        got |= 1u << q;
-      }
-    if (got != all && globaltimer_ns() - t0 > kPeerWaitNs) {
-      ok = false;
-      break;
-    }
-  }
-  float4 tot = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int q = 0; q < W; ++q) {  // rank order: the same bits on every rank
-    const float4 u = ((got >> q) & 1u) ? v[q] : make_float4(0.f, 0.f, 0.f, 0.f);
-    tot.x += u.x;
-    tot.y += u.y;
-    tot.z += u.z;
-    tot.w += u.w;
-  }
-  s4 = tot;
-  return __all_sync(0xffffffffu, ok);
+  return ll_allreduce_tile(a.ar_slots, a.ar_world, a.ar_rank, a.H / 16, nt, ep, s4, lane, kPeerWaitNs);
 }
 
 // ------------------------------------------------------------------ the kernel

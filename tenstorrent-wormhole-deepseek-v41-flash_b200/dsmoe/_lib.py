@@ -69,6 +69,8 @@ _SIGS = {
     "dsmoe_comm_open": ([_P, _P], _I),
     "dsmoe_comm_destroy": ([_P], _I),
     "dsmoe_moe_allreduce_supported": ([ctypes.POINTER(Layer), _P, _P, _I], _I),
+    "dsmoe_allreduce_rows": ([_P, _P, _I, _I, _P, _I, _P], _I),
+    "dsmoe_comm_check": ([_P, _P], _I),
     "dsmoe_moe_decode_allreduce": ([ctypes.POINTER(Layer), _P, _P, _I, _P, _P, _I, _P, _P, _P, _P, ctypes.c_size_t,
                                     _P], _I),
 }

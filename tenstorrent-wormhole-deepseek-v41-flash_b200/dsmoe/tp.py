@@ -79,6 +79,29 @@ class PeerComm:
                 self.handle = None
                 raise
 
+    def allreduce(self, x: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+        """Sum [B, hidden] (B <= 8, bf16 or fp32) over the group through the peer exchange, in one
+        launch (the reference's all_reduce_sum after the attention output projection,
+        dsv41/tt/attn.py:19-21). Every rank gets the same bits; rows beyond 8 go in several calls."""
+        from . import _lib as L
+        if x.dim() != 2 or x.shape[1] != self.hidden or x.device != self.device:
+            raise ValueError(f"x must be [rows, {self.hidden}] on {self.device}")
+        dt = {torch.bfloat16: L.DTYPE_BF16, torch.float32: L.DTYPE_F32}.get(x.dtype)
+        if dt is None:
+            raise TypeError("x must be bfloat16 or float32")
+        x = x.contiguous()
+        y = torch.empty_like(x) if out is None else out
+        for r0 in range(0, x.shape[0], 8):
+            r1 = min(x.shape[0], r0 + 8)
+            L.call("dsmoe_allreduce_rows", self.handle, L.ptr(x[r0:r1]), dt, r1 - r0, L.ptr(y[r0:r1]), dt,
+                   L.stream_of(x))
+        return y
+
+    def check(self) -> None:
+        """Synchronize and raise if a peer's tile did not arrive in time in allreduce()."""
+        from . import _lib as L
+        L.call("dsmoe_comm_check", self.handle, L.stream_of())
+
     def close(self) -> None:
         """Free this rank's buffer and unmap the peers' (synchronizes the device)."""
         from . import _lib as L

@@ -3,7 +3,8 @@ expert. Two all-reduce paths sum the ranks' partials (the role of dsv41/tt/attn.
 NCCL over the fp32 partials, and the peer exchange inside the decode kernel (tp.PeerComm). Both
 must match the oracle's whole layer on every rank; the in-kernel sum must also be bit-identical
 across ranks, stay right over many calls sharing one comm (epochs, slot parities) and under CUDA
-graph replay. Needs at least two GPUs; skipped otherwise."""
+graph replay; the stand-alone row all-reduce on the same comm must equal an fp32 NCCL sum rounded to
+bf16. Needs at least two GPUs; skipped otherwise."""
 import datetime
 import os
 import socket
@@ -88,6 +89,25 @@ def _worker(rank, world, port, root, out_q):
         m.check(1)
         extra["graph"] = graph_ok
         del g
+        # the stand-alone row all-reduce on the same comm (attention output projection): the sum of
+        # bf16 rows, identical to an fp32 NCCL sum rounded to bf16, the same bits on every rank
+        rows_ok = True
+        for B in (1, 5, 8, 13):
+            xr = torch.randn((B, 1024), generator=torch.Generator().manual_seed(100 + 10 * B + rank))
+            xr = xr.to(torch.bfloat16).to(dev)
+            yr = comm.allreduce(xr)
+            comm.check()
+            ref = xr.float()
+            dist.all_reduce(ref)
+            rows_ok &= bool(torch.equal(yr, ref.to(torch.bfloat16)))
+            allv = [torch.empty_like(yr) for _ in range(world)]
+            dist.all_gather(allv, yr)
+            rows_ok &= all(torch.equal(allv[0], v) for v in allv)
+        # and the decode kernel's exchange still pairs up after it (shared epochs)
+        m, xd, y0 = layers[1]
+        rows_ok &= bool(torch.equal(m.forward(xd), y0))
+        m.check(3)
+        extra["rows"] = rows_ok
         comm.close()
         dist.barrier()
         out_q.put((rank, res, extra, None))
@@ -121,6 +141,6 @@ def test_tp_forward_nccl(world):
         for path, fmt, B, ok, mar, cos in res:
             assert ok, (rank, path, fmt, B)
             assert mar < MAR_TOL and cos > COS_TOL, (rank, path, fmt, B, mar, cos)
-        assert extra == {"sequence": True, "graph": True}, (rank, extra)
+        assert extra == {"sequence": True, "graph": True, "rows": True}, (rank, extra)
     for p in procs:
         assert p.exitcode == 0
