@@ -20,10 +20,10 @@
 //   R  router quarter-rows (fp64 accumulation), spread round-robin over the warps, while the shared
 //      expert's weights (routing-independent) are prefetched into L2; then grid barrier A.
 //   P  every CTA computes the same scores, top-k and slot plan (shared memory).
-//   1  w1|w3 items (slot, 16-row tile, part) of the routed slots and of the shared expert (the last
-//      slot). A tile split between warps is published (one fence per batch, one counter per tile)
-//      and finished by its last contributor: clamp / SiLU / up -> h as e4m3 hi / lo rows in the
-//      workspace, and a per-slot count of finished tiles.
+//   1  w1|w3 tiles (16 rows of a slot: the routed slots, then the shared expert as the last slot),
+//      whole tiles per CTA; the CTA's warps split each tile's parts, and one warp (rotating) sums
+//      their partials in warp order: clamp / SiLU / up -> h as e4m3 hi / lo rows in the workspace,
+//      and a per-slot count of finished tiles.
 //   2  w2 items (slot, 16 output rows, 512 K of FP8 or 1024 K of FP4), slot-major, so a CTA touches
 //      at most two slots: once their tiles are counted it copies their h rows into shared memory.
 //      Routing weight on the fp32 partials; after grid barrier C every warp of the grid sums the
@@ -49,7 +49,8 @@ constexpr int FMAXK = DSMOE_MAX_TOPK;
 constexpr int FMAXS = FMAXB * FMAXK + 1;
 constexpr int FEMAX = 1024;            // routed experts
 constexpr int FHSLOTS = 2;             // slots whose h rows a CTA stages for phase 2
-constexpr int NPEND = 8;               // segments a warp holds before publishing them
+constexpr int NPEND = 8;               // segments a warp holds before publishing them (published-segment phase 1)
+constexpr int kMaxCtas = 256;          // CTAs (one per SM) the phase-1 partial scratch is sized for
 constexpr uint64_t kWaitNs = 1000000000ull;
 constexpr uint64_t kPeerWaitNs = 5000000000ull;  // a peer GPU's tile: ranks may start seconds apart
 
@@ -76,7 +77,7 @@ struct FusedArgs {
   float* scores;
   // scratch (workspace)
   double* rl;          // [8][E][4] router quarter-row partial logits
-  float* p13;          // [slots][T][p13max][32][8] w1|w3 tile-segment partials
+  float* p13;          // [CTA][2 parities][FW warps][32][8] w1|w3 partials of the CTA's current tiles
   float* p2;           // [NT][slots][p2max][32][4] w2 segment partials (token columns)
   uint8_t* hq;         // [slots] h rows, e4m3 hi / lo (hq_row)
   unsigned* cnt13;     // [slots][T]
@@ -127,7 +128,7 @@ __host__ __device__ inline SmemLayout smem_layout(int H, int I_loc, int B, int E
   o += xbytes > hbytes ? xbytes : hbytes;
   o = (o + 15) & ~size_t(15);
   L.bars = o;
-  o += (size_t)(NST + 2) * 8;  // stage barriers, the h barrier, the token-row barrier
+  o += (size_t)(NST + 6) * 8;  // stage barriers, the h barrier, the token-row barrier, 2 + 2 tile barriers
   L.plan = o;
   o += (sizeof(FPlan) + 15) & ~size_t(15);
   L.emask = o;
@@ -216,8 +217,8 @@ __device__ __forceinline__ int w2_range_start(const Geo& g, int nr, int s, int n
   return s < nr ? (s * g.NT + nt) * g.P2r : nr * g.NT * g.P2r + nt * g.P2s;
 }
 
-// Position of a warp's item in the phase-1 or phase-2 item space, advanced without divisions:
-// phase 1 (slot s, 16-row tile t, part p), phase 2 (slot s, n-tile t, part p). Routed slots come
+// Position of a warp's item in the phase-2 item space, advanced without divisions:
+// (slot s, n-tile t, part p). Routed slots come
 // first; slot nr is the shared expert, with its own part count.
 struct Cursor {
   int s, t, p;
@@ -250,6 +251,30 @@ __device__ __forceinline__ Cursor cursor2(const Geo& g, int nr, int i) {
   const W2Item w = w2_item(g, nr, i);
   return {w.s, w.nt, w.p};
 }
+
+// Phase 1: each CTA owns whole w1|w3 tiles, tile tau over [routed slots' tiles (slot-major), the
+// shared slot's tiles]; its span is cta_span(tiles, cta, G). The warps split every owned tile's P
+// parts into FW runs [P j / FW, P (j + 1) / FW); warp w takes run j = (w + k) % FW of tile k, so the
+// longer runs rotate over the warps. TCursor walks a warp's parts, tile k of the span.
+__device__ __forceinline__ int tile_nparts(const Geo& g, int nr, int tau) { return tau < nr * g.T ? g.P13r : g.P13s; }
+__device__ __forceinline__ int run_of(int w, int k) { return (w + k) % FW; }
+struct TCursor {
+  int k, p;
+  // to the warp's next part, skipping tiles where it has none (k == ntl at the end)
+  __device__ __forceinline__ void next(const Geo& g, int nr, int tau0, int ntl, int w) {
+    ++p;
+    while (k < ntl) {
+      const int P = tile_nparts(g, nr, tau0 + k);
+      if (p < P * (run_of(w, k) + 1) / FW) return;
+      if (++k < ntl) p = tile_nparts(g, nr, tau0 + k) * run_of(w, k) / FW;
+    }
+  }
+  __device__ __forceinline__ void start(const Geo& g, int nr, int tau0, int ntl, int w) {
+    k = 0;
+    p = (ntl > 0 ? tile_nparts(g, nr, tau0) * run_of(w, 0) / FW : 0) - 1;
+    next(g, nr, tau0, ntl, w);
+  }
+};
 
 __device__ __forceinline__ float fscore(float l, int func) {
   const double d = (double)l;
@@ -518,6 +543,8 @@ __device__ __forceinline__ void w13_combine(const float (&acc1)[2][4], const flo
   }
 }
 
+
+
 // Ordered sum of published partials (nv floats per lane, nv = 4 or 8): the offsets (in floats, from
 // base) come in distribution order; up to 8 loads are in flight at a time, added in that order.
 template <int NV>
@@ -570,6 +597,7 @@ __device__ __noinline__ void w13_reduce(const FusedArgs& a, const Geo& G, int si
 #pragma unroll
   for (int j = 0; j < 8; ++j) s[j] = sum.s[j];
 }
+
 
 // ------------------------------------------------------------------ w2
 // One w2 item of a slot (packed weights and scales in the stage; the slot's h rows in shared memory
@@ -749,7 +777,8 @@ struct Pend {
   int kind, s, t, np;
 };
 
-template <int RFMT>
+// TM: phase 1 with CTA-owned tiles (few tiles per CTA); otherwise published segments.
+template <int RFMT, bool TM>
 __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const SmemLayout SL = smem_layout(a.H, a.I_loc, a.B, a.E);
@@ -759,6 +788,8 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + SL.bars);
   uint64_t* hbar = full + NST;
   uint64_t* xbar = full + NST + 1;
+  uint64_t* tbar = full + NST + 2;  // [2] a tile's partials written (FW arrivals), by tile parity
+  uint64_t* rbar = full + NST + 4;  // [2] a tile's partials reduced (1 arrival), by tile parity
   FPlan& pl = *reinterpret_cast<FPlan*>(smem + SL.plan);
   unsigned* emask = reinterpret_cast<unsigned*>(smem + SL.emask);
   const int lo_off = a.B * a.H + 64;  // lo token rows after the hi rows (opposite bank half)
@@ -774,6 +805,10 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
 
   if (tid == 0) {
     for (int s = 0; s < NST + 2; ++s) mbar_init(&full[s], 1);  // stage barriers, h barrier, token-row barrier
+    mbar_init(&tbar[0], FW);
+    mbar_init(&tbar[1], FW);
+    mbar_init(&rbar[0], 1);
+    mbar_init(&rbar[1], 1);
     pl.abort = 0;
     fence_mbar_init();
   }
@@ -782,13 +817,15 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   // ---- the warp's item stream: items k < nR are router rows (phase R), the next n1 belong to phase
   // 1 and the last n2 to phase 2 (both known once the plan is). Item k lives in stage (k & 1).
   int kc = 0, ki = 0;  // next item to consume / to issue (warp-uniform)
-  int nr = 0, n1 = 0, n2 = 0, N1 = 0, NR1 = 0, N2 = 0;
-  Span run1{0, 0}, run2{0, 0};
+  int nr = 0, n1 = 0, n2 = 0, N2 = 0, N1 = 0, NR1 = 0;
+  int tau0 = 0, ntl = 0;  // phase 1 (TM): this CTA's tiles [tau0, tau0 + ntl)
+  Span run1{0, 0}, run2{0, 0};  // phase 1 (published segments) / phase 2 warp runs
   bool planned = false;
   const uint64_t pol_stream = l2_evict_first();
   auto stage_of = [&](int k) { return ring + (size_t)(warp * SPW + (k & 1)) * FSTAGE; };
   auto bar_of = [&](int k) { return &full[warp * SPW + (k & 1)]; };
-  Cursor ic1{0, 0, 0}, ic2{0, 0, 0};  // issue-side positions of the next phase-1 / phase-2 item
+  TCursor ic1{0, 0};
+  Cursor icP{0, 0, 0}, ic2{0, 0, 0};  // issue-side positions of the next phase-1 (TM / segments) / phase-2 item
   auto issue = [&](int k) {  // lane 0: item k's bytes into its stage
     const uint8_t* src;
     uint32_t bytes;
@@ -797,13 +834,25 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       src = reinterpret_cast<const uint8_t*>(a.wg + (long long)(i >> 2) * a.H + (i & 3) * (a.H / 4));
       bytes = (uint32_t)a.H;
     } else if (k < nR + n1) {
-      if (ic1.s < nr) {
-        const uint32_t ib = RFMT == DSMOE_FMT_FP8 ? kFp8W13Item : FCH * 1088;
-        src = a.r_w13 + (long long)pl.expert[ic1.s] * a.r_w13_eb + ic1.t * geo.tile13r + (long long)ic1.p * ib;
-        bytes = ib;
+      const uint32_t ib = RFMT == DSMOE_FMT_FP8 ? kFp8W13Item : FCH * 1088;
+      if constexpr (TM) {
+        const int tau = tau0 + ic1.k;
+        if (tau < nr * geo.T) {
+          const int sl = tau / geo.T, t = tau - sl * geo.T;
+          src = a.r_w13 + (long long)pl.expert[sl] * a.r_w13_eb + t * geo.tile13r + (long long)ic1.p * ib;
+          bytes = ib;
+        } else {
+          src = a.s_w13 + (tau - nr * geo.T) * geo.tile13s + (long long)ic1.p * kFp8W13Item;
+          bytes = kFp8W13Item;
+        }
       } else {
-        src = a.s_w13 + ic1.t * geo.tile13s + (long long)ic1.p * kFp8W13Item;
-        bytes = kFp8W13Item;
+        if (icP.s < nr) {
+          src = a.r_w13 + (long long)pl.expert[icP.s] * a.r_w13_eb + icP.t * geo.tile13r + (long long)icP.p * ib;
+          bytes = ib;
+        } else {
+          src = a.s_w13 + icP.t * geo.tile13s + (long long)icP.p * kFp8W13Item;
+          bytes = kFp8W13Item;
+        }
       }
     } else {
       const W2Item w = {ic2.s, ic2.t, ic2.p};
@@ -831,8 +880,12 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       if (lane == 0) issue(ki);
       if (ki >= nR + n1)
         ic2.next(nr, geo.NT, geo.P2r, geo.P2s);
-      else if (ki >= nR)
-        ic1.next(nr, geo.T, geo.P13r, geo.P13s);
+      else if (ki >= nR) {
+        if constexpr (TM)
+          ic1.next(geo, nr, tau0, ntl, warp);
+        else
+          icP.next(nr, geo.T, geo.P13r, geo.P13s);
+      }
       ++ki;
     }
   };
@@ -1050,17 +1103,29 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
 
 
 
-  // ---- the rest of the stream is known. Phase-1 items: routed slots (tiles of P13r items), then
-  // the shared expert as slot nr (tiles of P13s FP8 items).
+  // ---- the rest of the stream is known. Phase 1: this CTA's w1|w3 tiles (routed slots' tiles,
+  // then the shared expert's as slot nr), each tile's parts split over the warps; phase 2: w2 items.
   nr = pl.n_routed;
-  NR1 = nr * geo.T * geo.P13r;
-  N1 = NR1 + geo.T * geo.P13s;
-  run1 = warp_run(cta_span(N1, cta, G), warp);
-  n1 = run1.e - run1.s;
+  if constexpr (TM) {
+    const Span ts = cta_span((nr + 1) * geo.T, cta, G);
+    tau0 = ts.s;
+    ntl = ts.e - ts.s;
+    n1 = 0;
+    for (int k = 0; k < ntl; ++k) {
+      const int P = tile_nparts(geo, nr, tau0 + k), j = run_of(warp, k);
+      n1 += P * (j + 1) / FW - P * j / FW;
+    }
+    ic1.start(geo, nr, tau0, ntl, warp);
+  } else {  // items (slot, tile, part): routed slots' tiles of P13r items, then the shared slot's
+    NR1 = nr * geo.T * geo.P13r;
+    N1 = NR1 + geo.T * geo.P13s;
+    run1 = warp_run(cta_span(N1, cta, G), warp);
+    n1 = run1.e - run1.s;
+    icP = cursor1(geo, nr, NR1, run1.s);
+  }
   N2 = nr * geo.NT * geo.P2r + geo.NT * geo.P2s;
   run2 = warp_run(cta_span(N2, cta, G), warp);
   n2 = run2.e - run2.s;
-  ic1 = cursor1(geo, nr, NR1, run1.s);
   ic2 = cursor2(geo, nr, run2.s);
   planned = true;
   refill();
@@ -1071,6 +1136,93 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     for (int j = 0; j < 2; ++j)
       xr[j] = xq + (size_t)toks[min(4 * j + (lane >> 3), ntok - 1)] * a.H + ((lane >> 2) & 1) * lo_off + (lane & 3) * 16;
   };
+
+  if constexpr (TM) {
+  // ---- phase 1: w1|w3 of this CTA's tiles. Each warp accumulates its run of a tile's parts, writes
+  // its partial (8 floats per lane) to the CTA's slot of the scratch and arrives on the tile's
+  // barrier; warp k % FW sums the FW partials in warp order (deterministic), applies clamp / SiLU / up -> h
+  // rows, and counts the tile for its slot. Partial slots alternate by tile parity: a warp writes
+  // tile k's only after tile k - 2's reduction has read them.
+  {
+    float* gp = a.p13 + (size_t)cta * 2 * FW * 256;  // [parity][warp][32 lanes][8]
+    float acc1[2][4], acc3[2][4];
+    const uint8_t* xr[2] = {xq, xq};
+    for (int k = 0; k < ntl && !pl.abort; ++k) {
+      const int tau = tau0 + k;
+      const int sl = tau < nr * geo.T ? tau / geo.T : nr, t = tau - sl * geo.T;
+      const int sidx = sl < nr ? sl : a.sh_idx;
+      const int P = tile_nparts(geo, nr, tau), j = run_of(warp, k), pb = P * j / FW, pe = P * (j + 1) / FW;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc1[j][q] = acc3[j][q] = 0.f;
+      token_rows(xr, pl.tok[sl], pl.ntok[sl]);
+      const bool two = pl.ntok[sl] > 4;
+      for (int p = pb; p < pe; ++p) {
+        if (!wait_full(kc)) break;
+        const uint8_t* stage = stage_of(kc);
+        if (sl < nr) {
+          if (two)
+            w13_accum<RFMT, 2>(stage, xr, p, lane, acc1, acc3);
+          else
+            w13_accum<RFMT, 1>(stage, xr, p, lane, acc1, acc3);
+        } else {
+          if (two)
+            w13_accum<DSMOE_FMT_FP8, 2>(stage, xr, p, lane, acc1, acc3);
+          else
+            w13_accum<DSMOE_FMT_FP8, 1>(stage, xr, p, lane, acc1, acc3);
+        }
+        __syncwarp();
+        ++kc;
+        refill();
+      }
+      if (pl.abort) break;
+      float s8[8];
+      w13_combine(acc1, acc3, s8);
+      float* mine = gp + ((size_t)((k & 1) * FW + warp) * 32 + lane) * 8;
+      if (k >= 2 && !mbar_wait(&rbar[k & 1], ((k - 2) >> 1) & 1, kWaitNs)) {
+        if (lane == 0) {
+          atomicOr(a.status, ST_SLOT);
+          pl.abort = 1;
+        }
+        break;
+      }
+      *reinterpret_cast<float4*>(mine) = make_float4(s8[0], s8[1], s8[2], s8[3]);
+      *reinterpret_cast<float4*>(mine + 4) = make_float4(s8[4], s8[5], s8[6], s8[7]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tbar[k & 1]);
+      if (warp == k % FW) {
+        if (!mbar_wait(&tbar[k & 1], (k >> 1) & 1, kWaitNs)) {
+          if (lane == 0) {
+            atomicOr(a.status, ST_SLOT);
+            pl.abort = 1;
+          }
+          break;
+        }
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int w = 0; w < FW; ++w) {  // warp order
+          const float* src = gp + ((size_t)((k & 1) * FW + w) * 32 + lane) * 8;
+          const float4 u0 = *reinterpret_cast<const float4*>(src), u1 = *reinterpret_cast<const float4*>(src + 4);
+          v[0] += u0.x;
+          v[1] += u0.y;
+          v[2] += u0.z;
+          v[3] += u0.w;
+          v[4] += u1.x;
+          v[5] += u1.y;
+          v[6] += u1.z;
+          v[7] += u1.w;
+        }
+        w13_epilogue(a, pl, sidx, t, v, pl.ntok[sl], pl.tok[sl], sl < nr ? fmtf : 1.0f, lane);
+        fence_acq_rel_gpu();
+        __syncwarp();
+        if (lane == 0) {
+          atomicAdd(a.slot_done + sidx, 1u);
+          mbar_arrive(&rbar[k & 1]);
+        }
+      }
+    }
+  }
+  } else {
   // phase-1 tile (slot s, tile t): its first item and its part count
   auto tile_first = [&](int s, int t) { return s < nr ? (s * geo.T + t) * geo.P13r : NR1 + t * geo.P13s; };
   auto tile_parts = [&](int s) { return s < nr ? geo.P13r : geo.P13s; };
@@ -1176,6 +1328,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     }
     if (cur_s >= 0 && !pl.abort) end_seg();
     if (!pl.abort) publish();
+  }
   }
 
   // ---- phase 2 set-up: the h rows of the (at most FHSLOTS) slots of this CTA's span, once their
@@ -1335,7 +1488,10 @@ FusedScratch fused_scratch(int H, int I_loc, int E, int B, int topk, int r_fmt) 
   f.cnt13 = o; o += al2((size_t)f.slots * T * 4);
   f.slot_done = o; o += al2((size_t)f.slots * 4);
   f.rl = o; o += al2((size_t)B * E * 4 * 8);
-  f.p13 = o; o += al2((size_t)f.slots * T * f.p13max * 32 * 8 * 4);
+  // w1|w3 partials: the larger of the published-segment layout [slots][T][p13max][32][8] and the
+  // CTA-owned-tile layout [CTA][2][FW][32][8]
+  const size_t p13_seg = (size_t)f.slots * T * f.p13max * 32 * 8 * 4, p13_tm = (size_t)kMaxCtas * 2 * FW * 32 * 8 * 4;
+  f.p13 = o; o += al2(p13_seg > p13_tm ? p13_seg : p13_tm);
   f.p2 = o; o += al2((size_t)NT * f.slots * f.p2max * 32 * 4 * 4);
   f.hq = o; o += al2((size_t)f.slots * hq_slot_bytes(I_loc));
   f.total = o;
@@ -1345,7 +1501,7 @@ FusedScratch fused_scratch(int H, int I_loc, int E, int B, int topk, int r_fmt) 
 // Per-device constants, looked up once (attribute queries cost microseconds per call).
 struct DevInfo {
   int sms = 0, optin = 0;
-  bool attr_set[2] = {false, false};
+  bool attr_set[4] = {false, false, false, false};
   int pdl = -1;  // programmatic dependent launch with the cooperative attribute: -1 untested, 0 no, 1 yes
 };
 static DevInfo g_dev[64];
@@ -1368,6 +1524,7 @@ size_t fused_smem_bytes(int H, int I_loc, int B, int E) { return smem_layout(H, 
 bool fused_supported(const dsmoe_layer_t* L, int B) {
   if (B < 1 || B > FMAXB || L->n_experts > FEMAX || L->hidden % 512 != 0 || L->hidden > FSTAGE) return false;
   const DevInfo& d = dev_info();
+  if (d.sms > kMaxCtas) return false;
   if (fused_smem_bytes(L->hidden, L->inter_local, B, L->n_experts) > (size_t)d.optin) return false;
   const int NT = L->hidden / 16, I = L->inter_local;
   const int P2s = (I + FK2_8 - 1) / FK2_8;
@@ -1439,8 +1596,13 @@ int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* im
     }
   }
 
-  const int fi = L->routed.fmt == DSMOE_FMT_FP8 ? 0 : 1;
-  void (*kern)(FusedArgs) = fi == 0 ? moe_fused_kernel<DSMOE_FMT_FP8> : moe_fused_kernel<DSMOE_FMT_FP4>;
+  int fi = L->routed.fmt == DSMOE_FMT_FP8 ? 0 : 1;
+  // Phase 1 with CTA-owned tiles when the step has at most about two w1|w3 tiles per CTA (small
+  // intermediate slices: tensor parallelism over 4-8 GPUs); published segments otherwise.
+  const bool tm = (long long)(B * L->topk + 1) * (L->inter_local / 16) <= 2LL * sms;
+  void (*kern)(FusedArgs) = fi == 0 ? (tm ? moe_fused_kernel<DSMOE_FMT_FP8, true> : moe_fused_kernel<DSMOE_FMT_FP8, false>)
+                                    : (tm ? moe_fused_kernel<DSMOE_FMT_FP4, true> : moe_fused_kernel<DSMOE_FMT_FP4, false>);
+  fi += tm ? 2 : 0;
   if (!d.attr_set[fi]) {
     // the largest dynamic shared memory any call can ask for; set once per device and format
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess)
