@@ -1003,20 +1003,24 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     __syncthreads();
     if (cta == 0 && a.scores)
       for (int i = tid; i < n; i += FT) a.scores[i] = sc_s[i];
-    // top-k of token b (warp b): k rounds of (lane-local best, warp argmax); ties -> lower index
+    // top-k of token b (warp b): the token's biased scores in registers (expert lane + 32 j), then k
+    // rounds of (lane-local best, warp argmax), the winner's lane dropping it; ties -> lower index
     for (int b = warp; b < a.B; b += FW) {
-      float* v = bi_s + b * a.E;
+      const float* v = bi_s + b * a.E;
+      float rv[FEMAX / 32];
+#pragma unroll
+      for (int j = 0; j < FEMAX / 32; ++j) rv[j] = lane + 32 * j < a.E ? v[lane + 32 * j] : -INFINITY;
       float tot = 0.f;
       for (int r = 0; r < a.topk; ++r) {
         float best = -INFINITY;
-        int bi = 0x7FFFFFFF;
-        for (int e = lane; e < a.E; e += 32) {
-          const float x = v[e];
-          if (x > best) {
-            best = x;
-            bi = e;
+        int bj = -1;
+#pragma unroll
+        for (int j = 0; j < FEMAX / 32; ++j)
+          if (rv[j] > best) {  // strict: the lower index of a lane wins a tie
+            best = rv[j];
+            bj = j;
           }
-        }
+        int bi = bj < 0 ? 0x7FFFFFFF : lane + 32 * bj;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
           const float ov = __shfl_xor_sync(0xffffffffu, best, o);
@@ -1027,16 +1031,19 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
           }
         }
         if (bi == 0x7FFFFFFF) bi = 0;
+        if (lane == (bi & 31)) {
+#pragma unroll
+          for (int j = 0; j < FEMAX / 32; ++j)
+            if (j == (bi >> 5)) rv[j] = -INFINITY;
+        }
         const float w = sc_s[b * a.E + bi];
-        __syncwarp();
         if (lane == 0) {
           pl.sel[b][r] = bi;
           pl.selw[b][r] = w;
-          v[bi] = -INFINITY;
         }
-        __syncwarp();
         tot += w;
       }
+      __syncwarp();
       if (lane < a.topk) {
         const float w = pl.selw[b][lane] / (tot + 1e-20f) * a.route_scale;
         pl.selw[b][lane] = w;
@@ -1047,6 +1054,33 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       }
     }
     __syncthreads();
+    if (a.B == 1) {
+      // one token: its k (distinct) picks are the slots, in expert order (rank = picks below it)
+      if (warp == 0 && lane < a.topk) {
+        const int e = pl.sel[0][lane];
+        int rk = 0;
+        for (int r = 0; r < a.topk; ++r) rk += pl.sel[0][r] < e ? 1 : 0;
+        pl.expert[rk] = e;
+        pl.ntok[rk] = 1;
+        for (int c = 0; c < 8; ++c) {
+          pl.tok[rk][c] = 0;
+          pl.wt[rk][c] = c == 0 ? pl.selw[0][lane] : 0.f;
+          pl.col_of[rk][c] = c == 0 ? (signed char)0 : (signed char)-1;
+        }
+      }
+      if (tid == 0) {
+        const int sh = a.topk;  // the shared expert's slot
+        pl.n_routed = a.topk;
+        pl.expert[sh] = a.E;
+        pl.ntok[sh] = 1;
+        for (int c = 0; c < 8; ++c) {
+          pl.tok[sh][c] = 0;
+          pl.wt[sh][c] = 1.0f;
+          pl.col_of[sh][c] = c == 0 ? (signed char)0 : (signed char)-1;
+        }
+      }
+      __syncthreads();
+    } else {
     for (int i = tid; i < a.B * a.topk; i += FT) atomicOr(&emask[pl.sel[i / a.topk][i % a.topk]], 1u << (i / a.topk));
     __syncthreads();
     // slots in expert order: block-wide compaction of the experts with picks
@@ -1099,6 +1133,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       }
     }
     __syncthreads();
+    }
   }
 
 
