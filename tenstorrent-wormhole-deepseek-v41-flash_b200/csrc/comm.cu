@@ -61,7 +61,7 @@ __global__ void allreduce_rows_kernel(PeerExchange px, const void* x, int x_f32,
                                    : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[o]);
   }
   float4 s4 = make_float4(v[0], v[1], v[2], v[3]);
-  if (!ll_allreduce_tile(px.slots, px.world, px.rank, NT, nt, ep_s, s4, lane, kRowWaitNs) && lane == 0)
+  if (!ll_allreduce_tile(px.slots, px.world, px.rank, NT, nt, B, ep_s, s4, lane, kRowWaitNs) && lane == 0)
     atomicOr(px.ctl + 2, CS_PEER);
   const float r[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll

@@ -83,7 +83,7 @@ struct FusedArgs {
   unsigned* cnt13;     // [slots][T]
   unsigned* cnt2;      // [NT]
   unsigned* slot_done; // [slots] finished w1|w3 tiles per routed slot
-  unsigned* gbar;      // [0] arrivals, [1] generation
+  unsigned long long* gbar;  // grid-barrier arrivals since the workspace was reset
   unsigned* status;    // [0]
   int sh_idx;          // scratch slot index of the shared expert
   int slots, p13max, p2max;
@@ -173,15 +173,35 @@ __device__ __forceinline__ Span warp_run(Span cs, int w) {
   const int rs = cs.s + w * L + min(w, r);
   return {rs, rs + L + (w < r ? 1 : 0)};
 }
-// Item i of n belongs to CTA span / warp run as above. Calls f(first item of the segment - a) for
-// every warp run that intersects [a, b), in order.
+// Split of an item space whose first n1 items (routed experts) cost w1 each and the other n - n1
+// (the shared expert) w2: CTA c takes the items whose cost position falls in [c C / G, (c+1) C / G),
+// C the total cost. With FP4 routed experts an item holds twice the weights of a shared FP8 item,
+// so w1 = 2, w2 = 1 gives every CTA the same work; 2 n G < 2^32 (host check) keeps it 32-bit.
+struct Split {
+  int n, n1, w1, w2;
+  __device__ __forceinline__ int bound(int c, int G) const {
+    const unsigned C = (unsigned)n1 * w1 + (unsigned)(n - n1) * w2;
+    const unsigned q = (unsigned)c * C, a1 = (unsigned)n1 * w1 * (unsigned)G;
+    const unsigned g1 = (unsigned)w1 * G, g2 = (unsigned)w2 * G;
+    if (q <= a1) return (int)((q + g1 - 1) / g1);
+    return min(n, n1 + (int)((q - a1 + g2 - 1) / g2));
+  }
+  __device__ __forceinline__ Span span(int c, int G) const { return {bound(c, G), bound(c + 1, G)}; }
+  __device__ __forceinline__ int first_cta(int i, int G) const {  // a guess, refined by the caller
+    const unsigned C = (unsigned)n1 * w1 + (unsigned)(n - n1) * w2;
+    const unsigned pos = i < n1 ? (unsigned)i * w1 : (unsigned)n1 * w1 + (unsigned)(i - n1) * w2;
+    return C ? (int)(((unsigned long long)pos * G) / C) : 0;
+  }
+};
+// Item i of the split belongs to CTA span / warp run as above. Calls f(first item of the segment -
+// a) for every warp run that intersects [a, b), in order.
 template <class F>
-__device__ __forceinline__ void for_segments(int n, int G, int a, int b, F&& f) {
-  int c = (int)(((unsigned)a * (unsigned)G) / (unsigned)n);
-  while (c + 1 < G && cta_span(n, c + 1, G).s <= a) ++c;
-  while (c > 0 && cta_span(n, c, G).s > a) --c;
+__device__ __forceinline__ void for_segments(const Split& sp, int G, int a, int b, F&& f) {
+  int c = min(sp.first_cta(a, G), G - 1);
+  while (c + 1 < G && sp.span(c + 1, G).s <= a) ++c;
+  while (c > 0 && sp.span(c, G).s > a) --c;
   for (; c < G; ++c) {
-    const Span cs = cta_span(n, c, G);
+    const Span cs = sp.span(c, G);
     if (cs.s >= b) break;
     for (int w = 0; w < FW; ++w) {
       const Span r = warp_run(cs, w);
@@ -295,32 +315,81 @@ __device__ __forceinline__ uint32_t ld_relaxed_u32(const unsigned* p) {
 }
 
 // ------------------------------------------------------------------ grid barrier (bounded)
-// Arrive: the CTA's writes are ordered before it by the caller's __syncthreads and this thread's
-// fence; the last arrival resets the count and bumps the generation with release semantics.
-// Wait: relaxed polling, one acquire fence once the generation moved.
-// With `ep_ctl`, the last arrival also stores `ep` there (the peer exchange's epoch: every CTA read
-// the previous one before it arrived).
-__device__ __forceinline__ unsigned grid_arrive(unsigned* gbar, int G, unsigned* ep_ctl = nullptr,
-                                                unsigned ep = 0u) {
-  const unsigned g0 = ld_acquire_u32(gbar + 1);
-  fence_acq_rel_gpu();
-  unsigned old;
-  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(gbar) : "memory");
-  if (old == (unsigned)G - 1) {
-    if (ep_ctl) asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(ep_ctl), "r"(ep) : "memory");
-    asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(gbar) : "memory");
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(gbar + 1) : "memory");
-  }
-  return g0;
+// One 64-bit arrival counter per workspace, zeroed when the workspace is reset and otherwise only
+// increased: each barrier of each launch adds G (one arrival per CTA). Barrier j of a launch is
+// complete once the counter reaches base + (j + 1) G, where base is the counter read at launch start
+// rounded down to a multiple of G: every earlier launch added a multiple of G, and fewer than G
+// arrivals of this launch can precede any CTA's read (its own is missing).
+// Arrive: a gpu-scope fence (the CTA's writes, ordered by the caller's __syncthreads) and a relaxed
+// add, so the arriving thread waits for no reply. Wait: relaxed polling, one acquire fence at the end.
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
-__device__ __forceinline__ bool grid_wait(unsigned* gbar, unsigned g0, const unsigned* status) {
+__device__ __forceinline__ unsigned long long grid_base(const unsigned long long* gbar, int G) {
+  const unsigned long long c = ld_relaxed_u64(gbar);
+  return c - c % (unsigned long long)G;
+}
+__device__ __forceinline__ void grid_arrive(unsigned long long* gbar) {
+  fence_acq_rel_gpu();
+  asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;" ::"l"(gbar) : "memory");
+}
+__device__ __forceinline__ bool grid_wait(const unsigned long long* gbar, unsigned long long target,
+                                          const unsigned* status) {
   const uint64_t t0 = globaltimer_ns();
-  while (ld_relaxed_u32(gbar + 1) == g0) {
+  while ((long long)(ld_relaxed_u64(gbar) - target) < 0) {
     if (ld_relaxed_u32(status) != 0u) return false;
     if (globaltimer_ns() - t0 > kWaitNs) return false;
   }
   fence_acq_rel_gpu();
   return true;
+}
+
+// ------------------------------------------------------------------ top-k
+// Order-preserving key of a score (a larger score has a larger key, -0 and +0 the same one); NaN
+// gets the lowest key, 0, like an expert that does not exist, so it is never preferred.
+__device__ __forceinline__ unsigned score_key(float f) {
+  const unsigned u = f == 0.f ? 0u : __float_as_uint(f);
+  return f != f ? 0u : u ^ ((unsigned)((int)u >> 31) | 0x80000000u);
+}
+constexpr int FKJ = 12;  // keys per lane covering 384 experts
+
+// Top-k of one token by one warp: keys of v[e] (scores + selection bias) for e = lane + 32 j, k
+// rounds of lane-local best (the lowest j among equal keys), warp max, then the lowest index holding
+// it (ties -> lower index); the winner's lane drops it. sel[r] / selw[r] (= sc[winner]) by lane 0;
+// tot = the sum of the k selected scores.
+template <int NJ>
+__device__ __forceinline__ void topk_token(const float* v, const float* sc, int E, int k, int lane, int* sel,
+                                           float* selw, float& tot) {
+  unsigned key[NJ];
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) key[j] = lane + 32 * j < E ? score_key(v[lane + 32 * j]) : 0u;
+  tot = 0.f;
+  for (int r = 0; r < k; ++r) {
+    unsigned bk = 0u;
+    int bj = 0;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j)
+      if (key[j] > bk) {  // strict: the lower index of a lane wins a tie
+        bk = key[j];
+        bj = j;
+      }
+    const unsigned m = __reduce_max_sync(0xffffffffu, bk);
+    unsigned bi = __reduce_min_sync(0xffffffffu, bk == m ? (unsigned)(lane + 32 * bj) : 0xFFFFFFFFu);
+    if (bi >= (unsigned)E) bi = 0u;  // no expert left (k > E, rejected by the host)
+    if (lane == (int)(bi & 31u)) {
+#pragma unroll
+      for (int j = 0; j < NJ; ++j)
+        if (j == (int)(bi >> 5)) key[j] = 0u;
+    }
+    const float w = sc[bi];
+    if (lane == 0) {
+      sel[r] = (int)bi;
+      selw[r] = w;
+    }
+    tot += w;
+  }
 }
 
 // ------------------------------------------------------------------ router
@@ -375,15 +444,19 @@ __device__ void router_item(const FusedArgs& a, const uint8_t* stage, const __nv
 
 // ------------------------------------------------------------------ token rows
 // Token rows (bf16 in shared memory for B <= FXB, else global) -> per-token power-of-2 pre-scale
-// (amax * 2^-p in [128, 256)) -> e4m3 hi / lo rows in B-operand order (qk_off). All threads; ends
-// with __syncthreads.
+// (amax * 2^-p in [128, 256)) -> e4m3 hi / lo rows in B-operand order (qk_off). Run by warps 1..FW-1
+// (warp 0 is at the grid barrier meanwhile), synchronised among themselves by named barrier 1.
+__device__ __forceinline__ void bar_sync_setup() {
+  asm volatile("bar.sync 1, %0;" ::"r"(FT - 32) : "memory");
+}
 __device__ void setup_tokens(const FusedArgs& a, uint8_t* xq, __nv_bfloat16* xs, FPlan& pl, int lo_off) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x - 32, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int NT = FT - 32;
   const int nv = a.H / 8;  // uint4 per row
   for (int b = 0; b < a.B; ++b) {
     const uint4* src = reinterpret_cast<const uint4*>((a.B <= FXB ? xs : a.x) + (long long)b * a.H);
     float m = 0.f;
-    for (int v = tid; v < nv; v += FT) {
+    for (int v = tid; v < nv; v += NT) {
       const uint4 u = src[v];
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -393,10 +466,10 @@ __device__ void setup_tokens(const FusedArgs& a, uint8_t* xq, __nv_bfloat16* xs,
     m = warp_max(m);
     if (lane == 0) pl.red[warp][b] = m;
   }
-  __syncthreads();
+  bar_sync_setup();
   if (tid < a.B) {
     float m = 0.f;
-    for (int w = 0; w < FW; ++w) m = fmaxf(m, pl.red[w][tid]);
+    for (int w = 1; w < FW; ++w) m = fmaxf(m, pl.red[w][tid]);
     int p = 0;
     if (m > 0.f && m <= 3.0e38f) {
       int e2;
@@ -406,9 +479,9 @@ __device__ void setup_tokens(const FusedArgs& a, uint8_t* xq, __nv_bfloat16* xs,
     pl.xscale[tid] = ldexpf(1.0f, p);
     pl.xinv[tid] = ldexpf(1.0f, -p);
   }
-  __syncthreads();
+  bar_sync_setup();
   const int nch = a.H / 32;
-  for (int i = tid; i < a.B * nch; i += FT) {
+  for (int i = tid; i < a.B * nch; i += NT) {
     const int b = i / nch, c = i - b * nch;
     const uint4* src = reinterpret_cast<const uint4*>((a.B <= FXB ? xs : a.x) + (long long)b * a.H + 32 * c);
     const float inv = pl.xinv[b];
@@ -435,7 +508,6 @@ __device__ void setup_tokens(const FusedArgs& a, uint8_t* xq, __nv_bfloat16* xs,
       *reinterpret_cast<uint2*>(rh + lo_off + tt * 16) = make_uint2(l0 | (l1 << 16), l2 | (l3 << 16));
     }
   }
-  __syncthreads();
 }
 
 // ------------------------------------------------------------------ w1|w3
@@ -588,11 +660,11 @@ __device__ __forceinline__ float* p13_slot(const FusedArgs& a, const Geo& G, int
 
 // Sum of a w1|w3 tile's published segments, in distribution order: the tile's items are
 // [a0, a0 + P) of the phase-1 item space (N1 items).
-__device__ __noinline__ void w13_reduce(const FusedArgs& a, const Geo& G, int sidx, int t, int a0, int P, int N1,
-                                        int lane, float* s) {
+__device__ __noinline__ void w13_reduce(const FusedArgs& a, const Geo& G, int sidx, int t, int a0, int P,
+                                        const Split& sp1, int lane, float* s) {
   const float* base = p13_slot(a, G, sidx, t, 0, lane);
   SegSum<8> sum(base);
-  for_segments(N1, gridDim.x, a0, a0 + P, [&](int q) { sum.add(q * 32 * 8); });
+  for_segments(sp1, gridDim.x, a0, a0 + P, [&](int q) { sum.add(q * 32 * 8); });
   sum.flush();
 #pragma unroll
   for (int j = 0; j < 8; ++j) s[j] = sum.s[j];
@@ -767,7 +839,7 @@ __device__ __forceinline__ void w2_store_y(const FusedArgs& a, int nt, float4 s4
 // s4: this rank's partial of output tile nt in, the sum over ranks out (exchange.cuh). False if a
 // peer's words did not arrive within kPeerWaitNs (s4 is then incomplete).
 __device__ __noinline__ bool ar_tile(const FusedArgs& a, int nt, unsigned ep, float4& s4, int lane) {
-  return ll_allreduce_tile(a.ar_slots, a.ar_world, a.ar_rank, a.H / 16, nt, ep, s4, lane, kPeerWaitNs);
+  return ll_allreduce_tile(a.ar_slots, a.ar_world, a.ar_rank, a.H / 16, nt, a.B, ep, s4, lane, kPeerWaitNs);
 }
 
 // ------------------------------------------------------------------ the kernel
@@ -818,6 +890,9 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   // 1 and the last n2 to phase 2 (both known once the plan is). Item k lives in stage (k & 1).
   int kc = 0, ki = 0;  // next item to consume / to issue (warp-uniform)
   int nr = 0, n1 = 0, n2 = 0, N2 = 0, N1 = 0, NR1 = 0;
+  // cost of a routed item relative to a shared (FP8) one: FP4 items hold twice the weights
+  constexpr int wr = RFMT == DSMOE_FMT_FP4 ? 2 : 1;
+  Split sp1{0, 0, 1, 1}, sp2{0, 0, 1, 1};  // phase-1 (published segments) / phase-2 item splits
   int tau0 = 0, ntl = 0;  // phase 1 (TM): this CTA's tiles [tau0, tau0 + ntl)
   Span run1{0, 0}, run2{0, 0};  // phase 1 (published segments) / phase 2 warp runs
   bool planned = false;
@@ -903,12 +978,14 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   auto drain = [&]() {  // every copy this warp issued lands before the CTA exits
     for (int k = kc; k < ki; ++k) mbar_wait(bar_of(k), (k >> 1) & 1, kWaitNs);
   };
-  // bounded grid barrier by thread 0, with the CTA's __syncthreads around it; false = abandon the call
-  auto grid_sync = [&]() -> bool {
+  // bounded grid barrier j (0 = A, 1 = C) by thread 0, with the CTA's __syncthreads around it;
+  // false = abandon the call. gbase: thread 0's launch base of the arrival counter.
+  unsigned long long gbase = 0;
+  auto grid_sync = [&](int j) -> bool {
     __syncthreads();
     if (tid == 0 && !pl.abort) {
-      const unsigned g0 = grid_arrive(a.gbar, G);
-      if (!grid_wait(a.gbar, g0, a.status)) {
+      grid_arrive(a.gbar);
+      if (!grid_wait(a.gbar, gbase + (unsigned long long)(j + 1) * G, a.status)) {
         atomicOr(a.status, ST_GRID);
         pl.abort = 1;
       }
@@ -920,26 +997,15 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   // Prologue on constant data only (router rows, shared expert weights). With a programmatic
   // dependent launch it overlaps the previous kernel of the stream, which may still be running.
   refill();  // router rows stream in while the token rows arrive
-  // the shared expert's weights do not depend on routing: pull them into L2 now (each warp a slice)
-  if (lane == 0) {
-    const long long b13 = (long long)geo.T * geo.tile13s, b2 = (long long)geo.NT * geo.tile2s;
-    const long long piece = 16384, n13 = (b13 + piece - 1) / piece, n2p = (b2 + piece - 1) / piece;
-    for (long long q = (long long)cta * FW + warp; q < n13 + n2p; q += (long long)G * FW) {
-      const bool w2p = q >= n13;
-      const long long off = (w2p ? q - n13 : q) * piece, tot = w2p ? b2 : b13;
-      const uint32_t len = (uint32_t)min(piece, tot - off);
-      const uint8_t* src = (w2p ? a.s_w2 : a.s_w13) + off;
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(len) : "memory");
-    }
-  }
   // Past this point the previous kernel of the stream has completed and its writes are visible:
   // this call's tokens (often that kernel's output), the workspace, the exchange epoch. The next
   // kernel may be scheduled now; it cannot be resident on an SM before this grid's CTA there exits.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tid == 0) {
-    // the peer exchange's epoch of this call: one past the last call's (read before barrier A,
-    // whose last arrival stores it back)
+    gbase = grid_base(a.gbar, G);
+    // the peer exchange's epoch of this call: one past the last call's (every CTA reads it before
+    // barrier A; CTA 0 stores it back once the barrier has passed)
     pl.ar_epoch = a.ar_world > 1 ? *(volatile unsigned*)a.ar_ctl + 1u : 0u;
     if (a.B <= FXB) {  // bf16 token rows for the router, one bulk copy
       mbar_expect_tx(xbar, (uint32_t)(a.B * a.H * 2));
@@ -969,15 +1035,34 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       refill();
     }
   }
-  // ---- grid barrier A (every router row of the step is done); the token rows are converted to
-  // e4m3 hi / lo while the other CTAs arrive
+  // The shared expert's weights do not depend on routing: pull them into L2 while the grid waits for
+  // barrier A and plans (each warp a slice; after the router rows, which are on the critical path).
+  if (lane == 0) {
+    const long long b13 = (long long)geo.T * geo.tile13s, b2 = (long long)geo.NT * geo.tile2s;
+    const long long piece = 16384, n13 = (b13 + piece - 1) / piece, n2p = (b2 + piece - 1) / piece;
+    for (long long q = (long long)cta * FW + warp; q < n13 + n2p; q += (long long)G * FW) {
+      const bool w2p = q >= n13;
+      const long long off = (w2p ? q - n13 : q) * piece, tot = w2p ? b2 : b13;
+      const uint32_t len = (uint32_t)min(piece, tot - off);
+      const uint8_t* src = (w2p ? a.s_w2 : a.s_w13) + off;
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(len) : "memory");
+    }
+  }
+  // ---- grid barrier A (every router row of the step is done): warp 0 arrives and waits while
+  // warps 1.. convert the token rows to e4m3 hi / lo
   __syncthreads();
-  unsigned genA = 0;
-  if (tid == 0 && !pl.abort) genA = grid_arrive(a.gbar, G, a.ar_world > 1 ? a.ar_ctl : nullptr, pl.ar_epoch);
-  setup_tokens(a, xq, xs, pl, lo_off);
-  if (tid == 0 && !pl.abort && !grid_wait(a.gbar, genA, a.status)) {
-    atomicOr(a.status, ST_GRID);
-    pl.abort = 1;
+  if (warp == 0) {
+    if (tid == 0 && !pl.abort) {
+      grid_arrive(a.gbar);
+      if (!grid_wait(a.gbar, gbase + (unsigned long long)G, a.status)) {
+        atomicOr(a.status, ST_GRID);
+        pl.abort = 1;
+      } else if (cta == 0 && a.ar_world > 1) {  // every CTA read the old epoch before it arrived
+        asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(a.ar_ctl), "r"(pl.ar_epoch) : "memory");
+      }
+    }
+  } else {
+    setup_tokens(a, xq, xs, pl, lo_off);
   }
   __syncthreads();
   if (pl.abort) {
@@ -991,58 +1076,44 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     float* sc_s = reinterpret_cast<float*>(ring);  // [B][E] scores
     float* bi_s = sc_s + a.B * a.E;                // [B][E] scores + selection bias
     const int n = a.B * a.E;
-    for (int i = tid; i < n; i += FT) {
-      const double* r4 = a.rl + (long long)i * 4;
-      const double l = ((ld_cg_f64(r4) + ld_cg_f64(r4 + 1)) + ld_cg_f64(r4 + 2)) + ld_cg_f64(r4 + 3);
-      const int b = i / a.E, e = i - b * a.E;
-      const bool vl = a.bias_vl != nullptr && a.image_mask != nullptr && a.image_mask[b] != 0;
-      const float s = fscore(__double2float_rn(l), a.score_func);
-      sc_s[i] = s;
-      bi_s[i] = s + (vl ? a.bias_vl : a.bias)[e];
+    for (int i0 = tid; i0 < n; i0 += 2 * FT) {  // two logits per thread per pass, all loads first
+      double q[2][4];
+      float bias[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int i = i0 + u * FT;
+        if (i < n) {
+          const double* r4 = a.rl + (long long)i * 4;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) q[u][c] = ld_cg_f64(r4 + c);
+          const int b = i / a.E, e = i - b * a.E;
+          const bool vl = a.bias_vl != nullptr && a.image_mask != nullptr && a.image_mask[b] != 0;
+          bias[u] = (vl ? a.bias_vl : a.bias)[e];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int i = i0 + u * FT;
+        if (i < n) {
+          const double l = ((q[u][0] + q[u][1]) + q[u][2]) + q[u][3];
+          const float s = fscore(__double2float_rn(l), a.score_func);
+          sc_s[i] = s;
+          bi_s[i] = s + bias[u];
+        }
+      }
     }
     __syncthreads();
     if (cta == 0 && a.scores)
       for (int i = tid; i < n; i += FT) a.scores[i] = sc_s[i];
-    // top-k of token b (warp b): the token's biased scores in registers (expert lane + 32 j), then k
-    // rounds of (lane-local best, warp argmax), the winner's lane dropping it; ties -> lower index
+    // top-k of token b (warp b): the token's biased scores in registers (expert lane + 32 j) as
+    // order-preserving keys, then k rounds of (lane-local best, warp max, lowest index holding it),
+    // the winner's lane dropping it; ties -> lower index
     for (int b = warp; b < a.B; b += FW) {
-      const float* v = bi_s + b * a.E;
-      float rv[FEMAX / 32];
-#pragma unroll
-      for (int j = 0; j < FEMAX / 32; ++j) rv[j] = lane + 32 * j < a.E ? v[lane + 32 * j] : -INFINITY;
       float tot = 0.f;
-      for (int r = 0; r < a.topk; ++r) {
-        float best = -INFINITY;
-        int bj = -1;
-#pragma unroll
-        for (int j = 0; j < FEMAX / 32; ++j)
-          if (rv[j] > best) {  // strict: the lower index of a lane wins a tie
-            best = rv[j];
-            bj = j;
-          }
-        int bi = bj < 0 ? 0x7FFFFFFF : lane + 32 * bj;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-          if (ov > best || (ov == best && oi < bi)) {
-            best = ov;
-            bi = oi;
-          }
-        }
-        if (bi == 0x7FFFFFFF) bi = 0;
-        if (lane == (bi & 31)) {
-#pragma unroll
-          for (int j = 0; j < FEMAX / 32; ++j)
-            if (j == (bi >> 5)) rv[j] = -INFINITY;
-        }
-        const float w = sc_s[b * a.E + bi];
-        if (lane == 0) {
-          pl.sel[b][r] = bi;
-          pl.selw[b][r] = w;
-        }
-        tot += w;
-      }
+      if (a.E <= 32 * FKJ)
+        topk_token<FKJ>(bi_s + b * a.E, sc_s + b * a.E, a.E, a.topk, lane, pl.sel[b], pl.selw[b], tot);
+      else
+        topk_token<FEMAX / 32>(bi_s + b * a.E, sc_s + b * a.E, a.E, a.topk, lane, pl.sel[b], pl.selw[b], tot);
       __syncwarp();
       if (lane < a.topk) {
         const float w = pl.selw[b][lane] / (tot + 1e-20f) * a.route_scale;
@@ -1154,12 +1225,14 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   } else {  // items (slot, tile, part): routed slots' tiles of P13r items, then the shared slot's
     NR1 = nr * geo.T * geo.P13r;
     N1 = NR1 + geo.T * geo.P13s;
-    run1 = warp_run(cta_span(N1, cta, G), warp);
+    sp1 = Split{N1, NR1, wr, 1};
+    run1 = warp_run(sp1.span(cta, G), warp);
     n1 = run1.e - run1.s;
     icP = cursor1(geo, nr, NR1, run1.s);
   }
   N2 = nr * geo.NT * geo.P2r + geo.NT * geo.P2s;
-  run2 = warp_run(cta_span(N2, cta, G), warp);
+  sp2 = Split{N2, nr * geo.NT * geo.P2r, wr, 1};
+  run2 = warp_run(sp2.span(cta, G), warp);
   n2 = run2.e - run2.s;
   ic2 = cursor2(geo, nr, run2.s);
   planned = true;
@@ -1270,24 +1343,26 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     if (npend == 0) return;
     fence_acq_rel_gpu();
     __syncwarp();
-    unsigned last = 0;  // bit i: this warp completed pending segment i's tile
-    for (int i = 0; i < npend; ++i) {
-      const Pend e = pend[i];
-      if (e.kind == 3) continue;
-      const int sidx = e.s < nr ? e.s : a.sh_idx;
-      unsigned* cnt = a.cnt13 + sidx * geo.T + e.t;
-      unsigned old = 0;
-      if (lane == 0) old = atomicAdd(cnt, (unsigned)e.np);
-      old = __shfl_sync(0xffffffffu, old, 0);
-      if ((int)old + e.np == tile_parts(e.s)) last |= 1u << i;
-    }
+    // lane i counts pending segment i's items on its tile, all lanes at once (one round trip)
+    unsigned* mycnt = nullptr;
+    int mynp = 0, myparts = 0;
+    for (int i = 0; i < npend; ++i)
+      if (i == lane && pend[i].kind != 3) {
+        mycnt = a.cnt13 + (pend[i].s < nr ? pend[i].s : a.sh_idx) * geo.T + pend[i].t;
+        mynp = pend[i].np;
+        myparts = tile_parts(pend[i].s);
+      }
+    unsigned old = 0;
+    if (mycnt) old = atomicAdd(mycnt, (unsigned)mynp);
+    // bit i: this warp completed pending segment i's tile
+    const unsigned last = __ballot_sync(0xffffffffu, mycnt != nullptr && (int)old + mynp == myparts);
     if (last) fence_acq_rel_gpu();
     for (int i = 0; i < npend; ++i) {
       if (!((last >> i) & 1u)) continue;
       const Pend e = pend[i];
       const int sidx = e.s < nr ? e.s : a.sh_idx;
       float s8[8];
-      w13_reduce(a, geo, sidx, e.t, tile_first(e.s, e.t), tile_parts(e.s), N1, lane, s8);
+      w13_reduce(a, geo, sidx, e.t, tile_first(e.s, e.t), tile_parts(e.s), sp1, lane, s8);
       float v[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[j] = s8[j];
@@ -1368,7 +1443,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
 
   // ---- phase 2 set-up: the h rows of the (at most FHSLOTS) slots of this CTA's span, once their
   // w1|w3 tiles are all finished, into the token-row region (free after phase 1)
-  const Span span2 = cta_span(N2, cta, G);
+  const Span span2 = sp2.span(cta, G);
   int sA = 0, sB = -1;
   if (span2.e > span2.s) {
     sA = w2_item(geo, nr, span2.s).s;
@@ -1474,7 +1549,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   // ---- grid barrier C, then each CTA finishes its 16-row output tiles nt = cta + G * j: the warps
   // split each tile's positions into fixed chunks summed in order, and the chunk sums are added in
   // chunk order -> y (deterministic)
-  if (!grid_sync()) return;
+  if (!grid_sync(1)) return;
   const int nn = cta < geo.NT ? (geo.NT - 1 - cta) / G + 1 : 0;
   if (nn > 0) {
     const int P = nr * geo.P2r + geo.P2s;
@@ -1565,7 +1640,9 @@ bool fused_supported(const dsmoe_layer_t* L, int B) {
   const int P2s = (I + FK2_8 - 1) / FK2_8;
   const int P2r = L->routed.fmt == DSMOE_FMT_FP8 ? P2s : (I + FK2_4 - 1) / FK2_4;
   const long long n2max = (long long)B * L->topk * NT * P2r + (long long)NT * P2s;
-  const long long span = (n2max + d.sms - 1) / d.sms;
+  // the longest phase-2 CTA span (items split by cost, routed FP4 items counting twice)
+  const long long c2 = (L->routed.fmt == DSMOE_FMT_FP4 ? 2 : 1) * (long long)B * L->topk * NT * P2r + (long long)NT * P2s;
+  const long long span = (c2 + d.sms - 1) / d.sms + 1;
   const long long T = I / 16, n1max = (long long)(B * L->topk + 1) * T * ((L->hidden / 32) / FCH);
   const long long nmax = n1max > n2max ? n1max : n2max;
   if (nmax * d.sms >= (1LL << 31) || 4LL * L->n_experts * d.sms >= (1LL << 31)) return false;
@@ -1613,7 +1690,7 @@ int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* im
   a.cnt13 = (unsigned*)(ws + f.cnt13);
   a.cnt2 = (unsigned*)(ws + f.cnt2);
   a.slot_done = (unsigned*)(ws + f.slot_done);
-  a.gbar = (unsigned*)(ws + f.gbar);
+  a.gbar = (unsigned long long*)(ws + f.gbar);
   a.status = (unsigned*)(ws + f.status);
   a.sh_idx = FMAXB * L->topk;
   a.slots = f.slots;
