@@ -570,7 +570,7 @@ extern "C" int dsmoe_moe_check(const dsmoe_layer_t* L, int B, void* workspace, s
     return cuda_status("moe_check: read status");
   if (status == 0) return DSMOE_OK;
   // a bounded wait expired: clear the scratch counters so the next call starts clean
-  cudaMemsetAsync(base + f.gbar, 0, f.rl - f.gbar, st);
+  cudaMemsetAsync(base + f.gbar, 0, f.p13 - f.gbar, st);  // counters, status and tagged router partials
   cudaStreamSynchronize(st);
   set_error("moe_decode: a bounded device wait expired (status 0x%x); workspace counters were reset", status);
   return DSMOE_ERR_TIMEOUT;

@@ -76,7 +76,7 @@ struct FusedArgs {
   float* wt;
   float* scores;
   // scratch (workspace)
-  double* rl;          // [8][E][4] router quarter-row partial logits
+  unsigned long long* rl;  // [8][E][4] router quarter-row partial logits, two epoch-tagged words each
   float* p13;          // [CTA][2 parities][FW warps][32][8] w1|w3 partials of the CTA's current tiles
   float* p2;           // [NT][slots][p2max][32][4] w2 segment partials (token columns)
   uint8_t* hq;         // [slots] h rows, e4m3 hi / lo (hq_row)
@@ -108,6 +108,7 @@ struct FPlan {
   int wcnt[FW];
   int abort;
   unsigned ar_epoch;
+  unsigned rl_epoch;  // this launch's tag on the router partials
 };
 
 // Shared-memory carve-up (host and device agree): stage ring; token rows (e4m3 hi rows [B][H], lo
@@ -319,7 +320,8 @@ __device__ __forceinline__ uint32_t ld_relaxed_u32(const unsigned* p) {
 // increased: each barrier of each launch adds G (one arrival per CTA). Barrier j of a launch is
 // complete once the counter reaches base + (j + 1) G, where base is the counter read at launch start
 // rounded down to a multiple of G: every earlier launch added a multiple of G, and fewer than G
-// arrivals of this launch can precede any CTA's read (its own is missing).
+// arrivals of this launch can precede any CTA's read (its own is missing). base / G therefore
+// numbers the launches on a workspace, which tags the router partials (see rl_store).
 // Arrive: a gpu-scope fence (the CTA's writes, ordered by the caller's __syncthreads) and a relaxed
 // add, so the arriving thread waits for no reply. Wait: relaxed polling, one acquire fence at the end.
 __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
@@ -356,40 +358,61 @@ __device__ __forceinline__ unsigned score_key(float f) {
 constexpr int FKJ = 12;  // keys per lane covering 384 experts
 
 // Top-k of one token by one warp: keys of v[e] (scores + selection bias) for e = lane + 32 j, k
-// rounds of lane-local best (the lowest j among equal keys), warp max, then the lowest index holding
-// it (ties -> lower index); the winner's lane drops it. sel[r] / selw[r] (= sc[winner]) by lane 0;
-// tot = the sum of the k selected scores.
+// rounds of lane-local best (a tree over the lane's keys, the lower j winning a tie), warp max,
+// then the lowest index holding it (ties -> lower index); the winner's lane drops it. Lane r keeps
+// round r's pick; sel[r] / selw[r] (= sc[pick]) are written by lane r after the rounds, and tot is
+// the sum of the k selected scores in round order.
 template <int NJ>
 __device__ __forceinline__ void topk_token(const float* v, const float* sc, int E, int k, int lane, int* sel,
                                            float* selw, float& tot) {
   unsigned key[NJ];
 #pragma unroll
   for (int j = 0; j < NJ; ++j) key[j] = lane + 32 * j < E ? score_key(v[lane + 32 * j]) : 0u;
-  tot = 0.f;
+  unsigned mine = 0u;
   for (int r = 0; r < k; ++r) {
-    unsigned bk = 0u;
-    int bj = 0;
+    unsigned bk[NJ];
+    int bj[NJ];
 #pragma unroll
-    for (int j = 0; j < NJ; ++j)
-      if (key[j] > bk) {  // strict: the lower index of a lane wins a tie
-        bk = key[j];
-        bj = j;
-      }
-    const unsigned m = __reduce_max_sync(0xffffffffu, bk);
-    unsigned bi = __reduce_min_sync(0xffffffffu, bk == m ? (unsigned)(lane + 32 * bj) : 0xFFFFFFFFu);
+    for (int j = 0; j < NJ; ++j) {
+      bk[j] = key[j];
+      bj[j] = j;
+    }
+#pragma unroll
+    for (int w = 1; w < NJ; w *= 2)
+#pragma unroll
+      for (int j = 0; j + w < NJ; j += 2 * w)
+        if (bk[j + w] > bk[j]) {  // strict: the lower j keeps a tie
+          bk[j] = bk[j + w];
+          bj[j] = bj[j + w];
+        }
+    const unsigned m = __reduce_max_sync(0xffffffffu, bk[0]);
+    unsigned bi = __reduce_min_sync(0xffffffffu, bk[0] == m ? (unsigned)(lane + 32 * bj[0]) : 0xFFFFFFFFu);
     if (bi >= (unsigned)E) bi = 0u;  // no expert left (k > E, rejected by the host)
+    if (lane == r) mine = bi;
     if (lane == (int)(bi & 31u)) {
 #pragma unroll
       for (int j = 0; j < NJ; ++j)
         if (j == (int)(bi >> 5)) key[j] = 0u;
     }
-    const float w = sc[bi];
-    if (lane == 0) {
-      sel[r] = (int)bi;
-      selw[r] = w;
-    }
-    tot += w;
   }
+  const float w = lane < k ? sc[mine] : 0.f;
+  if (lane < k) {
+    sel[lane] = (int)mine;
+    selw[lane] = w;
+  }
+  tot = 0.f;
+  for (int r = 0; r < k; ++r) tot += __shfl_sync(0xffffffffu, w, r);
+}
+
+// ------------------------------------------------------------------ router partials
+// A router partial (fp64) is two 8-byte words, each carrying 32 bits of the value and the launch's
+// tag in its high half. An aligned 8-byte store is single-copy atomic, so a reader that finds the
+// tag in both words has the whole value; this replaces a grid barrier between the router and the
+// plan. Tags are launch numbers + 1: a zeroed workspace never matches, and a reset zeroes the words
+// with the barrier counter.
+__device__ __forceinline__ void rl_store(unsigned long long* p, double v, unsigned ep) {
+  const unsigned long long b = (unsigned long long)__double_as_longlong(v), t = (unsigned long long)ep << 32;
+  st_ll2(p, t | (b >> 32), t | (b & 0xFFFFFFFFull));
 }
 
 // ------------------------------------------------------------------ router
@@ -397,7 +420,7 @@ __device__ __forceinline__ void topk_token(const float* v, const float* sc, int 
 // product exact in fp64 and accumulated there (rounded to fp32 once, after the four quarters).
 // x comes from shared memory (B <= FXB) or global memory; both through one generic pointer.
 __device__ void router_item(const FusedArgs& a, const uint8_t* stage, const __nv_bfloat16* xsrc, int r, int q,
-                            int lane) {
+                            int lane, unsigned ep) {
   const float4* wv = reinterpret_cast<const float4*>(stage);
   const int n4 = a.H / 16;  // float4 per quarter
   for (int b0 = 0; b0 < a.B; b0 += 2) {  // two tokens at a time (one for an odd last), four chains each
@@ -423,7 +446,7 @@ __device__ void router_item(const FusedArgs& a, const uint8_t* stage, const __nv
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const double v = warp_sum_d((acc[j][0] + acc[j][1]) + (acc[j][2] + acc[j][3]));
-        if (lane == 0) a.rl[((long long)(b0 + j) * a.E + r) * 4 + q] = v;
+        if (lane == 0) rl_store(a.rl + 2 * (((long long)(b0 + j) * a.E + r) * 4 + q), v, ep);
       }
     } else {
       double acc[4] = {0.0, 0.0, 0.0, 0.0};
@@ -437,26 +460,22 @@ __device__ void router_item(const FusedArgs& a, const uint8_t* stage, const __nv
         acc[3] = fma((double)__uint_as_float(u0.y & 0xFFFF0000u), (double)w.w, acc[3]);
       }
       const double v = warp_sum_d((acc[0] + acc[1]) + (acc[2] + acc[3]));
-      if (lane == 0) a.rl[((long long)b0 * a.E + r) * 4 + q] = v;
+      if (lane == 0) rl_store(a.rl + 2 * (((long long)b0 * a.E + r) * 4 + q), v, ep);
     }
   }
 }
 
 // ------------------------------------------------------------------ token rows
 // Token rows (bf16 in shared memory for B <= FXB, else global) -> per-token power-of-2 pre-scale
-// (amax * 2^-p in [128, 256)) -> e4m3 hi / lo rows in B-operand order (qk_off). Run by warps 1..FW-1
-// (warp 0 is at the grid barrier meanwhile), synchronised among themselves by named barrier 1.
-__device__ __forceinline__ void bar_sync_setup() {
-  asm volatile("bar.sync 1, %0;" ::"r"(FT - 32) : "memory");
-}
+// (amax * 2^-p in [128, 256)) -> e4m3 hi / lo rows in B-operand order (qk_off). All threads; ends
+// with __syncthreads.
 __device__ void setup_tokens(const FusedArgs& a, uint8_t* xq, __nv_bfloat16* xs, FPlan& pl, int lo_off) {
-  const int tid = threadIdx.x - 32, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  constexpr int NT = FT - 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nv = a.H / 8;  // uint4 per row
   for (int b = 0; b < a.B; ++b) {
     const uint4* src = reinterpret_cast<const uint4*>((a.B <= FXB ? xs : a.x) + (long long)b * a.H);
     float m = 0.f;
-    for (int v = tid; v < nv; v += NT) {
+    for (int v = tid; v < nv; v += FT) {
       const uint4 u = src[v];
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -466,10 +485,10 @@ __device__ void setup_tokens(const FusedArgs& a, uint8_t* xq, __nv_bfloat16* xs,
     m = warp_max(m);
     if (lane == 0) pl.red[warp][b] = m;
   }
-  bar_sync_setup();
+  __syncthreads();
   if (tid < a.B) {
     float m = 0.f;
-    for (int w = 1; w < FW; ++w) m = fmaxf(m, pl.red[w][tid]);
+    for (int w = 0; w < FW; ++w) m = fmaxf(m, pl.red[w][tid]);
     int p = 0;
     if (m > 0.f && m <= 3.0e38f) {
       int e2;
@@ -479,9 +498,9 @@ __device__ void setup_tokens(const FusedArgs& a, uint8_t* xq, __nv_bfloat16* xs,
     pl.xscale[tid] = ldexpf(1.0f, p);
     pl.xinv[tid] = ldexpf(1.0f, -p);
   }
-  bar_sync_setup();
+  __syncthreads();
   const int nch = a.H / 32;
-  for (int i = tid; i < a.B * nch; i += NT) {
+  for (int i = tid; i < a.B * nch; i += FT) {
     const int b = i / nch, c = i - b * nch;
     const uint4* src = reinterpret_cast<const uint4*>((a.B <= FXB ? xs : a.x) + (long long)b * a.H + 32 * c);
     const float inv = pl.xinv[b];
@@ -508,6 +527,7 @@ __device__ void setup_tokens(const FusedArgs& a, uint8_t* xq, __nv_bfloat16* xs,
       *reinterpret_cast<uint2*>(rh + lo_off + tt * 16) = make_uint2(l0 | (l1 << 16), l2 | (l3 << 16));
     }
   }
+  __syncthreads();
 }
 
 // ------------------------------------------------------------------ w1|w3
@@ -978,8 +998,9 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   auto drain = [&]() {  // every copy this warp issued lands before the CTA exits
     for (int k = kc; k < ki; ++k) mbar_wait(bar_of(k), (k >> 1) & 1, kWaitNs);
   };
-  // bounded grid barrier j (0 = A, 1 = C) by thread 0, with the CTA's __syncthreads around it;
-  // false = abandon the call. gbase: thread 0's launch base of the arrival counter.
+  // bounded grid barrier j (the launch has one, C: j = 0) by thread 0, with the CTA's
+  // __syncthreads around it; false = abandon the call. gbase: thread 0's launch base of the arrival
+  // counter.
   unsigned long long gbase = 0;
   auto grid_sync = [&](int j) -> bool {
     __syncthreads();
@@ -1004,8 +1025,9 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tid == 0) {
     gbase = grid_base(a.gbar, G);
-    // the peer exchange's epoch of this call: one past the last call's (every CTA reads it before
-    // barrier A; CTA 0 stores it back once the barrier has passed)
+    pl.rl_epoch = (unsigned)((gbase / (unsigned long long)G) % 0xFFFFFFFFull) + 1u;
+    // the peer exchange's epoch of this call: one past the last call's (every CTA reads it here;
+    // CTA 0 stores it back after grid barrier C)
     pl.ar_epoch = a.ar_world > 1 ? *(volatile unsigned*)a.ar_ctl + 1u : 0u;
     if (a.B <= FXB) {  // bf16 token rows for the router, one bulk copy
       mbar_expect_tx(xbar, (uint32_t)(a.B * a.H * 2));
@@ -1013,8 +1035,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     }
   }
   for (int e = tid; e < a.E; e += FT) emask[e] = 0u;
-  if (tid == 0)  // finished-tile counts per slot start from zero after grid barrier A
-    for (int i = cta; i < a.slots; i += G) a.slot_done[i] = 0u;
+  // (the finished-tile counts per slot were zeroed at the end of the previous launch)
 
   if (a.B <= FXB && !mbar_wait(xbar, 0, kWaitNs)) {
     if (tid == 0) {
@@ -1022,6 +1043,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       pl.abort = 1;
     }
   }
+  __syncthreads();  // pl.rl_epoch
 
   // ---- phase R: router quarter-rows
   {
@@ -1029,7 +1051,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     while (kc < nR) {
       if (!wait_full(kc)) break;
       const int i = rspan.s + warp + FW * kc;
-      router_item(a, stage_of(kc), xsrc, i >> 2, i & 3, lane);
+      router_item(a, stage_of(kc), xsrc, i >> 2, i & 3, lane, pl.rl_epoch);
       __syncwarp();
       ++kc;
       refill();
@@ -1048,23 +1070,8 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(len) : "memory");
     }
   }
-  // ---- grid barrier A (every router row of the step is done): warp 0 arrives and waits while
-  // warps 1.. convert the token rows to e4m3 hi / lo
-  __syncthreads();
-  if (warp == 0) {
-    if (tid == 0 && !pl.abort) {
-      grid_arrive(a.gbar);
-      if (!grid_wait(a.gbar, gbase + (unsigned long long)G, a.status)) {
-        atomicOr(a.status, ST_GRID);
-        pl.abort = 1;
-      } else if (cta == 0 && a.ar_world > 1) {  // every CTA read the old epoch before it arrived
-        asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(a.ar_ctl), "r"(pl.ar_epoch) : "memory");
-      }
-    }
-  } else {
-    setup_tokens(a, xq, xs, pl, lo_off);
-  }
-  __syncthreads();
+  // token rows -> e4m3 hi / lo while the other CTAs' router partials arrive
+  setup_tokens(a, xq, xs, pl, lo_off);
   if (pl.abort) {
     drain();
     return;
@@ -1076,21 +1083,48 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     float* sc_s = reinterpret_cast<float*>(ring);  // [B][E] scores
     float* bi_s = sc_s + a.B * a.E;                // [B][E] scores + selection bias
     const int n = a.B * a.E;
-    for (int i0 = tid; i0 < n; i0 += 2 * FT) {  // two logits per thread per pass, all loads first
+    // every router partial of the launch, polled until both words carry this launch's tag (no grid
+    // barrier); two logits per thread per pass, all their loads in flight together
+    const unsigned ep = pl.rl_epoch;
+    const uint64_t t0 = globaltimer_ns();
+    for (int i0 = tid; i0 < n; i0 += 2 * FT) {
       double q[2][4];
       float bias[2];
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int i = i0 + u * FT;
         if (i < n) {
-          const double* r4 = a.rl + (long long)i * 4;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) q[u][c] = ld_cg_f64(r4 + c);
           const int b = i / a.E, e = i - b * a.E;
           const bool vl = a.bias_vl != nullptr && a.image_mask != nullptr && a.image_mask[b] != 0;
           bias[u] = (vl ? a.bias_vl : a.bias)[e];
         }
       }
+      unsigned need = 0u;  // bit 4u + c: partial c of logit u still missing
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+        if (i0 + u * FT < n) need |= 0xFu << (4 * u);
+      while (need != 0u) {
+        unsigned long long w[2][4][2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            if ((need >> (4 * u + c)) & 1u) ld_ll2(a.rl + 2 * ((long long)(i0 + u * FT) * 4 + c), w[u][c][0], w[u][c][1]);
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            if (((need >> (4 * u + c)) & 1u) && (unsigned)(w[u][c][0] >> 32) == ep && (unsigned)(w[u][c][1] >> 32) == ep) {
+              q[u][c] = __longlong_as_double((long long)((w[u][c][0] << 32) | (w[u][c][1] & 0xFFFFFFFFull)));
+              need &= ~(1u << (4 * u + c));
+            }
+        if (need != 0u && (ld_relaxed_u32(a.status) != 0u || globaltimer_ns() - t0 > kWaitNs)) {
+          atomicOr(a.status, ST_GRID);
+          pl.abort = 1;
+          break;
+        }
+      }
+      if (need != 0u) break;
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int i = i0 + u * FT;
@@ -1103,6 +1137,10 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       }
     }
     __syncthreads();
+    if (pl.abort) {
+      drain();
+      return;
+    }
     if (cta == 0 && a.scores)
       for (int i = tid; i < n; i += FT) a.scores[i] = sc_s[i];
     // top-k of token b (warp b): the token's biased scores in registers (expert lane + 32 j) as
@@ -1549,7 +1587,14 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   // ---- grid barrier C, then each CTA finishes its 16-row output tiles nt = cta + G * j: the warps
   // split each tile's positions into fixed chunks summed in order, and the chunk sums are added in
   // chunk order -> y (deterministic)
-  if (!grid_sync(1)) return;
+  if (!grid_sync(0)) return;
+  // every CTA is past its phase-2 waits on the finished-tile counts: zero them for the next launch
+  // (which starts after this grid completes), and store the exchange epoch every CTA read at start
+  if (tid == 0) {
+    for (int i = cta; i < a.slots; i += G) a.slot_done[i] = 0u;
+    if (cta == 0 && a.ar_world > 1)
+      asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(a.ar_ctl), "r"(pl.ar_epoch) : "memory");
+  }
   const int nn = cta < geo.NT ? (geo.NT - 1 - cta) / G + 1 : 0;
   if (nn > 0) {
     const int P = nr * geo.P2r + geo.P2s;
@@ -1597,7 +1642,7 @@ FusedScratch fused_scratch(int H, int I_loc, int E, int B, int topk, int r_fmt) 
   f.cnt2 = o; o += al2((size_t)NT * 4);
   f.cnt13 = o; o += al2((size_t)f.slots * T * 4);
   f.slot_done = o; o += al2((size_t)f.slots * 4);
-  f.rl = o; o += al2((size_t)B * E * 4 * 8);
+  f.rl = o; o += al2((size_t)B * E * 4 * 16);
   // w1|w3 partials: the larger of the published-segment layout [slots][T][p13max][32][8] and the
   // CTA-owned-tile layout [CTA][2][FW][32][8]
   const size_t p13_seg = (size_t)f.slots * T * f.p13max * 32 * 8 * 4, p13_tm = (size_t)kMaxCtas * 2 * FW * 32 * 8 * 4;
@@ -1683,7 +1728,7 @@ int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* im
   a.idx = idx;
   a.wt = wt;
   a.scores = scores;
-  a.rl = (double*)(ws + f.rl);
+  a.rl = (unsigned long long*)(ws + f.rl);
   a.p13 = (float*)(ws + f.p13);
   a.p2 = (float*)(ws + f.p2);
   a.hq = ws + f.hq;
