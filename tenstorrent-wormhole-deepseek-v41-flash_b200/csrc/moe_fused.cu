@@ -870,7 +870,9 @@ struct Pend {
 };
 
 // TM: phase 1 with CTA-owned tiles (few tiles per CTA); otherwise published segments.
-template <int RFMT, bool TM>
+// NTX: the most n-tiles of 4 tokens a slot can need (1 for B <= 4, 2 above); with NTX = 1 the
+// two-n-tile code is not compiled in, which keeps the streaming loops small in the instruction cache.
+template <int RFMT, bool TM, int NTX>
 __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const SmemLayout SL = smem_layout(a.H, a.I_loc, a.B, a.E);
@@ -921,6 +923,22 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   auto bar_of = [&](int k) { return &full[warp * SPW + (k & 1)]; };
   TCursor ic1{0, 0};
   Cursor icP{0, 0, 0}, ic2{0, 0, 0};  // issue-side positions of the next phase-1 (TM / segments) / phase-2 item
+  // the packed bytes of phase-2 item (slot c.s, n-tile c.t, part c.p)
+  auto w2_src = [&](const Cursor& c, const uint8_t*& src, uint32_t& bytes) {
+    const W2Item w = {c.s, c.t, c.p};
+    if (w.s < nr && RFMT == DSMOE_FMT_FP4) {
+      const int c0 = 16 * w.p;
+      src = a.r_w2 + (long long)pl.expert[w.s] * a.r_w2_eb + w.nt * geo.tile2r + (long long)c0 * 544;
+      bytes = (uint32_t)(min(16, a.I_loc / 64 - c0) * 544);
+    } else {
+      const uint8_t* tile = w.s < nr ? a.r_w2 + (long long)pl.expert[w.s] * a.r_w2_eb + w.nt * geo.tile2r
+                                     : a.s_w2 + w.nt * geo.tile2s;
+      const int KC = a.I_loc / 32, c0 = 16 * w.p;
+      const int n0 = min(8, KC - c0), n1c = min(8, KC - c0 - 8);
+      src = tile + (long long)(2 * w.p) * kFp8W2Item;
+      bytes = (uint32_t)(n0 * 512 + 32 + (n0 == 8 && n1c > 0 ? n1c * 512 + 32 : 0));
+    }
+  };
   auto issue = [&](int k) {  // lane 0: item k's bytes into its stage
     const uint8_t* src;
     uint32_t bytes;
@@ -950,19 +968,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
         }
       }
     } else {
-      const W2Item w = {ic2.s, ic2.t, ic2.p};
-      if (w.s < nr && RFMT == DSMOE_FMT_FP4) {
-        const int c0 = 16 * w.p;
-        src = a.r_w2 + (long long)pl.expert[w.s] * a.r_w2_eb + w.nt * geo.tile2r + (long long)c0 * 544;
-        bytes = (uint32_t)(min(16, a.I_loc / 64 - c0) * 544);
-      } else {
-        const uint8_t* tile = w.s < nr ? a.r_w2 + (long long)pl.expert[w.s] * a.r_w2_eb + w.nt * geo.tile2r
-                                       : a.s_w2 + w.nt * geo.tile2s;
-        const int KC = a.I_loc / 32, c0 = 16 * w.p;
-        const int n0 = min(8, KC - c0), n1c = min(8, KC - c0 - 8);
-        src = tile + (long long)(2 * w.p) * kFp8W2Item;
-        bytes = (uint32_t)(n0 * 512 + 32 + (n0 == 8 && n1c > 0 ? n1c * 512 + 32 : 0));
-      }
+      w2_src(ic2, src, bytes);
     }
     // The warp's reads of this stage (its previous item) have all completed: each fed an MMA whose
     // result was consumed before this refill, so the copy cannot overtake them.
@@ -1303,7 +1309,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) acc1[j][q] = acc3[j][q] = 0.f;
       token_rows(xr, pl.tok[sl], pl.ntok[sl]);
-      const bool two = pl.ntok[sl] > 4;
+      const bool two = NTX == 2 && pl.ntok[sl] > 4;
       for (int p = pb; p < pe; ++p) {
         if (!wait_full(kc)) break;
         const uint8_t* stage = stage_of(kc);
@@ -1457,7 +1463,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
         token_rows(xr, pl.tok[s], pl.ntok[s]);
       }
       const uint8_t* stage = stage_of(kc);
-      const bool two = pl.ntok[s] > 4;
+      const bool two = NTX == 2 && pl.ntok[s] > 4;
       if (s < nr) {
         if (two)
           w13_accum<RFMT, 2>(stage, xr, p, lane, acc1, acc3);
@@ -1567,12 +1573,12 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       const uint8_t* stage = stage_of(kc);
       const int ntok = pl.ntok[w.s];
       if (w.s < nr) {
-        if (ntok > 4)
+        if (NTX == 2 && ntok > 4)
           w2_accum<RFMT, 2>(a, stage, hbase, rp, ntok, w.p, lane, tot);
         else
           w2_accum<RFMT, 1>(a, stage, hbase, rp, ntok, w.p, lane, tot);
       } else {
-        if (ntok > 4)
+        if (NTX == 2 && ntok > 4)
           w2_accum<DSMOE_FMT_FP8, 2>(a, stage, hbase, rp, ntok, w.p, lane, tot);
         else
           w2_accum<DSMOE_FMT_FP8, 1>(a, stage, hbase, rp, ntok, w.p, lane, tot);
@@ -1656,7 +1662,7 @@ FusedScratch fused_scratch(int H, int I_loc, int E, int B, int topk, int r_fmt) 
 // Per-device constants, looked up once (attribute queries cost microseconds per call).
 struct DevInfo {
   int sms = 0, optin = 0;
-  bool attr_set[4] = {false, false, false, false};
+  bool attr_set[8] = {false, false, false, false, false, false, false, false};
   int pdl = -1;  // programmatic dependent launch with the cooperative attribute: -1 untested, 0 no, 1 yes
 };
 static DevInfo g_dev[64];
@@ -1757,9 +1763,13 @@ int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* im
   // Phase 1 with CTA-owned tiles when the step has at most about two w1|w3 tiles per CTA (small
   // intermediate slices: tensor parallelism over 4-8 GPUs); published segments otherwise.
   const bool tm = (long long)(B * L->topk + 1) * (L->inter_local / 16) <= 2LL * sms;
-  void (*kern)(FusedArgs) = fi == 0 ? (tm ? moe_fused_kernel<DSMOE_FMT_FP8, true> : moe_fused_kernel<DSMOE_FMT_FP8, false>)
-                                    : (tm ? moe_fused_kernel<DSMOE_FMT_FP4, true> : moe_fused_kernel<DSMOE_FMT_FP4, false>);
-  fi += tm ? 2 : 0;
+  const bool b4 = B <= 4;
+  void (*kern)(FusedArgs) =
+      fi == 0 ? (tm ? (b4 ? moe_fused_kernel<DSMOE_FMT_FP8, true, 1> : moe_fused_kernel<DSMOE_FMT_FP8, true, 2>)
+                    : (b4 ? moe_fused_kernel<DSMOE_FMT_FP8, false, 1> : moe_fused_kernel<DSMOE_FMT_FP8, false, 2>))
+              : (tm ? (b4 ? moe_fused_kernel<DSMOE_FMT_FP4, true, 1> : moe_fused_kernel<DSMOE_FMT_FP4, true, 2>)
+                    : (b4 ? moe_fused_kernel<DSMOE_FMT_FP4, false, 1> : moe_fused_kernel<DSMOE_FMT_FP4, false, 2>));
+  fi += (tm ? 2 : 0) + (b4 ? 4 : 0);
   if (!d.attr_set[fi]) {
     // the largest dynamic shared memory any call can ask for; set once per device and format
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin) != cudaSuccess)
