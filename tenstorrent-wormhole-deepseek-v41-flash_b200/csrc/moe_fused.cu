@@ -17,9 +17,11 @@
 // tile it shares with other warps; every sum over partials runs in a fixed order derived from the
 // deterministic distribution, so results do not depend on timing.
 // Phases:
-//   R  router quarter-rows (fp64 accumulation), spread round-robin over the warps, while the shared
-//      expert's weights (routing-independent) are prefetched into L2; then grid barrier A.
-//   P  every CTA computes the same scores, top-k and slot plan (shared memory).
+//   R  router quarter-rows (fp64 accumulation), spread round-robin over the warps, each partial
+//      stored with the launch's tag; then the shared expert's weights (routing-independent) are
+//      prefetched into L2 and the token rows converted to e4m3 hi / lo.
+//   P  every CTA polls every tagged router partial (no grid barrier) and computes the same scores,
+//      top-k and slot plan (shared memory).
 //   1  w1|w3 tiles (16 rows of a slot: the routed slots, then the shared expert as the last slot),
 //      whole tiles per CTA; the CTA's warps split each tile's parts, and one warp (rotating) sums
 //      their partials in warp order: clamp / SiLU / up -> h as e4m3 hi / lo rows in the workspace,
@@ -1064,7 +1066,8 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     }
   }
   // The shared expert's weights do not depend on routing: pull them into L2 while the grid waits for
-  // barrier A and plans (each warp a slice; after the router rows, which are on the critical path).
+  // the other CTAs' router partials and plans (each warp a slice; after the router rows, which are
+  // on the critical path).
   if (lane == 0) {
     const long long b13 = (long long)geo.T * geo.tile13s, b2 = (long long)geo.NT * geo.tile2s;
     const long long piece = 16384, n13 = (b13 + piece - 1) / piece, n2p = (b2 + piece - 1) / piece;
