@@ -72,6 +72,8 @@ def parse():
                          "an N-GPU run, without its all-reduce); the output is labelled as emulated")
     ap.add_argument("--allreduce", choices=["p2p", "nccl"], default="p2p",
                     help="N > 1: sum the partials inside the layer kernel over NVLink peers (default) or with NCCL")
+    ap.add_argument("--no-stack", dest="stack_in_bench", action="store_false",
+                    help="decode mode at N >= 4: skip the 40-layer stack measurement reported beside the line")
     return ap.parse_args()
 
 
@@ -95,11 +97,31 @@ def workload_config(args, world):
 
 # ------------------------------------------------------------------ reference arm (CPU)
 
+def _synth_module():
+    """dsmoe/synth.py loaded as a plain file: the CPU arm uses its seeded quantizers (torch only) and
+    must not import the dsmoe package, whose __init__ loads the CUDA library."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("_bench_synth", os.path.join(PKG_DIR, "dsmoe", "synth.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+_CPU_LAYERS = {}
+
+
 def cpu_layers_setup(seed, pool=6):
     """Router at full size; the chosen experts' weights come from a pool of ``pool`` experts per
-    format (expert e -> pool[e % pool]); the arithmetic per step is the full layer's."""
+    format (expert e -> pool[e % pool]); the arithmetic per step is the full layer's. Built once per
+    seed and process."""
+    if seed not in _CPU_LAYERS:
+        _CPU_LAYERS[seed] = _cpu_layers_build(seed, pool)
+    return _CPU_LAYERS[seed]
+
+
+def _cpu_layers_build(seed, pool):
     import torch
-    from dsmoe import synth
+    synth = _synth_module()
     gen = torch.Generator().manual_seed(seed)
     layers = []
     for fmt in ("fp8", "fp4"):
@@ -234,6 +256,67 @@ class ClockSampler:
                 "the timed region plus one synchronous sample between two timed steps"}
 
 
+def _oracle_expert(ew):
+    from oracle import moe as OM
+    n = lambda t: t.cpu().numpy()
+    return OM.QuantExpert(ew.fmt, n(ew.w1), n(ew.s1), n(ew.w3), n(ew.s3), n(ew.w2), n(ew.s2))
+
+
+def check_parity(args, layers, refs, layer_launch, xin, yout, idx_st, comm, rank, world, dev):
+    """Outside the timed region: one call of every layer on the first token variant, checked
+    (a) at N > 1 for the same bits on every rank (all-gather), (b) on rank 0 against the oracle
+    holding the experts that call routes to (max-abs-rel and cosine of the bf16 output against the
+    fp32-dequant reference, router indices bit-exact); at N > 1 with the peer exchange, also the
+    stand-alone row all-reduce against an fp32 NCCL sum rounded to bf16 (bit-equal, same bits on every
+    rank). Every rank takes the same collective steps."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    out = {"tolerance": {"max_abs_rel": 1e-2, "cosine": 0.9999}}
+    ok = True
+    for li, nm in enumerate(layer_formats(args)):
+        layer_launch(li, 0)
+        torch.cuda.synchronize(dev)
+        y = yout[li].clone()
+        ent = {}
+        if world > 1:
+            allv = [torch.empty_like(y) for _ in range(world)]
+            dist.all_gather(allv, y)
+            ent["same_bits_all_ranks"] = all(torch.equal(allv[0], v) for v in allv)
+            ok &= ent["same_bits_all_ranks"]
+        if rank == 0:
+            from oracle import moe as OM
+            yr, ridx, _ = OM.moe_forward(refs[li], xin[li][0].float().cpu().numpy())
+            mar, cos = OM.compare(y.float().cpu().numpy(), yr)
+            ent.update(idx_match=bool(np.array_equal(idx_st[li][0].cpu().numpy(), ridx)), max_abs_rel=mar,
+                       cosine=cos, tokens=int(y.shape[0]))
+            ok &= ent["idx_match"] and mar < 1e-2 and cos > 0.9999
+        out[f"{nm}_layer"] = ent
+    if world > 1 and comm is not None:  # the attention-output all-reduce on the same comm
+        rows_ok = True
+        for Br in (1, 5, 8):
+            g = torch.Generator(device=dev).manual_seed(args.seed + 100 * Br + rank)
+            xr = torch.randn((Br, H), generator=g, device=dev).to(torch.bfloat16)
+            yr = comm.allreduce(xr)
+            comm.check()
+            ref = xr.float()
+            dist.all_reduce(ref)
+            rows_ok &= bool(torch.equal(yr, ref.to(torch.bfloat16)))
+            allv = [torch.empty_like(yr) for _ in range(world)]
+            dist.all_gather(allv, yr)
+            rows_ok &= all(torch.equal(allv[0], v) for v in allv)
+        out["allreduce_rows"] = {"equals_fp32_nccl_sum_in_bf16": rows_ok, "rows": [1, 5, 8]}
+        ok &= rows_ok
+    for m in layers:
+        m.check(args.batch)
+    if world > 1:  # rank 0's oracle verdict on every rank
+        t = torch.tensor([1 if ok else 0], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        ok = bool(t.item())
+    out["ok"] = bool(ok)
+    return out
+
+
 def measured_peak():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -261,20 +344,43 @@ def ours(args):
     if not 1 <= B <= L.MAX_DECODE_TOKENS:
         raise SystemExit(f"--batch must be in 1..{L.MAX_DECODE_TOKENS}")
 
-    # ---- resident layers (same seed on every rank: rank r packs its slice)
+    # ---- tokens first (their own generator), so that the parity step's routing is known before the
+    # experts are generated and rank 0 can keep the experts it needs for the oracle check
     t_setup = time.time()
+    pool = 256
+    toks = dsmoe.make_tokens(pool + B, H, torch.Generator(device=dev).manual_seed(args.seed + 7), device=dev)
+    n_layers = len(layer_formats(args))
+    NV = 7  # token variants: step s uses variant s % NV, so routing changes from step to step
+    xin = [[toks[(v * n_layers + li) * 7 % pool:][:B] for v in range(NV)] for li in range(n_layers)]
+    # ---- resident layers (same seed on every rank: rank r packs its slice)
     gen = torch.Generator(device=dev).manual_seed(args.seed)
-    layers = []
-    for fmt in layer_formats(args):
+    layers, refs = [], []
+    for li, fmt in enumerate(layer_formats(args)):
         NE = args.experts
         m = dsmoe.MoE(H, I, NE, TOPK, fmt, "sigmoid", ROUTE_SCALE, rank=rank, world=world, device=dev, max_tokens=B)
-        m.load_router(dsmoe.make_router(NE, H, gen, device=dev))
-        m.load_shared(dsmoe.make_expert("fp8", H, I, gen, device=dev))
+        rw = dsmoe.make_router(NE, H, gen, device=dev)
+        m.load_router(rw)
+        sh = dsmoe.make_expert("fp8", H, I, gen, device=dev)
+        m.load_shared(sh)
+        need = set()
+        if rank == 0:  # the experts the oracle routes the parity step's tokens to
+            from oracle import moe as OM
+            ridx, _, _ = OM.route(xin[li][0].float().cpu().numpy(), rw.wg.cpu().numpy(), rw.bias.cpu().numpy(), TOPK,
+                                  "sigmoid", ROUTE_SCALE)
+            need = set(ridx.ravel().tolist())
+        kept = {}
         for e in range(NE):
-            m.load_expert(e, dsmoe.make_expert(fmt, H, I, gen, device=dev))
+            ew = dsmoe.make_expert(fmt, H, I, gen, device=dev)
+            m.load_expert(e, ew)
+            if e in need:
+                kept[e] = ew.to("cpu")
+            del ew
+        if rank == 0:
+            refs.append(OM.MoELayer(rw.wg.cpu().numpy(), rw.bias.cpu().numpy(),
+                                    [_oracle_expert(kept[e]) if e in kept else None for e in range(NE)],
+                                    _oracle_expert(sh.to("cpu")), TOPK, "sigmoid", ROUTE_SCALE))
+        del rw, sh, kept
         layers.append(m)
-    pool = 256
-    toks = dsmoe.make_tokens(pool + B, H, gen, device=dev)
     torch.cuda.synchronize()
     comm = None
     if world > 1 and args.allreduce == "p2p":
@@ -286,10 +392,7 @@ def ours(args):
 
     flush = torch.empty(256 * 1024 * 1024 if args.l2_flush else 1, dtype=torch.uint8, device=dev)
     K, W = args.steps, args.warmup
-    n_layers = len(layers)
     stream = torch.cuda.current_stream(dev)
-    NV = 7  # token variants: step s uses variant s % NV, so routing changes from step to step
-    xin = [[toks[(v * n_layers + li) * 7 % pool:][:B] for v in range(NV)] for li in range(n_layers)]
     idx_st = [[torch.zeros((B, TOPK), dtype=torch.int64, device=dev) for _ in range(NV)] for _ in range(n_layers)]
     idx_log = torch.zeros((K + W, n_layers, B, TOPK), dtype=torch.int64, device=dev)
     part = [torch.empty((B, H), dtype=torch.float32, device=dev) for _ in range(n_layers)]
@@ -323,7 +426,8 @@ def ours(args):
         for li in range(n_layers):
             layer_launch(li, v)
     torch.cuda.synchronize()
-    gev = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_layers + 1)] for _ in range(NV)]
+    parity = check_parity(args, layers, refs, layer_launch, xin, yout, idx_st, comm, rank, world, dev)
+    gev =[[torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_layers + 1)] for _ in range(NV)]
     pev = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)] for _ in range(NV)]
     graphs, pgraphs = None, None
     timing_mode = ("cuda-graph replay per step: the step time from graphs with timestamp nodes at their ends only, "
@@ -446,17 +550,19 @@ def ours(args):
     achieved = dom["gbs"]
     traffic = read_traffic(dom_name, B, world)
 
-    # ---- e2e through the public API (pinned host tokens in, outputs read back every step)
-    xh = torch.empty((pool + B, H), dtype=torch.bfloat16).pin_memory()
-    xh.copy_(toks.cpu())
+    # ---- e2e through the public API: every step copies its layers' tokens from pinned host memory
+    # (one copy for the step), runs MoE.forward per layer and reads every layer's output back
+    xh = torch.empty((NV, n_layers * B, H), dtype=torch.bfloat16).pin_memory()
+    for v in range(NV):
+        for li in range(n_layers):
+            xh[v, li * B:(li + 1) * B].copy_(xin[li][v].cpu())
     yh = [torch.empty((B, H), dtype=torch.bfloat16).pin_memory() for _ in range(n_layers)]
-    xd = [torch.empty((B, H), dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
+    xd = torch.empty((n_layers * B, H), dtype=torch.bfloat16, device=dev)
 
     def e2e_step(s):
+        xd.copy_(xh[s % NV], non_blocking=True)
         for li, m in enumerate(layers):
-            j = (s * n_layers + li) * 7 % pool
-            xd[li].copy_(xh[j:j + B], non_blocking=True)
-            yh[li].copy_(m.forward(xd[li]), non_blocking=True)
+            yh[li].copy_(m.forward(xd[li * B:(li + 1) * B]), non_blocking=True)
         torch.cuda.synchronize()
 
     for s in range(W):
@@ -469,10 +575,22 @@ def ours(args):
     e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / K, dev)
     e2e_val = e2e_ms * 1e3 / (n_layers * B)
 
+    # ---- the 40-layer resident stack (config 4) when it fits: layers 2..39 hold copies of the two
+    # benchmark layers' expert bytes in their own memory, each with its own router
+    stack40 = None
+    if world >= 4 and args.stack_in_bench:
+        stack40 = stack_from_layers(args, layers, comm, dev, rank, world, 40)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = run_cpu(args, steps=1000, warmup=1, budget_s=args.cpu_budget)
         cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        by_b = {}
+        for Bc in (1, 4, 8):  # BASELINE's CPU plan: the same layer pair at batch 1, 4 and 8
+            a2 = argparse.Namespace(**{**vars(args), "batch": Bc})
+            r = run_cpu(a2, steps=1000, warmup=1, budget_s=args.cpu_budget / 3)
+            by_b[str(Bc)] = {"value": r["value"], "unit": UNIT, "ms_per_step": r["ms_per_step"], "steps": r["steps"]}
+        cpu["by_batch"] = by_b
 
     clocks = clk.summary()
     if rank == 0:
@@ -496,6 +614,9 @@ def ours(args):
             "e2e": {"value": round(e2e_val, 3), "unit": UNIT, "h2d_bytes_per_step": n_layers * B * H * 2,
                     "d2h_bytes_per_step": n_layers * B * H * 2},
             "gpu_launches": K * n_layers * launches_per_layer,
+            "parity": parity,
+            "stack40_ms_per_token": stack40["ms_per_token"] if stack40 else None,
+            "stack40": stack40,
             "timing": timing_mode,
             "clocks": clocks,
             "setup_s": round(setup_s, 1),
@@ -668,6 +789,130 @@ def sweep_mode(args):
                       "warmup": args.warmup, "experts": args.experts, "peak_hbm_gbs": peak, "rows": rows}), flush=True)
 
 
+def time_stack(layers, comm, dev, steps, warmup, seed):
+    """One decode token (B = 1) through every layer, y of a layer being x of the next, as one CUDA
+    graph (the MoE half of the reference's per-token DecodeTrace, dsv41/tt/model.py:262-446).
+    Returns (ms per token, mean us per layer of the first half, of the second half), max over ranks:
+    the time per token from a graph with events at its ends only (consecutive layer kernels overlap,
+    programmatic dependent launch), the per-layer split from a second graph with events between layers."""
+    import torch
+    import torch.distributed as dist
+    import dsmoe
+    from dsmoe import _lib as L
+    from dsmoe.tp import max_over_ranks
+    B, nl = 1, len(layers)
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    xs = [torch.empty((B, H), dtype=torch.bfloat16, device=dev) for _ in range(nl + 1)]
+    idx = [torch.empty((B, TOPK), dtype=torch.int64, device=dev) for _ in range(nl)]
+    tokpool = dsmoe.make_tokens(64, H, torch.Generator(device=dev).manual_seed(seed + 3), device=dev)
+
+    def layer(li):
+        m = layers[li]
+        st_ = torch.cuda.current_stream(dev).cuda_stream
+        if comm is not None:
+            L.call("dsmoe_moe_decode_allreduce", m._layer, comm.handle, L.ptr(xs[li]), B, None, L.ptr(xs[li + 1]),
+                   L.DTYPE_BF16, L.ptr(idx[li]), None, None, L.ptr(m.workspace), m.workspace.numel(), st_)
+        else:
+            L.call("dsmoe_moe_decode", m._layer, L.ptr(xs[li]), B, None, L.ptr(xs[li + 1]), L.DTYPE_BF16,
+                   L.ptr(idx[li]), None, None, L.ptr(m.workspace), m.workspace.numel(), st_)
+
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+    xs[0].copy_(tokpool[:B])
+    for li in range(nl):
+        layer(li)
+    torch.cuda.synchronize(dev)
+    ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(nl + 1)]
+    pe = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)]
+    g, gp = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for li in range(nl):
+            ev[li].record()
+            layer(li)
+        ev[nl].record()
+    with torch.cuda.graph(gp):
+        pe[0].record()
+        for li in range(nl):
+            layer(li)
+        pe[1].record()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    lt = [[] for _ in range(nl)]
+    st = []
+    for split in (False, True):
+        for s in range(warmup + steps):
+            xs[0].copy_(tokpool[s % 64:s % 64 + B])  # a new token each step
+            (g if split else gp).replay()
+            torch.cuda.synchronize(dev)
+            if s >= warmup:
+                if split:
+                    for li in range(nl):
+                        lt[li].append(ev[li].elapsed_time(ev[li + 1]))
+                else:
+                    st.append(pe[0].elapsed_time(pe[1]))
+    for m in layers:
+        m.check(B)
+    del g, gp  # released before any process group goes away
+    half = nl // 2
+    ms_tok = max_over_ranks(statistics.mean(st), dev)
+    a_us = max_over_ranks(statistics.mean(statistics.mean(lt[li]) for li in range(half)) * 1e3, dev)
+    b_us = max_over_ranks(statistics.mean(statistics.mean(lt[li]) for li in range(half, nl)) * 1e3, dev)
+    return ms_tok, a_us, b_us
+
+
+def stack_from_layers(args, layers, comm, dev, rank, world, n_total):
+    """Config 4 beside the decode line: ``n_total`` resident layers (first half FP8, second half FP4)
+    at B = 1. The two benchmark layers are the first FP8 and FP4 layers; every other layer gets its
+    own memory holding a copy of their expert bytes and its own seeded router, so each layer streams
+    its own weights and routes differently. Built only when it fits in every rank's free memory."""
+    import torch
+    import torch.distributed as dist
+    import dsmoe
+    by_fmt = {m.fmt: m for m in layers}
+    if set(by_fmt) != {"fp8", "fp4"}:
+        return None
+    per = {f: by_fmt[f].routed.nbytes + by_fmt[f].shared.nbytes + by_fmt[f].workspace.numel() + 16e6 for f in by_fmt}
+    need = (n_total // 2 - 1) * (per["fp8"] + per["fp4"])
+    free, _ = torch.cuda.mem_get_info(dev)
+    fits = torch.tensor([1 if need < free - 4e9 else 0], device=dev)
+    if world > 1:
+        dist.all_reduce(fits, op=dist.ReduceOp.MIN)
+    if not bool(fits.item()):
+        return {"skipped": f"{n_total} layers need {need / 1e9:.0f} GB more per GPU than is free"}
+    t0 = time.time()
+    gen = torch.Generator(device=dev).manual_seed(args.seed + 11)
+    stack = []
+    for fmt in ("fp8", "fp4"):
+        src = by_fmt[fmt]
+        for j in range(n_total // 2):
+            if j == 0:
+                stack.append(src)
+                continue
+            m = dsmoe.MoE(H, I, src.n_experts, TOPK, fmt, "sigmoid", ROUTE_SCALE, rank=rank, world=world, device=dev,
+                          max_tokens=8)
+            m.load_router(dsmoe.make_router(src.n_experts, H, gen, device=dev))
+            m.routed.w13.copy_(src.routed.w13)
+            m.routed.w2.copy_(src.routed.w2)
+            m.shared.w13.copy_(src.shared.w13)
+            m.shared.w2.copy_(src.shared.w2)
+            if comm is not None:
+                m.use_comm(comm)
+            stack.append(m)
+    torch.cuda.synchronize(dev)
+    build_s = time.time() - t0
+    ms_tok, fp8_us, fp4_us = time_stack(stack, comm, dev, max(10, args.steps), max(3, args.warmup), args.seed)
+    del stack
+    torch.cuda.empty_cache()
+    return {"ms_per_token": round(ms_tok, 4), "layers": n_total, "batch": 1,
+            "layer_us": {"fp8": round(fp8_us, 2), "fp4": round(fp4_us, 2)},
+            "weights": "layers 0 (FP8) and 20 (FP4) are the benchmark layers; the others hold copies of their expert "
+                       "bytes in their own memory, each with its own seeded router",
+            "timing": "CUDA events at the ends of one graph of all layers (y of a layer feeds the next), max over ranks",
+            "build_s": round(build_s, 1)}
+
+
 def stack_mode(args):
     """Config: the 40-layer MoE stack (layers 0-19 FP8, 20-39 FP4), decode batch 1, every layer's
     experts resident, each GPU holding 1/N of every expert, each layer ending in its all-reduce (in
@@ -678,8 +923,7 @@ def stack_mode(args):
     import torch
     import torch.distributed as dist
     import dsmoe
-    from dsmoe import _lib as L
-    from dsmoe.tp import PeerComm, env_rank_world, max_over_ranks
+    from dsmoe.tp import PeerComm, env_rank_world
     rank, local, world = env_rank_world()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -713,66 +957,8 @@ def stack_mode(args):
         for m in layers:
             m.use_comm(comm)
     setup_s = time.time() - t0
-    B = 1
     nl = len(layers)
-    xs = [torch.empty((B, H), dtype=torch.bfloat16, device=dev) for _ in range(nl + 1)]
-    idx = [torch.empty((B, TOPK), dtype=torch.int64, device=dev) for _ in range(nl)]
-    tokpool = dsmoe.make_tokens(64, H, torch.Generator(device=dev).manual_seed(args.seed + 3), device=dev)
-
-    def layer(li):
-        m = layers[li]
-        st_ = torch.cuda.current_stream(dev).cuda_stream
-        if comm is not None:
-            L.call("dsmoe_moe_decode_allreduce", m._layer, comm.handle, L.ptr(xs[li]), B, None, L.ptr(xs[li + 1]),
-                   L.DTYPE_BF16, L.ptr(idx[li]), None, None, L.ptr(m.workspace), m.workspace.numel(), st_)
-        else:
-            L.call("dsmoe_moe_decode", m._layer, L.ptr(xs[li]), B, None, L.ptr(xs[li + 1]), L.DTYPE_BF16,
-                   L.ptr(idx[li]), None, None, L.ptr(m.workspace), m.workspace.numel(), st_)
-
-    if world > 1:
-        dist.barrier()
-        torch.cuda.synchronize(dev)
-    xs[0].copy_(tokpool[:B])
-    for li in range(nl):
-        layer(li)
-    torch.cuda.synchronize(dev)
-    # two graphs of the same step: timestamps at its ends only (consecutive layer kernels overlap,
-    # programmatic dependent launch) for the time per token; timestamps between layers for the split
-    ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(nl + 1)]
-    pe = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)]
-    g, gp = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        for li in range(nl):
-            ev[li].record()
-            layer(li)
-        ev[nl].record()
-    with torch.cuda.graph(gp):
-        pe[0].record()
-        for li in range(nl):
-            layer(li)
-        pe[1].record()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    lt = [[] for _ in range(nl)]
-    st = []
-    for split in (False, True):
-        for s in range(args.warmup + args.steps):
-            xs[0].copy_(tokpool[s % 64:s % 64 + B])  # a new token each step
-            (g if split else gp).replay()
-            torch.cuda.synchronize(dev)
-            if s >= args.warmup:
-                if split:
-                    for li in range(nl):
-                        lt[li].append(ev[li].elapsed_time(ev[li + 1]))
-                else:
-                    st.append(pe[0].elapsed_time(pe[1]))
-    for m in layers:
-        m.check(B)
-    del g, gp
-    ms_tok = max_over_ranks(statistics.mean(st), dev)
-    fp8_us = max_over_ranks(statistics.mean(statistics.mean(lt[li]) for li in range(pairs)) * 1e3, dev)
-    fp4_us = max_over_ranks(statistics.mean(statistics.mean(lt[li]) for li in range(pairs, nl)) * 1e3, dev)
+    ms_tok, fp8_us, fp4_us = time_stack(layers, comm, dev, args.steps, args.warmup, args.seed)
     if rank == 0:
         print(json.dumps({
             "mode": "stack", "metric": "MoE stack ms/token (decode batch 1, all experts resident)",

@@ -164,6 +164,8 @@ DSMOE_API int dsmoe_router(const dsmoe_layer_t* layer, const void* x, int B, con
  * larger calls return DSMOE_ERR_ARG). For callers that cannot provide device scratch memory.
  * The first call on a device (with that device current) resolves the array's address and must
  * come before any stream capture; calls on one device must not overlap (they share the array).
+ * The resolved address is kept for the life of the process: it is not valid across a
+ * cudaDeviceReset or a re-created primary context of that device.
  * Same outputs as dsmoe_router. No counterpart in the reference. */
 DSMOE_API int dsmoe_router_noalloc(const dsmoe_layer_t* layer, const void* x, int B, const uint8_t* image_mask,
                                    int64_t* idx, float* wt, float* scores, void* stream);
@@ -174,7 +176,9 @@ DSMOE_API int dsmoe_router_noalloc(const dsmoe_layer_t* layer, const void* x, in
  * For B <= 8 (hidden a multiple of 512, <= 1024 experts) the layer runs as one persistent kernel
  * that keeps counters and a grid barrier in the workspace: the workspace must be zero-filled once
  * before its first use (calls leave it reusable), and calls sharing one workspace must not overlap
- * on the GPU. Every device-side wait is bounded; dsmoe_moe_check reports an expired wait.
+ * on the GPU. Every device-side wait is bounded; dsmoe_moe_check reports an expired wait. After
+ * an expired wait the workspace's status word stays set, and every later persistent call on that
+ * workspace writes NaN into y (it never leaves y unwritten) until dsmoe_moe_check resets it.
  * y: [B, H]; y_dtype DSMOE_DTYPE_BF16 (final output) or DSMOE_DTYPE_F32 (this GPU's partial sum,
  * before the all-reduce). idx/wt/scores as in dsmoe_router (each may be NULL). */
 DSMOE_API int dsmoe_moe_decode(const dsmoe_layer_t* layer, const void* x, int B, const uint8_t* image_mask,

@@ -857,6 +857,21 @@ __device__ __forceinline__ void w2_store_y(const FusedArgs& a, int nt, float4 s4
   }
 }
 
+// A call that gave up (an expired bounded wait, in this launch or one before it on the same
+// workspace: the status word stays set until dsmoe_moe_check resets it) writes NaN into the rows
+// of y this CTA owns (16-row tiles nt = cta + G j), so no caller reads stale memory as a result.
+__device__ __noinline__ void poison_y(const FusedArgs& a) {
+  const int NT = a.H / 16, G = gridDim.x;
+  for (int nt = blockIdx.x; nt < NT; nt += G)
+    for (int i = threadIdx.x; i < 16 * a.B; i += blockDim.x) {
+      const long long o = (long long)(i >> 4) * a.H + nt * 16 + (i & 15);
+      if (a.y_f32)
+        reinterpret_cast<float*>(a.y)[o] = __int_as_float(0x7FC00000);
+      else
+        reinterpret_cast<__nv_bfloat16*>(a.y)[o] = __ushort_as_bfloat16((unsigned short)0x7FC0);
+    }
+}
+
 // ------------------------------------------------------------------ peer all-reduce
 // s4: this rank's partial of output tile nt in, the sum over ranks out (exchange.cuh). False if a
 // peer's words did not arrive within kPeerWaitNs (s4 is then incomplete).
@@ -1083,6 +1098,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   setup_tokens(a, xq, xs, pl, lo_off);
   if (pl.abort) {
     drain();
+    poison_y(a);
     return;
   }
 
@@ -1148,6 +1164,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
     __syncthreads();
     if (pl.abort) {
       drain();
+      poison_y(a);
       return;
     }
     if (cta == 0 && a.scores)
@@ -1531,6 +1548,7 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   __syncthreads();
   if (pl.abort) {
     drain();
+    poison_y(a);
     return;
   }
   if (sB >= sA && !mbar_wait(hbar, 0, kWaitNs)) {
@@ -1596,7 +1614,10 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
   // ---- grid barrier C, then each CTA finishes its 16-row output tiles nt = cta + G * j: the warps
   // split each tile's positions into fixed chunks summed in order, and the chunk sums are added in
   // chunk order -> y (deterministic)
-  if (!grid_sync(0)) return;
+  if (!grid_sync(0)) {
+    poison_y(a);
+    return;
+  }
   // every CTA is past its phase-2 waits on the finished-tile counts: zero them for the next launch
   // (which starts after this grid completes), and store the exchange epoch every CTA read at start
   if (tid == 0) {
@@ -1623,6 +1644,8 @@ __global__ void __launch_bounds__(FT, 1) moe_fused_kernel(FusedArgs a) {
       }
       if (a.ar_world > 1 && !ar_tile(a, cta + G * warp, pl.ar_epoch, s4, lane)) {
         if (lane == 0) atomicOr(a.status, ST_PEER);
+        s4 = make_float4(__int_as_float(0x7FC00000), __int_as_float(0x7FC00000), __int_as_float(0x7FC00000),
+                         __int_as_float(0x7FC00000));
       }
       w2_store_y(a, cta + G * warp, s4, lane);
     }

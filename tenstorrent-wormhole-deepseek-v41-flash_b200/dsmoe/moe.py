@@ -24,15 +24,15 @@ LIMIT = 10.0  # SwiGLU clamp (dsv41/tt/moe.py:15)
 
 
 def _check_x(x: torch.Tensor, hidden: int, device) -> torch.Tensor:
-    if not x.is_cuda:
-        raise ValueError("dsmoe runs on CUDA tensors only")
-    if x.dtype != torch.bfloat16:
-        raise TypeError(f"x must be bfloat16, got {x.dtype}")
-    if x.dim() != 2 or x.shape[1] != hidden:
-        raise ValueError(f"x must be [tokens, {hidden}], got {tuple(x.shape)}")
-    if x.device != device:
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != hidden or x.device != device:
+        if not x.is_cuda:
+            raise ValueError("dsmoe runs on CUDA tensors only")
+        if x.dtype != torch.bfloat16:
+            raise TypeError(f"x must be bfloat16, got {x.dtype}")
+        if x.dim() != 2 or x.shape[1] != hidden:
+            raise ValueError(f"x must be [tokens, {hidden}], got {tuple(x.shape)}")
         raise ValueError(f"x is on {x.device}, layer on {device}")
-    return x.contiguous()
+    return x if x.is_contiguous() else x.contiguous()
 
 
 class MoE:
@@ -61,6 +61,7 @@ class MoE:
         nbytes = L.lib.dsmoe_moe_workspace_bytes(self._layer, self.max_tokens)
         # zero-filled once: the persistent kernel keeps counters and a grid barrier here
         self.workspace = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        self._ws = (self.workspace.data_ptr(), self.workspace.numel())
         self.comm = None  # tp.PeerComm: all-reduce inside the decode kernel
         self._prefill_ws: Optional[torch.Tensor] = None  # grown on demand by prefill()
 
@@ -169,19 +170,22 @@ class MoE:
         self.comm = comm
 
     def forward(self, x: torch.Tensor, image_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """y [B, H] bf16: the full layer output (partials all-reduced when world > 1)."""
+        """y [B, H] bf16: the full layer output (partials all-reduced when world > 1).
+
+        If a bounded device wait of an earlier call on this layer's workspace expired, the kernel
+        writes NaN rows instead of y until ``check()`` resets the workspace."""
         if self.world == 1:
             return self._run(x, image_mask, None, L.DTYPE_BF16)
         if self.comm is not None and self.comm.handle is not None:
             x = _check_x(x, self.hidden, self.device)
             B = x.shape[0]
             if B <= self.max_tokens and L.lib.dsmoe_moe_allreduce_supported(self._layer, self.comm.handle,
-                                                                             L.ptr(x), B):
+                                                                             x.data_ptr(), B):
                 y = torch.empty((B, self.hidden), dtype=torch.bfloat16, device=self.device)
                 mask = self._mask(image_mask, B)
-                L.call("dsmoe_moe_decode_allreduce", self._layer, self.comm.handle, L.ptr(x), B, L.ptr(mask),
-                       L.ptr(y), L.DTYPE_BF16, None, None, None, L.ptr(self.workspace), self.workspace.numel(),
-                       L.stream_of(x))
+                L.check(L.lib.dsmoe_moe_decode_allreduce(
+                    self._layer, self.comm.handle, x.data_ptr(), B, L.ptr(mask), y.data_ptr(), L.DTYPE_BF16, None,
+                    None, None, self._ws[0], self._ws[1], torch.cuda.current_stream(self.device).cuda_stream))
                 return y
         part = self._run(x, image_mask, None, L.DTYPE_F32)
         torch.distributed.all_reduce(part, group=self.group)
@@ -203,8 +207,12 @@ class MoE:
         if out is None:
             out = torch.empty((B, self.hidden), dtype=torch.float32 if y_dtype == L.DTYPE_F32 else torch.bfloat16,
                               device=self.device)
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        if B <= self.max_tokens and image_mask is None and idx is None and wt is None:  # one launch, no slicing
+            L.check(L.lib.dsmoe_moe_decode(self._layer, x.data_ptr(), B, None, out.data_ptr(), y_dtype, None, None,
+                                           None, self._ws[0], self._ws[1], st))
+            return out
         mask = self._mask(image_mask, B)
-        st = L.stream_of(x)
         for b0 in range(0, B, self.max_tokens):
             b1 = min(B, b0 + self.max_tokens)
             L.call("dsmoe_moe_decode", self._layer, L.ptr(x[b0:b1]), b1 - b0,

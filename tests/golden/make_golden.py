@@ -2,7 +2,10 @@
 
 Run in a container that has the reference checkout (it is not needed afterwards):
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref PATH]
+
+PATH is the reference checkout: by default the DSV41_REFERENCE environment variable, else a
+directory named ``reference`` beside this repository.
 
 What runs:
 * ``dsv41/ref/kernel.py`` -- the reference's plain-PyTorch operator shim -- imported from the
@@ -115,7 +118,8 @@ def ref_route(logits, bias, topk, score_func, route_scale):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("DSV41_REFERENCE")
+                    or os.path.join(os.path.dirname(ROOT), "reference"))
     args = ap.parse_args()
     K = load_kernel(args.ref, fakequant=False)
     KQ = load_kernel(args.ref, fakequant=True)

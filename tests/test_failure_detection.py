@@ -3,7 +3,9 @@ an error status the host reads, and leave the CUDA context usable.
 
 Two processes share one GPU and build a world-2 peer exchange (handles traded over a gloo group).
 Rank 1 maps its buffer and then does nothing, so rank 0's waits for rank 1's tiles run out:
-- the decode kernel's in-kernel all-reduce (5 s bound) -> MoE.check raises DsmoeError (timeout);
+- the decode kernel's in-kernel all-reduce (5 s bound) -> a call made before MoE.check returns NaN
+  rows at once, MoE.check raises DsmoeError (timeout), and after that reset the layer's own partial
+  matches the oracle again;
 - the stand-alone row all-reduce (5 s bound) -> PeerComm.check raises DsmoeError (timeout).
 Only rank 0 launches kernels, and each wait is bounded by %globaltimer; no kernel waits on another
 kernel. This is the device-side counterpart of a collective that never completes because a peer is
@@ -49,12 +51,30 @@ def _worker(rank, port, root, out_q):
             x = torch.randn((1, 1024), generator=torch.Generator().manual_seed(1)).to(torch.bfloat16).to(dev)
             t0 = time.time()
             m.forward(x)
+            torch.cuda.synchronize(dev)
+            res["decode_s"] = time.time() - t0
+            # a call made before check(): the status word is still set, so it gives up at once and
+            # returns NaN rows instead of stale memory
+            t0 = time.time()
+            y2 = m.forward(x)
+            torch.cuda.synchronize(dev)
+            res["flagged_nan"] = bool(torch.isnan(y2.float()).all().item())
+            res["flagged_s"] = time.time() - t0
             try:
                 m.check(1)
                 res["decode"] = "no error"
             except DsmoeError as e:
                 res["decode"] = "timeout" if "wait expired" in str(e) else repr(e)
-            res["decode_s"] = time.time() - t0
+            # after check() reset the workspace, the same layer computes correctly again (its fp32
+            # partial needs no peer): counters, barrier and tagged router partials were cleared
+            import numpy as np
+            from oracle import moe as OM
+            from _util import to_oracle_layer
+            part = m.partial(x).cpu().numpy()
+            ref, _, _ = OM.moe_forward(to_oracle_layer(spec), x.float().cpu().numpy(), 0, 2, return_partial=True)
+            mar, cos = OM.compare(part, ref)
+            res["after_reset"] = bool(mar < 2e-3 and cos > 0.99999 and np.isfinite(part).all())
+            m.check(1)
             t0 = time.time()
             comm_rows.allreduce(x)
             try:
@@ -96,6 +116,8 @@ def test_peer_wait_expires_and_is_reported():
         assert err is None, (rank, err)
     res = got[0][1]
     assert res["decode"] == "timeout", res
+    assert res["flagged_nan"] and res["flagged_s"] < 4.0, res
+    assert res["after_reset"], res
     assert res["rows"] == "timeout", res
     assert 4.0 < res["decode_s"] < 60.0 and 4.0 < res["rows_s"] < 60.0, res
     assert res["alive"], res

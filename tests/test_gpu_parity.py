@@ -109,8 +109,11 @@ def test_router_full_size(dev, B, sf):
     m.load_router(rw)
     idx, wt, sc = m.route(x.to(dev))
     ridx, rwt, rsc = OM.route(x.float().numpy(), rw.wg.numpy(), rw.bias.numpy(), 6, sf, 2.5)
+    # A token whose 6th and 7th biased scores lie within 1e-6 could flip between two correct
+    # orderings; on these seeds no token comes that close, so every index is compared bit-exact.
     tie = OM.near_tie(x.float().numpy(), rw.wg.numpy(), rw.bias.numpy(), 6, sf, eps=1e-6)
-    ok = (idx.cpu().numpy() == ridx).all(axis=1) | tie
+    assert int(tie.sum()) == 0, f"{int(tie.sum())} near-tie tokens: pick other seeds"
+    ok = (idx.cpu().numpy() == ridx).all(axis=1)
     assert ok.all(), f"index mismatch on tokens {np.nonzero(~ok)[0]}"
     assert np.array_equal(sc.cpu().numpy().view(np.uint32), rsc.view(np.uint32)) or \
         np.allclose(sc.cpu().numpy(), rsc, rtol=2e-7, atol=0)
@@ -222,9 +225,10 @@ def test_tp_partials_on_one_gpu(dev, fmt, world):
 
 
 @pytest.mark.parametrize("fmt", ["fp8", "fp4"])
-def test_full_size_layer_b1(dev, fmt):
-    """The benchmark layer at full size (H 5120, I 2048, 384 experts + shared), generated on the GPU;
-    the 6 routed experts actually chosen and the shared expert are checked against the oracle."""
+def test_full_size_layer(dev, fmt):
+    """The benchmark layer at full size (H 5120, I 2048, 384 experts + shared), generated on the GPU,
+    at decode batches 1, 4 and 8 (configs C1 / C2): the routed experts those tokens choose and the
+    shared expert are kept on the CPU and checked against the oracle."""
     from dsmoe import MoE, make_expert, make_router, make_tokens
     gen = torch.Generator(device=dev).manual_seed(2024)
     H, I, E = 5120, 2048, 384
@@ -234,7 +238,8 @@ def test_full_size_layer_b1(dev, fmt):
     shared = make_expert("fp8", H, I, gen, device=dev)
     m.load_shared(shared)
     kept = {}
-    x = make_tokens(2, H, gen, device=dev)
+    batches = ((0, 1), (1, 5), (5, 13))  # B = 1, 4, 8
+    x = make_tokens(13, H, gen, device=dev)
     ridx_all, _, _ = OM.route(x.float().cpu().numpy(), rw.wg.cpu().numpy(), rw.bias.cpu().numpy())
     need = set(ridx_all.ravel().tolist())
     for e in range(E):
@@ -246,14 +251,60 @@ def test_full_size_layer_b1(dev, fmt):
     from _util import to_oracle_expert
     experts = [to_oracle_expert(kept[e]) if e in kept else None for e in range(E)]
     ref = OM.MoELayer(rw.wg.cpu().numpy(), rw.bias.cpu().numpy(), experts, to_oracle_expert(shared.to("cpu")))
-    for b in range(2):
-        xb = x[b:b + 1]
+    for b0, b1 in batches:
+        xb = x[b0:b1]
         y = bf16_np(m.forward(xb))
         yr, ridx, _ = OM.moe_forward(ref, xb.float().cpu().numpy())
         idx, _, _ = m.route(xb)
         assert np.array_equal(idx.cpu().numpy(), ridx)
         mar, cos = OM.compare(y, yr)
-        assert mar < MAR_TOL and cos > COS_TOL, (b, mar, cos)
+        assert mar < MAR_TOL and cos > COS_TOL, (b1 - b0, mar, cos)
+    m.check(8)
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "fp4"])
+@pytest.mark.parametrize("B", [1, 5])
+def test_outlier_channels(dev, fmt, B):
+    """Hidden states with a few outlier channels (4 channels at 300x the rest, as real residual
+    streams have) go through the per-token power-of-two pre-scale and the e4m3 hi / lo split, and
+    drive many gate / up values into the SwiGLU clamps, so h mixes clamped and small values: the
+    layer must stay within the north-star tolerance of the oracle."""
+    spec = make_layer_cpu(fmt, 1024, 512, 32, seed=3100 + B)
+    m = to_gpu_moe(spec, device=dev)
+    ref = to_oracle_layer(spec)
+    x = torch.randn((B, 1024), generator=torch.Generator().manual_seed(31 + B))
+    x[:, [7, 300, 555, 1000]] *= 300.0
+    x = x.to(torch.bfloat16)
+    y = bf16_np(m.forward(x.to(dev)))
+    yr, ridx, _ = OM.moe_forward(ref, x.float().numpy())
+    idx, _, _ = m.route(x.to(dev))
+    assert np.array_equal(idx.cpu().numpy(), ridx)
+    mar, cos = OM.compare(y, yr)
+    assert mar < MAR_TOL and cos > COS_TOL, (mar, cos)
+    m.check(B)
+
+
+@pytest.mark.parametrize("fmt", ["fp8"])
+def test_real_width_tp8_slices(dev, fmt):
+    """The real model's intermediate width, 2304, split over 8 ranks: 288 rows per rank, so FP8
+    128-row scale blocks straddle the slices (dsv41/ref/fp4lib.c:114-115, dsv41/tt/moe.py:42-45).
+    Every rank's partial matches the oracle's partial of the same rows; the partials sum to the layer."""
+    spec = make_layer_cpu(fmt, 1024, 2304, 16, seed=2304)
+    ref = to_oracle_layer(spec)
+    x = torch.randn((3, 1024), generator=torch.Generator().manual_seed(288)).to(torch.bfloat16)
+    tot = None
+    for r in range(8):
+        m = to_gpu_moe(spec, rank=r, world=8, device=dev)
+        assert m.routed.inter_local == 288
+        p = m.partial(x.to(dev)).cpu().numpy().astype(np.float64)
+        m.check(3)
+        pr, _, _ = OM.moe_forward(ref, x.float().numpy(), r, 8, return_partial=True)
+        mar, cos = OM.compare(p, pr)
+        assert mar < 2e-3 and cos > 0.99999, (r, mar, cos)
+        tot = p if tot is None else tot + p
+    yr, _, _ = OM.moe_forward(ref, x.float().numpy())
+    mar, cos = OM.compare(F.bf16_round(tot.astype(np.float32)), yr)
+    assert mar < MAR_TOL and cos > COS_TOL
 
 
 # ------------------------------------------------------------------ kernel.py surface

@@ -4,7 +4,8 @@ NCCL over the fp32 partials, and the peer exchange inside the decode kernel (tp.
 must match the oracle's whole layer on every rank; the in-kernel sum must also be bit-identical
 across ranks, stay right over many calls sharing one comm (epochs, slot parities) and under CUDA
 graph replay; the stand-alone row all-reduce on the same comm must equal an fp32 NCCL sum rounded to
-bf16. Needs at least two GPUs; skipped otherwise."""
+bf16. Runs at world 2, 4 and 8 (at 8 every rank holds 64 of the 512 intermediate rows: half an FP8
+128-row scale block); each world is skipped when fewer GPUs are visible."""
 import datetime
 import os
 import socket
@@ -117,7 +118,7 @@ def _worker(rank, world, port, root, out_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_forward_nccl(world):
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
