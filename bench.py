@@ -35,6 +35,10 @@ UNIT = "us/layer/token"
 H, I, E, TOPK = 5120, 2048, 384, 6
 ROUTE_SCALE = 2.5
 NOMINAL_HBM_GBS = 8000.0
+DTYPE_TC = ("tcgen05: FP8 layers e4m3 x e4m3 (kind::f8f6f4, fp32 128x128 block scales on the fp32 block "
+            "accumulators), FP4 layers e2m1 x e4m3 with e8m0 32-K scales (kind::mxf8f6f4.block_scale); fp32 "
+            "accumulation; tokens as e4m3 hi/lo pairs")
+DTYPE_FRAG = "e4m3 x e4m3 -> f32 (FP8 weights as stored, FP4 expanded to e4m3; tokens as e4m3 hi/lo pairs)"
 FALLBACK_HBM_GBS = 6650.0
 
 # algorithmic bytes (weights + scales) per expert and per router (fp32 weight + bias)
@@ -72,9 +76,21 @@ def parse():
                          "an N-GPU run, without its all-reduce); the output is labelled as emulated")
     ap.add_argument("--allreduce", choices=["p2p", "nccl"], default="p2p",
                     help="N > 1: sum the partials inside the layer kernel over NVLink peers (default) or with NCCL")
+    ap.add_argument("--decode-store", choices=["tc", "frag"], default="frag",
+                    help="resident store of decode layers of 1..8 tokens: the fragment layout (mma.sync kernel, "
+                         "default) or the tensor-core layout (tcgen05 kernel)")
     ap.add_argument("--no-stack", dest="stack_in_bench", action="store_false",
                     help="decode mode at N >= 4: skip the 40-layer stack measurement reported beside the line")
     return ap.parse_args()
+
+
+DECODE_STORE = "frag"
+
+
+def decode_layouts(B):
+    """Resident store of a decode benchmark layer: ``--decode-store`` for 1..8 tokens, the fragment
+    layout for larger batches."""
+    return (DECODE_STORE,) if B <= 8 else ("frag",)
 
 
 def layer_formats(args):
@@ -357,7 +373,8 @@ def ours(args):
     layers, refs = [], []
     for li, fmt in enumerate(layer_formats(args)):
         NE = args.experts
-        m = dsmoe.MoE(H, I, NE, TOPK, fmt, "sigmoid", ROUTE_SCALE, rank=rank, world=world, device=dev, max_tokens=B)
+        m = dsmoe.MoE(H, I, NE, TOPK, fmt, "sigmoid", ROUTE_SCALE, rank=rank, world=world, device=dev, max_tokens=B,
+                      layouts=decode_layouts(B))
         rw = dsmoe.make_router(NE, H, gen, device=dev)
         m.load_router(rw)
         sh = dsmoe.make_expert("fp8", H, I, gen, device=dev)
@@ -597,7 +614,7 @@ def ours(args):
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": round(ms_per_step, 5), "higher_is_better": False, "scaling": "strong",
-            "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 (FP8 weights as stored, FP4 expanded to e4m3; tokens as e4m3 hi/lo pairs)",
+            "vs_baseline": None, "dtype": DTYPE_TC if decode_layouts(B) == ("tc",) else DTYPE_FRAG,
             "data": "synthetic (seeded N(0,0.02) weights quantized per the config, N(0,1) bf16 tokens)",
             "config": workload_config(args, world),
             "hbm_gbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9, 1),
@@ -873,7 +890,7 @@ def stack_from_layers(args, layers, comm, dev, rank, world, n_total):
     by_fmt = {m.fmt: m for m in layers}
     if set(by_fmt) != {"fp8", "fp4"}:
         return None
-    per = {f: by_fmt[f].routed.nbytes + by_fmt[f].shared.nbytes + by_fmt[f].workspace.numel() + 16e6 for f in by_fmt}
+    per = {f: by_fmt[f].nbytes + by_fmt[f].workspace.numel() + 16e6 for f in by_fmt}
     need = (n_total // 2 - 1) * (per["fp8"] + per["fp4"])
     free, _ = torch.cuda.mem_get_info(dev)
     fits = torch.tensor([1 if need < free - 4e9 else 0], device=dev)
@@ -891,12 +908,9 @@ def stack_from_layers(args, layers, comm, dev, rank, world, n_total):
                 stack.append(src)
                 continue
             m = dsmoe.MoE(H, I, src.n_experts, TOPK, fmt, "sigmoid", ROUTE_SCALE, rank=rank, world=world, device=dev,
-                          max_tokens=8)
+                          max_tokens=8, layouts=tuple(src.stores))
             m.load_router(dsmoe.make_router(src.n_experts, H, gen, device=dev))
-            m.routed.w13.copy_(src.routed.w13)
-            m.routed.w2.copy_(src.routed.w2)
-            m.shared.w13.copy_(src.shared.w13)
-            m.shared.w2.copy_(src.shared.w2)
+            m.copy_experts_from(src)
             if comm is not None:
                 m.use_comm(comm)
             stack.append(m)
@@ -945,7 +959,8 @@ def stack_mode(args):
     gen = torch.Generator(device=dev).manual_seed(args.seed)
     layers = []
     for fmt in fmts:  # each layer its own uniform-random router and experts
-        m = dsmoe.MoE(H, I, E, TOPK, fmt, "sigmoid", ROUTE_SCALE, rank=rank, world=slices, device=dev, max_tokens=8)
+        m = dsmoe.MoE(H, I, E, TOPK, fmt, "sigmoid", ROUTE_SCALE, rank=rank, world=slices, device=dev, max_tokens=8,
+                      layouts=decode_layouts(1))
         m.load_router(dsmoe.make_router(E, H, gen, device=dev))
         m.load_shared(dsmoe.make_expert("fp8", H, I, gen, device=dev))
         for e in range(E):
@@ -981,7 +996,9 @@ def stack_mode(args):
 
 
 def main():
+    global DECODE_STORE
     args = parse()
+    DECODE_STORE = args.decode_store
     if args.impl == "reference":
         reference_arm(args)
     elif args.mode == "prefill":

@@ -54,15 +54,21 @@ extern "C" {
  * the "virtual bucket" rule of dsv41/tt/moe.py:184-187 with a bucket of 8 rows. */
 #define DSMOE_SLOT_TOKENS 8
 
-/* One expert set of one layer on this GPU, in the packed resident layout written by
- * dsmoe_store_pack_expert (each expert's w1|w3 tiles, then its w2 tiles, scales co-located). */
+/* Resident store layouts. */
+#define DSMOE_LAYOUT_FRAG 0  /* packed fragment-order tiles, scales co-located (dsmoe_store_pack_expert) */
+#define DSMOE_LAYOUT_TC 1    /* checkpoint row-major weights + per-tile scale tables, read by the
+                                tensor-core decode path through TMA tensor maps (dsmoe_store_tc_pack_expert) */
+
+/* One expert set of one layer on this GPU, in one of the resident layouts. */
 typedef struct dsmoe_store {
   const uint8_t* w13;          /* [n_experts][w13_expert_bytes] */
   const uint8_t* w2;           /* [n_experts][w2_expert_bytes]  */
-  long long w13_expert_bytes;  /* dsmoe_store_expert_bytes() */
+  long long w13_expert_bytes;  /* dsmoe_store_expert_bytes() / dsmoe_store_tc_expert_bytes() */
   long long w2_expert_bytes;
   int fmt;                     /* DSMOE_FMT_* */
   int n_experts;
+  int layout;                  /* DSMOE_LAYOUT_* (0 for a zero-initialised struct) */
+  int row0;                    /* DSMOE_LAYOUT_TC: first intermediate row of this GPU's slice */
 } dsmoe_store_t;
 
 /* One MoE layer on this GPU: router, routed experts and the shared expert.
@@ -143,6 +149,25 @@ DSMOE_API int dsmoe_store_pack_expert(int fmt, int hidden, int inter, int row0, 
 DSMOE_API int dsmoe_store_unpack_expert(int fmt, int hidden, int inter, int row0, int inter_local,
                               const uint8_t* w13_src, const uint8_t* w2_src, float* w1, float* w3,
                               float* w2, void* stream);
+
+/* Tensor-core store (DSMOE_LAYOUT_TC): the expert's rows [row0, row0 + inter_local) kept in the
+ * checkpoint's own row-major order (FP8 bytes / packed FP4 bytes as stored), w2 rows padded to whole
+ * 128-K blocks, and the scales rearranged into per-tile tables; the decode kernel's TMA tensor maps
+ * tile and swizzle the weights on the fly. Same inputs and slice rules as dsmoe_store_pack_expert
+ * (hidden a multiple of 128; row0, inter_local and inter multiples of 32). Replaces the same
+ * reference packers (dsv41/tt/store.py:66-89; dsv41/ref/fp4lib.c:116-186). Destinations 1024-byte
+ * aligned; expert strides from dsmoe_store_tc_expert_bytes. */
+DSMOE_API int dsmoe_store_tc_expert_bytes(int fmt, int hidden, int inter, int row0, int inter_local,
+                                          long long* w13_bytes, long long* w2_bytes);
+DSMOE_API int dsmoe_store_tc_pack_expert(int fmt, int hidden, int inter, int row0, int inter_local,
+                                         const uint8_t* w1, const void* s1, const uint8_t* w3, const void* s3,
+                                         const uint8_t* w2, const void* s2, uint8_t* w13_dst, uint8_t* w2_dst,
+                                         void* stream);
+/* Inverse of dsmoe_store_tc_pack_expert through its scale tables, dequantized to fp32
+ * (w1, w3 [inter_local, H], w2 [H, inter_local]): proves the layout lossless. */
+DSMOE_API int dsmoe_store_tc_unpack_expert(int fmt, int hidden, int inter, int row0, int inter_local,
+                                           const uint8_t* w13_src, const uint8_t* w2_src, float* w1, float* w3,
+                                           float* w2, void* stream);
 
 /* ---- router and MoE forward --------------------------------------------------------------- */
 

@@ -365,8 +365,13 @@ static size_t fused_region(const dsmoe_layer_t* L) {
   return fused_scratch(L->hidden, L->inter_local, L->n_experts, 8, L->topk, L->routed.fmt).total;
 }
 
+static bool is_tc(const dsmoe_layer_t* L) { return L->routed.layout == DSMOE_LAYOUT_TC; }
+
+// The multi-kernel path's scratch (dsmoe_router, B > 8) starts after the persistent kernel's, which
+// stays at the front: the tensor-core path's (counters included) or the fragment path's.
 static WsLayout ws_layout_for(const dsmoe_layer_t* L, int B) {
-  return ws_layout(B, L->hidden, L->n_experts, L->topk, L->inter_local > 0 ? L->inter_local : 0, fused_region(L));
+  const size_t base = is_tc(L) ? tc_scratch(L).total : fused_region(L);
+  return ws_layout(B, L->hidden, L->n_experts, L->topk, L->inter_local > 0 ? L->inter_local : 0, base);
 }
 
 static int validate(const dsmoe_layer_t* L, int B, bool need_experts) {
@@ -389,10 +394,26 @@ static int validate(const dsmoe_layer_t* L, int B, bool need_experts) {
                 "the shared expert must be one FP8 expert");
   DSMOE_REQUIRE(R.n_experts == L->n_experts, DSMOE_ERR_ARG, "routed store holds %d experts, layer has %d",
                 R.n_experts, L->n_experts);
+  DSMOE_REQUIRE(R.layout == S.layout && (R.layout == DSMOE_LAYOUT_FRAG || R.layout == DSMOE_LAYOUT_TC),
+                DSMOE_ERR_ARG, "store layouts %d / %d", R.layout, S.layout);
+  long long e13, e2;
+  if (R.layout == DSMOE_LAYOUT_TC) {
+    DSMOE_REQUIRE(R.row0 == S.row0, DSMOE_ERR_ARG, "routed and shared slices differ");
+    DSMOE_REQUIRE(dsmoe_store_tc_expert_bytes(R.fmt, L->hidden, R.row0 + L->inter_local, R.row0, L->inter_local, &e13,
+                                              &e2) == DSMOE_OK, DSMOE_ERR_ARG, "tc store geometry");
+    DSMOE_REQUIRE(R.w13_expert_bytes == e13 && R.w2_expert_bytes == e2, DSMOE_ERR_ARG,
+                  "routed tc store strides (%lld, %lld) differ from (%lld, %lld)", R.w13_expert_bytes,
+                  R.w2_expert_bytes, e13, e2);
+    dsmoe_store_tc_expert_bytes(DSMOE_FMT_FP8, L->hidden, R.row0 + L->inter_local, R.row0, L->inter_local, &e13, &e2);
+    DSMOE_REQUIRE(S.w13_expert_bytes == e13 && S.w2_expert_bytes == e2, DSMOE_ERR_ARG, "shared tc store strides");
+    DSMOE_REQUIRE(R.w13 && R.w2 && S.w13 && S.w2, DSMOE_ERR_ARG, "store pointers are null");
+    DSMOE_REQUIRE((((uintptr_t)R.w13 | (uintptr_t)R.w2 | (uintptr_t)S.w13 | (uintptr_t)S.w2) & 1023) == 0,
+                  DSMOE_ERR_ALIGN, "tc store pointers must be 1024-byte aligned");
+    return DSMOE_OK;
+  }
   const int kq = R.fmt == DSMOE_FMT_FP8 ? 32 : 64;
   DSMOE_REQUIRE(L->inter_local > 0 && L->inter_local % kq == 0, DSMOE_ERR_ARG,
                 "inter_local %d must be a multiple of %d", L->inter_local, kq);
-  long long e13, e2;
   dsmoe_store_expert_bytes(R.fmt, L->hidden, L->inter_local, &e13, &e2);
   DSMOE_REQUIRE(R.w13_expert_bytes == e13 && R.w2_expert_bytes == e2, DSMOE_ERR_ARG,
                 "routed store strides (%lld, %lld) differ from the packed sizes (%lld, %lld)",
@@ -458,6 +479,7 @@ extern "C" int dsmoe_router(const dsmoe_layer_t* L, const void* x, int B, const 
 }
 
 static bool takes_fused(const dsmoe_layer_t* L, const void* x, int B) {
+  if (is_tc(L)) return tc_supported(L, B) && ((uintptr_t)x & 15) == 0;
   return fused_region(L) > 0 && fused_supported(L, B) && ((uintptr_t)x & 15) == 0;  // 16-byte token loads
 }
 
@@ -476,6 +498,18 @@ static int moe_decode_impl(const dsmoe_layer_t* L, const void* x, int B, const u
                 w.total);
   uint8_t* ws = (uint8_t*)workspace;
   cudaStream_t st = (cudaStream_t)stream;
+  if (is_tc(L)) {
+    DSMOE_REQUIRE(workspace_bytes >= tc_scratch(L).total, DSMOE_ERR_WORKSPACE, "moe_decode: workspace %zu < %zu",
+                  workspace_bytes, tc_scratch(L).total);
+    DSMOE_REQUIRE(takes_fused(L, x, B), DSMOE_ERR_UNSUPPORTED,
+                  "moe_decode: the tensor-core store serves batches of 1..8 (x 16-byte aligned); batch %d", B);
+    if (events) {
+      for (int i = 0; i < 3; ++i) cudaEventRecord((cudaEvent_t)events[i], st);
+    }
+    rc = launch_tc(L, x, B, image_mask, y, y_dtype, idx, wt, scores, ws, st, px);
+    if (events) cudaEventRecord((cudaEvent_t)events[3], st);
+    return rc;
+  }
   if (takes_fused(L, x, B)) return launch_fused(L, x, B, image_mask, y, y_dtype, idx, wt, scores, ws, st, events, px);
   DSMOE_REQUIRE(!px, DSMOE_ERR_UNSUPPORTED, "moe_decode_allreduce: batch %d / layer shape not on the persistent path", B);
   RouterArgs ra = router_args(L, x, B, image_mask, idx, wt, scores, ws, w);
@@ -559,9 +593,23 @@ extern "C" int dsmoe_moe_check(const dsmoe_layer_t* L, int B, void* workspace, s
   int rc = validate(L, B, true);
   if (rc) return rc;
   DSMOE_REQUIRE(workspace, DSMOE_ERR_ARG, "moe_check: workspace null");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (is_tc(L)) {
+    const TcScratch f = tc_scratch(L);
+    if (workspace_bytes < f.total) return DSMOE_OK;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return cuda_status("moe_check: synchronize");
+    uint8_t* base = (uint8_t*)workspace;
+    unsigned status = 0;
+    if (cudaMemcpy(&status, base + f.status, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+      return cuda_status("moe_check: read status");
+    if (status == 0) return DSMOE_OK;
+    cudaMemsetAsync(base, 0, f.counters_end, st);  // grid counter, status, tagged partials and counters
+    cudaStreamSynchronize(st);
+    set_error("moe_decode: a bounded device wait expired (status 0x%x); workspace counters were reset", status);
+    return DSMOE_ERR_TIMEOUT;
+  }
   const WsLayout w = ws_layout_for(L, B);
   if (fused_region(L) == 0 || workspace_bytes < w.total) return DSMOE_OK;
-  cudaStream_t st = (cudaStream_t)stream;
   if (cudaStreamSynchronize(st) != cudaSuccess) return cuda_status("moe_check: synchronize");
   const FusedScratch f = fused_scratch(L->hidden, L->inter_local, L->n_experts, 8, L->topk, L->routed.fmt);
   uint8_t* base = (uint8_t*)workspace;

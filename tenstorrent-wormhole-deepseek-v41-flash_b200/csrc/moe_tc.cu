@@ -1,0 +1,1662 @@
+// One persistent tcgen05 kernel per MoE layer for decode batches of 1..8 tokens, on the TC store
+// (tcstore.cuh: checkpoint row-major weights, tiled and swizzled by the TMA tensor engine).
+//
+// Replaces, per decode token and MoE layer, the reference's device router GEMV + host top-k +
+// host->device control write + SlotCat gather + w1/w3/shared matmuls + Q20 SwiGLU + w2 matmuls +
+// all_gather/sum all-reduce (dsv41/tt/model.py:400-442; dsv41/tt/moe.py:108-180;
+// dsv41/kernels/slot_cat.cpp; dsv41/tt/attn.py:19-21) with one launch that streams every weight
+// byte of the step once.
+//
+// Each CTA (one per SM) runs a warp-specialised pipeline over a ring of shared-memory stages, one
+// 128-K block of one 128-row weight tile per stage:
+//   warp 0      TMA producer: cp.async.bulk.tensor loads of the weight tile (FP8 bytes as stored;
+//               FP4 widened by the TMA to the padded e2m1 form the tensor core reads) and the
+//               tile's scales, L2 evict-first.
+//   warp 1      MMA issuer: tcgen05.mma M 128, N 16 (columns 0..7: e4m3 "hi" parts of the 8
+//               token slots, 8..15: their "lo" parts, x ~ hi + lo / 16), K 32 per instruction,
+//               accumulators in tensor memory. FP8: kind::f8f6f4, one accumulator per 128-K scale
+//               block (the non-MX fp32 block scales are applied by the epilogue); FP4:
+//               kind::mxf8f6f4.block_scale with A = e2m1 and the checkpoint's e8m0 scales in
+//               tensor memory, so the tensor core applies the 32-K group scales itself.
+//   warp 2      phase-2 operand producer: copies each w2 stage's B tile (the slot's SwiGLU output h
+//               as e4m3 hi / lo rows) once every w1|w3 tile of that slot is finished, grid-wide.
+//   warp 3      finisher: sums a tile's ordered partials once its last contribution lands
+//               (w1|w3 tile: clamp / SiLU / up -> h; w2 output tile: routed + shared -> y, then
+//               the NVLink peer all-reduce at N > 1).
+//   warps 4-7   epilogue: tcgen05.ld of the accumulators (one TMEM lane quadrant each), block
+//               scales, routing weights, ordered partials; FP4 scale factors into tensor memory.
+// Before the pipeline roles start, warps 1-7 compute the router (fp64-exact logits, tagged
+// partials shared through global memory), convert the tokens to the MMA's B tile and plan the slots
+// (experts chosen by any token, in expert order, then the shared expert). The producer streams the
+// shared expert's w1|w3 (routing-independent) from the first cycle, while the router runs.
+//
+// Work split: four flat sequences of stages -- shared w1|w3, routed w1|w3 (slot, 64-row tile, K
+// block), shared w2, routed w2 (slot, 128-row output tile, K block) -- each cut into contiguous
+// per-CTA ranges ("stream-K"). A run of one CTA inside one tile is a unit: its result is one
+// partial, stored at the CTA's contributor index within the tile, and the tile's last contribution
+// (a launch-tagged counter) hands the tile to that CTA's finisher, which sums the partials in
+// contributor order: results are deterministic and independent of timing. Counters carry the
+// launch number in their high half, so they never need resetting; there is no grid barrier.
+// Every wait is bounded (%globaltimer); on expiry the kernel sets a status bit, stops, lets its
+// copies land and writes NaN into its share of y.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "exchange.cuh"
+#include "tcstore.cuh"
+
+namespace dsmoe {
+namespace tc {
+
+constexpr int NW = 8, NT = NW * 32;
+constexpr int MAXB = 8;                  // tokens per call
+constexpr int MAXK = DSMOE_MAX_TOPK;
+constexpr int MAXSLOT = MAXB * MAXK + 1;  // routed slots + the shared expert
+constexpr int MAXE = 1024;
+constexpr int MAXC = 6;                  // contributors (CTAs) per tile: bounds the per-CTA range length
+constexpr int SA = 16384;                // stage A: 128 rows x 128 K (one byte per element in shared memory)
+constexpr int SB = 2048;                 // stage B (w2 phase): 16 rows x 128 K e4m3
+constexpr int STAGE = SA + SB + 1024;    // + 1 KB for the stage's scales (FP4 512 B, FP8 16 B)
+constexpr int NACC8 = 8;                 // FP8 block accumulators (16 TMEM columns each)
+constexpr uint32_t TM_ACC4 = 128, TM_SFA = 160, TM_SFB = 240, TM_COLS = 256;
+constexpr int MAXS = 20;                 // ring stages (TM_SFA + 4 MAXS <= TM_SFB)
+constexpr int QCAP = 64;                 // finisher job queue
+constexpr uint64_t kWait = 1000000000ull;
+constexpr uint64_t kPeerWait = 5000000000ull;
+
+enum : unsigned { ST_MBAR = 1u, ST_CNT = 2u, ST_PLAN = 4u, ST_PEER = 16u };
+
+struct TcArgs {
+  CUtensorMap tm_r13, tm_r2, tm_s13, tm_s2;  // routed / shared w1|w3 (4-D) and w2 (3-D) tensor maps
+  int H, I_loc, row0, E, B, topk, score_func;
+  float route_scale;
+  int r_fmt;
+  int P1, KB1, KB2, MT2, S, slot_cap;
+  const float* wg;
+  const float* bias;
+  const float* bias_vl;
+  const uint8_t* image_mask;
+  const __nv_bfloat16* x;
+  const uint8_t* r13;  // routed expert blocks (scale tables after the weights)
+  const uint8_t* r2;
+  long long r_eb13, r_eb2, r_d13, r_d2;
+  const uint8_t* s13;  // shared expert (FP8)
+  const uint8_t* s2;
+  long long s_d13, s_d2;
+  void* y;
+  int y_f32;
+  int64_t* idx;
+  float* wt;
+  float* scores;
+  // workspace
+  unsigned long long* gbar;
+  unsigned* status;
+  unsigned long long* rl;     // [8][E][4] router quarter-row partials, two tagged words each
+  unsigned long long* cnt13;  // [slot_cap][P1] tagged stage counts of w1|w3 tiles
+  unsigned long long* cnt2;   // [MT2] tagged stage counts of w2 output tiles
+  unsigned long long* sdone;  // [slot_cap] tagged finished w1|w3 tiles per slot
+  float* p13;                 // [slot_cap][P1][MAXC][128][8]
+  float* p2;                  // [MT2][slot_cap][MAXC][128][8]
+  uint8_t* hb;                // [slot_cap][KB2][2048] h as the w2 B tile (e4m3 hi / lo, SW128)
+  int ar_world, ar_rank;
+  unsigned* ar_ctl;
+  unsigned long long* ar_slots[kMaxWorld];
+};
+
+struct TcPlan {
+  int nr;                 // routed slots
+  int expert[MAXSLOT];    // slot -> routed expert
+  float w[MAXSLOT][MAXB]; // routing weight of slot s for token t (0 when t did not choose it)
+  int sel[MAXB][MAXK];
+  float selw[MAXB][MAXK];
+  float xscale[MAXB];
+  unsigned tag;           // this launch's number + 1
+  unsigned ar_epoch;
+  volatile int ready;     // plan published (producer, helpers)
+  volatile int abort;
+};
+
+// ------------------------------------------------------------------ stream-K split of a sequence
+// n stages, spt stages per tile. At most ge CTAs take part, each a contiguous range of at least
+// ceil(spt / (MAXC - 1)) stages, so at most MAXC CTAs touch any tile.
+struct Split {
+  int n, spt, ge;
+  __host__ __device__ void init(int n_, int spt_, int G) {
+    n = n_;
+    spt = spt_;
+    const int mn = (spt + MAXC - 2) / (MAXC - 1);
+    ge = n / (mn > 0 ? mn : 1);
+    ge = ge < 1 ? 1 : (ge > G ? G : ge);
+  }
+  __host__ __device__ int lo(int c) const { return c < ge ? (int)((long long)n * c / ge) : n; }
+  __host__ __device__ int hi(int c) const { return c < ge ? (int)((long long)n * (c + 1) / ge) : n; }
+  __host__ __device__ int owner(int s) const {  // the CTA whose range holds stage s
+    int c = (int)((long long)s * ge / (n > 0 ? n : 1));
+    if (c >= ge) c = ge - 1;
+    while (c + 1 < ge && lo(c + 1) <= s) ++c;
+    while (c > 0 && lo(c) > s) --c;
+    return c;
+  }
+};
+
+// The four sequences of a launch (kinds 0..3) and the position of a CTA in them.
+struct Work {
+  Split sp[4];
+  int nr;
+  __device__ void init(const TcArgs& a, int nr_) {
+    nr = nr_;
+    const int G = gridDim.x;
+    sp[0].init(a.P1 * a.KB1, a.KB1, G);
+    sp[1].init(nr * a.P1 * a.KB1, a.KB1, G);
+    sp[2].init(a.MT2 * a.KB2, a.KB2, G);
+    sp[3].init(nr * a.MT2 * a.KB2, a.KB2, G);
+  }
+};
+
+// A unit: one CTA's contiguous run of K blocks inside one tile of one sequence (kinds 0..3 =
+// shared w1|w3, routed w1|w3, shared w2, routed w2). Each CTA's units are listed once per launch in
+// shared memory; every pipeline role walks that list, stage by stage, with register-only loops.
+struct Unit {
+  short kind, slot;  // slot: routed slot, or -1 for the shared expert
+  short tile, j0;    // w1|w3: 64-row tile p; w2: output tile m; first K block
+  short n, jc;       // K blocks; this CTA's contributor index within the tile
+  int expert;        // routed expert (0 for the shared expert)
+  int tile_id;       // tile index within the kind's sequence
+};
+constexpr int UMAX = 48;  // units per kind and CTA (the splits give at most about 20)
+
+__device__ __forceinline__ int contrib_count(const Split& sp, int tile_id) {
+  return sp.owner(tile_id * sp.spt + sp.spt - 1) - sp.owner(tile_id * sp.spt) + 1;
+}
+
+// ------------------------------------------------------------------ small device helpers
+__device__ __forceinline__ unsigned long long ld_relaxed64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned ld_relaxed32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Add `add` to a counter tagged with this launch's number (a stale tag counts as 0); returns the new
+// count. Release: the caller's writes are ordered before it by the fence.
+__device__ __forceinline__ unsigned tag_add(unsigned long long* p, unsigned tag, unsigned add) {
+  fence_acq_rel_gpu();
+  unsigned long long old = ld_relaxed64(p);
+  for (int it = 0; it < 1 << 20; ++it) {
+    const unsigned cnt = (unsigned)(old >> 32) == tag ? (unsigned)old : 0u;
+    const unsigned long long nv = ((unsigned long long)tag << 32) | (cnt + add);
+    const unsigned long long prev = atomicCAS(p, old, nv);
+    if (prev == old) {
+      fence_acq_rel_gpu();
+      return cnt + add;
+    }
+    old = prev;
+  }
+  return 0u;
+}
+__device__ __forceinline__ unsigned tag_count(const unsigned long long* p, unsigned tag) {
+  const unsigned long long v = ld_relaxed64(p);
+  return (unsigned)(v >> 32) == tag ? (unsigned)v : 0u;
+}
+
+__device__ __forceinline__ float fscore_tc(float l, int func) {
+  const double d = (double)l;
+  const double s = func == DSMOE_SCORE_SIGMOID ? 1.0 / (1.0 + exp(-d)) : sqrt(d > 20.0 ? d : log1p(exp(d)));
+  return __double2float_rn(s);
+}
+__device__ __forceinline__ unsigned score_key_tc(float f) {
+  const unsigned u = f == 0.f ? 0u : __float_as_uint(f);
+  return f != f ? 0u : u ^ ((unsigned)((int)u >> 31) | 0x80000000u);
+}
+__device__ __forceinline__ void rl_put(unsigned long long* p, double v, unsigned ep) {
+  const unsigned long long b = (unsigned long long)__double_as_longlong(v), t = (unsigned long long)ep << 32;
+  st_ll2(p, t | (b >> 32), t | (b & 0xFFFFFFFFull));
+}
+__device__ __forceinline__ float silu_tc(float v) { return v / (1.0f + expf(-v)); }
+
+// Offset of 16-byte chunk cc (0..7) of row r in a K-major SW128 tile with 128-byte rows.
+__device__ __forceinline__ uint32_t sw128_off(int r, int cc) { return (uint32_t)(r * 128 + ((cc ^ (r & 7)) << 4)); }
+
+// Named barrier whose participants all get the OR of their predicates: decisions taken after it are
+// the same in every participating warp (so no warp leaves a barrier sequence the others are in).
+__device__ __forceinline__ bool bar_any(int id, int n, bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r) : "r"((uint32_t)p), "r"(id), "r"(n) : "memory");
+  return r != 0;
+}
+
+// ------------------------------------------------------------------ tcgen05 / TMA wrappers
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void mma_f8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_mx(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t sfa, uint32_t sfb,
+                                       uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+__device__ __forceinline__ void tm_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tm_st4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tma_4d(void* dst, const CUtensorMap* tm, int c0, int c1, int c2, int c3, uint64_t* bar,
+                                       uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
+// ------------------------------------------------------------------ shared-memory carve-up
+struct TcSmem {
+  size_t ring, xb, bars, plan, emask, etab, fin, queue, units, misc, total;
+};
+__host__ __device__ inline TcSmem tc_smem(int H, int S, int E) {
+  TcSmem L;
+  size_t o = 0;
+  L.ring = o;
+  o += (size_t)S * STAGE;
+  L.xb = o;  // the w1|w3 B tile; before it is built, the plan's scores ([8][E] twice)
+  const size_t xb = (size_t)(H / 128) * 2048, scr = (size_t)2 * MAXB * E * 4;
+  o += (xb > scr ? xb : scr + 15) & ~size_t(15);
+  L.bars = o;
+  o += (size_t)(3 * S + 2 * NACC8 + 5) * 8;
+  o = (o + 15) & ~size_t(15);
+  L.plan = o;
+  o += (sizeof(TcPlan) + 15) & ~size_t(15);
+  L.emask = o;
+  o += (size_t)MAXE * 4;
+  L.etab = o;
+  o += 2 * 256 * 4;  // two units' FP8 scale tables: 4 floats per 128-K block, <= 64 blocks
+  L.fin = o;
+  o += 128 * 8 * 4;
+  L.queue = o;
+  o += (QCAP + 4) * 4;
+  L.units = o;
+  o += 4 * UMAX * sizeof(Unit) + 16;
+  L.misc = o;
+  o += 64;
+  L.total = o + 1024;  // + alignment slack of the dynamic shared memory base
+  return L;
+}
+
+// ------------------------------------------------------------------ router (warps 1..7)
+// Quarter-rows of the router spread over the CTAs; each warp a quarter-row at a time: its H / 4
+// fp32 weights in registers, the dot product with every token in fp64 (each product exact), stored
+// as a tagged partial.
+__device__ __noinline__ void router_rows(const TcArgs& a, int w7, int lane, unsigned tag) {
+  const int G = gridDim.x, nq = 4 * a.E;
+  const int s0 = (int)((long long)nq * blockIdx.x / G), s1 = (int)((long long)nq * (blockIdx.x + 1) / G);
+  const int n4 = a.H / 16;  // float4 per quarter-row
+  for (int it = s0 + w7; it < s1; it += 7) {
+    const int r = it >> 2, q = it & 3;
+    const float4* wrow = reinterpret_cast<const float4*>(a.wg + (long long)r * a.H + q * (a.H / 4));
+    float4 wv[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (lane + 32 * i < n4) {
+        const uint4 u = ld_stream16(wrow + lane + 32 * i);
+        wv[i] = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w));
+      }
+    for (int b = 0; b < a.B; ++b) {
+      const __nv_bfloat16* xr = a.x + (long long)b * a.H + q * (a.H / 4);
+      double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0, acc3 = 0.0;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int f = lane + 32 * i;
+        if (f < n4) {
+          const uint2 u = *reinterpret_cast<const uint2*>(xr + 4 * f);
+          acc0 = fma((double)__uint_as_float(u.x << 16), (double)wv[i].x, acc0);
+          acc1 = fma((double)__uint_as_float(u.x & 0xFFFF0000u), (double)wv[i].y, acc1);
+          acc2 = fma((double)__uint_as_float(u.y << 16), (double)wv[i].z, acc2);
+          acc3 = fma((double)__uint_as_float(u.y & 0xFFFF0000u), (double)wv[i].w, acc3);
+        }
+      }
+      const double v = warp_sum_d((acc0 + acc1) + (acc2 + acc3));
+      if (lane == 0) rl_put(a.rl + 2 * (((long long)b * a.E + r) * 4 + q), v, tag);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ plan (warps 1..7, 224 threads)
+// Scores of every (token, expert) from the tagged router partials (polled, bounded), top-k per token
+// (ties -> lower index), weights / (sum + 1e-20) * route_scale, then the slots: the experts any token
+// chose, in expert order, each with its per-token routing weight. sc / bi: [B][E] scratch.
+__device__ __noinline__ bool make_plan(const TcArgs& a, TcPlan& pl, float* sc, float* bi, unsigned* emask, int t7) {
+  const int w7 = t7 >> 5, lane = t7 & 31;
+  const int n = a.B * a.E;
+  const unsigned tag = pl.tag;
+  const uint64_t t0 = globaltimer_ns();
+  for (int i0 = t7; i0 < n; i0 += 2 * 224) {
+    double q[2][4];
+    unsigned need = 0u;
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+      if (i0 + u * 224 < n) need |= 0xFu << (4 * u);
+    while (need != 0u) {
+      unsigned long long w[2][4][2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if ((need >> (4 * u + c)) & 1u) ld_ll2(a.rl + 2 * ((long long)(i0 + u * 224) * 4 + c), w[u][c][0], w[u][c][1]);
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (((need >> (4 * u + c)) & 1u) && (unsigned)(w[u][c][0] >> 32) == tag && (unsigned)(w[u][c][1] >> 32) == tag) {
+            q[u][c] = __longlong_as_double((long long)((w[u][c][0] << 32) | (w[u][c][1] & 0xFFFFFFFFull)));
+            need &= ~(1u << (4 * u + c));
+          }
+      if (need != 0u && (ld_relaxed32(a.status) != 0u || globaltimer_ns() - t0 > kWait)) {
+        atomicOr(a.status, ST_PLAN);
+        pl.abort = 1;
+        break;
+      }
+    }
+    if (need != 0u) break;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = i0 + u * 224;
+      if (i < n) {
+        const int b = i / a.E, e = i - b * a.E;
+        const bool vl = a.bias_vl != nullptr && a.image_mask != nullptr && a.image_mask[b] != 0;
+        const float s = fscore_tc(__double2float_rn(((q[u][0] + q[u][1]) + q[u][2]) + q[u][3]), a.score_func);
+        sc[i] = s;
+        bi[i] = s + (vl ? a.bias_vl : a.bias)[e];
+      }
+    }
+  }
+  if (bar_any(1, 224, pl.abort != 0)) return false;
+  if (blockIdx.x == 0 && a.scores)
+    for (int i = t7; i < n; i += 224) a.scores[i] = sc[i];
+  // top-k of token b by warp b % 7: keys of the lane's experts (lane + 32 j) in registers
+  for (int b = w7; b < a.B; b += 7) {
+    constexpr int NJ = MAXE / 32;
+    const float* v = bi + b * a.E;
+    unsigned key[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) key[j] = lane + 32 * j < a.E ? score_key_tc(v[lane + 32 * j]) : 0u;
+    unsigned mine = 0u;
+    for (int r = 0; r < a.topk; ++r) {
+      unsigned bk = 0u;
+      int bj = 0;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j)
+        if (key[j] > bk) {  // strict: the lower j keeps a tie
+          bk = key[j];
+          bj = j;
+        }
+      const unsigned m = __reduce_max_sync(0xffffffffu, bk);
+      unsigned bi_ = __reduce_min_sync(0xffffffffu, bk == m ? (unsigned)(lane + 32 * bj) : 0xFFFFFFFFu);
+      if (bi_ >= (unsigned)a.E) bi_ = 0u;
+      if (lane == r) mine = bi_;
+      if (lane == (int)(bi_ & 31u)) {
+#pragma unroll
+        for (int j = 0; j < NJ; ++j)
+          if (j == (int)(bi_ >> 5)) key[j] = 0u;
+      }
+    }
+    const float wv = lane < a.topk ? sc[b * a.E + mine] : 0.f;
+    float tot = 0.f;
+    for (int r = 0; r < a.topk; ++r) tot += __shfl_sync(0xffffffffu, wv, r);
+    if (lane < a.topk) {
+      const float w = wv / (tot + 1e-20f) * a.route_scale;
+      pl.sel[b][lane] = (int)mine;
+      pl.selw[b][lane] = w;
+      if (blockIdx.x == 0) {
+        if (a.idx) a.idx[b * a.topk + lane] = mine;
+        if (a.wt) a.wt[b * a.topk + lane] = w;
+      }
+    }
+  }
+  named_bar_sync(1, 224);
+  if (a.B == 1) {
+    // one token: its k distinct picks are the slots, in expert order
+    if (w7 == 0 && lane < a.topk) {
+      const int e = pl.sel[0][lane];
+      int rk = 0;
+      for (int r = 0; r < a.topk; ++r) rk += pl.sel[0][r] < e ? 1 : 0;
+      pl.expert[rk] = e;
+      pl.w[rk][0] = pl.selw[0][lane];
+      for (int t = 1; t < MAXB; ++t) pl.w[rk][t] = 0.f;
+    }
+    if (t7 == 0) pl.nr = a.topk;
+  } else {
+    for (int e = t7; e < a.E; e += 224) emask[e] = 0u;
+    named_bar_sync(1, 224);
+    for (int i = t7; i < a.B * a.topk; i += 224) atomicOr(&emask[pl.sel[i / a.topk][i % a.topk]], 1u << (i / a.topk));
+    named_bar_sync(1, 224);
+    if (w7 == 0) {  // compaction in expert order, 32 experts per step
+      int base = 0;
+      for (int e0 = 0; e0 < a.E; e0 += 32) {
+        const int e = e0 + lane;
+        const unsigned m = e < a.E ? emask[e] : 0u;
+        const unsigned bal = __ballot_sync(0xffffffffu, m != 0u);
+        if (m != 0u) {
+          const int s = base + __popc(bal & ((1u << lane) - 1u));
+          pl.expert[s] = e;
+          for (int t = 0; t < MAXB; ++t) {
+            float w = 0.f;
+            if (t < a.B && ((m >> t) & 1u))
+              for (int r = 0; r < a.topk; ++r)
+                if (pl.sel[t][r] == e) w = pl.selw[t][r];
+            pl.w[s][t] = w;
+          }
+        }
+        base += __popc(bal);
+      }
+      if (lane == 0) pl.nr = base;
+    }
+  }
+  named_bar_sync(1, 224);
+  return true;
+}
+
+// Token rows -> per-token power-of-two pre-scale (amax 2^-p in [128, 256)) -> the MMA's B tile of
+// the w1|w3 phase: [H / 128 blocks][16 rows][128 B], K-major SW128; row t < 8 holds the e4m3 "hi"
+// part of token t, row 8 + t its "lo" part (x 2^-p ~ hi + lo / 16); rows of tokens >= B are zero.
+__device__ __noinline__ void build_xb(const TcArgs& a, uint8_t* xb, TcPlan& pl, float* red, int t7) {
+  const int w7 = t7 >> 5, lane = t7 & 31;
+  for (int b = 0; b < a.B; ++b) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.x + (long long)b * a.H);
+    float m = 0.f;
+    for (int v = t7; v < a.H / 8; v += 224) {
+      const uint4 u = src[v];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h)
+        m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w[h] << 16)), fabsf(__uint_as_float(w[h] & 0xFFFF0000u))));
+    }
+    m = warp_max(m);
+    if (lane == 0) red[b * 8 + w7] = m;
+  }
+  named_bar_sync(1, 224);
+  if (t7 < a.B) {
+    float m = 0.f;
+    for (int w = 0; w < 7; ++w) m = fmaxf(m, red[t7 * 8 + w]);
+    int p = 0;
+    if (m > 0.f && m <= 3.0e38f) {
+      int e2;
+      frexpf(m, &e2);
+      p = e2 - 8;
+    }
+    pl.xscale[t7] = ldexpf(1.0f, p);
+  }
+  named_bar_sync(1, 224);
+  const int nc = a.H / 16;
+  for (int i = t7; i < MAXB * nc; i += 224) {
+    const int b = i / nc, c = i - b * nc;
+    uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
+    if (b < a.B) {
+      const float inv = 1.0f / pl.xscale[b];
+      const uint4* src = reinterpret_cast<const uint4*>(a.x + (long long)b * a.H + 16 * c);
+      const uint4 u0 = src[0], u1 = src[1];
+      const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+      for (int h = 0; h < 8; ++h) {
+        uint32_t h2, l2;
+        split2_e4m3(__uint_as_float(w[h] << 16) * inv, __uint_as_float(w[h] & 0xFFFF0000u) * inv, h2, l2);
+        hw[h >> 1] |= h2 << (16 * (h & 1));
+        lw[h >> 1] |= l2 << (16 * (h & 1));
+      }
+    }
+    uint8_t* blk = xb + (size_t)(c >> 3) * 2048;
+    *reinterpret_cast<uint4*>(blk + sw128_off(b, c & 7)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(blk + sw128_off(8 + b, c & 7)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> the tensor core's reads
+  named_bar_sync(1, 224);
+}
+
+// ------------------------------------------------------------------ pipeline state in shared memory
+struct Pipe {
+  uint8_t* ring;
+  uint8_t* xb;
+  uint64_t* full;   // [S] stage bytes landed (A, FP4 scales, and the B tile of a w2 stage)
+  uint64_t* empty;  // [S] stage consumed by the MMAs
+  uint64_t* sfr;    // [S] FP4 scale factors of the stage in tensor memory (4 epilogue warps); one phase
+                    // per FP4 stage of the slot only
+  uint64_t* accf;   // [NACC8] FP8 block accumulator complete
+  uint64_t* accr;   // [NACC8] FP8 block accumulator read (4 epilogue warps)
+  uint64_t* a4f;    // [2] FP4 unit accumulator complete
+  uint64_t* a4r;    // [2] FP4 unit accumulator read (4 epilogue warps)
+  uint64_t* mdone;  // every MMA of the CTA complete
+  int* queue;       // [QCAP] finisher jobs
+  volatile int* qtail;
+  volatile int* edone;   // the epilogue has queued its last job
+  volatile int* issued;  // stages armed by the producer
+  const Unit* units;     // [4][UMAX]
+  const int* ucnt;       // [4]
+  uint32_t tm;
+  int S;
+};
+
+__device__ __forceinline__ bool pwait(const TcArgs& a, TcPlan& pl, uint64_t* bar, uint32_t par) {
+  if (pl.abort) return false;
+  if (!mbar_wait(bar, par, kWait)) {
+    atomicOr(a.status, ST_MBAR);
+    pl.abort = 1;
+    return false;
+  }
+  return true;
+}
+
+// FP8 scale segment of K step k of block j: the 128-K block of the full expert it falls in. A
+// segment of a w2 stage may continue into the next stage when the slice starts inside a block.
+__device__ __forceinline__ int seg_key(int row0, int kind, int j, int k) {
+  return kind < 2 ? j : (row0 + 128 * j + 32 * k) >> 7;
+}
+__device__ __forceinline__ int seg_next(int row0, int kind, int j) {
+  return kind < 2 ? j + 1 : (row0 + 128 * (j + 1)) >> 7;
+}
+__device__ __forceinline__ int ksteps(int I_loc, int kind, int j) { return kind < 2 ? 4 : min(4, (I_loc - 128 * j) / 32); }
+
+// Position in a CTA's stream: (kind, unit, K block) and the ring stage g.
+struct Cur {
+  int k, u, j, g;
+  __device__ void start(const Pipe& P, int kmin) {
+    k = kmin;
+    u = 0;
+    j = 0;
+    g = 0;
+    settle(P);
+  }
+  __device__ void settle(const Pipe& P) {  // to the first block of the current or a later unit
+    while (k < 4 && u >= P.ucnt[k]) {
+      ++k;
+      u = 0;
+    }
+    if (k < 4) j = P.units[k * UMAX + u].j0;
+  }
+  __device__ bool valid() const { return k < 4; }
+  __device__ void next(const Pipe& P) {
+    const Unit& U = P.units[k * UMAX + u];
+    ++g;
+    if (++j >= U.j0 + U.n) {
+      ++u;
+      settle(P);
+    }
+  }
+};
+
+__device__ __forceinline__ void backoff() { __nanosleep(64); }
+
+// ---- warp 0, lane 0: TMA producer. One 128 x 128 tensor box per stage (plus an FP4 block's scales).
+__device__ __noinline__ void role_producer(const TcArgs& a, TcPlan& pl, const Pipe P) {
+  const uint64_t pol = l2_evict_first();
+  int slot = 0, ph = 0, g = 0;
+  for (int k = 0; k < 4 && !pl.abort; ++k) {
+    if (k == 1) {  // routed work needs the plan
+      const uint64_t t0 = globaltimer_ns();
+      while (!pl.ready && !pl.abort) {
+        backoff();
+        if (globaltimer_ns() - t0 > kWait) {
+          atomicOr(a.status, ST_PLAN);
+          pl.abort = 1;
+        }
+      }
+      if (pl.abort) break;
+      __threadfence_block();  // the routed units and the plan, written before `ready`
+    }
+    const bool w13 = k < 2, routed = k & 1;
+    const bool f4 = routed && a.r_fmt == DSMOE_FMT_FP4;
+    const CUtensorMap* tm = w13 ? (routed ? &a.tm_r13 : &a.tm_s13) : (routed ? &a.tm_r2 : &a.tm_s2);
+    const int per = w13 ? a.KB1 : a.KB2;
+    const uint32_t bytes = (f4 ? 8192u + 512u : (uint32_t)SA) + (w13 ? 0u : (uint32_t)SB);
+    const int nu = P.ucnt[k];
+    for (int u = 0; u < nu && !pl.abort; ++u) {
+      const Unit U = P.units[k * UMAX + u];
+      const uint8_t* eb = w13 ? a.r13 + (long long)U.expert * a.r_eb13 : a.r2 + (long long)U.expert * a.r_eb2;
+      for (int j = U.j0; j < U.j0 + U.n; ++j) {
+        if (g >= P.S && !pwait(a, pl, &P.empty[slot], ph ^ 1)) break;
+        uint8_t* A = P.ring + (size_t)slot * STAGE;
+        const int blk = U.tile * per + j;
+        mbar_expect_tx(&P.full[slot], bytes);
+        tma_4d(A, tm, 0, 0, blk, U.expert, &P.full[slot], pol);
+        if (f4) bulk_g2s_hint(A + SA + SB, eb + (long long)blk * (8192 + 512) + 8192, 512, &P.full[slot], pol);
+        ++g;
+        *P.issued = g;
+        if (++slot == P.S) {
+          slot = 0;
+          ph ^= 1;
+        }
+      }
+    }
+  }
+  // every copy issued lands before the CTA may exit (the MMAs consumed all of them unless aborted)
+  for (int q = max(0, g - P.S); q < g; ++q) mbar_wait(&P.full[q % P.S], (q / P.S) & 1, kWait);
+}
+
+// ---- warp 2, lane 0: the B tile (h of the slot) of every w2 stage, once the slot is finished
+__device__ __noinline__ void role_hcopy(const TcArgs& a, TcPlan& pl, const Pipe P, int SH) {
+  int g = 0;
+  for (int k = 0; k < 2; ++k)
+    for (int u = 0; u < P.ucnt[k]; ++u) g += P.units[k * UMAX + u].n;
+  int slot = g % P.S;
+  int ready_slot = -2;
+  for (int k = 2; k < 4 && !pl.abort; ++k) {
+    for (int u = 0; u < P.ucnt[k] && !pl.abort; ++u) {
+      const Unit U = P.units[k * UMAX + u];
+      const int si = U.slot < 0 ? SH : U.slot;
+      for (int j = U.j0; j < U.j0 + U.n && !pl.abort; ++j) {
+        const uint64_t t0 = globaltimer_ns();
+        while (*P.issued <= g && !pl.abort) {  // the producer has armed this stage's barrier
+          backoff();
+          if (globaltimer_ns() - t0 > kWait) {
+            atomicOr(a.status, ST_MBAR);
+            pl.abort = 1;
+          }
+        }
+        if (si != ready_slot) {
+          while (tag_count(a.sdone + si, pl.tag) < (unsigned)a.P1 && !pl.abort) {
+            backoff();
+            if (ld_relaxed32(a.status) != 0u || globaltimer_ns() - t0 > kWait) {
+              atomicOr(a.status, ST_CNT);
+              pl.abort = 1;
+            }
+          }
+          if (pl.abort) break;
+          fence_acq_rel_gpu();
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          ready_slot = si;
+        }
+        bulk_g2s(P.ring + (size_t)slot * STAGE + SA, a.hb + ((long long)si * a.KB2 + j) * 2048, SB, &P.full[slot]);
+        ++g;
+        if (++slot == P.S) slot = 0;
+      }
+    }
+  }
+}
+
+// ---- warp 1, lane 0: MMA issuer
+__device__ __noinline__ void role_mma(const TcArgs& a, TcPlan& pl, const Pipe P) {
+  constexpr uint32_t idesc8 = (1u << 4) | ((16u >> 3) << 17) | ((128u >> 4) << 24);
+  constexpr uint32_t idescx = (5u << 7) | ((16u >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24);
+  int slot = 0, ph = 0, nseg = 0, n4 = 0, cur_a = 0, cur_g = -1;
+  uint32_t c4 = 0u;  // FP4 uses per ring slot, mod 2 (bit s): the phases of its scale-factor barrier
+  bool open = false, ok = true;
+  const uint32_t ring = smem_u32(P.ring), xb = smem_u32(P.xb);
+  for (int k = 0; k < 4 && ok; ++k) {
+    const bool f4 = (k & 1) && a.r_fmt == DSMOE_FMT_FP4;
+    for (int u = 0; u < P.ucnt[k] && ok; ++u) {
+      const Unit U = P.units[k * UMAX + u];
+      for (int j = U.j0; j < U.j0 + U.n; ++j) {
+        const bool first = j == U.j0, last = j == U.j0 + U.n - 1;
+        if (!pwait(a, pl, &P.full[slot], ph)) {
+          ok = false;
+          break;
+        }
+        if (f4) {
+          if (!pwait(a, pl, &P.sfr[slot], (c4 >> slot) & 1u)) {
+            ok = false;
+            break;
+          }
+          c4 ^= 1u << slot;
+        }
+        fence_after();
+        const uint32_t aA = ring + slot * STAGE;
+        const uint32_t bB = k < 2 ? xb + j * 2048 : aA + SA;
+        const int nk = ksteps(a.I_loc, k, j);
+        if (f4) {
+          const int par = n4 & 1;
+          if (first && n4 >= 2) {
+            if (!pwait(a, pl, &P.a4r[par], ((n4 >> 1) - 1) & 1)) {
+              ok = false;
+              break;
+            }
+            fence_after();
+          }
+          for (int q = 0; q < nk; ++q)
+            mma_mx(P.tm + TM_ACC4 + 16 * par, desc_sw128(aA + 32 * q), desc_sw128(bB + 32 * q),
+                   idescx | ((uint32_t)q << 29) | ((uint32_t)q << 4), (P.tm + TM_SFA + 4 * slot) | ((uint32_t)q << 30),
+                   (P.tm + TM_SFB) | ((uint32_t)q << 30), (first && q == 0) ? 0u : 1u);
+          commit(&P.empty[slot]);
+          if (last) {
+            commit(&P.a4f[par]);
+            ++n4;
+          }
+        } else {
+          for (int q = 0; q < nk; ++q) {
+            const int gk = seg_key(a.row0, k, j, q);
+            bool fresh = false;
+            if (!open || gk != cur_g) {
+              if (open) commit(&P.accf[cur_a]);
+              cur_a = nseg % NACC8;
+              if (nseg >= NACC8) {
+                if (!pwait(a, pl, &P.accr[cur_a], ((nseg / NACC8) - 1) & 1)) {
+                  ok = false;
+                  break;
+                }
+                fence_after();
+              }
+              ++nseg;
+              cur_g = gk;
+              open = true;
+              fresh = true;
+            }
+            mma_f8(P.tm + 16 * cur_a, desc_sw128(aA + 32 * q), desc_sw128(bB + 32 * q), idesc8, fresh ? 0u : 1u);
+          }
+          if (!ok) break;
+          commit(&P.empty[slot]);
+          if (last || seg_next(a.row0, k, j) != cur_g) {  // the segment does not continue into the next stage
+            commit(&P.accf[cur_a]);
+            open = false;
+          }
+        }
+        if (++slot == P.S) {
+          slot = 0;
+          ph ^= 1;
+        }
+      }
+    }
+  }
+  commit(P.mdone);  // completes once every MMA issued above has
+  mbar_wait(P.mdone, 0, kWait);
+}
+
+// ---- warps 4-7: epilogue. Thread = accumulator row m = 32 q + lane (TMEM lane quadrant q).
+__device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pipe P, float* etab, int q, int lane,
+                                           int SH) {
+  Work wk;
+  wk.init(a, pl.nr);
+  const int m = 32 * q + lane;
+  const uint32_t trow = P.tm + ((uint32_t)(32 * q) << 16);
+  const int look = P.S > 2 ? 2 : P.S - 1;
+  const bool fp4l = a.r_fmt == DSMOE_FMT_FP4;
+  int nseg = 0, n4 = 0, cur_g = -1, seg_j = 0, seg_w = 0, unit = 0;
+  bool open = false, live = true;
+  float acc[MAXB];
+  Cur sf;  // runs ahead over the stream: FP4 scale factors of a stage into tensor memory
+  sf.start(P, 0);
+  auto store_sf = [&]() {
+    const int slot = sf.g % P.S;
+    if ((sf.k & 1) && fp4l && pwait(a, pl, &P.full[slot], (sf.g / P.S) & 1)) {
+      const uint4 v = *reinterpret_cast<const uint4*>(P.ring + (size_t)slot * STAGE + SA + SB + 16 * lane);
+      tm_st4(trow + TM_SFA + 4 * slot, v.x, v.y, v.z, v.w);
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&P.sfr[slot]);
+    }
+    sf.next(P);
+  };
+  // Control flow here is the same in all four warps whatever happens (named barriers below): after an
+  // expired wait the loop keeps walking the stream but skips the waits and the work.
+  int g = 0;
+  for (int k = 0; k < 4; ++k) {
+    const bool f4 = (k & 1) && fp4l, w13 = k < 2;
+    for (int u = 0; u < P.ucnt[k]; ++u) {
+      const Unit U = P.units[k * UMAX + u];
+      float* tab = etab + (unit & 1) * 256;
+#pragma unroll
+      for (int t = 0; t < MAXB; ++t) acc[t] = 0.f;
+      live = !bar_any(2, 128, pl.abort != 0);  // the same in all four warps: a unit after a failure is skipped
+      if (!f4 && live) {  // the unit's FP8 scale table (4 floats per block), read once by the four warps
+        const uint8_t* st = w13 ? (U.slot >= 0 ? a.r13 + (long long)U.expert * a.r_eb13 + a.r_d13 : a.s13 + a.s_d13)
+                                : (U.slot >= 0 ? a.r2 + (long long)U.expert * a.r_eb2 + a.r_d2 : a.s2 + a.s_d2);
+        const float* src = reinterpret_cast<const float*>(st) + (long long)(U.tile * (w13 ? a.KB1 : a.KB2) + U.j0) * 4;
+        for (int i = m; i < 4 * U.n; i += 128) tab[i] = __ldg(src + i);
+        named_bar_sync(2, 128);
+      }
+      for (int j = U.j0; j < U.j0 + U.n; ++j, ++g) {
+        const bool last = j == U.j0 + U.n - 1;
+        // Never wait ahead on a w2 stage while this CTA still owes w1|w3 partials: w2 stages wait for
+        // every CTA's w1|w3 work of their slot (so that wait could depend on this very epilogue).
+        while (sf.valid() && sf.g <= g + look && (sf.k < 2 || k >= 2)) store_sf();
+        if (f4) {
+          if (last) {
+            const int par = n4 & 1;
+            if (pwait(a, pl, &P.a4f[par], (n4 >> 1) & 1)) {
+              fence_after();
+              float d[16];
+              tm_ld16(trow + TM_ACC4 + 16 * par, d);
+              fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&P.a4r[par]);
+#pragma unroll
+              for (int t = 0; t < MAXB; ++t) acc[t] = d[t] + d[8 + t] * kLoInv;
+            }
+            ++n4;
+          }
+        } else {
+          // FP8: the same segments as the MMA issuer; a closed segment's accumulator times its scale
+          auto close_seg = [&]() {
+            const int slot_a = nseg % NACC8;
+            const bool got = pwait(a, pl, &P.accf[slot_a], (nseg / NACC8) & 1);
+            ++nseg;
+            if (!got) return;
+            fence_after();
+            float d[16];
+            tm_ld16(trow + 16 * slot_a, d);
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&P.accr[slot_a]);
+            float s;
+            if (w13) {  // row block of this row: w1 rows 0..63, w3 rows 64..127 of the tile
+              const int mat = m >> 6, r = 64 * U.tile + (m & 63);
+              const bool second = ((a.row0 + r) >> 7) != ((a.row0 + 64 * U.tile) >> 7);
+              s = tab[4 * (seg_j - U.j0) + 2 * mat + (second ? 1 : 0)];
+            } else {
+              s = tab[4 * (seg_j - U.j0) + seg_w];
+            }
+#pragma unroll
+            for (int t = 0; t < MAXB; ++t) acc[t] = fmaf(d[t] + d[8 + t] * kLoInv, s, acc[t]);
+          };
+          const int nk = ksteps(a.I_loc, k, j);
+          for (int qk = 0; qk < nk; ++qk) {
+            const int gk = seg_key(a.row0, k, j, qk);
+            if (!open || gk != cur_g) {
+              if (open) close_seg();
+              open = true;
+              cur_g = gk;
+              seg_j = j;  // scale table entry: .x / .y of the block where the segment starts
+              seg_w = (!w13 && gk != ((a.row0 + 128 * j) >> 7)) ? 1 : 0;
+            }
+          }
+          if (last || seg_next(a.row0, k, j) != cur_g) {
+            close_seg();
+            open = false;
+          }
+        }
+      }
+      // the unit's partial: 128 rows x 8 token columns, at this CTA's contributor index of the tile
+      const int si = U.slot < 0 ? SH : U.slot;
+      float* dst;
+      if (w13) {
+        dst = a.p13 + (((long long)si * a.P1 + U.tile) * MAXC + U.jc) * 1024;
+#pragma unroll
+        for (int t = 0; t < MAXB; ++t) acc[t] *= pl.xscale[t];
+      } else {
+        dst = a.p2 + (((long long)U.tile * a.slot_cap + si) * MAXC + U.jc) * 1024;
+#pragma unroll
+        for (int t = 0; t < MAXB; ++t) acc[t] *= (U.slot >= 0 && live ? pl.w[U.slot][t] : 1.0f) * (1.0f / kHScale);
+      }
+      if (live && !pl.abort) {
+        float4* d4 = reinterpret_cast<float4*>(dst + m * 8);
+        d4[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        if (a.B > 4) d4[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      }
+      named_bar_sync(2, 128);
+      if (m == 0 && live && !pl.abort) {
+        unsigned long long* cnt = w13 ? a.cnt13 + (long long)si * a.P1 + U.tile : a.cnt2 + U.tile;
+        const unsigned total = w13 ? (unsigned)a.KB1 : (unsigned)((pl.nr + 1) * a.KB2);
+        const unsigned c = tag_add(cnt, pl.tag, (unsigned)U.n);
+        if (c == 0u) {
+          atomicOr(a.status, ST_CNT);
+          pl.abort = 1;
+        } else if (c == total) {  // last contribution: the tile goes to this CTA's finisher
+          const int tail = *P.qtail;
+          P.queue[tail % QCAP] = w13 ? (si << 8) | U.tile : (1 << 30) | U.tile;
+          __threadfence_block();
+          *P.qtail = tail + 1;
+        }
+      }
+      ++unit;
+    }
+  }
+  named_bar_sync(2, 128);
+  if (m == 0) {
+    __threadfence_block();
+    *P.edone = 1;
+  }
+}
+
+// The units of kind k for this CTA (one thread).
+__device__ void build_units(const TcArgs& a, const TcPlan& pl, int k, Unit* out, int* cnt, unsigned* status) {
+  Split sp;
+  const int G = gridDim.x, per = k < 2 ? a.P1 : a.MT2, spt = k < 2 ? a.KB1 : a.KB2;
+  const int tiles = (k & 1) ? pl.nr * per : per;
+  sp.init(tiles * spt, spt, G);
+  const int hi = sp.hi(blockIdx.x);
+  int n = 0;
+  for (int s = sp.lo(blockIdx.x); s < hi;) {
+    const int tid_ = s / spt, t0 = tid_ * spt, e = min(t0 + spt, hi);
+    if (n == UMAX) {
+      atomicOr(status, ST_PLAN);
+      break;
+    }
+    Unit U;
+    U.kind = (short)k;
+    U.slot = (short)((k & 1) ? tid_ / per : -1);
+    U.tile = (short)((k & 1) ? tid_ - U.slot * per : tid_);
+    U.j0 = (short)(s - t0);
+    U.n = (short)(e - s);
+    U.jc = (short)(blockIdx.x - sp.owner(t0));
+    U.expert = (k & 1) ? pl.expert[U.slot] : 0;
+    U.tile_id = tid_;
+    out[n++] = U;
+    s = e;
+  }
+  *cnt = n;
+}
+
+// ---- the peer all-reduce of eight consecutive 16-row tiles (one 128-row output tile) by one warp:
+// every tile's words go to every peer first, then all tiles of all peers are polled together.
+// Same slots, epochs and words as ll_allreduce_tile (exchange.cuh), so both share one comm.
+__device__ __noinline__ bool ll_allreduce_tiles8(unsigned long long* const* slots, int W, int r, int NTt, int nt0, int B,
+                                                unsigned ep, float4 (&s4)[8], int lane, uint64_t limit_ns) {
+  bool ok = true;
+  if (2 * (lane & 3) < B) {
+    const bool one = B == 1;
+    const int par = (int)(ep & 1u);
+    for (int d = 1; d < W; ++d) {
+      const int q = r + d < W ? r + d : r + d - W;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        unsigned long long* p = slots[q] + ar_slot(par, r, W, NTt, nt0 + u, lane);
+        st_ll2(p, ll_word(s4[u].x, ep), ll_word(one ? s4[u].z : s4[u].y, ep));
+        if (!one) st_ll2(p + 2, ll_word(s4[u].z, ep), ll_word(s4[u].w, ep));
+      }
+    }
+    float4 tot[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) tot[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    // ranks in order: the same bits on every rank
+    const uint64_t t0 = globaltimer_ns();
+    for (int q = 0; q < W && ok; ++q) {
+      if (q == r) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float4 v = one ? make_float4(s4[u].x, 0.f, s4[u].z, 0.f) : s4[u];
+          tot[u].x += v.x;
+          tot[u].y += v.y;
+          tot[u].z += v.z;
+          tot[u].w += v.w;
+        }
+        continue;
+      }
+      unsigned got = 0u;
+      float4 v[8];
+      while (got != 0xFFu) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (!((got >> u) & 1u)) {
+            const unsigned long long* p = slots[r] + ar_slot(par, q, W, NTt, nt0 + u, lane);
+            unsigned long long x0, x1, x2 = 0ull, x3 = 0ull;
+            ld_ll2(p, x0, x1);
+            if (!one) ld_ll2(p + 2, x2, x3);
+            const bool here = (unsigned)(x0 >> 32) == ep && (unsigned)(x1 >> 32) == ep &&
+                              (one || ((unsigned)(x2 >> 32) == ep && (unsigned)(x3 >> 32) == ep));
+            if (here) {
+              v[u] = one ? make_float4(__uint_as_float((unsigned)x0), 0.f, __uint_as_float((unsigned)x1), 0.f)
+                         : make_float4(__uint_as_float((unsigned)x0), __uint_as_float((unsigned)x1),
+                                       __uint_as_float((unsigned)x2), __uint_as_float((unsigned)x3));
+              got |= 1u << u;
+            }
+          }
+        if (got != 0xFFu && globaltimer_ns() - t0 > limit_ns) {
+          ok = false;
+          break;
+        }
+      }
+      if (!ok) break;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        tot[u].x += v[u].x;
+        tot[u].y += v[u].y;
+        tot[u].z += v[u].z;
+        tot[u].w += v[u].w;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) s4[u] = tot[u];
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
+// ---- warp 3: finisher. Sums a finished tile's partials in contributor order.
+// Loads the sum of a tile's partials ([MAXC][128 rows][8]) for rows 4 lane .. 4 lane + 3, B tokens,
+// into fin[128][8]; the partials list is (slot index, contributor count) pairs in summation order.
+__device__ __noinline__ void sum_partials(const float* const* bases, const int* counts, int nlist, int B, float* fin, int lane) {
+  float s[4][MAXB];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int t = 0; t < MAXB; ++t) s[r][t] = 0.f;
+  for (int li = 0; li < nlist; ++li) {
+    const float* base = bases[li] + 4 * lane * 8;
+    for (int j0 = 0; j0 < counts[li]; j0 += 4) {  // four partials' loads in flight, added in order
+      float4 v[4][4][2];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj)
+        if (j0 + jj < counts[li])
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const float* p = base + (j0 + jj) * 1024 + r * 8;
+            const uint4 u = ld_cg16(p);
+            v[jj][r][0] = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w));
+            if (B > 4) {
+              const uint4 u2 = ld_cg16(p + 4);
+              v[jj][r][1] = make_float4(__uint_as_float(u2.x), __uint_as_float(u2.y), __uint_as_float(u2.z), __uint_as_float(u2.w));
+            }
+          }
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj)
+        if (j0 + jj < counts[li])
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            s[r][0] += v[jj][r][0].x;
+            s[r][1] += v[jj][r][0].y;
+            s[r][2] += v[jj][r][0].z;
+            s[r][3] += v[jj][r][0].w;
+            if (B > 4) {
+              s[r][4] += v[jj][r][1].x;
+              s[r][5] += v[jj][r][1].y;
+              s[r][6] += v[jj][r][1].z;
+              s[r][7] += v[jj][r][1].w;
+            }
+          }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int t = 0; t < MAXB; ++t) fin[(4 * lane + r) * 8 + t] = s[r][t];
+  __syncwarp();
+}
+
+// w1|w3 tile p of slot index si finished: h = SiLU(min(g, 10)) * clamp(u, +-10) (times kHScale) of its
+// 64 intermediate rows, as e4m3 hi / lo bytes into the slot's w2 B tile; then the slot's count.
+__device__ __noinline__ void finish_w13(const TcArgs& a, TcPlan& pl, const Work& wk, int si, int p, int SH, float* fin, int lane) {
+  const int kind = si == SH ? 0 : 1;
+  const int tile_id = kind == 0 ? p : si * a.P1 + p;
+  const float* base = a.p13 + ((long long)si * a.P1 + p) * MAXC * 1024;
+  const int nc = contrib_count(wk.sp[kind], tile_id);
+  sum_partials(&base, &nc, 1, a.B, fin, lane);
+  // h for rows r = lane, lane + 32 (gate row r, up row 64 + r), every token; into fin rows 0..63
+  float h[2][MAXB];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int t = 0; t < MAXB; ++t) {
+      const int r = lane + 32 * i;
+      const float gv = fminf(fin[r * 8 + t], 10.0f);
+      const float uv = fminf(fmaxf(fin[(64 + r) * 8 + t], -10.0f), 10.0f);
+      h[i][t] = t < a.B ? silu_tc(gv) * uv * kHScale : 0.f;
+    }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int t = 0; t < MAXB; ++t) fin[t * 64 + lane + 32 * i] = h[i][t];  // [token][row]
+  __syncwarp();
+  // 16 B pieces: (B-tile row n = hi / lo of token n % 8, chunk of 16 K) -> SW128 position
+  uint8_t* blk = a.hb + ((long long)si * a.KB2 + (p >> 1)) * 2048;
+  const bool last_half = p == a.P1 - 1 && (p & 1) == 0;  // the block's second half lies past the slice: zero it
+  for (int it = lane; it < 64 + (last_half ? 64 : 0); it += 32) {
+    const int n = (it & 63) >> 2, c4 = it & 3;
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if (it < 64) {
+      const int t = n & 7;
+      const bool lo = n >= 8;
+      const float* v = fin + t * 64 + 16 * c4;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        uint32_t h2, l2;
+        split2_e4m3(v[2 * q], v[2 * q + 1], h2, l2);
+        w[q >> 1] |= (lo ? l2 : h2) << (16 * (q & 1));
+      }
+    }
+    const int cc = (it < 64 ? (p & 1) * 4 : 4) + c4;
+    *reinterpret_cast<uint4*>(blk + sw128_off(n, cc)) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  __syncwarp();
+  if (lane == 0 && tag_add(a.sdone + si, pl.tag, 1u) == 0u) {
+    atomicOr(a.status, ST_CNT);
+    pl.abort = 1;
+  }
+  __syncwarp();
+}
+
+// Output tile m finished: y rows [128 m, 128 m + 128) = sum over the routed slots (in order) and the
+// shared expert of their partials; at N > 1 summed over the ranks through the peer exchange.
+__device__ __noinline__ void finish_w2(const TcArgs& a, TcPlan& pl, const Work& wk, int m, int SH, float* fin, int lane) {
+  const int nl = pl.nr + 1;
+  bool ok = true;
+  // partials of slots in order, in batches that fit the local lists
+  float acc[4][MAXB];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int t = 0; t < MAXB; ++t) acc[r][t] = 0.f;
+  for (int l0 = 0; l0 < nl; l0 += 8) {
+    const float* bases[8];
+    int counts[8];
+    const int nb = min(8, nl - l0);
+    for (int i = 0; i < nb; ++i) {
+      const int s = l0 + i;
+      const int si = s < pl.nr ? s : SH;
+      const int kind = s < pl.nr ? 3 : 2;
+      const int tile_id = s < pl.nr ? s * a.MT2 + m : m;
+      bases[i] = a.p2 + ((long long)m * a.slot_cap + si) * MAXC * 1024;
+      counts[i] = contrib_count(wk.sp[kind], tile_id);
+    }
+    sum_partials(bases, counts, nb, a.B, fin, lane);
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int t = 0; t < MAXB; ++t) acc[r][t] += fin[(4 * lane + r) * 8 + t];
+    __syncwarp();
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int t = 0; t < MAXB; ++t) fin[(4 * lane + r) * 8 + t] = acc[r][t];
+  __syncwarp();
+  if (a.ar_world > 1) {
+    // eight 16-row tiles through the exchange: every tile's words sent first, then all polled
+    const int t0 = 2 * (lane & 3);
+    float4 s4[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int r = 16 * u + (lane >> 2);
+      s4[u] = make_float4(fin[r * 8 + t0], fin[r * 8 + t0 + 1], fin[(r + 8) * 8 + t0], fin[(r + 8) * 8 + t0 + 1]);
+    }
+    ok = ll_allreduce_tiles8(a.ar_slots, a.ar_world, a.ar_rank, a.H / 16, 8 * m, a.B, pl.ar_epoch, s4, lane, kPeerWait);
+    __syncwarp();
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int r = 16 * u + (lane >> 2);
+      if (t0 < a.B) {
+        fin[r * 8 + t0] = s4[u].x;
+        fin[r * 8 + t0 + 1] = s4[u].y;
+        fin[(r + 8) * 8 + t0] = s4[u].z;
+        fin[(r + 8) * 8 + t0 + 1] = s4[u].w;
+      }
+    }
+    __syncwarp();
+    if (!ok && lane == 0) atomicOr(a.status, ST_PEER);
+  }
+  // y rows 4 lane .. 4 lane + 3 of every token
+  for (int t = 0; t < a.B; ++t) {
+    float v[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) v[r] = ok ? fin[(4 * lane + r) * 8 + t] : __int_as_float(0x7FC00000);
+    const long long o = (long long)t * a.H + 128 * m + 4 * lane;
+    if (a.y_f32) {
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + o) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+      const __nv_bfloat162 p0 = __floats2bfloat162_rn(v[0], v[1]), p1 = __floats2bfloat162_rn(v[2], v[3]);
+      *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.y) + o) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&p0), *reinterpret_cast<const uint32_t*>(&p1));
+    }
+  }
+  __syncwarp();
+}
+
+__device__ __noinline__ void role_finisher(const TcArgs& a, TcPlan& pl, Pipe& P, float* fin, int lane, int SH) {
+  Work wk;
+  wk.init(a, pl.nr);
+  int head = 0;
+  uint64_t t0 = globaltimer_ns();
+  while (true) {
+    int job = -1;
+    if (lane == 0) {
+      while (true) {
+        if (head < *P.qtail) {
+          job = P.queue[head % QCAP];
+          break;
+        }
+        if (*P.edone && head >= *P.qtail) break;
+        if (pl.abort) break;
+        backoff();
+        if (globaltimer_ns() - t0 > 4 * kWait) {  // the epilogue has not finished in time
+          atomicOr(a.status, ST_CNT);
+          pl.abort = 1;
+          break;
+        }
+      }
+    }
+    job = __shfl_sync(0xffffffffu, job, 0);
+    if (job < 0) break;
+    ++head;
+    t0 = globaltimer_ns();
+    fence_acq_rel_gpu();  // acquire: the other CTAs' partials
+    if (job & (1 << 30))
+      finish_w2(a, pl, wk, job & 0xFFFF, SH, fin, lane);
+    else
+      finish_w13(a, pl, wk, job >> 8, job & 0xFF, SH, fin, lane);
+  }
+}
+
+// ------------------------------------------------------------------ the kernel
+__global__ void __launch_bounds__(NT, 1) moe_tc_kernel(const __grid_constant__ TcArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const TcSmem L = tc_smem(a.H, a.S, a.E);
+  Pipe P;
+  P.S = a.S;
+  P.ring = sm + L.ring;
+  P.xb = sm + L.xb;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.bars);
+  P.full = bars;
+  P.empty = bars + a.S;
+  P.sfr = bars + 2 * a.S;
+  P.accf = bars + 3 * a.S;
+  P.accr = P.accf + NACC8;
+  P.a4f = P.accr + NACC8;
+  P.a4r = P.a4f + 2;
+  P.mdone = P.a4r + 2;
+  TcPlan& pl = *reinterpret_cast<TcPlan*>(sm + L.plan);
+  unsigned* emask = reinterpret_cast<unsigned*>(sm + L.emask);
+  float* etab = reinterpret_cast<float*>(sm + L.etab);
+  float* fin = reinterpret_cast<float*>(sm + L.fin);
+  P.queue = reinterpret_cast<int*>(sm + L.queue);
+  P.qtail = reinterpret_cast<volatile int*>(P.queue + QCAP);
+  P.edone = P.qtail + 1;
+  P.issued = P.qtail + 2;
+  Unit* units = reinterpret_cast<Unit*>(sm + L.units);
+  int* ucnt = reinterpret_cast<int*>(units + 4 * UMAX);
+  P.units = units;
+  P.ucnt = ucnt;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + L.misc);
+  unsigned long long* gbase_s = reinterpret_cast<unsigned long long*>(sm + L.misc + 8);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = gridDim.x, SH = a.slot_cap - 1;
+
+  if (tid == 0) {
+    for (int s = 0; s < a.S; ++s) {
+      mbar_init(&P.full[s], 1);
+      mbar_init(&P.empty[s], 1);
+      mbar_init(&P.sfr[s], 4);
+    }
+    for (int i = 0; i < NACC8; ++i) {
+      mbar_init(&P.accf[i], 1);
+      mbar_init(&P.accr[i], 4);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&P.a4f[i], 1);
+      mbar_init(&P.a4r[i], 4);
+    }
+    mbar_init(P.mdone, 1);
+    // the shared expert's units do not depend on routing: listed now, so its weights stream at once
+    build_units(a, pl, 0, units, &ucnt[0], a.status);
+    build_units(a, pl, 2, units + 2 * UMAX, &ucnt[2], a.status);
+    ucnt[1] = ucnt[3] = 0;
+    pl.nr = 0;
+    pl.tag = 0u;
+    pl.ar_epoch = 0u;
+    pl.ready = 0;
+    pl.abort = 0;
+    *P.qtail = 0;
+    *P.edone = 0;
+    *P.issued = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)), "r"(TM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  P.tm = *tslot;
+
+  if (warp == 0) {
+    // Constant weights only: with a programmatic dependent launch this overlaps the previous kernel.
+    if (lane == 0) role_producer(a, pl, P);
+  } else {
+    // Past this point the previous kernel in the stream has completed (tokens, workspace, epoch).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int t7 = tid - 32;
+    if (t7 == 0) {
+      const unsigned long long c = ld_relaxed64(a.gbar);
+      const unsigned long long gb = c - c % (unsigned long long)G;
+      *gbase_s = gb;
+      pl.tag = (unsigned)((gb / (unsigned long long)G) % 0xFFFFFFFFull) + 1u;
+      pl.ar_epoch = a.ar_world > 1 ? *(volatile unsigned*)a.ar_ctl + 1u : 0u;
+      if (ld_relaxed32(a.status) != 0u) pl.abort = 1;  // an earlier call gave up: stop until reset
+      fence_acq_rel_gpu();
+      asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;" ::"l"(a.gbar) : "memory");  // read the epoch
+      asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    }
+    bool ok = !bar_any(1, 224, pl.abort != 0);
+    if (ok) {
+      router_rows(a, warp - 1, lane, pl.tag);
+      float* scr = reinterpret_cast<float*>(P.xb);
+      ok = make_plan(a, pl, scr, scr + MAXB * a.E, emask, t7);
+    }
+    if (ok) {
+      build_xb(a, P.xb, pl, fin, t7);
+      if (warp >= 4) {  // B-side scale factors of the block-scaled MMA: 1.0 for every row and group
+        tm_st4(P.tm + ((uint32_t)(32 * (warp - 4)) << 16) + TM_SFB, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
+        fence_before();
+      }
+    }
+    // The routed units follow from the plan. Without one (a failed set-up: `ok` is the same in every
+    // warp here) every role walks the shared expert's stages only, and skips them (the call has
+    // already given up).
+    if (t7 == 0) {
+      if (!ok) pl.nr = 0;
+      build_units(a, pl, 1, units + UMAX, &ucnt[1], a.status);
+      build_units(a, pl, 3, units + 3 * UMAX, &ucnt[3], a.status);
+    }
+    named_bar_sync(1, 224);
+    if (t7 == 0) {
+      __threadfence_block();
+      pl.ready = 1;
+    }
+    if (warp == 1) {
+      if (lane == 0) role_mma(a, pl, P);
+    } else if (warp == 2) {
+      if (lane == 0) role_hcopy(a, pl, P, SH);
+    } else if (warp == 3) {
+      role_finisher(a, pl, P, fin, lane, SH);
+    } else {
+      role_epilogue(a, pl, P, etab, warp - 4, lane, SH);
+    }
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(P.tm), "r"(TM_COLS) : "memory");
+  if (blockIdx.x == 0 && tid == 0 && a.ar_world > 1) {
+    // every CTA has read the exchange epoch (one arrival each at its start): publish the next one
+    const uint64_t t0 = globaltimer_ns();
+    while ((long long)(ld_relaxed64(a.gbar) - (*gbase_s + (unsigned long long)G)) < 0) {
+      if (globaltimer_ns() - t0 > kWait) {
+        atomicOr(a.status, ST_CNT);
+        break;
+      }
+    }
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(a.ar_ctl), "r"(pl.ar_epoch) : "memory");
+  }
+  // A call that gave up (here or in an earlier call on this workspace) leaves NaN in its share of y
+  // (128-row tiles m = cta + G j) rather than stale memory.
+  if (ld_relaxed32(a.status) != 0u) {
+    for (int m = blockIdx.x; m < a.MT2; m += G)
+      for (int i = tid; i < 128 * a.B; i += NT) {
+        const long long o = (long long)(i >> 7) * a.H + 128 * m + (i & 127);
+        if (a.y_f32)
+          reinterpret_cast<float*>(a.y)[o] = __int_as_float(0x7FC00000);
+        else
+          reinterpret_cast<__nv_bfloat16*>(a.y)[o] = __ushort_as_bfloat16((unsigned short)0x7FC0);
+      }
+  }
+}
+
+}  // namespace tc
+
+// ------------------------------------------------------------------ host side
+// Workspace of the tensor-core path (laid out for 8 tokens whatever the call's batch): the grid
+// counter and the status word at the same offsets as the persistent fragment-layout path, then the
+// tagged router partials and counters (cleared together by dsmoe_moe_check), then partials and h.
+TcScratch tc_scratch(const dsmoe_layer_t* L) {
+  TcScratch f{};
+  const int P1 = (L->inter_local + 63) / 64, KB2 = (L->inter_local + 127) / 128, MT2 = L->hidden / 128;
+  f.slot_cap = tc::MAXB * L->topk + 1;
+  auto al = [](size_t v) { return (v + 255) & ~size_t(255); };
+  size_t o = 0;
+  f.gbar = o; o += al(8);
+  f.status = o; o += al(4);
+  f.rl = o; o += al((size_t)tc::MAXB * L->n_experts * 4 * 16);
+  f.cnt13 = o; o += al((size_t)f.slot_cap * P1 * 8);
+  f.cnt2 = o; o += al((size_t)MT2 * 8);
+  f.sdone = o; o += al((size_t)f.slot_cap * 8);
+  f.counters_end = o;
+  f.p13 = o; o += al((size_t)f.slot_cap * P1 * tc::MAXC * 4096);
+  f.p2 = o; o += al((size_t)MT2 * f.slot_cap * tc::MAXC * 4096);
+  f.hb = o; o += al((size_t)f.slot_cap * KB2 * 2048);
+  f.total = o;
+  return f;
+}
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::mutex g_tc_mu;
+
+struct TcKey {
+  const void* p[4];
+  int H, I_loc, row0, E, fmt;
+  bool operator==(const TcKey& o) const {
+    return p[0] == o.p[0] && p[1] == o.p[1] && p[2] == o.p[2] && p[3] == o.p[3] && H == o.H && I_loc == o.I_loc &&
+           row0 == o.row0 && E == o.E && fmt == o.fmt;
+  }
+};
+struct TcMaps {
+  TcKey key;
+  CUtensorMap r13, r2, s13, s2;
+  bool used;
+};
+constexpr int kMapCache = 512;
+TcMaps g_maps[kMapCache];
+int g_maps_next = 0;
+
+int encode(CUtensorMap* m, bool fp4, int rank, const void* base, const cuuint64_t* dims, const cuuint64_t* strides,
+           const cuuint32_t* box) {
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  const CUresult r = g_encode(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, rank,
+                              const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  DSMOE_REQUIRE(r == CUDA_SUCCESS, DSMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return DSMOE_OK;
+}
+
+// An expert set's w1|w3 or w2 blocks as a 4-D tensor {K in a block (128), rows (128), block, expert}:
+// one box is one contiguous block.
+int encode_store(const dsmoe_store_t& st, int H, int I_loc, CUtensorMap* m13, CUtensorMap* m2) {
+  const TcGeom g = tc_geom(st.fmt, H, I_loc + st.row0, st.row0, I_loc);
+  const bool f4 = st.fmt == DSMOE_FMT_FP4;
+  const cuuint32_t box[4] = {128, 128, 1, 1};
+  const cuuint64_t d13[4] = {128, 128, (cuuint64_t)g.P1 * g.KB1, (cuuint64_t)st.n_experts};
+  const cuuint64_t s13[3] = {(cuuint64_t)g.row_bytes, (cuuint64_t)g.blk, (cuuint64_t)st.w13_expert_bytes};
+  int rc = encode(m13, f4, 4, st.w13, d13, s13, box);
+  if (rc) return rc;
+  const cuuint64_t d2[4] = {128, 128, (cuuint64_t)g.MT2 * g.KB2, (cuuint64_t)st.n_experts};
+  const cuuint64_t s2[3] = {(cuuint64_t)g.row_bytes, (cuuint64_t)g.blk, (cuuint64_t)st.w2_expert_bytes};
+  return encode(m2, f4, 4, st.w2, d2, s2, box);
+}
+
+int get_maps(const dsmoe_layer_t* L, TcMaps** out) {
+  std::lock_guard<std::mutex> lk(g_tc_mu);
+  if (!g_encode) {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return cuda_status("moe_tc: cuTensorMapEncodeTiled entry point");
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  TcKey k{{L->routed.w13, L->routed.w2, L->shared.w13, L->shared.w2}, L->hidden, L->inter_local,
+          L->routed.row0, L->n_experts, L->routed.fmt};
+  for (int i = 0; i < kMapCache; ++i)
+    if (g_maps[i].used && g_maps[i].key == k) {
+      *out = &g_maps[i];
+      return DSMOE_OK;
+    }
+  TcMaps& m = g_maps[g_maps_next];
+  g_maps_next = (g_maps_next + 1) % kMapCache;
+  m.used = false;
+  int rc = encode_store(L->routed, L->hidden, L->inter_local, &m.r13, &m.r2);
+  if (!rc) rc = encode_store(L->shared, L->hidden, L->inter_local, &m.s13, &m.s2);
+  if (rc) return rc;
+  m.key = k;
+  m.used = true;
+  *out = &m;
+  return DSMOE_OK;
+}
+
+struct TcDev {
+  int sms = 0, optin = 0;
+  bool attr = false;
+  int pdl = -1;
+};
+TcDev g_tcdev[64];
+
+}  // namespace
+
+bool tc_supported(const dsmoe_layer_t* L, int B) {
+  if (B < 1 || B > tc::MAXB || L->n_experts > tc::MAXE || L->hidden % 128 || L->hidden > 8192 ||
+      L->inter_local % 32 || L->inter_local < 64 || L->inter_local > 8192 || L->topk > tc::MAXK)
+    return false;
+  if (L->routed.layout != DSMOE_LAYOUT_TC || L->shared.layout != DSMOE_LAYOUT_TC || L->shared.fmt != DSMOE_FMT_FP8 ||
+      L->shared.n_experts != 1 || L->shared.row0 != L->routed.row0)
+    return false;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  TcDev& d = g_tcdev[dev & 63];
+  if (d.sms == 0) {
+    cudaDeviceGetAttribute(&d.optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return tc::tc_smem(L->hidden, 3, L->n_experts).total <= (size_t)d.optin;
+}
+
+int launch_tc(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image_mask, void* y, int y_dtype,
+              int64_t* idx, float* wt, float* scores, uint8_t* ws, cudaStream_t st, const PeerExchange* px) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  TcDev& d = g_tcdev[dev & 63];
+  TcMaps* maps = nullptr;
+  int rc = get_maps(L, &maps);
+  if (rc) return rc;
+  const TcScratch f = tc_scratch(L);
+  tc::TcArgs a{};
+  a.tm_r13 = maps->r13;
+  a.tm_r2 = maps->r2;
+  a.tm_s13 = maps->s13;
+  a.tm_s2 = maps->s2;
+  a.H = L->hidden;
+  a.I_loc = L->inter_local;
+  a.row0 = L->routed.row0;
+  a.E = L->n_experts;
+  a.B = B;
+  a.topk = L->topk;
+  a.score_func = L->score_func;
+  a.route_scale = L->route_scale;
+  a.r_fmt = L->routed.fmt;
+  const TcGeom gr = tc_geom(L->routed.fmt, L->hidden, L->inter_local + a.row0, a.row0, L->inter_local);
+  const TcGeom gs = tc_geom(DSMOE_FMT_FP8, L->hidden, L->inter_local + a.row0, a.row0, L->inter_local);
+  a.P1 = gr.P1;
+  a.KB1 = gr.KB1;
+  a.KB2 = gr.KB2;
+  a.MT2 = gr.MT2;
+  // as many ring stages as fit next to the B tile and the rest (at most MAXS)
+  int S = tc::MAXS;
+  while (S > 0 && tc::tc_smem(L->hidden, S, L->n_experts).total > (size_t)d.optin) --S;
+  DSMOE_REQUIRE(S >= 3, DSMOE_ERR_UNSUPPORTED, "moe_tc: shared memory for %d stages only", S);
+  a.S = S;
+  a.slot_cap = f.slot_cap;
+  a.wg = L->gate_w;
+  a.bias = L->gate_bias;
+  a.bias_vl = L->gate_bias_vl;
+  a.image_mask = image_mask;
+  a.x = (const __nv_bfloat16*)x;
+  a.r13 = L->routed.w13;
+  a.r2 = L->routed.w2;
+  a.r_eb13 = L->routed.w13_expert_bytes;
+  a.r_eb2 = L->routed.w2_expert_bytes;
+  a.r_d13 = gr.d13;
+  a.r_d2 = gr.d2;
+  a.s13 = L->shared.w13;
+  a.s2 = L->shared.w2;
+  a.s_d13 = gs.d13;
+  a.s_d2 = gs.d2;
+  a.y = y;
+  a.y_f32 = y_dtype == DSMOE_DTYPE_F32;
+  a.idx = idx;
+  a.wt = wt;
+  a.scores = scores;
+  a.gbar = (unsigned long long*)(ws + f.gbar);
+  a.status = (unsigned*)(ws + f.status);
+  a.rl = (unsigned long long*)(ws + f.rl);
+  a.cnt13 = (unsigned long long*)(ws + f.cnt13);
+  a.cnt2 = (unsigned long long*)(ws + f.cnt2);
+  a.sdone = (unsigned long long*)(ws + f.sdone);
+  a.p13 = (float*)(ws + f.p13);
+  a.p2 = (float*)(ws + f.p2);
+  a.hb = ws + f.hb;
+  if (px && px->world > 1) {
+    DSMOE_REQUIRE(px->hidden == L->hidden && px->world <= kMaxWorld && px->rank >= 0 && px->rank < px->world,
+                  DSMOE_ERR_ARG, "moe_tc: exchange for hidden %d, world %d, rank %d", px->hidden, px->world, px->rank);
+    a.ar_world = px->world;
+    a.ar_rank = px->rank;
+    a.ar_ctl = px->ctl;
+    for (int q = 0; q < px->world; ++q) {
+      DSMOE_REQUIRE(px->slots[q], DSMOE_ERR_ARG, "moe_tc: exchange slots of rank %d not mapped", q);
+      a.ar_slots[q] = px->slots[q];
+    }
+  }
+  const size_t smem = tc::tc_smem(L->hidden, S, L->n_experts).total;
+  if (!d.attr) {
+    if (cudaFuncSetAttribute(tc::moe_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, d.optin) != cudaSuccess)
+      return cuda_status("moe_tc: set smem");
+    d.attr = true;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(d.sms);
+  cfg.blockDim = dim3(tc::NT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (d.pdl < 0) cudaStreamIsCapturing(st, &cap);
+  const bool try_pdl = d.pdl == 1 || (d.pdl < 0 && cap == cudaStreamCaptureStatusNone);
+  cfg.numAttrs = try_pdl ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, tc::moe_tc_kernel, a);
+  if (try_pdl && d.pdl < 0) {
+    if (e == cudaSuccess) {
+      d.pdl = 1;
+    } else {
+      cudaGetLastError();
+      d.pdl = 0;
+      cfg.numAttrs = 1;
+      e = cudaLaunchKernelEx(&cfg, tc::moe_tc_kernel, a);
+    }
+  }
+  if (e != cudaSuccess) {
+    set_error("moe_tc launch: %s", cudaGetErrorString(e));
+    cudaGetLastError();
+    return DSMOE_ERR_CUDA;
+  }
+  return DSMOE_OK;
+}
+
+}  // namespace dsmoe

@@ -62,6 +62,15 @@ struct FusedScratch {
 FusedScratch fused_scratch(int H, int I_loc, int E, int B, int topk, int r_fmt);
 bool fused_supported(const dsmoe_layer_t* L, int B);
 
+// Scratch of the tensor-core decode path (moe_tc.cu) in the caller's workspace; the grid counter
+// and the status word sit at the same offsets as in FusedScratch.
+struct TcScratch {
+  size_t gbar, status, rl, cnt13, cnt2, sdone, counters_end, p13, p2, hb, total;
+  int slot_cap;
+};
+TcScratch tc_scratch(const dsmoe_layer_t* L);
+bool tc_supported(const dsmoe_layer_t* L, int B);
+
 // Peer exchange of the persistent kernel's all-reduce (comm.cu owns the memory). Every rank has one
 // exchange buffer: a control word (the epoch of its last call) and the slots its peers write,
 // [2 parities][world source ranks][hidden / 16 output tiles][32 lanes][4 words]; slots[q] is rank
@@ -75,6 +84,8 @@ struct PeerExchange {
 inline size_t exchange_slot_words(int world, int hidden) { return 2ull * world * (hidden / 16) * 128; }
 // The exchange of an opened comm (comm.cu), or nullptr.
 const PeerExchange* comm_exchange(const dsmoe_comm_t* c);
+int launch_tc(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image_mask, void* y, int y_dtype,
+              int64_t* idx, float* wt, float* scores, uint8_t* ws, cudaStream_t st, const PeerExchange* px);
 
 int launch_fused(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image_mask, void* y, int y_dtype,
                  int64_t* idx, float* wt, float* scores, uint8_t* ws, cudaStream_t st, void* const* events,

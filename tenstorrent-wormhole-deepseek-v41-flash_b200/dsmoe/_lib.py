@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(_HERE, "libdsmoe.so")
 
 OK, ERR_ARG, ERR_ALIGN, ERR_CUDA, ERR_WORKSPACE, ERR_TIMEOUT, ERR_UNSUPPORTED = 0, -1, -2, -3, -4, -5, -6
 FMT_FP8, FMT_FP4 = 0, 1
+LAYOUT_FRAG, LAYOUT_TC = 0, 1
 SCORE_SIGMOID, SCORE_SQRTSOFTPLUS = 0, 1
 DTYPE_F32, DTYPE_BF16, DTYPE_E4M3 = 0, 1, 2
 MAX_DECODE_TOKENS = 64
@@ -33,7 +34,7 @@ class DsmoeError(RuntimeError):
 class Store(ctypes.Structure):
     _fields_ = [("w13", ctypes.c_void_p), ("w2", ctypes.c_void_p),
                 ("w13_expert_bytes", ctypes.c_longlong), ("w2_expert_bytes", ctypes.c_longlong),
-                ("fmt", ctypes.c_int), ("n_experts", ctypes.c_int)]
+                ("fmt", ctypes.c_int), ("n_experts", ctypes.c_int), ("layout", ctypes.c_int), ("row0", ctypes.c_int)]
 
 
 class Layer(ctypes.Structure):
@@ -54,6 +55,9 @@ _SIGS = {
     "dsmoe_store_expert_bytes": ([_I, _I, _I, ctypes.POINTER(_LL), ctypes.POINTER(_LL)], _I),
     "dsmoe_store_pack_expert": ([_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
     "dsmoe_store_unpack_expert": ([_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P], _I),
+    "dsmoe_store_tc_expert_bytes": ([_I, _I, _I, _I, _I, ctypes.POINTER(_LL), ctypes.POINTER(_LL)], _I),
+    "dsmoe_store_tc_pack_expert": ([_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
+    "dsmoe_store_tc_unpack_expert": ([_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P], _I),
     "dsmoe_moe_workspace_bytes": ([ctypes.POINTER(Layer), _I], ctypes.c_size_t),
     "dsmoe_router": ([ctypes.POINTER(Layer), _P, _I, _P, _P, _P, _P, _P, ctypes.c_size_t, _P], _I),
     "dsmoe_router_noalloc": ([ctypes.POINTER(Layer), _P, _I, _P, _P, _P, _P, _P], _I),

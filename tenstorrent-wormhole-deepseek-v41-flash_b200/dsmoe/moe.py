@@ -23,6 +23,13 @@ from .synth import ExpertWeights, RouterWeights
 LIMIT = 10.0  # SwiGLU clamp (dsv41/tt/moe.py:15)
 
 
+def tc_geometry_ok(hidden: int, inter_local: int, n_experts: int, topk: int) -> bool:
+    """Shapes the tensor-core decode kernel takes (whole 128-K blocks of hidden up to 8192, at least
+    64 intermediate rows per GPU in 32-row steps, up to 1024 experts and top-8)."""
+    return (hidden % 128 == 0 and 0 < hidden <= 8192 and 64 <= inter_local <= 8192 and inter_local % 32 == 0
+            and n_experts <= 1024 and topk <= 8)
+
+
 def _check_x(x: torch.Tensor, hidden: int, device) -> torch.Tensor:
     if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != hidden or x.device != device:
         if not x.is_cuda:
@@ -44,35 +51,60 @@ class MoE:
 
     def __init__(self, hidden: int, inter: int, n_experts: int, topk: int = 6, fmt: str = "fp8",
                  score_func: str = "sigmoid", route_scale: float = 2.5, rank: int = 0, world: int = 1,
-                 group=None, device=None, max_tokens: int = L.MAX_DECODE_TOKENS):
+                 group=None, device=None, max_tokens: int = L.MAX_DECODE_TOKENS, layouts=("tc", "frag")):
+        """``layouts``: the resident stores to keep. "tc" serves decode calls of 1..8 tokens on the
+        tensor-core kernel; "frag" serves larger batches and prefill (and decode when "tc" is absent)."""
         if score_func not in L.SCORE_NAMES:
             raise ValueError(f"score_func must be one of {sorted(L.SCORE_NAMES)}")
+        layouts = tuple(dict.fromkeys(layouts))
+        if not layouts or any(lay not in ("tc", "frag") for lay in layouts):
+            raise ValueError("layouts must be a non-empty subset of ('tc', 'frag')")
+        loc = inter // world if world > 0 and inter % world == 0 else 0
+        if "tc" in layouts and not tc_geometry_ok(hidden, loc, n_experts, topk):
+            if layouts == ("tc",):
+                raise ValueError(f"the tensor-core store does not take hidden {hidden}, {loc} rows per GPU, "
+                                 f"{n_experts} experts, top-{topk}")
+            layouts = tuple(lay for lay in layouts if lay != "tc")
+        if "frag" in layouts and fmt == "fp4" and loc % 64 and "tc" in layouts:
+            layouts = ("tc",)  # the fragment layout keeps FP4 slices in 64-row steps only
         self.hidden, self.inter, self.n_experts, self.topk = hidden, inter, n_experts, topk
         self.fmt, self.score_func, self.route_scale = fmt, score_func, float(route_scale)
         self.rank, self.world, self.group = rank, world, group
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-        self.routed = ExpertStore(fmt, hidden, inter, n_experts, rank, world, self.device)
-        self.shared = ExpertStore("fp8", hidden, inter, 1, rank, world, self.device)
+        self.stores = {lay: (ExpertStore(fmt, hidden, inter, n_experts, rank, world, self.device, lay),
+                             ExpertStore("fp8", hidden, inter, 1, rank, world, self.device, lay)) for lay in layouts}
+        self.routed, self.shared = self.stores["frag" if "frag" in self.stores else "tc"]
         self.wg = torch.zeros((n_experts, hidden), dtype=torch.float32, device=self.device)
         self.bias = torch.zeros((n_experts,), dtype=torch.float32, device=self.device)
         self.bias_vl: Optional[torch.Tensor] = None
         self.max_tokens = min(max_tokens, L.MAX_DECODE_TOKENS)
-        self._layer = self._make_layer()
-        nbytes = L.lib.dsmoe_moe_workspace_bytes(self._layer, self.max_tokens)
-        # zero-filled once: the persistent kernel keeps counters and a grid barrier here
-        self.workspace = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
-        self._ws = (self.workspace.data_ptr(), self.workspace.numel())
+        self._dec_layout = "tc" if "tc" in self.stores else "frag"
+        self._layers = {lay: self._make_layer(lay) for lay in self.stores}
+        # workspaces, zero-filled once: the persistent kernels keep counters and tagged partials there
+        self._wss = {lay: torch.zeros(L.lib.dsmoe_moe_workspace_bytes(self._layers[lay], self.max_tokens),
+                                      dtype=torch.uint8, device=self.device) for lay in self.stores}
+        self._bind()
         self.comm = None  # tp.PeerComm: all-reduce inside the decode kernel
         self._prefill_ws: Optional[torch.Tensor] = None  # grown on demand by prefill()
 
+    def _bind(self):
+        """The decode layer (tensor-core store when kept) and the batched layer (fragment store)."""
+        self._layer = self._layers[self._dec_layout]
+        self.workspace = self._wss[self._dec_layout]
+        self._ws = (self.workspace.data_ptr(), self.workspace.numel())
+        self._dec_max = 8 if self._dec_layout == "tc" else self.max_tokens
+        self._layer_b = self._layers.get("frag")
+        self.workspace_b = self._wss.get("frag")
+
     # ---------------------------------------------------------------- loading
-    def _make_layer(self) -> L.Layer:
+    def _make_layer(self, layout: str) -> L.Layer:
+        routed, shared = self.stores[layout]
         lay = L.Layer()
-        lay.hidden, lay.inter_local, lay.n_experts = self.hidden, self.routed.inter_local, self.n_experts
+        lay.hidden, lay.inter_local, lay.n_experts = self.hidden, routed.inter_local, self.n_experts
         lay.topk, lay.score_func, lay.route_scale = self.topk, L.SCORE_NAMES[self.score_func], self.route_scale
         lay.gate_w, lay.gate_bias = self.wg.data_ptr(), self.bias.data_ptr()
         lay.gate_bias_vl = self.bias_vl.data_ptr() if self.bias_vl is not None else None
-        lay.routed, lay.shared = self.routed.c_struct(), self.shared.c_struct()
+        lay.routed, lay.shared = routed.c_struct(), shared.c_struct()
         return lay
 
     def load_router(self, rw: RouterWeights) -> None:
@@ -80,17 +112,26 @@ class MoE:
         self.bias.copy_(rw.bias)
         if rw.bias_vl is not None:
             self.bias_vl = rw.bias_vl.to(self.device, torch.float32).contiguous()
-        self._layer = self._make_layer()
+        self._layers = {lay: self._make_layer(lay) for lay in self.stores}
+        self._bind()
 
     def load_expert(self, e: int, ew: ExpertWeights) -> None:
-        self.routed.pack(e, ew)
+        for routed, _ in self.stores.values():
+            routed.pack(e, ew)
 
     def load_shared(self, ew: ExpertWeights) -> None:
-        self.shared.pack(0, ew)
+        for _, shared in self.stores.values():
+            shared.pack(0, ew)
+
+    def copy_experts_from(self, other: "MoE") -> None:
+        """Every expert's bytes from a layer of the same geometry (another resident copy)."""
+        for lay, (routed, shared) in self.stores.items():
+            routed.copy_from(other.stores[lay][0])
+            shared.copy_from(other.stores[lay][1])
 
     @property
     def nbytes(self) -> int:
-        return self.routed.nbytes + self.shared.nbytes + self.wg.numel() * 4 + self.bias.numel() * 4
+        return sum(r.nbytes + s.nbytes for r, s in self.stores.values()) + self.wg.numel() * 4 + self.bias.numel() * 4
 
     # ---------------------------------------------------------------- router
     def route(self, x: torch.Tensor, image_mask: Optional[torch.Tensor] = None):
@@ -139,14 +180,16 @@ class MoE:
         wt = wt.to(self.device, torch.float32).contiguous()
         if idx.shape != (P, self.topk) or wt.shape != (P, self.topk):
             raise ValueError(f"idx / wt must be [{P}, {self.topk}]")
-        nbytes = L.lib.dsmoe_moe_prefill_workspace_bytes(self._layer, P)
+        if self._layer_b is None:
+            raise ValueError("prefill reads the fragment store: build the layer with 'frag' in layouts")
+        nbytes = L.lib.dsmoe_moe_prefill_workspace_bytes(self._layer_b, P)
         if nbytes == 0:
             raise ValueError(f"prefill does not support this layer with {P} tokens")
         if self._prefill_ws is None or self._prefill_ws.numel() < nbytes:
             self._prefill_ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
         f32 = partial or self.world > 1
         y = torch.empty((P, self.hidden), dtype=torch.float32 if f32 else torch.bfloat16, device=self.device)
-        L.call("dsmoe_moe_prefill", self._layer, L.ptr(x), P, L.ptr(idx), L.ptr(wt), L.ptr(y),
+        L.call("dsmoe_moe_prefill", self._layer_b, L.ptr(x), P, L.ptr(idx), L.ptr(wt), L.ptr(y),
                L.DTYPE_F32 if f32 else L.DTYPE_BF16, L.ptr(self._prefill_ws), self._prefill_ws.numel(), L.stream_of(x))
         if partial or self.world == 1:
             return y
@@ -158,7 +201,7 @@ class MoE:
     def prefill_check(self, P: int) -> None:
         """Synchronize and raise if the last prefill call's bounded waits expired or an index was bad."""
         if self._prefill_ws is not None:
-            L.call("dsmoe_moe_prefill_check", self._layer, P, L.ptr(self._prefill_ws), self._prefill_ws.numel(),
+            L.call("dsmoe_moe_prefill_check", self._layer_b, P, L.ptr(self._prefill_ws), self._prefill_ws.numel(),
                    L.stream_of(self._prefill_ws))
 
     def use_comm(self, comm) -> None:
@@ -179,8 +222,8 @@ class MoE:
         if self.comm is not None and self.comm.handle is not None:
             x = _check_x(x, self.hidden, self.device)
             B = x.shape[0]
-            if B <= self.max_tokens and L.lib.dsmoe_moe_allreduce_supported(self._layer, self.comm.handle,
-                                                                             x.data_ptr(), B):
+            if B <= self._dec_max and L.lib.dsmoe_moe_allreduce_supported(self._layer, self.comm.handle,
+                                                                           x.data_ptr(), B):
                 y = torch.empty((B, self.hidden), dtype=torch.bfloat16, device=self.device)
                 mask = self._mask(image_mask, B)
                 L.check(L.lib.dsmoe_moe_decode_allreduce(
@@ -197,9 +240,17 @@ class MoE:
     decode = forward
 
     def check(self, B: int = 1) -> None:
-        """Synchronize and raise if a bounded device-side wait expired in an earlier call."""
-        L.call("dsmoe_moe_check", self._layer, min(B, self.max_tokens), L.ptr(self.workspace),
-               self.workspace.numel(), L.stream_of(self.workspace))
+        """Synchronize and raise if a bounded device-side wait expired in an earlier call (every
+        store's workspace is checked and, after an expired wait, reset)."""
+        err = None
+        for lay, ws in self._wss.items():
+            try:
+                L.call("dsmoe_moe_check", self._layers[lay], min(B, self.max_tokens), L.ptr(ws), ws.numel(),
+                       L.stream_of(ws))
+            except L.DsmoeError as e:
+                err = err or e
+        if err is not None:
+            raise err
 
     def _run(self, x, image_mask, out, y_dtype, idx=None, wt=None):
         x = _check_x(x, self.hidden, self.device)
@@ -208,17 +259,22 @@ class MoE:
             out = torch.empty((B, self.hidden), dtype=torch.float32 if y_dtype == L.DTYPE_F32 else torch.bfloat16,
                               device=self.device)
         st = torch.cuda.current_stream(self.device).cuda_stream
-        if B <= self.max_tokens and image_mask is None and idx is None and wt is None:  # one launch, no slicing
+        if B <= self._dec_max and image_mask is None and idx is None and wt is None:  # one launch, no slicing
             L.check(L.lib.dsmoe_moe_decode(self._layer, x.data_ptr(), B, None, out.data_ptr(), y_dtype, None, None,
                                            None, self._ws[0], self._ws[1], st))
             return out
         mask = self._mask(image_mask, B)
-        for b0 in range(0, B, self.max_tokens):
-            b1 = min(B, b0 + self.max_tokens)
-            L.call("dsmoe_moe_decode", self._layer, L.ptr(x[b0:b1]), b1 - b0,
+        # up to 8 tokens on the decode store; larger batches on the fragment store's batched path
+        if B <= self._dec_max or self._layer_b is None:
+            lay, ws, step = self._layer, self.workspace, self._dec_max
+        else:
+            lay, ws, step = self._layer_b, self.workspace_b, self.max_tokens
+        for b0 in range(0, B, step):
+            b1 = min(B, b0 + step)
+            L.call("dsmoe_moe_decode", lay, L.ptr(x[b0:b1]), b1 - b0,
                    L.ptr(mask[b0:b1] if mask is not None else None), L.ptr(out[b0:b1]), y_dtype,
                    L.ptr(idx[b0:b1] if idx is not None else None), L.ptr(wt[b0:b1] if wt is not None else None),
-                   None, L.ptr(self.workspace), self.workspace.numel(), st)
+                   None, L.ptr(ws), ws.numel(), st)
         return out
 
 

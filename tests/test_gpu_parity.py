@@ -284,7 +284,7 @@ def test_outlier_channels(dev, fmt, B):
     m.check(B)
 
 
-@pytest.mark.parametrize("fmt", ["fp8"])
+@pytest.mark.parametrize("fmt", ["fp8", "fp4"])
 def test_real_width_tp8_slices(dev, fmt):
     """The real model's intermediate width, 2304, split over 8 ranks: 288 rows per rank, so FP8
     128-row scale blocks straddle the slices (dsv41/ref/fp4lib.c:114-115, dsv41/tt/moe.py:42-45).
