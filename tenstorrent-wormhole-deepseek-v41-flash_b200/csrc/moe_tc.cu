@@ -60,6 +60,7 @@ constexpr int SA = 16384;                // stage A: 128 rows x 128 K (one byte 
 constexpr int SB = 2048;                 // stage B (w2 phase): 16 rows x 128 K e4m3
 constexpr int STAGE = SA + SB + 1024;    // + 1 KB for the stage's scales (FP4 512 B, FP8 16 B)
 constexpr int NACC8 = 8;                 // FP8 block accumulators (16 TMEM columns each)
+constexpr int kDepth8 = 4;               // FP8 stages (16 KB) in flight per CTA
 constexpr uint32_t TM_ACC4 = 128, TM_SFA = 160, TM_SFB = 240, TM_COLS = 256;
 constexpr int MAXS = 20;                 // ring stages (TM_SFA + 4 MAXS <= TM_SFB)
 constexpr int QCAP = 64;                 // finisher job queue
@@ -94,9 +95,11 @@ struct TcArgs {
   unsigned long long* gbar;
   unsigned* status;
   unsigned long long* rl;     // [8][E][4] router quarter-row partials, two tagged words each
-  unsigned long long* cnt13;  // [slot_cap][P1] tagged stage counts of w1|w3 tiles
-  unsigned long long* cnt2;   // [MT2] tagged stage counts of w2 output tiles
-  unsigned long long* sdone;  // [slot_cap] tagged finished w1|w3 tiles per slot
+  // Counters, one set per launch parity (the set of launch tag t is cnt + (t & 1) cnt_words; the set
+  // of the next launch is zeroed while this one runs): [slot_cap][P1] stage counts of w1|w3 tiles,
+  // [MT2] stage counts of w2 output tiles, [slot_cap] finished w1|w3 tiles per slot.
+  unsigned long long* cnt;
+  int cnt_words;
   float* p13;                 // [slot_cap][P1][MAXC][128][8]
   float* p2;                  // [MT2][slot_cap][MAXC][128][8]
   uint8_t* hb;                // [slot_cap][KB2][2048] h as the w2 B tile (e4m3 hi / lo, SW128)
@@ -105,18 +108,6 @@ struct TcArgs {
   unsigned long long* ar_slots[kMaxWorld];
 };
 
-struct TcPlan {
-  int nr;                 // routed slots
-  int expert[MAXSLOT];    // slot -> routed expert
-  float w[MAXSLOT][MAXB]; // routing weight of slot s for token t (0 when t did not choose it)
-  int sel[MAXB][MAXK];
-  float selw[MAXB][MAXK];
-  float xscale[MAXB];
-  unsigned tag;           // this launch's number + 1
-  unsigned ar_epoch;
-  volatile int ready;     // plan published (producer, helpers)
-  volatile int abort;
-};
 
 // ------------------------------------------------------------------ stream-K split of a sequence
 // n stages, spt stages per tile. At most ge CTAs take part, each a contiguous range of at least
@@ -130,10 +121,12 @@ struct Split {
     ge = n / (mn > 0 ? mn : 1);
     ge = ge < 1 ? 1 : (ge > G ? G : ge);
   }
-  __host__ __device__ int lo(int c) const { return c < ge ? (int)((long long)n * c / ge) : n; }
-  __host__ __device__ int hi(int c) const { return c < ge ? (int)((long long)n * (c + 1) / ge) : n; }
+  // n * G stays below 2^32 for every supported shape (n <= 65 slots x 128 tiles x 64 blocks), so the
+  // boundaries take 32-bit unsigned divisions.
+  __host__ __device__ int lo(int c) const { return c < ge ? (int)((unsigned)n * (unsigned)c / (unsigned)ge) : n; }
+  __host__ __device__ int hi(int c) const { return c < ge ? (int)((unsigned)n * (unsigned)(c + 1) / (unsigned)ge) : n; }
   __host__ __device__ int owner(int s) const {  // the CTA whose range holds stage s
-    int c = (int)((long long)s * ge / (n > 0 ? n : 1));
+    int c = (int)((unsigned)s * (unsigned)ge / (unsigned)(n > 0 ? n : 1));
     if (c >= ge) c = ge - 1;
     while (c + 1 < ge && lo(c + 1) <= s) ++c;
     while (c > 0 && lo(c) > s) --c;
@@ -153,6 +146,24 @@ struct Work {
     sp[2].init(a.MT2 * a.KB2, a.KB2, G);
     sp[3].init(nr * a.MT2 * a.KB2, a.KB2, G);
   }
+};
+
+struct TcPlan {
+  int nr;                 // routed slots
+  int expert[MAXSLOT];    // slot -> routed expert
+  float w[MAXSLOT][MAXB]; // routing weight of slot s for token t (0 when t did not choose it)
+  int sel[MAXB][MAXK];
+  float selw[MAXB][MAXK];
+  float xscale[MAXB];
+  Work wk;                // the launch's four stream-K splits (after the plan)
+  unsigned long long* cnt13;  // this launch's counter set (see TcArgs::cnt)
+  unsigned long long* cnt2;
+  unsigned long long* sdone;
+  int efl;                // epilogue: what the unit just closed leaves to finish (0, 1 = w1|w3 tile, 2 = w2 tile)
+  unsigned tag;           // this launch's number + 1
+  unsigned ar_epoch;
+  volatile int ready;     // plan published (producer, helpers)
+  volatile int abort;
 };
 
 // A unit: one CTA's contiguous run of K blocks inside one tile of one sequence (kinds 0..3 =
@@ -177,33 +188,18 @@ __device__ __forceinline__ unsigned long long ld_relaxed64(const unsigned long l
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+// L2 prefetch of a contiguous range (16-byte aligned start, size a multiple of 16 bytes).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes & ~15u) : "memory");
+}
+__device__ __forceinline__ void st_relaxed64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 __device__ __forceinline__ unsigned ld_relaxed32(const unsigned* p) {
   unsigned v;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-// Add `add` to a counter tagged with this launch's number (a stale tag counts as 0); returns the new
-// count. Release: the caller's writes are ordered before it by the fence.
-__device__ __forceinline__ unsigned tag_add(unsigned long long* p, unsigned tag, unsigned add) {
-  fence_acq_rel_gpu();
-  unsigned long long old = ld_relaxed64(p);
-  for (int it = 0; it < 1 << 20; ++it) {
-    const unsigned cnt = (unsigned)(old >> 32) == tag ? (unsigned)old : 0u;
-    const unsigned long long nv = ((unsigned long long)tag << 32) | (cnt + add);
-    const unsigned long long prev = atomicCAS(p, old, nv);
-    if (prev == old) {
-      fence_acq_rel_gpu();
-      return cnt + add;
-    }
-    old = prev;
-  }
-  return 0u;
-}
-__device__ __forceinline__ unsigned tag_count(const unsigned long long* p, unsigned tag) {
-  const unsigned long long v = ld_relaxed64(p);
-  return (unsigned)(v >> 32) == tag ? (unsigned)v : 0u;
-}
-
 __device__ __forceinline__ float fscore_tc(float l, int func) {
   const double d = (double)l;
   const double s = func == DSMOE_SCORE_SIGMOID ? 1.0 / (1.0 + exp(-d)) : sqrt(d > 20.0 ? d : log1p(exp(d)));
@@ -212,10 +208,6 @@ __device__ __forceinline__ float fscore_tc(float l, int func) {
 __device__ __forceinline__ unsigned score_key_tc(float f) {
   const unsigned u = f == 0.f ? 0u : __float_as_uint(f);
   return f != f ? 0u : u ^ ((unsigned)((int)u >> 31) | 0x80000000u);
-}
-__device__ __forceinline__ void rl_put(unsigned long long* p, double v, unsigned ep) {
-  const unsigned long long b = (unsigned long long)__double_as_longlong(v), t = (unsigned long long)ep << 32;
-  st_ll2(p, t | (b >> 32), t | (b & 0xFFFFFFFFull));
 }
 __device__ __forceinline__ float silu_tc(float v) { return v / (1.0f + expf(-v)); }
 
@@ -247,16 +239,14 @@ __device__ __forceinline__ void mma_f8(uint32_t d, uint64_t a, uint64_t b, uint3
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
 __device__ __forceinline__ void mma_mx(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t sfa, uint32_t sfb,
                                        uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
-      : "memory");
+      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb));
 }
 __device__ __forceinline__ void tm_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
@@ -286,16 +276,17 @@ __device__ __forceinline__ void tma_4d(void* dst, const CUtensorMap* tm, int c0,
 
 // ------------------------------------------------------------------ shared-memory carve-up
 struct TcSmem {
-  size_t ring, xb, bars, plan, emask, etab, fin, queue, units, misc, total;
+  size_t efin, ring, xb, scr, bars, plan, emask, etab, fin, queue, units, misc, total;
 };
-__host__ __device__ inline TcSmem tc_smem(int H, int S, int E) {
+__host__ __device__ inline TcSmem tc_smem(int H, int S, int E, int B) {
   TcSmem L;
   size_t o = 0;
   L.ring = o;
   o += (size_t)S * STAGE;
-  L.xb = o;  // the w1|w3 B tile; before it is built, the plan's scores ([8][E] twice)
-  const size_t xb = (size_t)(H / 128) * 2048, scr = (size_t)2 * MAXB * E * 4;
-  o += (xb > scr ? xb : scr + 15) & ~size_t(15);
+  L.xb = o;  // the w1|w3 B tile
+  o += (size_t)(H / 128) * 2048;
+  L.scr = o;  // the plan's scores and biased scores, [B][E] each
+  o += ((size_t)2 * B * E * 4 + 15) & ~size_t(15);
   L.bars = o;
   o += (size_t)(3 * S + 2 * NACC8 + 5) * 8;
   o = (o + 15) & ~size_t(15);
@@ -307,6 +298,8 @@ __host__ __device__ inline TcSmem tc_smem(int H, int S, int E) {
   o += 2 * 256 * 4;  // two units' FP8 scale tables: 4 floats per 128-K block, <= 64 blocks
   L.fin = o;
   o += 128 * 8 * 4;
+  L.efin = o;  // the epilogue's finishing scratch: [64][8] + [8][64] floats, then [MAXSLOT] counts
+  o += 2 * 64 * 8 * 4 + ((MAXSLOT * 4 + 15) & ~15);
   L.queue = o;
   o += (QCAP + 4) * 4;
   L.units = o;
@@ -317,74 +310,191 @@ __host__ __device__ inline TcSmem tc_smem(int H, int S, int E) {
   return L;
 }
 
-// ------------------------------------------------------------------ router (warps 1..7)
-// Quarter-rows of the router spread over the CTAs; each warp a quarter-row at a time: its H / 4
-// fp32 weights in registers, the dot product with every token in fp64 (each product exact), stored
-// as a tagged partial.
-__device__ __noinline__ void router_rows(const TcArgs& a, int w7, int lane, unsigned tag) {
-  const int G = gridDim.x, nq = 4 * a.E;
-  const int s0 = (int)((long long)nq * blockIdx.x / G), s1 = (int)((long long)nq * (blockIdx.x + 1) / G);
+// ------------------------------------------------------------------ router (warps 2..7)
+// Quarter-rows of the router spread over the CTAs: H / 4 fp32 weights of a quarter-row in a warp's
+// registers, the dot product with every token in fp64 (each product exact), stored as a tagged
+// partial that every CTA's plan gathers.
+__device__ __forceinline__ void warp_sum_d2(double& u, double& v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const double su = __shfl_xor_sync(0xffffffffu, u, o), sv = __shfl_xor_sync(0xffffffffu, v, o);
+    u += su;
+    v += sv;
+  }
+}
+// Two quarter-rows per warp pass, interleaved: both rows' weights and the first token's values for
+// both are loaded before any is used, and the two dot products share their latency chains. NI =
+// float4 per lane of a quarter-row (H / 512, rounded up).
+template <int NI>
+__device__ __noinline__ void router_rows_t(const TcArgs& a, int w, int nw, int lane, int s0, int s1, double* qs) {
   const int n4 = a.H / 16;  // float4 per quarter-row
-  for (int it = s0 + w7; it < s1; it += 7) {
-    const int r = it >> 2, q = it & 3;
-    const float4* wrow = reinterpret_cast<const float4*>(a.wg + (long long)r * a.H + q * (a.H / 4));
-    float4 wv[16];
+  for (int it0 = s0 + 2 * w; it0 < s1; it0 += 2 * nw) {
+    const bool two = it0 + 1 < s1;
+    float4 wv[2][NI];
+    uint2 xv[2][NI];
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
-      if (lane + 32 * i < n4) {
-        const uint4 u = ld_stream16(wrow + lane + 32 * i);
-        wv[i] = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w));
-      }
-    for (int b = 0; b < a.B; ++b) {
-      const __nv_bfloat16* xr = a.x + (long long)b * a.H + q * (a.H / 4);
-      double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0, acc3 = 0.0;
+    for (int h = 0; h < 2; ++h) {
+      const int it = it0 + h;
+      const float4* wrow = reinterpret_cast<const float4*>(a.wg + (long long)(it >> 2) * a.H + (it & 3) * (a.H / 4));
+      const __nv_bfloat16* xr = a.x + (it & 3) * (a.H / 4);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < NI; ++i) {
         const int f = lane + 32 * i;
-        if (f < n4) {
-          const uint2 u = *reinterpret_cast<const uint2*>(xr + 4 * f);
-          acc0 = fma((double)__uint_as_float(u.x << 16), (double)wv[i].x, acc0);
-          acc1 = fma((double)__uint_as_float(u.x & 0xFFFF0000u), (double)wv[i].y, acc1);
-          acc2 = fma((double)__uint_as_float(u.y << 16), (double)wv[i].z, acc2);
-          acc3 = fma((double)__uint_as_float(u.y & 0xFFFF0000u), (double)wv[i].w, acc3);
+        if ((h == 0 || two) && f < n4) {
+          const uint4 u = ld_stream16(wrow + f);
+          wv[h][i] = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w));
+          xv[h][i] = *reinterpret_cast<const uint2*>(xr + 4 * f);
+        } else {
+          wv[h][i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          xv[h][i] = make_uint2(0u, 0u);
         }
       }
-      const double v = warp_sum_d((acc0 + acc1) + (acc2 + acc3));
-      if (lane == 0) rl_put(a.rl + 2 * (((long long)b * a.E + r) * 4 + q), v, tag);
+    }
+    for (int b = 0; b < a.B; ++b) {
+      if (b > 0) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const __nv_bfloat16* xr = a.x + (long long)b * a.H + ((it0 + h) & 3) * (a.H / 4);
+#pragma unroll
+          for (int i = 0; i < NI; ++i) {
+            const int f = lane + 32 * i;
+            if ((h == 0 || two) && f < n4) xv[h][i] = *reinterpret_cast<const uint2*>(xr + 4 * f);
+          }
+        }
+      }
+      double acc[2][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[h][c] = 0.0;
+#pragma unroll
+      for (int i = 0; i < NI; ++i)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint2 u = xv[h][i];
+          acc[h][0] = fma((double)__uint_as_float(u.x << 16), (double)wv[h][i].x, acc[h][0]);
+          acc[h][1] = fma((double)__uint_as_float(u.x & 0xFFFF0000u), (double)wv[h][i].y, acc[h][1]);
+          acc[h][2] = fma((double)__uint_as_float(u.y << 16), (double)wv[h][i].z, acc[h][2]);
+          acc[h][3] = fma((double)__uint_as_float(u.y & 0xFFFF0000u), (double)wv[h][i].w, acc[h][3]);
+        }
+      double v0 = (acc[0][0] + acc[0][1]) + (acc[0][2] + acc[0][3]);
+      double v1 = (acc[1][0] + acc[1][1]) + (acc[1][2] + acc[1][3]);
+      warp_sum_d2(v0, v1);
+      if (lane == 0) {
+        qs[(it0 - s0) * MAXB + b] = v0;
+        if (two) qs[(it0 + 1 - s0) * MAXB + b] = v1;
+      }
+    }
+  }
+}
+// This CTA's share of the router, rows [E c / G, E (c + 1) / G): fp32 weights times bf16 tokens,
+// each product exact in fp64 and summed in fp64 per quarter-row (warps w = 0..nw-1, named barrier 4),
+// the four quarters added in order, rounded to fp32 and scored; published as one tagged 8-byte word
+// (launch tag, fp32 score) per (token, expert). qs: shared scratch of [4 rows][MAXB] doubles.
+__device__ __noinline__ void router_rows(const TcArgs& a, TcPlan& pl, int w, int nw, int lane, double* qs) {
+  const int G = gridDim.x;
+  const int r0 = (int)((unsigned)a.E * (unsigned)blockIdx.x / (unsigned)G);
+  const int r1 = (int)((unsigned)a.E * (unsigned)(blockIdx.x + 1) / (unsigned)G);
+  if (a.H <= 5120)
+    router_rows_t<10>(a, w, nw, lane, 4 * r0, 4 * r1, qs);
+  else
+    router_rows_t<16>(a, w, nw, lane, 4 * r0, 4 * r1, qs);
+  named_bar_sync(4, 32 * nw);
+  const unsigned long long tg = (unsigned long long)pl.tag << 32;
+  for (int i = 32 * w + lane; i < (r1 - r0) * a.B; i += 32 * nw) {
+    const int rr = i / a.B, b = i - rr * a.B;
+    const double* q = qs + 4 * rr * MAXB + b;
+    const float sc = fscore_tc(__double2float_rn(((q[0] + q[MAXB]) + q[2 * MAXB]) + q[3 * MAXB]), a.score_func);
+    st_relaxed64(a.rl + (long long)b * a.E + r0 + rr, tg | __float_as_uint(sc));
+  }
+  named_bar_sync(4, 32 * nw);  // qs is read above; the warps reuse that memory afterwards
+}
+
+// ------------------------------------------------------------------ plan (warps 2-3, 64 threads)
+// Scores of every (token, expert) from the tagged router partials (polled, bounded), top-k per token
+// (ties -> lower index), weights / (sum + 1e-20) * route_scale, then the slots: the experts any token
+// chose, in expert order, each with its per-token routing weight. sc / bi: [B][E] scratch.
+// Top-k of token b (one warp): experts lane + 32 j, j < NJ, as order-preserving keys in registers,
+// each packed with its j (lower j wins a tie) so that a lane's best is a depth-log2(NJ) max tree;
+// then the warp's best key and, among lanes holding it, the lowest expert. Ties go to the lower
+// expert index. Weights: score / (sum + 1e-20) * route_scale.
+template <int NJ>
+__device__ void topk_token(const TcArgs& a, TcPlan& pl, const float* sc, const float* bi, int b, int lane) {
+  const float* v = bi + b * a.E;
+  unsigned long long pk[NJ];
+#pragma unroll
+  for (int j = 0; j < NJ; ++j)
+    pk[j] = lane + 32 * j < a.E ? ((unsigned long long)score_key_tc(v[lane + 32 * j]) << 32) | (unsigned)(NJ - 1 - j) : 0ull;
+  unsigned mine = 0u;
+  for (int r = 0; r < a.topk; ++r) {
+    unsigned long long t[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) t[j] = pk[j];
+#pragma unroll
+    for (int w = NJ / 2; w >= 1; w /= 2)
+#pragma unroll
+      for (int j = 0; j < w; ++j) t[j] = t[j] > t[j + w] ? t[j] : t[j + w];
+    const unsigned bk = (unsigned)(t[0] >> 32);
+    const int bj = NJ - 1 - (int)(t[0] & 0xFFFFu);
+    const unsigned m = __reduce_max_sync(0xffffffffu, bk);
+    unsigned bi_ = __reduce_min_sync(0xffffffffu, bk == m ? (unsigned)(lane + 32 * bj) : 0xFFFFFFFFu);
+    if (bi_ >= (unsigned)a.E) bi_ = 0u;
+    if (lane == r) mine = bi_;
+    if (lane == (int)(bi_ & 31u)) {
+#pragma unroll
+      for (int j = 0; j < NJ; ++j)
+        if (j == (int)(bi_ >> 5)) pk[j] = 0ull;
+    }
+  }
+  const float wv = lane < a.topk ? sc[b * a.E + mine] : 0.f;
+  float tot = 0.f;
+  for (int r = 0; r < a.topk; ++r) tot += __shfl_sync(0xffffffffu, wv, r);
+  if (lane < a.topk) {
+    const float w = wv / (tot + 1e-20f) * a.route_scale;
+    pl.sel[b][lane] = (int)mine;
+    pl.selw[b][lane] = w;
+    if (blockIdx.x == 0) {
+      if (a.idx) a.idx[b * a.topk + lane] = mine;
+      if (a.wt) a.wt[b * a.topk + lane] = w;
     }
   }
 }
 
-// ------------------------------------------------------------------ plan (warps 1..7, 224 threads)
-// Scores of every (token, expert) from the tagged router partials (polled, bounded), top-k per token
-// (ties -> lower index), weights / (sum + 1e-20) * route_scale, then the slots: the experts any token
-// chose, in expert order, each with its per-token routing weight. sc / bi: [B][E] scratch.
+constexpr int PT = 64, BAR_PLAN = 3;  // plan threads (warps 2 and 3) and their named barrier
 __device__ __noinline__ bool make_plan(const TcArgs& a, TcPlan& pl, float* sc, float* bi, unsigned* emask, int t7) {
   const int w7 = t7 >> 5, lane = t7 & 31;
   const int n = a.B * a.E;
   const unsigned tag = pl.tag;
   const uint64_t t0 = globaltimer_ns();
-  for (int i0 = t7; i0 < n; i0 += 2 * 224) {
-    double q[2][4];
+  // Eight (token, expert) scores per thread and pass, their tagged words and biases all loaded before
+  // any is checked: one memory round trip per pass once every CTA has published its rows.
+  constexpr int NB = 8;
+  for (int i0 = t7; i0 < n; i0 += NB * PT) {
+    unsigned long long w[NB];
+    float bs[NB];
     unsigned need = 0u;
 #pragma unroll
-    for (int u = 0; u < 2; ++u)
-      if (i0 + u * 224 < n) need |= 0xFu << (4 * u);
+    for (int u = 0; u < NB; ++u) {
+      const int i = i0 + u * PT;
+      if (i < n) {
+        need |= 1u << u;
+        const int b = i / a.E, e = i - b * a.E;
+        const bool vl = a.bias_vl != nullptr && a.image_mask != nullptr && a.image_mask[b] != 0;
+        bs[u] = (vl ? a.bias_vl : a.bias)[e];
+      }
+    }
     while (need != 0u) {
-      unsigned long long w[2][4][2];
 #pragma unroll
-      for (int u = 0; u < 2; ++u)
+      for (int u = 0; u < NB; ++u)
+        if ((need >> u) & 1u) w[u] = ld_relaxed64(a.rl + i0 + u * PT);
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          if ((need >> (4 * u + c)) & 1u) ld_ll2(a.rl + 2 * ((long long)(i0 + u * 224) * 4 + c), w[u][c][0], w[u][c][1]);
-#pragma unroll
-      for (int u = 0; u < 2; ++u)
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          if (((need >> (4 * u + c)) & 1u) && (unsigned)(w[u][c][0] >> 32) == tag && (unsigned)(w[u][c][1] >> 32) == tag) {
-            q[u][c] = __longlong_as_double((long long)((w[u][c][0] << 32) | (w[u][c][1] & 0xFFFFFFFFull)));
-            need &= ~(1u << (4 * u + c));
-          }
+      for (int u = 0; u < NB; ++u)
+        if (((need >> u) & 1u) && (unsigned)(w[u] >> 32) == tag) {
+          const float sv = __uint_as_float((unsigned)w[u]);
+          sc[i0 + u * PT] = sv;
+          bi[i0 + u * PT] = sv + bs[u];
+          need &= ~(1u << u);
+        }
       if (need != 0u && (ld_relaxed32(a.status) != 0u || globaltimer_ns() - t0 > kWait)) {
         atomicOr(a.status, ST_PLAN);
         pl.abort = 1;
@@ -392,62 +502,22 @@ __device__ __noinline__ bool make_plan(const TcArgs& a, TcPlan& pl, float* sc, f
       }
     }
     if (need != 0u) break;
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int i = i0 + u * 224;
-      if (i < n) {
-        const int b = i / a.E, e = i - b * a.E;
-        const bool vl = a.bias_vl != nullptr && a.image_mask != nullptr && a.image_mask[b] != 0;
-        const float s = fscore_tc(__double2float_rn(((q[u][0] + q[u][1]) + q[u][2]) + q[u][3]), a.score_func);
-        sc[i] = s;
-        bi[i] = s + (vl ? a.bias_vl : a.bias)[e];
-      }
-    }
   }
-  if (bar_any(1, 224, pl.abort != 0)) return false;
+  if (bar_any(BAR_PLAN, PT, pl.abort != 0)) return false;
   if (blockIdx.x == 0 && a.scores)
-    for (int i = t7; i < n; i += 224) a.scores[i] = sc[i];
-  // top-k of token b by warp b % 7: keys of the lane's experts (lane + 32 j) in registers
-  for (int b = w7; b < a.B; b += 7) {
-    constexpr int NJ = MAXE / 32;
-    const float* v = bi + b * a.E;
-    unsigned key[NJ];
-#pragma unroll
-    for (int j = 0; j < NJ; ++j) key[j] = lane + 32 * j < a.E ? score_key_tc(v[lane + 32 * j]) : 0u;
-    unsigned mine = 0u;
-    for (int r = 0; r < a.topk; ++r) {
-      unsigned bk = 0u;
-      int bj = 0;
-#pragma unroll
-      for (int j = 0; j < NJ; ++j)
-        if (key[j] > bk) {  // strict: the lower j keeps a tie
-          bk = key[j];
-          bj = j;
-        }
-      const unsigned m = __reduce_max_sync(0xffffffffu, bk);
-      unsigned bi_ = __reduce_min_sync(0xffffffffu, bk == m ? (unsigned)(lane + 32 * bj) : 0xFFFFFFFFu);
-      if (bi_ >= (unsigned)a.E) bi_ = 0u;
-      if (lane == r) mine = bi_;
-      if (lane == (int)(bi_ & 31u)) {
-#pragma unroll
-        for (int j = 0; j < NJ; ++j)
-          if (j == (int)(bi_ >> 5)) key[j] = 0u;
-      }
-    }
-    const float wv = lane < a.topk ? sc[b * a.E + mine] : 0.f;
-    float tot = 0.f;
-    for (int r = 0; r < a.topk; ++r) tot += __shfl_sync(0xffffffffu, wv, r);
-    if (lane < a.topk) {
-      const float w = wv / (tot + 1e-20f) * a.route_scale;
-      pl.sel[b][lane] = (int)mine;
-      pl.selw[b][lane] = w;
-      if (blockIdx.x == 0) {
-        if (a.idx) a.idx[b * a.topk + lane] = mine;
-        if (a.wt) a.wt[b * a.topk + lane] = w;
-      }
-    }
+    for (int i = t7; i < n; i += PT) a.scores[i] = sc[i];
+  // top-k of token b by warp b % 2: keys of the lane's experts (lane + 32 j) in registers
+  for (int b = w7; b < a.B; b += PT / 32) {
+    if (a.E <= 128)
+      topk_token<4>(a, pl, sc, bi, b, lane);
+    else if (a.E <= 256)
+      topk_token<8>(a, pl, sc, bi, b, lane);
+    else if (a.E <= 512)
+      topk_token<16>(a, pl, sc, bi, b, lane);
+    else
+      topk_token<32>(a, pl, sc, bi, b, lane);
   }
-  named_bar_sync(1, 224);
+  named_bar_sync(BAR_PLAN, PT);
   if (a.B == 1) {
     // one token: its k distinct picks are the slots, in expert order
     if (w7 == 0 && lane < a.topk) {
@@ -460,10 +530,10 @@ __device__ __noinline__ bool make_plan(const TcArgs& a, TcPlan& pl, float* sc, f
     }
     if (t7 == 0) pl.nr = a.topk;
   } else {
-    for (int e = t7; e < a.E; e += 224) emask[e] = 0u;
-    named_bar_sync(1, 224);
-    for (int i = t7; i < a.B * a.topk; i += 224) atomicOr(&emask[pl.sel[i / a.topk][i % a.topk]], 1u << (i / a.topk));
-    named_bar_sync(1, 224);
+    for (int e = t7; e < a.E; e += PT) emask[e] = 0u;
+    named_bar_sync(BAR_PLAN, PT);
+    for (int i = t7; i < a.B * a.topk; i += PT) atomicOr(&emask[pl.sel[i / a.topk][i % a.topk]], 1u << (i / a.topk));
+    named_bar_sync(BAR_PLAN, PT);
     if (w7 == 0) {  // compaction in expert order, 32 experts per step
       int base = 0;
       for (int e0 = 0; e0 < a.E; e0 += 32) {
@@ -486,29 +556,81 @@ __device__ __noinline__ bool make_plan(const TcArgs& a, TcPlan& pl, float* sc, f
       if (lane == 0) pl.nr = base;
     }
   }
-  named_bar_sync(1, 224);
+  named_bar_sync(BAR_PLAN, PT);
   return true;
 }
 
 // Token rows -> per-token power-of-two pre-scale (amax 2^-p in [128, 256)) -> the MMA's B tile of
 // the w1|w3 phase: [H / 128 blocks][16 rows][128 B], K-major SW128; row t < 8 holds the e4m3 "hi"
 // part of token t, row 8 + t its "lo" part (x 2^-p ~ hi + lo / 16); rows of tokens >= B are zero.
+// 224 threads (warps 1-7); thread t7 owns the 16-element chunk columns c = t7 + 224 r of every token.
+// With up to XBT tokens and XC columns a thread (H <= 7168) the chunks are loaded once, all before
+// their first use, and stay in registers; otherwise the conversion loads them again.
+constexpr int XT = 224, XC = 2, XBT = 4;
+__device__ __forceinline__ float amax16(const uint4& u0, const uint4& u1) {
+  const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+  float m = 0.f;
+#pragma unroll
+  for (int h = 0; h < 8; ++h)
+    m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w[h] << 16)), fabsf(__uint_as_float(w[h] & 0xFFFF0000u))));
+  return m;
+}
+__device__ __forceinline__ void put_xb(uint8_t* xb, int b, int c, float inv, const uint4& u0, const uint4& u1) {
+  uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
+  const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+  for (int h = 0; h < 8; ++h) {
+    uint32_t h2, l2;
+    split2_e4m3(__uint_as_float(w[h] << 16) * inv, __uint_as_float(w[h] & 0xFFFF0000u) * inv, h2, l2);
+    hw[h >> 1] |= h2 << (16 * (h & 1));
+    lw[h >> 1] |= l2 << (16 * (h & 1));
+  }
+  uint8_t* blk = xb + (size_t)(c >> 3) * 2048;
+  *reinterpret_cast<uint4*>(blk + sw128_off(b, c & 7)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+  *reinterpret_cast<uint4*>(blk + sw128_off(8 + b, c & 7)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+}
 __device__ __noinline__ void build_xb(const TcArgs& a, uint8_t* xb, TcPlan& pl, float* red, int t7) {
   const int w7 = t7 >> 5, lane = t7 & 31;
-  for (int b = 0; b < a.B; ++b) {
-    const uint4* src = reinterpret_cast<const uint4*>(a.x + (long long)b * a.H);
-    float m = 0.f;
-    for (int v = t7; v < a.H / 8; v += 224) {
-      const uint4 u = src[v];
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  const int nc = a.H / 16;
+  const bool keep = nc <= XT * XC && a.B <= XBT;
+  uint4 v[XBT][XC][2];
+  if (keep) {
 #pragma unroll
-      for (int h = 0; h < 4; ++h)
-        m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w[h] << 16)), fabsf(__uint_as_float(w[h] & 0xFFFF0000u))));
-    }
-    m = warp_max(m);
-    if (lane == 0) red[b * 8 + w7] = m;
+    for (int b = 0; b < XBT; ++b)
+#pragma unroll
+      for (int r = 0; r < XC; ++r) {
+        const int c = t7 + XT * r;
+        if (b < a.B && c < nc) {
+          const uint4* src = reinterpret_cast<const uint4*>(a.x + (long long)b * a.H + 16 * c);
+          v[b][r][0] = src[0];
+          v[b][r][1] = src[1];
+        }
+      }
   }
-  named_bar_sync(1, 224);
+  // the whole tile to zero while the loads are in flight (the rows of absent tokens stay zero)
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  for (int o = t7; o < a.KB1 * 128; o += XT) reinterpret_cast<uint4*>(xb)[o] = z;
+  if (keep) {
+#pragma unroll
+    for (int b = 0; b < XBT; ++b) {
+      if (b >= a.B) break;
+      float m = 0.f;
+#pragma unroll
+      for (int r = 0; r < XC; ++r)
+        if (t7 + XT * r < nc) m = fmaxf(m, amax16(v[b][r][0], v[b][r][1]));
+      m = warp_max(m);
+      if (lane == 0) red[b * 8 + w7] = m;
+    }
+  } else {
+    for (int b = 0; b < a.B; ++b) {
+      const uint4* src = reinterpret_cast<const uint4*>(a.x + (long long)b * a.H);
+      float m = 0.f;
+      for (int c = t7; c < nc; c += XT) m = fmaxf(m, amax16(src[2 * c], src[2 * c + 1]));
+      m = warp_max(m);
+      if (lane == 0) red[b * 8 + w7] = m;
+    }
+  }
+  named_bar_sync(1, XT);
   if (t7 < a.B) {
     float m = 0.f;
     for (int w = 0; w < 7; ++w) m = fmaxf(m, red[t7 * 8 + w]);
@@ -520,30 +642,25 @@ __device__ __noinline__ void build_xb(const TcArgs& a, uint8_t* xb, TcPlan& pl, 
     }
     pl.xscale[t7] = ldexpf(1.0f, p);
   }
-  named_bar_sync(1, 224);
-  const int nc = a.H / 16;
-  for (int i = t7; i < MAXB * nc; i += 224) {
-    const int b = i / nc, c = i - b * nc;
-    uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
-    if (b < a.B) {
-      const float inv = 1.0f / pl.xscale[b];
-      const uint4* src = reinterpret_cast<const uint4*>(a.x + (long long)b * a.H + 16 * c);
-      const uint4 u0 = src[0], u1 = src[1];
-      const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+  named_bar_sync(1, XT);
+  if (keep) {
 #pragma unroll
-      for (int h = 0; h < 8; ++h) {
-        uint32_t h2, l2;
-        split2_e4m3(__uint_as_float(w[h] << 16) * inv, __uint_as_float(w[h] & 0xFFFF0000u) * inv, h2, l2);
-        hw[h >> 1] |= h2 << (16 * (h & 1));
-        lw[h >> 1] |= l2 << (16 * (h & 1));
-      }
+    for (int b = 0; b < XBT; ++b) {
+      if (b >= a.B) break;
+      const float inv = 1.0f / pl.xscale[b];
+#pragma unroll
+      for (int r = 0; r < XC; ++r)
+        if (t7 + XT * r < nc) put_xb(xb, b, t7 + XT * r, inv, v[b][r][0], v[b][r][1]);
     }
-    uint8_t* blk = xb + (size_t)(c >> 3) * 2048;
-    *reinterpret_cast<uint4*>(blk + sw128_off(b, c & 7)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    *reinterpret_cast<uint4*>(blk + sw128_off(8 + b, c & 7)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  } else {
+    for (int b = 0; b < a.B; ++b) {
+      const uint4* src = reinterpret_cast<const uint4*>(a.x + (long long)b * a.H);
+      const float inv = 1.0f / pl.xscale[b];
+      for (int c = t7; c < nc; c += XT) put_xb(xb, b, c, inv, src[2 * c], src[2 * c + 1]);
+    }
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> the tensor core's reads
-  named_bar_sync(1, 224);
+  named_bar_sync(1, XT);
 }
 
 // ------------------------------------------------------------------ pipeline state in shared memory
@@ -592,11 +709,11 @@ __device__ __forceinline__ int ksteps(int I_loc, int kind, int j) { return kind 
 // Position in a CTA's stream: (kind, unit, K block) and the ring stage g.
 struct Cur {
   int k, u, j, g;
-  __device__ void start(const Pipe& P, int kmin) {
+  __device__ void start(const Pipe& P, int kmin, int g0) {
     k = kmin;
     u = 0;
     j = 0;
-    g = 0;
+    g = g0;
     settle(P);
   }
   __device__ void settle(const Pipe& P) {  // to the first block of the current or a later unit
@@ -619,22 +736,28 @@ struct Cur {
 
 __device__ __forceinline__ void backoff() { __nanosleep(64); }
 
+// Waits (bounded) until the plan and the routed units are published.
+__device__ void wait_ready(const TcArgs& a, TcPlan& pl) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!pl.ready && !pl.abort) {
+    backoff();
+    if (globaltimer_ns() - t0 > kWait) {
+      atomicOr(a.status, ST_PLAN);
+      pl.abort = 1;
+    }
+  }
+  __threadfence_block();  // the routed units and the plan, written before `ready`
+}
+
 // ---- warp 0, lane 0: TMA producer. One 128 x 128 tensor box per stage (plus an FP4 block's scales).
-__device__ __noinline__ void role_producer(const TcArgs& a, TcPlan& pl, const Pipe P) {
+__device__ __noinline__ void role_producer(const TcArgs& a, TcPlan& pl, const Pipe& Pin) {
+  const Pipe P = Pin;
   const uint64_t pol = l2_evict_first();
   int slot = 0, ph = 0, g = 0;
   for (int k = 0; k < 4 && !pl.abort; ++k) {
     if (k == 1) {  // routed work needs the plan
-      const uint64_t t0 = globaltimer_ns();
-      while (!pl.ready && !pl.abort) {
-        backoff();
-        if (globaltimer_ns() - t0 > kWait) {
-          atomicOr(a.status, ST_PLAN);
-          pl.abort = 1;
-        }
-      }
+      wait_ready(a, pl);
       if (pl.abort) break;
-      __threadfence_block();  // the routed units and the plan, written before `ready`
     }
     const bool w13 = k < 2, routed = k & 1;
     const bool f4 = routed && a.r_fmt == DSMOE_FMT_FP4;
@@ -646,7 +769,15 @@ __device__ __noinline__ void role_producer(const TcArgs& a, TcPlan& pl, const Pi
       const Unit U = P.units[k * UMAX + u];
       const uint8_t* eb = w13 ? a.r13 + (long long)U.expert * a.r_eb13 : a.r2 + (long long)U.expert * a.r_eb2;
       for (int j = U.j0; j < U.j0 + U.n; ++j) {
-        if (g >= P.S && !pwait(a, pl, &P.empty[slot], ph ^ 1)) break;
+        // At most `depth` stages in flight: the weight bytes HBM needs to run at full rate (about 64 KB a
+        // SM), and no more, since every extra byte in flight is queueing delay for the kernel's other
+        // memory traffic (router, partials, exchange). Stages complete in order, so waiting for stage
+        // g - depth also frees slot g % S.
+        const int depth = f4 ? P.S : min(P.S, kDepth8);
+        if (g >= depth) {
+          const int q = g - depth;
+          if (!pwait(a, pl, &P.empty[q % P.S], (q / P.S) & 1)) break;
+        }
         uint8_t* A = P.ring + (size_t)slot * STAGE;
         const int blk = U.tile * per + j;
         mbar_expect_tx(&P.full[slot], bytes);
@@ -666,7 +797,8 @@ __device__ __noinline__ void role_producer(const TcArgs& a, TcPlan& pl, const Pi
 }
 
 // ---- warp 2, lane 0: the B tile (h of the slot) of every w2 stage, once the slot is finished
-__device__ __noinline__ void role_hcopy(const TcArgs& a, TcPlan& pl, const Pipe P, int SH) {
+__device__ __noinline__ void role_hcopy(const TcArgs& a, TcPlan& pl, const Pipe& Pin, int SH) {
+  const Pipe P = Pin;
   int g = 0;
   for (int k = 0; k < 2; ++k)
     for (int u = 0; u < P.ucnt[k]; ++u) g += P.units[k * UMAX + u].n;
@@ -686,7 +818,7 @@ __device__ __noinline__ void role_hcopy(const TcArgs& a, TcPlan& pl, const Pipe 
           }
         }
         if (si != ready_slot) {
-          while (tag_count(a.sdone + si, pl.tag) < (unsigned)a.P1 && !pl.abort) {
+          while (ld_relaxed64(pl.sdone + si) < (unsigned long long)a.P1 && !pl.abort) {
             backoff();
             if (ld_relaxed32(a.status) != 0u || globaltimer_ns() - t0 > kWait) {
               atomicOr(a.status, ST_CNT);
@@ -706,17 +838,45 @@ __device__ __noinline__ void role_hcopy(const TcArgs& a, TcPlan& pl, const Pipe 
   }
 }
 
+// Instruction descriptors: FP8 x FP8 (kind::f8f6f4) and e2m1 x e4m3 with e8m0 block scales
+// (kind::mxf8f6f4), both M = 128, N = 16, fp32 accumulate.
+constexpr uint32_t kIdesc8 = (1u << 4) | ((16u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t kIdescX = (5u << 7) | ((16u >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24);
+
+// The four 32-K MMAs of one stage, issued back to back. A 32-byte step along K is +2 in the start
+// address field of a 128-byte-swizzled descriptor (stage bases are 1 KB aligned, so the field
+// never carries); every operand is known before the first MMA goes out, which keeps the issuing
+// thread's serial latency out of the tensor core's way.
+__device__ __forceinline__ void mma4_f8(uint32_t d, uint64_t da, uint64_t db, uint32_t acc0) {
+  mma_f8(d, da, db, kIdesc8, acc0);
+  mma_f8(d, da + 2, db + 2, kIdesc8, 1u);
+  mma_f8(d, da + 4, db + 4, kIdesc8, 1u);
+  mma_f8(d, da + 6, db + 6, kIdesc8, 1u);
+}
+__device__ __forceinline__ void mma4_mx(uint32_t d, uint64_t da, uint64_t db, uint32_t sfa, uint32_t sfb,
+                                        uint32_t acc0) {
+  mma_mx(d, da, db, kIdescX, sfa, sfb, acc0);
+  mma_mx(d, da + 2, db + 2, kIdescX | (1u << 29) | (1u << 4), sfa | (1u << 30), sfb | (1u << 30), 1u);
+  mma_mx(d, da + 4, db + 4, kIdescX | (2u << 29) | (2u << 4), sfa | (2u << 30), sfb | (2u << 30), 1u);
+  mma_mx(d, da + 6, db + 6, kIdescX | (3u << 29) | (3u << 4), sfa | (3u << 30), sfb | (3u << 30), 1u);
+}
+
 // ---- warp 1, lane 0: MMA issuer
-__device__ __noinline__ void role_mma(const TcArgs& a, TcPlan& pl, const Pipe P) {
-  constexpr uint32_t idesc8 = (1u << 4) | ((16u >> 3) << 17) | ((128u >> 4) << 24);
-  constexpr uint32_t idescx = (5u << 7) | ((16u >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24);
+__device__ __noinline__ void role_mma(const TcArgs& a, TcPlan& pl, const Pipe& Pin) {
+  const Pipe P = Pin;
   int slot = 0, ph = 0, nseg = 0, n4 = 0, cur_a = 0, cur_g = -1;
   uint32_t c4 = 0u;  // FP4 uses per ring slot, mod 2 (bit s): the phases of its scale-factor barrier
   bool open = false, ok = true;
   const uint32_t ring = smem_u32(P.ring), xb = smem_u32(P.xb);
+  const bool w2_aligned = (a.row0 & 127) == 0;  // every w2 stage is then one FP8 scale segment
   for (int k = 0; k < 4 && ok; ++k) {
+    if (k == 1) {  // the routed units exist once the plan is published
+      wait_ready(a, pl);
+      if (pl.abort) break;
+    }
     const bool f4 = (k & 1) && a.r_fmt == DSMOE_FMT_FP4;
-    for (int u = 0; u < P.ucnt[k] && ok; ++u) {
+    const int nu = P.ucnt[k];
+    for (int u = 0; u < nu && ok; ++u) {
       const Unit U = P.units[k * UMAX + u];
       for (int j = U.j0; j < U.j0 + U.n; ++j) {
         const bool first = j == U.j0, last = j == U.j0 + U.n - 1;
@@ -734,6 +894,7 @@ __device__ __noinline__ void role_mma(const TcArgs& a, TcPlan& pl, const Pipe P)
         fence_after();
         const uint32_t aA = ring + slot * STAGE;
         const uint32_t bB = k < 2 ? xb + j * 2048 : aA + SA;
+        const uint64_t da = desc_sw128(aA), db = desc_sw128(bB);
         const int nk = ksteps(a.I_loc, k, j);
         if (f4) {
           const int par = n4 & 1;
@@ -744,22 +905,43 @@ __device__ __noinline__ void role_mma(const TcArgs& a, TcPlan& pl, const Pipe P)
             }
             fence_after();
           }
-          for (int q = 0; q < nk; ++q)
-            mma_mx(P.tm + TM_ACC4 + 16 * par, desc_sw128(aA + 32 * q), desc_sw128(bB + 32 * q),
-                   idescx | ((uint32_t)q << 29) | ((uint32_t)q << 4), (P.tm + TM_SFA + 4 * slot) | ((uint32_t)q << 30),
-                   (P.tm + TM_SFB) | ((uint32_t)q << 30), (first && q == 0) ? 0u : 1u);
+          const uint32_t d = P.tm + TM_ACC4 + 16 * par, sfa = P.tm + TM_SFA + 4 * slot, sfb = P.tm + TM_SFB;
+          if (nk == 4) {
+            mma4_mx(d, da, db, sfa, sfb, first ? 0u : 1u);
+          } else {
+            for (int q = 0; q < nk; ++q)
+              mma_mx(d, da + 2 * q, db + 2 * q, kIdescX | ((uint32_t)q << 29) | ((uint32_t)q << 4),
+                     sfa | ((uint32_t)q << 30), sfb | ((uint32_t)q << 30), (first && q == 0) ? 0u : 1u);
+          }
           commit(&P.empty[slot]);
           if (last) {
             commit(&P.a4f[par]);
             ++n4;
           }
-        } else {
+        } else if (nk == 4 && (k < 2 || w2_aligned)) {  // the stage is exactly one scale segment
+          if (open) {
+            commit(&P.accf[cur_a]);
+            open = false;
+          }
+          cur_a = nseg & (NACC8 - 1);
+          if (nseg >= NACC8) {
+            if (!pwait(a, pl, &P.accr[cur_a], ((nseg / NACC8) - 1) & 1)) {
+              ok = false;
+              break;
+            }
+            fence_after();
+          }
+          ++nseg;
+          mma4_f8(P.tm + 16 * cur_a, da, db, 0u);
+          commit(&P.empty[slot]);
+          commit(&P.accf[cur_a]);
+        } else {  // w2 stage of a slice that starts inside a 128-row block: segments change mid-stage
           for (int q = 0; q < nk; ++q) {
             const int gk = seg_key(a.row0, k, j, q);
             bool fresh = false;
             if (!open || gk != cur_g) {
               if (open) commit(&P.accf[cur_a]);
-              cur_a = nseg % NACC8;
+              cur_a = nseg & (NACC8 - 1);
               if (nseg >= NACC8) {
                 if (!pwait(a, pl, &P.accr[cur_a], ((nseg / NACC8) - 1) & 1)) {
                   ok = false;
@@ -772,7 +954,7 @@ __device__ __noinline__ void role_mma(const TcArgs& a, TcPlan& pl, const Pipe P)
               open = true;
               fresh = true;
             }
-            mma_f8(P.tm + 16 * cur_a, desc_sw128(aA + 32 * q), desc_sw128(bB + 32 * q), idesc8, fresh ? 0u : 1u);
+            mma_f8(P.tm + 16 * cur_a, da + 2 * q, db + 2 * q, kIdesc8, fresh ? 0u : 1u);
           }
           if (!ok) break;
           commit(&P.empty[slot]);
@@ -792,23 +974,159 @@ __device__ __noinline__ void role_mma(const TcArgs& a, TcPlan& pl, const Pipe P)
   mbar_wait(P.mdone, 0, kWait);
 }
 
+// ---- finishing by the last contributor's epilogue (warps 4-7, 128 threads, named barrier 2)
+// w1|w3 tile p of slot index si: the tile's partials summed in contributor order (this CTA's own from
+// registers, the others' rows loaded together), h = SiLU(min(g, 10)) * clamp(u, +-10) * kHScale for
+// its 64 intermediate rows (gate row r in thread r, up row in thread 64 + r), as e4m3 hi / lo bytes
+// into the slot's w2 B tile; then the slot's count of finished tiles.
+__device__ __noinline__ void epi_finish_w13(const TcArgs& a, TcPlan& pl, int kind, int si, int p, int tile_id, int jc,
+                                            const float (&own)[MAXB], int m, float* ef) {
+  const int nc = contrib_count(pl.wk.sp[kind], tile_id);
+  const float* base = a.p13 + ((long long)si * a.P1 + p) * MAXC * 1024 + m * 8;
+  uint4 v[MAXC][2];
+#pragma unroll
+  for (int j = 0; j < MAXC; ++j)
+    if (j < nc && j != jc) {
+      v[j][0] = ld_cg16(base + j * 1024);
+      if (a.B > 4) v[j][1] = ld_cg16(base + j * 1024 + 4);
+    }
+  float s[MAXB];
+#pragma unroll
+  for (int t = 0; t < MAXB; ++t) s[t] = 0.f;
+#pragma unroll
+  for (int j = 0; j < MAXC; ++j)
+    if (j < nc) {
+      if (j == jc) {
+#pragma unroll
+        for (int t = 0; t < MAXB; ++t) s[t] += own[t];
+      } else {
+        s[0] += __uint_as_float(v[j][0].x);
+        s[1] += __uint_as_float(v[j][0].y);
+        s[2] += __uint_as_float(v[j][0].z);
+        s[3] += __uint_as_float(v[j][0].w);
+        if (a.B > 4) {
+          s[4] += __uint_as_float(v[j][1].x);
+          s[5] += __uint_as_float(v[j][1].y);
+          s[6] += __uint_as_float(v[j][1].z);
+          s[7] += __uint_as_float(v[j][1].w);
+        }
+      }
+    }
+  if (m >= 64) {
+#pragma unroll
+    for (int t = 0; t < MAXB; ++t) ef[(m - 64) * 8 + t] = s[t];
+  }
+  named_bar_sync(2, 128);
+  float* hs = ef + 64 * 8;  // [token][row]
+  if (m < 64) {
+#pragma unroll
+    for (int t = 0; t < MAXB; ++t) {
+      const float gv = fminf(s[t], 10.0f);
+      const float uv = fminf(fmaxf(ef[m * 8 + t], -10.0f), 10.0f);
+      hs[t * 64 + m] = t < a.B ? silu_tc(gv) * uv * kHScale : 0.f;
+    }
+  }
+  named_bar_sync(2, 128);
+  // 16 B pieces: (B-tile row n = hi / lo of token n % 8, chunk of 16 K) -> SW128 position
+  uint8_t* blk = a.hb + ((long long)si * a.KB2 + (p >> 1)) * 2048;
+  const bool last_half = p == a.P1 - 1 && (p & 1) == 0;  // the block's second half lies past the slice: zero it
+  if (m < 64 || last_half) {
+    const int n = (m & 63) >> 2, c4 = m & 3;
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if (m < 64) {
+      const int t = n & 7;
+      const bool lo = n >= 8;
+      const float* hv = hs + t * 64 + 16 * c4;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        uint32_t h2, l2;
+        split2_e4m3(hv[2 * q], hv[2 * q + 1], h2, l2);
+        w[q >> 1] |= (lo ? l2 : h2) << (16 * (q & 1));
+      }
+    }
+    const int cc = (m < 64 ? (p & 1) * 4 : 4) + c4;
+    *reinterpret_cast<uint4*>(blk + sw128_off(n, cc)) = make_uint4(w[0], w[1], w[2], w[3]);
+    asm volatile("fence.proxy.async.global;" ::: "memory");  // the B tile is read by bulk copies
+  }
+  named_bar_sync(2, 128);
+  if (m == 0) {
+    fence_acq_rel_gpu();  // release: every thread's B-tile bytes (ordered by the barrier) before the count
+    atomicAdd(pl.sdone + si, 1ull);
+  }
+}
+
+// Output tile mt at N = 1: y rows [128 mt, 128 mt + 128) = the sum over the routed slots (in order)
+// and the shared expert of their partials in contributor order; row m in thread m, eight partial rows
+// loaded together per pass.
+__device__ __noinline__ void epi_finish_w2(const TcArgs& a, TcPlan& pl, int mt, int SH, int m, int* ecnt) {
+  const int nr = pl.nr, nl = nr + 1;
+  for (int i = m; i < nl; i += 128) ecnt[i] = contrib_count(pl.wk.sp[i < nr ? 3 : 2], i < nr ? i * a.MT2 + mt : mt);
+  named_bar_sync(2, 128);
+  const float* base = a.p2 + (long long)mt * a.slot_cap * MAXC * 1024 + m * 8;
+  float s[MAXB];
+#pragma unroll
+  for (int t = 0; t < MAXB; ++t) s[t] = 0.f;
+  int li = 0, j = 0;
+  while (li < nl) {
+    uint4 v[8][2];
+    bool on[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      while (li < nl && j >= ecnt[li]) {
+        ++li;
+        j = 0;
+      }
+      on[q] = li < nl;
+      if (on[q]) {
+        const float* src = base + ((long long)(li < nr ? li : SH) * MAXC + j) * 1024;
+        v[q][0] = ld_cg16(src);
+        if (a.B > 4) v[q][1] = ld_cg16(src + 4);
+        ++j;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (on[q]) {
+        s[0] += __uint_as_float(v[q][0].x);
+        s[1] += __uint_as_float(v[q][0].y);
+        s[2] += __uint_as_float(v[q][0].z);
+        s[3] += __uint_as_float(v[q][0].w);
+        if (a.B > 4) {
+          s[4] += __uint_as_float(v[q][1].x);
+          s[5] += __uint_as_float(v[q][1].y);
+          s[6] += __uint_as_float(v[q][1].z);
+          s[7] += __uint_as_float(v[q][1].w);
+        }
+      }
+  }
+#pragma unroll
+  for (int t = 0; t < MAXB; ++t) {
+    if (t >= a.B) break;
+    const long long o = (long long)t * a.H + 128 * mt + m;
+    if (a.y_f32)
+      reinterpret_cast<float*>(a.y)[o] = s[t];
+    else
+      reinterpret_cast<__nv_bfloat16*>(a.y)[o] = __float2bfloat16_rn(s[t]);
+  }
+}
+
 // ---- warps 4-7: epilogue. Thread = accumulator row m = 32 q + lane (TMEM lane quadrant q).
-__device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pipe P, float* etab, int q, int lane,
-                                           int SH) {
-  Work wk;
-  wk.init(a, pl.nr);
+__device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pipe& Pin, float* etab, float* efin,
+                                           int q, int lane, int SH) {
+  const Pipe P = Pin;  // in registers from here on
   const int m = 32 * q + lane;
   const uint32_t trow = P.tm + ((uint32_t)(32 * q) << 16);
   const int look = P.S > 2 ? 2 : P.S - 1;
   const bool fp4l = a.r_fmt == DSMOE_FMT_FP4;
-  int nseg = 0, n4 = 0, cur_g = -1, seg_j = 0, seg_w = 0, unit = 0;
+  const bool w2_aligned = (a.row0 & 127) == 0;  // every w2 stage is then one FP8 scale segment
+  int nseg = 0, n4 = 0, cur_g = -1, seg_ti = 0, unit = 0;
   bool open = false, live = true;
   float acc[MAXB];
-  Cur sf;  // runs ahead over the stream: FP4 scale factors of a stage into tensor memory
-  sf.start(P, 0);
+  Cur sf;  // runs ahead over the routed stages: FP4 scale factors of a stage into tensor memory
+  sf.k = 4;
   auto store_sf = [&]() {
     const int slot = sf.g % P.S;
-    if ((sf.k & 1) && fp4l && pwait(a, pl, &P.full[slot], (sf.g / P.S) & 1)) {
+    if ((sf.k & 1) && pwait(a, pl, &P.full[slot], (sf.g / P.S) & 1)) {
       const uint4 v = *reinterpret_cast<const uint4*>(P.ring + (size_t)slot * STAGE + SA + SB + 16 * lane);
       tm_st4(trow + TM_SFA + 4 * slot, v.x, v.y, v.z, v.w);
       fence_before();
@@ -817,12 +1135,34 @@ __device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pi
     }
     sf.next(P);
   };
+  // A closed FP8 segment: its accumulator times the segment's scale (table entry ti) into acc.
+  auto close_seg = [&](const float* tab, int ti) {
+    const int slot_a = nseg & (NACC8 - 1);
+    const bool got = pwait(a, pl, &P.accf[slot_a], (nseg / NACC8) & 1);
+    ++nseg;
+    if (!got) return;
+    fence_after();
+    float d[16];
+    tm_ld16(trow + 16 * slot_a, d);
+    fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&P.accr[slot_a]);
+    const float s = tab[ti];
+#pragma unroll
+    for (int t = 0; t < MAXB; ++t) acc[t] = fmaf(d[t] + d[8 + t] * kLoInv, s, acc[t]);
+  };
   // Control flow here is the same in all four warps whatever happens (named barriers below): after an
   // expired wait the loop keeps walking the stream but skips the waits and the work.
   int g = 0;
   for (int k = 0; k < 4; ++k) {
+    if (k == 1) {  // the routed units exist once the plan is published
+      if (m == 0) wait_ready(a, pl);
+      named_bar_sync(2, 128);
+      if (fp4l) sf.start(P, 1, g);
+    }
     const bool f4 = (k & 1) && fp4l, w13 = k < 2;
-    for (int u = 0; u < P.ucnt[k]; ++u) {
+    const int nu = P.ucnt[k];
+    for (int u = 0; u < nu; ++u) {
       const Unit U = P.units[k * UMAX + u];
       float* tab = etab + (unit & 1) * 256;
 #pragma unroll
@@ -835,11 +1175,18 @@ __device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pi
         for (int i = m; i < 4 * U.n; i += 128) tab[i] = __ldg(src + i);
         named_bar_sync(2, 128);
       }
+      // w1|w3 rows: w1 rows 0..63, w3 rows 64..127 of the tile; the scale of this row's 128-row block
+      int toff = 0;
+      if (w13) {
+        const int mat = m >> 6, r = 64 * U.tile + (m & 63);
+        toff = 2 * mat + (((a.row0 + r) >> 7) != ((a.row0 + 64 * U.tile) >> 7) ? 1 : 0);
+      }
       for (int j = U.j0; j < U.j0 + U.n; ++j, ++g) {
         const bool last = j == U.j0 + U.n - 1;
         // Never wait ahead on a w2 stage while this CTA still owes w1|w3 partials: w2 stages wait for
         // every CTA's w1|w3 work of their slot (so that wait could depend on this very epilogue).
-        while (sf.valid() && sf.g <= g + look && (sf.k < 2 || k >= 2)) store_sf();
+        if (fp4l)
+          while (sf.valid() && sf.g <= g + look && (sf.k < 2 || k >= 2)) store_sf();
         if (f4) {
           if (last) {
             const int par = n4 & 1;
@@ -855,43 +1202,22 @@ __device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pi
             }
             ++n4;
           }
-        } else {
-          // FP8: the same segments as the MMA issuer; a closed segment's accumulator times its scale
-          auto close_seg = [&]() {
-            const int slot_a = nseg % NACC8;
-            const bool got = pwait(a, pl, &P.accf[slot_a], (nseg / NACC8) & 1);
-            ++nseg;
-            if (!got) return;
-            fence_after();
-            float d[16];
-            tm_ld16(trow + 16 * slot_a, d);
-            fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&P.accr[slot_a]);
-            float s;
-            if (w13) {  // row block of this row: w1 rows 0..63, w3 rows 64..127 of the tile
-              const int mat = m >> 6, r = 64 * U.tile + (m & 63);
-              const bool second = ((a.row0 + r) >> 7) != ((a.row0 + 64 * U.tile) >> 7);
-              s = tab[4 * (seg_j - U.j0) + 2 * mat + (second ? 1 : 0)];
-            } else {
-              s = tab[4 * (seg_j - U.j0) + seg_w];
-            }
-#pragma unroll
-            for (int t = 0; t < MAXB; ++t) acc[t] = fmaf(d[t] + d[8 + t] * kLoInv, s, acc[t]);
-          };
+        } else if (w13 || w2_aligned) {  // the stage is exactly one scale segment
+          close_seg(tab, 4 * (j - U.j0) + toff);
+        } else {  // w2 of a slice that starts inside a 128-row block: the same segments as the MMA issuer
           const int nk = ksteps(a.I_loc, k, j);
           for (int qk = 0; qk < nk; ++qk) {
             const int gk = seg_key(a.row0, k, j, qk);
             if (!open || gk != cur_g) {
-              if (open) close_seg();
+              if (open) close_seg(tab, seg_ti);
               open = true;
               cur_g = gk;
-              seg_j = j;  // scale table entry: .x / .y of the block where the segment starts
-              seg_w = (!w13 && gk != ((a.row0 + 128 * j) >> 7)) ? 1 : 0;
+              // scale table entry: .x / .y of the block where the segment starts
+              seg_ti = 4 * (j - U.j0) + (gk != ((a.row0 + 128 * j) >> 7) ? 1 : 0);
             }
           }
           if (last || seg_next(a.row0, k, j) != cur_g) {
-            close_seg();
+            close_seg(tab, seg_ti);
             open = false;
           }
         }
@@ -914,20 +1240,36 @@ __device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pi
         if (a.B > 4) d4[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
       }
       named_bar_sync(2, 128);
-      if (m == 0 && live && !pl.abort) {
-        unsigned long long* cnt = w13 ? a.cnt13 + (long long)si * a.P1 + U.tile : a.cnt2 + U.tile;
-        const unsigned total = w13 ? (unsigned)a.KB1 : (unsigned)((pl.nr + 1) * a.KB2);
-        const unsigned c = tag_add(cnt, pl.tag, (unsigned)U.n);
-        if (c == 0u) {
-          atomicOr(a.status, ST_CNT);
-          pl.abort = 1;
-        } else if (c == total) {  // last contribution: the tile goes to this CTA's finisher
-          const int tail = *P.qtail;
-          P.queue[tail % QCAP] = w13 ? (si << 8) | U.tile : (1 << 30) | U.tile;
-          __threadfence_block();
-          *P.qtail = tail + 1;
+      if (m == 0) {
+        int fk = 0;  // what this CTA finishes: 1 a w1|w3 tile, 2 a w2 tile (N = 1)
+        if (live && !pl.abort) {
+          unsigned long long* cnt = w13 ? pl.cnt13 + (long long)si * a.P1 + U.tile : pl.cnt2 + U.tile;
+          const unsigned long long total = w13 ? (unsigned long long)a.KB1 : (unsigned long long)((pl.nr + 1) * a.KB2);
+          fence_acq_rel_gpu();  // release: the partial of all 128 threads (ordered by the barrier)
+          const unsigned long long c = atomicAdd(cnt, (unsigned long long)U.n) + (unsigned long long)U.n;
+          if (c == total) {  // last contribution: acquire the other contributors' partials
+            fence_acq_rel_gpu();
+            if (w13 || a.ar_world <= 1) {
+              fk = w13 ? 1 : 2;
+            } else {  // N > 1: the exchange of the output tile runs on this CTA's finisher warp
+              const int tail = *P.qtail;
+              P.queue[tail % QCAP] = U.tile;
+              __threadfence_block();
+              *P.qtail = tail + 1;
+            }
+          } else if (c > total) {
+            atomicOr(a.status, ST_CNT);
+            pl.abort = 1;
+          }
         }
+        pl.efl = fk;
       }
+      named_bar_sync(2, 128);
+      const int fk = *reinterpret_cast<volatile int*>(&pl.efl);
+      if (fk == 1)
+        epi_finish_w13(a, pl, U.slot < 0 ? 0 : 1, si, U.tile, U.tile_id, U.jc, acc, m, efin);
+      else if (fk == 2)
+        epi_finish_w2(a, pl, U.tile, SH, m, reinterpret_cast<int*>(efin + 2 * 64 * 8));
       ++unit;
     }
   }
@@ -938,33 +1280,37 @@ __device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pi
   }
 }
 
-// The units of kind k for this CTA (one thread).
-__device__ void build_units(const TcArgs& a, const TcPlan& pl, int k, Unit* out, int* cnt, unsigned* status) {
+// The units of kind k for this CTA, one per lane of the calling warp (all 32 lanes call): unit u is
+// this CTA's part of the u-th tile its stage range touches.
+__device__ __noinline__ void build_units(const TcArgs& a, const TcPlan& pl, int nr, int k, Unit* out, int* cnt,
+                                         unsigned* status, int lane) {
   Split sp;
   const int G = gridDim.x, per = k < 2 ? a.P1 : a.MT2, spt = k < 2 ? a.KB1 : a.KB2;
-  const int tiles = (k & 1) ? pl.nr * per : per;
+  const int tiles = (k & 1) ? nr * per : per;
   sp.init(tiles * spt, spt, G);
-  const int hi = sp.hi(blockIdx.x);
-  int n = 0;
-  for (int s = sp.lo(blockIdx.x); s < hi;) {
-    const int tid_ = s / spt, t0 = tid_ * spt, e = min(t0 + spt, hi);
-    if (n == UMAX) {
+  const int lo = sp.lo(blockIdx.x), hi = sp.hi(blockIdx.x);
+  const int t0 = lo / spt, nu = hi > lo ? (hi - 1) / spt - t0 + 1 : 0;
+  if (nu > UMAX) {
+    if (lane == 0) {
       atomicOr(status, ST_PLAN);
-      break;
+      *cnt = 0;
     }
+    return;
+  }
+  for (int u = lane; u < nu; u += 32) {
+    const int tid_ = t0 + u, s = max(lo, tid_ * spt), e = min(hi, (tid_ + 1) * spt);
     Unit U;
     U.kind = (short)k;
     U.slot = (short)((k & 1) ? tid_ / per : -1);
     U.tile = (short)((k & 1) ? tid_ - U.slot * per : tid_);
-    U.j0 = (short)(s - t0);
+    U.j0 = (short)(s - tid_ * spt);
     U.n = (short)(e - s);
-    U.jc = (short)(blockIdx.x - sp.owner(t0));
+    U.jc = (short)(blockIdx.x - sp.owner(tid_ * spt));
     U.expert = (k & 1) ? pl.expert[U.slot] : 0;
     U.tile_id = tid_;
-    out[n++] = U;
-    s = e;
+    out[u] = U;
   }
-  *cnt = n;
+  if (lane == 0) *cnt = nu;
 }
 
 // ---- the peer all-reduce of eight consecutive 16-row tiles (one 128-row output tile) by one warp:
@@ -1041,50 +1387,72 @@ __device__ __noinline__ bool ll_allreduce_tiles8(unsigned long long* const* slot
   return __all_sync(0xffffffffu, ok);
 }
 
-// ---- warp 3: finisher. Sums a finished tile's partials in contributor order.
+// ---- warp 3: finisher (N > 1). Sums a finished output tile's partials in contributor order and runs
+// its peer exchange; at N = 1 the epilogue finishes every tile itself.
 // Loads the sum of a tile's partials ([MAXC][128 rows][8]) for rows 4 lane .. 4 lane + 3, B tokens,
-// into fin[128][8]; the partials list is (slot index, contributor count) pairs in summation order.
-__device__ __noinline__ void sum_partials(const float* const* bases, const int* counts, int nlist, int B, float* fin, int lane) {
+// into fin[128][8]. The partials form a list of nb <= 8 entries in summation order: entry i is slot
+// s = l0 + i (the shared slot SH once s >= nr), its partials at base + slot * estride, and lane i
+// holds its count. The list is walked as one flat sequence, CAP partials at a time with all their
+// loads in flight, so a tile costs one memory round trip per CAP partials whatever its slots.
+template <int CAP, bool WIDE>
+__device__ __forceinline__ void sum_partials_t(const float* base, long long estride, int l0, int nr, int SH,
+                                               const int (&pre)[9], float (&s)[4][MAXB], int lane) {
+  const int total = pre[8];
+  for (int f0 = 0; f0 < total; f0 += CAP) {
+    uint4 v[CAP][4][WIDE ? 2 : 1];
+#pragma unroll
+    for (int p = 0; p < CAP; ++p) {
+      const int f = f0 + p;
+      if (f < total) {
+        int li = 0, at = 0;
+#pragma unroll
+        for (int q = 1; q < 8; ++q)
+          if (f >= pre[q]) {
+            li = q;
+            at = pre[q];
+          }
+        const int sl = l0 + li < nr ? l0 + li : SH;
+        const float* src = base + sl * estride + (f - at) * 1024 + 4 * lane * 8;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          v[p][r][0] = ld_cg16(src + r * 8);
+          if (WIDE) v[p][r][WIDE ? 1 : 0] = ld_cg16(src + r * 8 + 4);
+        }
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < CAP; ++p)
+      if (f0 + p < total)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          s[r][0] += __uint_as_float(v[p][r][0].x);
+          s[r][1] += __uint_as_float(v[p][r][0].y);
+          s[r][2] += __uint_as_float(v[p][r][0].z);
+          s[r][3] += __uint_as_float(v[p][r][0].w);
+          if (WIDE) {
+            s[r][4] += __uint_as_float(v[p][r][WIDE ? 1 : 0].x);
+            s[r][5] += __uint_as_float(v[p][r][WIDE ? 1 : 0].y);
+            s[r][6] += __uint_as_float(v[p][r][WIDE ? 1 : 0].z);
+            s[r][7] += __uint_as_float(v[p][r][WIDE ? 1 : 0].w);
+          }
+        }
+  }
+}
+__device__ __noinline__ void sum_partials(const float* base, long long estride, int l0, int nr, int SH, int nb,
+                                          int cnt_lane, int B, float* fin, int lane) {
+  int pre[9];  // first flat index of each list entry (entries past the list start at the end)
+  pre[0] = 0;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) pre[q + 1] = pre[q] + (q < nb ? __shfl_sync(0xffffffffu, cnt_lane, q) : 0);
   float s[4][MAXB];
 #pragma unroll
   for (int r = 0; r < 4; ++r)
 #pragma unroll
     for (int t = 0; t < MAXB; ++t) s[r][t] = 0.f;
-  for (int li = 0; li < nlist; ++li) {
-    const float* base = bases[li] + 4 * lane * 8;
-    for (int j0 = 0; j0 < counts[li]; j0 += 4) {  // four partials' loads in flight, added in order
-      float4 v[4][4][2];
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj)
-        if (j0 + jj < counts[li])
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const float* p = base + (j0 + jj) * 1024 + r * 8;
-            const uint4 u = ld_cg16(p);
-            v[jj][r][0] = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w));
-            if (B > 4) {
-              const uint4 u2 = ld_cg16(p + 4);
-              v[jj][r][1] = make_float4(__uint_as_float(u2.x), __uint_as_float(u2.y), __uint_as_float(u2.z), __uint_as_float(u2.w));
-            }
-          }
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj)
-        if (j0 + jj < counts[li])
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            s[r][0] += v[jj][r][0].x;
-            s[r][1] += v[jj][r][0].y;
-            s[r][2] += v[jj][r][0].z;
-            s[r][3] += v[jj][r][0].w;
-            if (B > 4) {
-              s[r][4] += v[jj][r][1].x;
-              s[r][5] += v[jj][r][1].y;
-              s[r][6] += v[jj][r][1].z;
-              s[r][7] += v[jj][r][1].w;
-            }
-          }
-    }
-  }
+  if (B > 4)
+    sum_partials_t<3, true>(base, estride, l0, nr, SH, pre, s, lane);
+  else
+    sum_partials_t<6, false>(base, estride, l0, nr, SH, pre, s, lane);
 #pragma unroll
   for (int r = 0; r < 4; ++r)
 #pragma unroll
@@ -1092,63 +1460,9 @@ __device__ __noinline__ void sum_partials(const float* const* bases, const int* 
   __syncwarp();
 }
 
-// w1|w3 tile p of slot index si finished: h = SiLU(min(g, 10)) * clamp(u, +-10) (times kHScale) of its
-// 64 intermediate rows, as e4m3 hi / lo bytes into the slot's w2 B tile; then the slot's count.
-__device__ __noinline__ void finish_w13(const TcArgs& a, TcPlan& pl, const Work& wk, int si, int p, int SH, float* fin, int lane) {
-  const int kind = si == SH ? 0 : 1;
-  const int tile_id = kind == 0 ? p : si * a.P1 + p;
-  const float* base = a.p13 + ((long long)si * a.P1 + p) * MAXC * 1024;
-  const int nc = contrib_count(wk.sp[kind], tile_id);
-  sum_partials(&base, &nc, 1, a.B, fin, lane);
-  // h for rows r = lane, lane + 32 (gate row r, up row 64 + r), every token; into fin rows 0..63
-  float h[2][MAXB];
-#pragma unroll
-  for (int i = 0; i < 2; ++i)
-#pragma unroll
-    for (int t = 0; t < MAXB; ++t) {
-      const int r = lane + 32 * i;
-      const float gv = fminf(fin[r * 8 + t], 10.0f);
-      const float uv = fminf(fmaxf(fin[(64 + r) * 8 + t], -10.0f), 10.0f);
-      h[i][t] = t < a.B ? silu_tc(gv) * uv * kHScale : 0.f;
-    }
-  __syncwarp();
-#pragma unroll
-  for (int i = 0; i < 2; ++i)
-#pragma unroll
-    for (int t = 0; t < MAXB; ++t) fin[t * 64 + lane + 32 * i] = h[i][t];  // [token][row]
-  __syncwarp();
-  // 16 B pieces: (B-tile row n = hi / lo of token n % 8, chunk of 16 K) -> SW128 position
-  uint8_t* blk = a.hb + ((long long)si * a.KB2 + (p >> 1)) * 2048;
-  const bool last_half = p == a.P1 - 1 && (p & 1) == 0;  // the block's second half lies past the slice: zero it
-  for (int it = lane; it < 64 + (last_half ? 64 : 0); it += 32) {
-    const int n = (it & 63) >> 2, c4 = it & 3;
-    uint32_t w[4] = {0u, 0u, 0u, 0u};
-    if (it < 64) {
-      const int t = n & 7;
-      const bool lo = n >= 8;
-      const float* v = fin + t * 64 + 16 * c4;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        uint32_t h2, l2;
-        split2_e4m3(v[2 * q], v[2 * q + 1], h2, l2);
-        w[q >> 1] |= (lo ? l2 : h2) << (16 * (q & 1));
-      }
-    }
-    const int cc = (it < 64 ? (p & 1) * 4 : 4) + c4;
-    *reinterpret_cast<uint4*>(blk + sw128_off(n, cc)) = make_uint4(w[0], w[1], w[2], w[3]);
-  }
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-  __syncwarp();
-  if (lane == 0 && tag_add(a.sdone + si, pl.tag, 1u) == 0u) {
-    atomicOr(a.status, ST_CNT);
-    pl.abort = 1;
-  }
-  __syncwarp();
-}
-
 // Output tile m finished: y rows [128 m, 128 m + 128) = sum over the routed slots (in order) and the
 // shared expert of their partials; at N > 1 summed over the ranks through the peer exchange.
-__device__ __noinline__ void finish_w2(const TcArgs& a, TcPlan& pl, const Work& wk, int m, int SH, float* fin, int lane) {
+__device__ __noinline__ void finish_w2(const TcArgs& a, TcPlan& pl, int m, int SH, float* fin, int lane) {
   const int nl = pl.nr + 1;
   bool ok = true;
   // partials of slots in order, in batches that fit the local lists
@@ -1157,19 +1471,13 @@ __device__ __noinline__ void finish_w2(const TcArgs& a, TcPlan& pl, const Work& 
   for (int r = 0; r < 4; ++r)
 #pragma unroll
     for (int t = 0; t < MAXB; ++t) acc[r][t] = 0.f;
+  const int nr = pl.nr;
   for (int l0 = 0; l0 < nl; l0 += 8) {
-    const float* bases[8];
-    int counts[8];
-    const int nb = min(8, nl - l0);
-    for (int i = 0; i < nb; ++i) {
-      const int s = l0 + i;
-      const int si = s < pl.nr ? s : SH;
-      const int kind = s < pl.nr ? 3 : 2;
-      const int tile_id = s < pl.nr ? s * a.MT2 + m : m;
-      bases[i] = a.p2 + ((long long)m * a.slot_cap + si) * MAXC * 1024;
-      counts[i] = contrib_count(wk.sp[kind], tile_id);
-    }
-    sum_partials(bases, counts, nb, a.B, fin, lane);
+    // lane i < 8 counts the contributors of list entry i (slot l0 + i; the shared expert last)
+    const int nb = min(8, nl - l0), s = l0 + lane;
+    const int cnt = lane < nb ? contrib_count(pl.wk.sp[s < nr ? 3 : 2], s < nr ? s * a.MT2 + m : m) : 0;
+    sum_partials(a.p2 + (long long)m * a.slot_cap * MAXC * 1024, (long long)MAXC * 1024, l0, nr, SH, nb, cnt, a.B, fin,
+                 lane);
 #pragma unroll
     for (int r = 0; r < 4; ++r)
 #pragma unroll
@@ -1222,9 +1530,8 @@ __device__ __noinline__ void finish_w2(const TcArgs& a, TcPlan& pl, const Work& 
   __syncwarp();
 }
 
-__device__ __noinline__ void role_finisher(const TcArgs& a, TcPlan& pl, Pipe& P, float* fin, int lane, int SH) {
-  Work wk;
-  wk.init(a, pl.nr);
+__device__ __noinline__ void role_finisher(const TcArgs& a, TcPlan& pl, const Pipe& Pin, float* fin, int lane, int SH) {
+  const Pipe P = Pin;
   int head = 0;
   uint64_t t0 = globaltimer_ns();
   while (true) {
@@ -1250,10 +1557,7 @@ __device__ __noinline__ void role_finisher(const TcArgs& a, TcPlan& pl, Pipe& P,
     ++head;
     t0 = globaltimer_ns();
     fence_acq_rel_gpu();  // acquire: the other CTAs' partials
-    if (job & (1 << 30))
-      finish_w2(a, pl, wk, job & 0xFFFF, SH, fin, lane);
-    else
-      finish_w13(a, pl, wk, job >> 8, job & 0xFF, SH, fin, lane);
+    finish_w2(a, pl, job, SH, fin, lane);
   }
 }
 
@@ -1261,7 +1565,7 @@ __device__ __noinline__ void role_finisher(const TcArgs& a, TcPlan& pl, Pipe& P,
 __global__ void __launch_bounds__(NT, 1) moe_tc_kernel(const __grid_constant__ TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  const TcSmem L = tc_smem(a.H, a.S, a.E);
+  const TcSmem L = tc_smem(a.H, a.S, a.E, a.B);
   Pipe P;
   P.S = a.S;
   P.ring = sm + L.ring;
@@ -1279,6 +1583,7 @@ __global__ void __launch_bounds__(NT, 1) moe_tc_kernel(const __grid_constant__ T
   unsigned* emask = reinterpret_cast<unsigned*>(sm + L.emask);
   float* etab = reinterpret_cast<float*>(sm + L.etab);
   float* fin = reinterpret_cast<float*>(sm + L.fin);
+  float* efin = reinterpret_cast<float*>(sm + L.efin);
   P.queue = reinterpret_cast<int*>(sm + L.queue);
   P.qtail = reinterpret_cast<volatile int*>(P.queue + QCAP);
   P.edone = P.qtail + 1;
@@ -1293,6 +1598,14 @@ __global__ void __launch_bounds__(NT, 1) moe_tc_kernel(const __grid_constant__ T
   const int G = gridDim.x, SH = a.slot_cap - 1;
 
   if (tid == 0) {
+    // This CTA's router rows and the router biases into L2 now (constant data): the router and the
+    // plan then read them at L2 latency.
+    {
+      const int r0 = (int)((unsigned)a.E * (unsigned)blockIdx.x / (unsigned)G);
+      const int r1 = (int)((unsigned)a.E * (unsigned)(blockIdx.x + 1) / (unsigned)G);
+      if (r1 > r0) prefetch_l2(a.wg + (long long)r0 * a.H, (uint32_t)((r1 - r0) * a.H * 4));
+      if (a.bias != nullptr && ((uintptr_t)a.bias & 15) == 0 && (a.E & 3) == 0) prefetch_l2(a.bias, (uint32_t)(a.E * 4));
+    }
     for (int s = 0; s < a.S; ++s) {
       mbar_init(&P.full[s], 1);
       mbar_init(&P.empty[s], 1);
@@ -1307,11 +1620,9 @@ __global__ void __launch_bounds__(NT, 1) moe_tc_kernel(const __grid_constant__ T
       mbar_init(&P.a4r[i], 4);
     }
     mbar_init(P.mdone, 1);
-    // the shared expert's units do not depend on routing: listed now, so its weights stream at once
-    build_units(a, pl, 0, units, &ucnt[0], a.status);
-    build_units(a, pl, 2, units + 2 * UMAX, &ucnt[2], a.status);
     ucnt[1] = ucnt[3] = 0;
     pl.nr = 0;
+    pl.wk.init(a, 0);  // the shared expert's splits now; the routed ones once the plan is known
     pl.tag = 0u;
     pl.ar_epoch = 0u;
     pl.ready = 0;
@@ -1320,6 +1631,10 @@ __global__ void __launch_bounds__(NT, 1) moe_tc_kernel(const __grid_constant__ T
     *P.edone = 0;
     *P.issued = 0;
     fence_mbar_init();
+  }
+  if (warp == 0) {  // the shared expert's units do not depend on routing: listed now, so its weights stream at once
+    build_units(a, pl, 0, 0, units, &ucnt[0], a.status, lane);
+    build_units(a, pl, 0, 2, units + 2 * UMAX, &ucnt[2], a.status, lane);
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)), "r"(TM_COLS)
@@ -1343,46 +1658,60 @@ __global__ void __launch_bounds__(NT, 1) moe_tc_kernel(const __grid_constant__ T
       const unsigned long long gb = c - c % (unsigned long long)G;
       *gbase_s = gb;
       pl.tag = (unsigned)((gb / (unsigned long long)G) % 0xFFFFFFFFull) + 1u;
+      {
+        unsigned long long* mine = a.cnt + (long long)(pl.tag & 1u) * a.cnt_words;
+        unsigned long long* next = a.cnt + (long long)((pl.tag & 1u) ^ 1u) * a.cnt_words;
+        pl.cnt13 = mine;
+        pl.cnt2 = mine + a.slot_cap * a.P1;
+        pl.sdone = pl.cnt2 + a.MT2;
+        // the previous launch (parity of the next one) has completed: its counters go back to zero
+        for (int i = blockIdx.x; i < a.cnt_words; i += G) next[i] = 0ull;
+      }
       pl.ar_epoch = a.ar_world > 1 ? *(volatile unsigned*)a.ar_ctl + 1u : 0u;
       if (ld_relaxed32(a.status) != 0u) pl.abort = 1;  // an earlier call gave up: stop until reset
       fence_acq_rel_gpu();
       asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;" ::"l"(a.gbar) : "memory");  // read the epoch
       asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     }
-    bool ok = !bar_any(1, 224, pl.abort != 0);
-    if (ok) {
-      router_rows(a, warp - 1, lane, pl.tag);
-      float* scr = reinterpret_cast<float*>(P.xb);
-      ok = make_plan(a, pl, scr, scr + MAXB * a.E, emask, t7);
-    }
-    if (ok) {
-      build_xb(a, P.xb, pl, fin, t7);
+    // The B tile first (its first barrier also publishes the tag): the MMA issuer starts on the
+    // shared expert as soon as it exists, while warps 2-7 compute this CTA's router rows and warps
+    // 2-3 then gather every CTA's rows into the plan.
+    build_xb(a, P.xb, pl, fin, t7);
+    const bool ok0 = !bar_any(1, 224, pl.abort != 0);
+    if (warp == 1) {
+      if (lane == 0) role_mma(a, pl, P);
+    } else {
       if (warp >= 4) {  // B-side scale factors of the block-scaled MMA: 1.0 for every row and group
         tm_st4(P.tm + ((uint32_t)(32 * (warp - 4)) << 16) + TM_SFB, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
         fence_before();
       }
-    }
-    // The routed units follow from the plan. Without one (a failed set-up: `ok` is the same in every
-    // warp here) every role walks the shared expert's stages only, and skips them (the call has
-    // already given up).
-    if (t7 == 0) {
-      if (!ok) pl.nr = 0;
-      build_units(a, pl, 1, units + UMAX, &ucnt[1], a.status);
-      build_units(a, pl, 3, units + 3 * UMAX, &ucnt[3], a.status);
-    }
-    named_bar_sync(1, 224);
-    if (t7 == 0) {
-      __threadfence_block();
-      pl.ready = 1;
-    }
-    if (warp == 1) {
-      if (lane == 0) role_mma(a, pl, P);
-    } else if (warp == 2) {
-      if (lane == 0) role_hcopy(a, pl, P, SH);
-    } else if (warp == 3) {
-      role_finisher(a, pl, P, fin, lane, SH);
-    } else {
-      role_epilogue(a, pl, P, etab, warp - 4, lane, SH);
+      if (ok0) router_rows(a, pl, warp - 2, 6, lane, reinterpret_cast<double*>(efin));
+      if (warp >= 4) {
+        role_epilogue(a, pl, P, etab, efin, warp - 4, lane, SH);
+      } else {
+        const int tp = tid - 64;
+        float* scr = reinterpret_cast<float*>(sm + L.scr);
+        const bool ok = ok0 && make_plan(a, pl, scr, scr + a.B * a.E, emask, tp);
+        // The routed units follow from the plan. Without one (a failed set-up) every role walks the
+        // shared expert's stages only, and skips them (the call has already given up).
+        const int nr = ok ? pl.nr : 0;
+        build_units(a, pl, nr, warp == 2 ? 1 : 3, units + (warp == 2 ? 1 : 3) * UMAX, &ucnt[warp == 2 ? 1 : 3], a.status,
+                    lane);
+        named_bar_sync(BAR_PLAN, PT);
+        if (warp == 2) {
+          if (lane == 0) {  // the routed splits (the shared ones, read meanwhile, stay as they are)
+            pl.nr = nr;
+            pl.wk.nr = nr;
+            pl.wk.sp[1].init(nr * a.P1 * a.KB1, a.KB1, G);
+            pl.wk.sp[3].init(nr * a.MT2 * a.KB2, a.KB2, G);
+            __threadfence_block();
+            pl.ready = 1;
+          }
+          if (lane == 0) role_hcopy(a, pl, P, SH);
+        } else {
+          role_finisher(a, pl, P, fin, lane, SH);
+        }
+      }
     }
   }
   fence_before();
@@ -1430,9 +1759,8 @@ TcScratch tc_scratch(const dsmoe_layer_t* L) {
   f.gbar = o; o += al(8);
   f.status = o; o += al(4);
   f.rl = o; o += al((size_t)tc::MAXB * L->n_experts * 4 * 16);
-  f.cnt13 = o; o += al((size_t)f.slot_cap * P1 * 8);
-  f.cnt2 = o; o += al((size_t)MT2 * 8);
-  f.sdone = o; o += al((size_t)f.slot_cap * 8);
+  f.cnt_words = f.slot_cap * P1 + MT2 + f.slot_cap;
+  f.cnt = o; o += al((size_t)2 * f.cnt_words * 8);  // one counter set per launch parity
   f.counters_end = o;
   f.p13 = o; o += al((size_t)f.slot_cap * P1 * tc::MAXC * 4096);
   f.p2 = o; o += al((size_t)MT2 * f.slot_cap * tc::MAXC * 4096);
@@ -1541,7 +1869,9 @@ bool tc_supported(const dsmoe_layer_t* L, int B) {
     cudaDeviceGetAttribute(&d.optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
   }
-  return tc::tc_smem(L->hidden, 3, L->n_experts).total <= (size_t)d.optin;
+  // a CTA's router rows (E / SMs, rounded up) keep their quarter sums in the epilogue's scratch
+  if ((L->n_experts + d.sms - 1) / d.sms * 4 * tc::MAXB * 8 > 2 * 64 * 8 * 4) return false;
+  return tc::tc_smem(L->hidden, 3, L->n_experts, tc::MAXB).total <= (size_t)d.optin;
 }
 
 int launch_tc(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image_mask, void* y, int y_dtype,
@@ -1575,7 +1905,7 @@ int launch_tc(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image
   a.MT2 = gr.MT2;
   // as many ring stages as fit next to the B tile and the rest (at most MAXS)
   int S = tc::MAXS;
-  while (S > 0 && tc::tc_smem(L->hidden, S, L->n_experts).total > (size_t)d.optin) --S;
+  while (S > 0 && tc::tc_smem(L->hidden, S, L->n_experts, B).total > (size_t)d.optin) --S;
   DSMOE_REQUIRE(S >= 3, DSMOE_ERR_UNSUPPORTED, "moe_tc: shared memory for %d stages only", S);
   a.S = S;
   a.slot_cap = f.slot_cap;
@@ -1602,9 +1932,8 @@ int launch_tc(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image
   a.gbar = (unsigned long long*)(ws + f.gbar);
   a.status = (unsigned*)(ws + f.status);
   a.rl = (unsigned long long*)(ws + f.rl);
-  a.cnt13 = (unsigned long long*)(ws + f.cnt13);
-  a.cnt2 = (unsigned long long*)(ws + f.cnt2);
-  a.sdone = (unsigned long long*)(ws + f.sdone);
+  a.cnt = (unsigned long long*)(ws + f.cnt);
+  a.cnt_words = f.cnt_words;
   a.p13 = (float*)(ws + f.p13);
   a.p2 = (float*)(ws + f.p2);
   a.hb = ws + f.hb;
@@ -1619,7 +1948,7 @@ int launch_tc(const dsmoe_layer_t* L, const void* x, int B, const uint8_t* image
       a.ar_slots[q] = px->slots[q];
     }
   }
-  const size_t smem = tc::tc_smem(L->hidden, S, L->n_experts).total;
+  const size_t smem = tc::tc_smem(L->hidden, S, L->n_experts, B).total;
   if (!d.attr) {
     if (cudaFuncSetAttribute(tc::moe_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, d.optin) != cudaSuccess)
       return cuda_status("moe_tc: set smem");

@@ -65,8 +65,8 @@ bool fused_supported(const dsmoe_layer_t* L, int B);
 // Scratch of the tensor-core decode path (moe_tc.cu) in the caller's workspace; the grid counter
 // and the status word sit at the same offsets as in FusedScratch.
 struct TcScratch {
-  size_t gbar, status, rl, cnt13, cnt2, sdone, counters_end, p13, p2, hb, total;
-  int slot_cap;
+  size_t gbar, status, rl, cnt, counters_end, p13, p2, hb, total;
+  int slot_cap, cnt_words;
 };
 TcScratch tc_scratch(const dsmoe_layer_t* L);
 bool tc_supported(const dsmoe_layer_t* L, int B);
