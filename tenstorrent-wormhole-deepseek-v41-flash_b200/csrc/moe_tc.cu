@@ -61,8 +61,11 @@ constexpr int SB = 2048;                 // stage B (w2 phase): 16 rows x 128 K 
 constexpr int STAGE = SA + SB + 1024;    // + 1 KB for the stage's scales (FP4 512 B, FP8 16 B)
 constexpr int NACC8 = 8;                 // FP8 block accumulators (16 TMEM columns each)
 constexpr int kDepth8 = 4;               // FP8 stages (16 KB) in flight per CTA
-constexpr uint32_t TM_ACC4 = 128, TM_SFA = 160, TM_SFB = 240, TM_COLS = 256;
+// Tensor memory columns: FP8 block accumulators [0, 128), FP4 unit accumulators [2 parities][2 issuers]
+// at [128, 192), FP4 A scale factors 4 per ring slot from 192, B scale factors at 288.
+constexpr uint32_t TM_ACC4 = 128, TM_SFA = 192, TM_SFB = 288, TM_COLS = 512;
 constexpr int MAXS = 20;                 // ring stages (TM_SFA + 4 MAXS <= TM_SFB)
+constexpr int NISS = 2;                  // MMA issuing threads (lane 0 of warp 1 and, at N = 1, of warp 3)
 constexpr int QCAP = 64;                 // finisher job queue
 constexpr uint64_t kWait = 1000000000ull;
 constexpr uint64_t kPeerWait = 5000000000ull;
@@ -188,6 +191,14 @@ __device__ __forceinline__ unsigned long long ld_relaxed64(const unsigned long l
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ unsigned long long atom_add_acq_rel(unsigned long long* p, unsigned long long v) {
+  unsigned long long old;
+  asm volatile("atom.add.acq_rel.gpu.global.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void red_add_release(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.add.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 // L2 prefetch of a contiguous range (16-byte aligned start, size a multiple of 16 bytes).
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes & ~15u) : "memory");
@@ -288,7 +299,7 @@ __host__ __device__ inline TcSmem tc_smem(int H, int S, int E, int B) {
   L.scr = o;  // the plan's scores and biased scores, [B][E] each
   o += ((size_t)2 * B * E * 4 + 15) & ~size_t(15);
   L.bars = o;
-  o += (size_t)(3 * S + 2 * NACC8 + 5) * 8;
+  o += (size_t)(3 * S + 2 * NACC8 + 5 * NISS) * 8;
   o = (o + 15) & ~size_t(15);
   L.plan = o;
   o += (sizeof(TcPlan) + 15) & ~size_t(15);
@@ -673,9 +684,9 @@ struct Pipe {
                     // per FP4 stage of the slot only
   uint64_t* accf;   // [NACC8] FP8 block accumulator complete
   uint64_t* accr;   // [NACC8] FP8 block accumulator read (4 epilogue warps)
-  uint64_t* a4f;    // [2] FP4 unit accumulator complete
-  uint64_t* a4r;    // [2] FP4 unit accumulator read (4 epilogue warps)
-  uint64_t* mdone;  // every MMA of the CTA complete
+  uint64_t* a4f;    // [2 parities][NISS] FP4 unit accumulator of an issuer complete
+  uint64_t* a4r;    // [2 parities][NISS] FP4 unit accumulator of an issuer read (4 epilogue warps)
+  uint64_t* mdone;  // [NISS] every MMA of an issuer complete
   int* queue;       // [QCAP] finisher jobs
   volatile int* qtail;
   volatile int* edone;   // the epilogue has queued its last job
@@ -705,6 +716,7 @@ __device__ __forceinline__ int seg_next(int row0, int kind, int j) {
   return kind < 2 ? j + 1 : (row0 + 128 * (j + 1)) >> 7;
 }
 __device__ __forceinline__ int ksteps(int I_loc, int kind, int j) { return kind < 2 ? 4 : min(4, (I_loc - 128 * j) / 32); }
+__device__ __forceinline__ bool last_of(const Unit& U, int j) { return j == U.j0 + U.n - 1; }
 
 // Position in a CTA's stream: (kind, unit, K block) and the ring stage g.
 struct Cur {
@@ -771,13 +783,14 @@ __device__ __noinline__ void role_producer(const TcArgs& a, TcPlan& pl, const Pi
       for (int j = U.j0; j < U.j0 + U.n; ++j) {
         // At most `depth` stages in flight: the weight bytes HBM needs to run at full rate (about 64 KB a
         // SM), and no more, since every extra byte in flight is queueing delay for the kernel's other
-        // memory traffic (router, partials, exchange). Stages complete in order, so waiting for stage
-        // g - depth also frees slot g % S.
+        // memory traffic (router, partials, exchange).
         const int depth = f4 ? P.S : min(P.S, kDepth8);
         if (g >= depth) {
           const int q = g - depth;
           if (!pwait(a, pl, &P.empty[q % P.S], (q / P.S) & 1)) break;
         }
+        // the two MMA issuers may release stages out of order: the slot itself must be free too
+        if (g >= P.S && !pwait(a, pl, &P.empty[slot], ph ^ 1)) break;
         uint8_t* A = P.ring + (size_t)slot * STAGE;
         const int blk = U.tile * per + j;
         mbar_expect_tx(&P.full[slot], bytes);
@@ -861,11 +874,18 @@ __device__ __forceinline__ void mma4_mx(uint32_t d, uint64_t da, uint64_t db, ui
   mma_mx(d, da + 6, db + 6, kIdescX | (3u << 29) | (3u << 4), sfa | (3u << 30), sfb | (3u << 30), 1u);
 }
 
-// ---- warp 1, lane 0: MMA issuer
-__device__ __noinline__ void role_mma(const TcArgs& a, TcPlan& pl, const Pipe& Pin) {
+// ---- lane 0 of warp 1 (issuer 0) and, at N = 1, of warp 3 (issuer 1): MMA issuers. One issuing
+// thread is bound by its own serial latency (about one 4-MMA stage per 0.25 us), so at N = 1 two
+// threads issue alternate stages of the routed work: stage i of the stream after the shared w1|w3
+// phase goes to issuer i % 2 (issuer 0 keeps the shared w1|w3 stages, and every w2 stage of a slice
+// that starts inside a 128-row block, whose scale segments run across stages). The two never share
+// an accumulator: FP8 segments are distinct per stage, FP4 units accumulate per issuer (the epilogue
+// adds the two). At N > 1 warp 3 runs the finisher and issuer 0 takes every stage.
+__device__ __noinline__ void role_mma(const TcArgs& a, TcPlan& pl, const Pipe& Pin, int iss) {
   const Pipe P = Pin;
-  int slot = 0, ph = 0, nseg = 0, n4 = 0, cur_a = 0, cur_g = -1;
-  uint32_t c4 = 0u;  // FP4 uses per ring slot, mod 2 (bit s): the phases of its scale-factor barrier
+  int slot = 0, ph = 0, nseg = 0, n4 = 0, cur_a = 0, cur_g = -1, gi = 0;
+  int u4[2] = {0, 0};  // FP4 units of each accumulator parity this issuer has taken part in
+  uint32_t c4 = 0u;    // FP4 uses per ring slot, mod 2 (bit s): the phases of its scale-factor barrier
   bool open = false, ok = true;
   const uint32_t ring = smem_u32(P.ring), xb = smem_u32(P.xb);
   const bool w2_aligned = (a.row0 & 127) == 0;  // every w2 stage is then one FP8 scale segment
@@ -875,103 +895,111 @@ __device__ __noinline__ void role_mma(const TcArgs& a, TcPlan& pl, const Pipe& P
       if (pl.abort) break;
     }
     const bool f4 = (k & 1) && a.r_fmt == DSMOE_FMT_FP4;
+    const bool dual = a.ar_world <= 1 && k >= 1 && (k < 2 || f4 || w2_aligned);
     const int nu = P.ucnt[k];
     for (int u = 0; u < nu && ok; ++u) {
       const Unit U = P.units[k * UMAX + u];
-      for (int j = U.j0; j < U.j0 + U.n; ++j) {
-        const bool first = j == U.j0, last = j == U.j0 + U.n - 1;
-        if (!pwait(a, pl, &P.full[slot], ph)) {
+      // FP4: this issuer's stages of the unit are those of stream parity iss (all of them single-issue)
+      const int jf = (!dual || (gi & 1) == iss) ? U.j0 : U.j0 + 1;  // this issuer's first and last block
+      const int jl = U.j0 + U.n - 1 - ((dual && ((gi + U.n - 1) & 1) != iss) ? 1 : 0);
+      const int par = n4 & 1;
+      const uint32_t d4 = P.tm + TM_ACC4 + 16 * (2 * par + iss);
+      if (f4 && jf <= jl) {  // the accumulator's previous unit has been read by the epilogue
+        if (u4[par] >= 1 && !pwait(a, pl, &P.a4r[2 * par + iss], (u4[par] - 1) & 1)) {
           ok = false;
           break;
         }
-        if (f4) {
-          if (!pwait(a, pl, &P.sfr[slot], (c4 >> slot) & 1u)) {
+        fence_after();
+      }
+      for (int j = U.j0; j < U.j0 + U.n; ++j) {
+        const bool mine = k == 0 ? iss == 0 : (dual ? (gi & 1) == iss : iss == 0);
+        if (mine) {
+          if (!pwait(a, pl, &P.full[slot], ph)) {
             ok = false;
             break;
           }
-          c4 ^= 1u << slot;
-        }
-        fence_after();
-        const uint32_t aA = ring + slot * STAGE;
-        const uint32_t bB = k < 2 ? xb + j * 2048 : aA + SA;
-        const uint64_t da = desc_sw128(aA), db = desc_sw128(bB);
-        const int nk = ksteps(a.I_loc, k, j);
-        if (f4) {
-          const int par = n4 & 1;
-          if (first && n4 >= 2) {
-            if (!pwait(a, pl, &P.a4r[par], ((n4 >> 1) - 1) & 1)) {
-              ok = false;
-              break;
+          if (f4 && !pwait(a, pl, &P.sfr[slot], (c4 >> slot) & 1u)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t aA = ring + slot * STAGE;
+          const uint32_t bB = k < 2 ? xb + j * 2048 : aA + SA;
+          const uint64_t da = desc_sw128(aA), db = desc_sw128(bB);
+          const int nk = ksteps(a.I_loc, k, j);
+          if (f4) {
+            const uint32_t sfa = P.tm + TM_SFA + 4 * slot, sfb = P.tm + TM_SFB;
+            if (nk == 4) {
+              mma4_mx(d4, da, db, sfa, sfb, j == jf ? 0u : 1u);
+            } else {
+              for (int q = 0; q < nk; ++q)
+                mma_mx(d4, da + 2 * q, db + 2 * q, kIdescX | ((uint32_t)q << 29) | ((uint32_t)q << 4),
+                       sfa | ((uint32_t)q << 30), sfb | ((uint32_t)q << 30), (j == jf && q == 0) ? 0u : 1u);
             }
-            fence_after();
-          }
-          const uint32_t d = P.tm + TM_ACC4 + 16 * par, sfa = P.tm + TM_SFA + 4 * slot, sfb = P.tm + TM_SFB;
-          if (nk == 4) {
-            mma4_mx(d, da, db, sfa, sfb, first ? 0u : 1u);
-          } else {
-            for (int q = 0; q < nk; ++q)
-              mma_mx(d, da + 2 * q, db + 2 * q, kIdescX | ((uint32_t)q << 29) | ((uint32_t)q << 4),
-                     sfa | ((uint32_t)q << 30), sfb | ((uint32_t)q << 30), (first && q == 0) ? 0u : 1u);
-          }
-          commit(&P.empty[slot]);
-          if (last) {
-            commit(&P.a4f[par]);
-            ++n4;
-          }
-        } else if (nk == 4 && (k < 2 || w2_aligned)) {  // the stage is exactly one scale segment
-          if (open) {
-            commit(&P.accf[cur_a]);
-            open = false;
-          }
-          cur_a = nseg & (NACC8 - 1);
-          if (nseg >= NACC8) {
-            if (!pwait(a, pl, &P.accr[cur_a], ((nseg / NACC8) - 1) & 1)) {
-              ok = false;
-              break;
-            }
-            fence_after();
-          }
-          ++nseg;
-          mma4_f8(P.tm + 16 * cur_a, da, db, 0u);
-          commit(&P.empty[slot]);
-          commit(&P.accf[cur_a]);
-        } else {  // w2 stage of a slice that starts inside a 128-row block: segments change mid-stage
-          for (int q = 0; q < nk; ++q) {
-            const int gk = seg_key(a.row0, k, j, q);
-            bool fresh = false;
-            if (!open || gk != cur_g) {
-              if (open) commit(&P.accf[cur_a]);
-              cur_a = nseg & (NACC8 - 1);
-              if (nseg >= NACC8) {
-                if (!pwait(a, pl, &P.accr[cur_a], ((nseg / NACC8) - 1) & 1)) {
-                  ok = false;
-                  break;
-                }
-                fence_after();
+            commit(&P.empty[slot]);
+            if (j == jl) commit(&P.a4f[2 * par + iss]);
+          } else if (k < 2 || w2_aligned) {  // the stage is exactly one scale segment
+            cur_a = nseg & (NACC8 - 1);
+            if (nseg >= NACC8) {
+              if (!pwait(a, pl, &P.accr[cur_a], ((nseg / NACC8) - 1) & 1)) {
+                ok = false;
+                break;
               }
-              ++nseg;
-              cur_g = gk;
-              open = true;
-              fresh = true;
+              fence_after();
             }
-            mma_f8(P.tm + 16 * cur_a, da + 2 * q, db + 2 * q, kIdesc8, fresh ? 0u : 1u);
-          }
-          if (!ok) break;
-          commit(&P.empty[slot]);
-          if (last || seg_next(a.row0, k, j) != cur_g) {  // the segment does not continue into the next stage
+            if (nk == 4) {
+              mma4_f8(P.tm + 16 * cur_a, da, db, 0u);
+            } else {
+              for (int q = 0; q < nk; ++q) mma_f8(P.tm + 16 * cur_a, da + 2 * q, db + 2 * q, kIdesc8, q == 0 ? 0u : 1u);
+            }
+            commit(&P.empty[slot]);
             commit(&P.accf[cur_a]);
-            open = false;
+          } else {  // w2 of a slice that starts inside a 128-row block (issuer 0 only): segments change mid-stage
+            for (int q = 0; q < nk; ++q) {
+              const int gk = seg_key(a.row0, k, j, q);
+              bool fresh = false;
+              if (!open || gk != cur_g) {
+                if (open) commit(&P.accf[cur_a]);
+                cur_a = nseg & (NACC8 - 1);
+                if (nseg >= NACC8) {
+                  if (!pwait(a, pl, &P.accr[cur_a], ((nseg / NACC8) - 1) & 1)) {
+                    ok = false;
+                    break;
+                  }
+                  fence_after();
+                }
+                ++nseg;
+                cur_g = gk;
+                open = true;
+                fresh = true;
+              }
+              mma_f8(P.tm + 16 * cur_a, da + 2 * q, db + 2 * q, kIdesc8, fresh ? 0u : 1u);
+            }
+            if (!ok) break;
+            commit(&P.empty[slot]);
+            if (last_of(U, j) || seg_next(a.row0, k, j) != cur_g) {  // the segment does not continue into the next stage
+              commit(&P.accf[cur_a]);
+              open = false;
+            }
           }
         }
+        // both issuers follow the whole stream: ring position, FP8 segment count, FP4 slot phases
+        if (f4) c4 ^= 1u << slot;
+        else if (k < 2 || w2_aligned) ++nseg;
+        if (k >= 1) ++gi;
         if (++slot == P.S) {
           slot = 0;
           ph ^= 1;
         }
       }
+      if (f4) {
+        if (jf <= jl) ++u4[par];
+        ++n4;
+      }
     }
   }
-  commit(P.mdone);  // completes once every MMA issued above has
-  mbar_wait(P.mdone, 0, kWait);
+  commit(&P.mdone[iss]);  // completes once every MMA this thread issued has
+  mbar_wait(&P.mdone[iss], 0, kWait);
 }
 
 // ---- finishing by the last contributor's epilogue (warps 4-7, 128 threads, named barrier 2)
@@ -1049,29 +1077,21 @@ __device__ __noinline__ void epi_finish_w13(const TcArgs& a, TcPlan& pl, int kin
     asm volatile("fence.proxy.async.global;" ::: "memory");  // the B tile is read by bulk copies
   }
   named_bar_sync(2, 128);
-  if (m == 0) {
-    fence_acq_rel_gpu();  // release: every thread's B-tile bytes (ordered by the barrier) before the count
-    atomicAdd(pl.sdone + si, 1ull);
-  }
+  if (m == 0) red_add_release(pl.sdone + si, 1ull);  // release: every thread's B-tile bytes (ordered by the barrier)
 }
 
 // Output tile mt at N = 1: y rows [128 mt, 128 mt + 128) = the sum over the routed slots (in order)
-// and the shared expert of their partials in contributor order; row m in thread m, eight partial rows
-// loaded together per pass.
-__device__ __noinline__ void epi_finish_w2(const TcArgs& a, TcPlan& pl, int mt, int SH, int m, int* ecnt) {
-  const int nr = pl.nr, nl = nr + 1;
-  for (int i = m; i < nl; i += 128) ecnt[i] = contrib_count(pl.wk.sp[i < nr ? 3 : 2], i < nr ? i * a.MT2 + mt : mt);
-  named_bar_sync(2, 128);
-  const float* base = a.p2 + (long long)mt * a.slot_cap * MAXC * 1024 + m * 8;
-  float s[MAXB];
-#pragma unroll
-  for (int t = 0; t < MAXB; ++t) s[t] = 0.f;
+// and the shared expert of their partials in contributor order; row m in thread m, CAP partial rows
+// loaded together per pass (one pass for the usual 7 slots x 2 contributors).
+template <int CAP, bool WIDE>
+__device__ __forceinline__ void epi_sum_w2(const TcArgs& a, const float* base, const int* ecnt, int nl, int nr, int SH,
+                                           float (&s)[MAXB]) {
   int li = 0, j = 0;
   while (li < nl) {
-    uint4 v[8][2];
-    bool on[8];
+    uint4 v[CAP][WIDE ? 2 : 1];
+    bool on[CAP];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
+    for (int q = 0; q < CAP; ++q) {
       while (li < nl && j >= ecnt[li]) {
         ++li;
         j = 0;
@@ -1080,25 +1100,38 @@ __device__ __noinline__ void epi_finish_w2(const TcArgs& a, TcPlan& pl, int mt, 
       if (on[q]) {
         const float* src = base + ((long long)(li < nr ? li : SH) * MAXC + j) * 1024;
         v[q][0] = ld_cg16(src);
-        if (a.B > 4) v[q][1] = ld_cg16(src + 4);
+        if (WIDE) v[q][WIDE ? 1 : 0] = ld_cg16(src + 4);
         ++j;
       }
     }
 #pragma unroll
-    for (int q = 0; q < 8; ++q)
+    for (int q = 0; q < CAP; ++q)
       if (on[q]) {
         s[0] += __uint_as_float(v[q][0].x);
         s[1] += __uint_as_float(v[q][0].y);
         s[2] += __uint_as_float(v[q][0].z);
         s[3] += __uint_as_float(v[q][0].w);
-        if (a.B > 4) {
-          s[4] += __uint_as_float(v[q][1].x);
-          s[5] += __uint_as_float(v[q][1].y);
-          s[6] += __uint_as_float(v[q][1].z);
-          s[7] += __uint_as_float(v[q][1].w);
+        if (WIDE) {
+          s[4] += __uint_as_float(v[q][WIDE ? 1 : 0].x);
+          s[5] += __uint_as_float(v[q][WIDE ? 1 : 0].y);
+          s[6] += __uint_as_float(v[q][WIDE ? 1 : 0].z);
+          s[7] += __uint_as_float(v[q][WIDE ? 1 : 0].w);
         }
       }
   }
+}
+__device__ __noinline__ void epi_finish_w2(const TcArgs& a, TcPlan& pl, int mt, int SH, int m, int* ecnt) {
+  const int nr = pl.nr, nl = nr + 1;
+  for (int i = m; i < nl; i += 128) ecnt[i] = contrib_count(pl.wk.sp[i < nr ? 3 : 2], i < nr ? i * a.MT2 + mt : mt);
+  named_bar_sync(2, 128);
+  const float* base = a.p2 + (long long)mt * a.slot_cap * MAXC * 1024 + m * 8;
+  float s[MAXB];
+#pragma unroll
+  for (int t = 0; t < MAXB; ++t) s[t] = 0.f;
+  if (a.B > 4)
+    epi_sum_w2<8, true>(a, base, ecnt, nl, nr, SH, s);
+  else
+    epi_sum_w2<16, false>(a, base, ecnt, nl, nr, SH, s);
 #pragma unroll
   for (int t = 0; t < MAXB; ++t) {
     if (t >= a.B) break;
@@ -1119,7 +1152,8 @@ __device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pi
   const int look = P.S > 2 ? 2 : P.S - 1;
   const bool fp4l = a.r_fmt == DSMOE_FMT_FP4;
   const bool w2_aligned = (a.row0 & 127) == 0;  // every w2 stage is then one FP8 scale segment
-  int nseg = 0, n4 = 0, cur_g = -1, seg_ti = 0, unit = 0;
+  int nseg = 0, n4 = 0, cur_g = -1, seg_ti = 0, unit = 0, gi = 0;
+  uint32_t e4 = 0u;  // phase (bit 2 par + x) of each FP4 unit accumulator's barrier
   bool open = false, live = true;
   float acc[MAXB];
   Cur sf;  // runs ahead over the routed stages: FP4 scale factors of a stage into tensor memory
@@ -1164,6 +1198,8 @@ __device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pi
     const int nu = P.ucnt[k];
     for (int u = 0; u < nu; ++u) {
       const Unit U = P.units[k * UMAX + u];
+      const int gi0 = gi;  // stream index (after the shared w1|w3 phase) of the unit's first stage
+      if (k >= 1) gi += U.n;
       float* tab = etab + (unit & 1) * 256;
 #pragma unroll
       for (int t = 0; t < MAXB; ++t) acc[t] = 0.f;
@@ -1188,18 +1224,33 @@ __device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pi
         if (fp4l)
           while (sf.valid() && sf.g <= g + look && (sf.k < 2 || k >= 2)) store_sf();
         if (f4) {
-          if (last) {
+          if (last) {  // the unit's accumulators of both MMA issuers (issuer x holds the stages of stream parity x)
             const int par = n4 & 1;
-            if (pwait(a, pl, &P.a4f[par], (n4 >> 1) & 1)) {
-              fence_after();
-              float d[16];
-              tm_ld16(trow + TM_ACC4 + 16 * par, d);
-              fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&P.a4r[par]);
+            float hi[MAXB], lo[MAXB];
 #pragma unroll
-              for (int t = 0; t < MAXB; ++t) acc[t] = d[t] + d[8 + t] * kLoInv;
+            for (int t = 0; t < MAXB; ++t) hi[t] = lo[t] = 0.f;
+#pragma unroll
+            for (int x = 0; x < NISS; ++x) {
+              if (a.ar_world <= 1 ? (U.n >= 2 || (gi0 & 1) == x) : x == 0) {
+                const int bx = 2 * par + x;
+                if (pwait(a, pl, &P.a4f[bx], (e4 >> bx) & 1u)) {
+                  fence_after();
+                  float d[16];
+                  tm_ld16(trow + TM_ACC4 + 16 * bx, d);
+                  fence_before();
+                  __syncwarp();
+                  if (lane == 0) mbar_arrive(&P.a4r[bx]);
+#pragma unroll
+                  for (int t = 0; t < MAXB; ++t) {
+                    hi[t] += d[t];
+                    lo[t] += d[8 + t];
+                  }
+                }
+                e4 ^= 1u << bx;
+              }
             }
+#pragma unroll
+            for (int t = 0; t < MAXB; ++t) acc[t] = hi[t] + lo[t] * kLoInv;
             ++n4;
           }
         } else if (w13 || w2_aligned) {  // the stage is exactly one scale segment
@@ -1245,10 +1296,10 @@ __device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pi
         if (live && !pl.abort) {
           unsigned long long* cnt = w13 ? pl.cnt13 + (long long)si * a.P1 + U.tile : pl.cnt2 + U.tile;
           const unsigned long long total = w13 ? (unsigned long long)a.KB1 : (unsigned long long)((pl.nr + 1) * a.KB2);
-          fence_acq_rel_gpu();  // release: the partial of all 128 threads (ordered by the barrier)
-          const unsigned long long c = atomicAdd(cnt, (unsigned long long)U.n) + (unsigned long long)U.n;
-          if (c == total) {  // last contribution: acquire the other contributors' partials
-            fence_acq_rel_gpu();
+          // release: the partial of all 128 threads (ordered by the barrier); acquire: if this is the
+          // last contribution, the other contributors' partials
+          const unsigned long long c = atom_add_acq_rel(cnt, (unsigned long long)U.n) + (unsigned long long)U.n;
+          if (c == total) {
             if (w13 || a.ar_world <= 1) {
               fk = w13 ? 1 : 2;
             } else {  // N > 1: the exchange of the output tile runs on this CTA's finisher warp
@@ -1577,8 +1628,8 @@ __global__ void __launch_bounds__(NT, 1) moe_tc_kernel(const __grid_constant__ T
   P.accf = bars + 3 * a.S;
   P.accr = P.accf + NACC8;
   P.a4f = P.accr + NACC8;
-  P.a4r = P.a4f + 2;
-  P.mdone = P.a4r + 2;
+  P.a4r = P.a4f + 2 * NISS;
+  P.mdone = P.a4r + 2 * NISS;
   TcPlan& pl = *reinterpret_cast<TcPlan*>(sm + L.plan);
   unsigned* emask = reinterpret_cast<unsigned*>(sm + L.emask);
   float* etab = reinterpret_cast<float*>(sm + L.etab);
@@ -1615,11 +1666,11 @@ __global__ void __launch_bounds__(NT, 1) moe_tc_kernel(const __grid_constant__ T
       mbar_init(&P.accf[i], 1);
       mbar_init(&P.accr[i], 4);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 2 * NISS; ++i) {
       mbar_init(&P.a4f[i], 1);
       mbar_init(&P.a4r[i], 4);
     }
-    mbar_init(P.mdone, 1);
+    for (int i = 0; i < NISS; ++i) mbar_init(&P.mdone[i], 1);
     ucnt[1] = ucnt[3] = 0;
     pl.nr = 0;
     pl.wk.init(a, 0);  // the shared expert's splits now; the routed ones once the plan is known
@@ -1679,7 +1730,7 @@ __global__ void __launch_bounds__(NT, 1) moe_tc_kernel(const __grid_constant__ T
     build_xb(a, P.xb, pl, fin, t7);
     const bool ok0 = !bar_any(1, 224, pl.abort != 0);
     if (warp == 1) {
-      if (lane == 0) role_mma(a, pl, P);
+      if (lane == 0) role_mma(a, pl, P, 0);
     } else {
       if (warp >= 4) {  // B-side scale factors of the block-scaled MMA: 1.0 for every row and group
         tm_st4(P.tm + ((uint32_t)(32 * (warp - 4)) << 16) + TM_SFB, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
@@ -1708,8 +1759,10 @@ __global__ void __launch_bounds__(NT, 1) moe_tc_kernel(const __grid_constant__ T
             pl.ready = 1;
           }
           if (lane == 0) role_hcopy(a, pl, P, SH);
-        } else {
+        } else if (a.ar_world > 1) {
           role_finisher(a, pl, P, fin, lane, SH);
+        } else {  // N = 1: the epilogue finishes every tile; this warp is the second MMA issuer
+          if (lane == 0) role_mma(a, pl, P, 1);
         }
       }
     }
