@@ -59,11 +59,11 @@ constexpr int MAXC = 6;                  // contributors (CTAs) per tile: bounds
 constexpr int SA = 16384;                // stage A: 128 rows x 128 K (one byte per element in shared memory)
 constexpr int SB = 2048;                 // stage B (w2 phase): 16 rows x 128 K e4m3
 constexpr int STAGE = SA + SB + 1024;    // + 1 KB for the stage's scales (FP4 512 B, FP8 16 B)
-constexpr int NACC8 = 8;                 // FP8 block accumulators (16 TMEM columns each)
+constexpr int NACC8 = 16;                // FP8 block accumulators (16 TMEM columns each)
 constexpr int kDepth8 = 4;               // FP8 stages (16 KB) in flight per CTA
-// Tensor memory columns: FP8 block accumulators [0, 128), FP4 unit accumulators [2 parities][2 issuers]
-// at [128, 192), FP4 A scale factors 4 per ring slot from 192, B scale factors at 288.
-constexpr uint32_t TM_ACC4 = 128, TM_SFA = 192, TM_SFB = 288, TM_COLS = 512;
+// Tensor memory columns: FP8 block accumulators [0, 256), FP4 unit accumulators [2 parities][2 issuers]
+// at [256, 320), FP4 A scale factors 4 per ring slot from 320, B scale factors at 416.
+constexpr uint32_t TM_ACC4 = 256, TM_SFA = 320, TM_SFB = 416, TM_COLS = 512;
 constexpr int MAXS = 20;                 // ring stages (TM_SFA + 4 MAXS <= TM_SFB)
 constexpr int NISS = 2;                  // MMA issuing threads (lane 0 of warp 1 and, at N = 1, of warp 3)
 constexpr int QCAP = 64;                 // finisher job queue
@@ -259,16 +259,38 @@ __device__ __forceinline__ void mma_mx(uint32_t d, uint64_t a, uint64_t b, uint3
       "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
       "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb));
 }
+// Tensor-memory loads; the wait is inside the same statement, so no use of the registers can be
+// scheduled before the data has arrived.
 __device__ __forceinline__ void tm_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
         "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      : "r"(taddr)
+      : "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+// Two 16-column accumulators (any two addresses) with one wait.
+__device__ __forceinline__ void tm_ld16x2(uint32_t ta, uint32_t tb, float (&va)[16], float (&vb)[16]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%33];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(ta), "r"(tb)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    va[i] = __uint_as_float(r[i]);
+    vb[i] = __uint_as_float(r[16 + i]);
+  }
 }
 __device__ __forceinline__ void tm_st4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(a), "r"(b), "r"(c),
@@ -1185,6 +1207,30 @@ __device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pi
 #pragma unroll
     for (int t = 0; t < MAXB; ++t) acc[t] = fmaf(d[t] + d[8 + t] * kLoInv, s, acc[t]);
   };
+  // Two consecutive closed segments (tables entries ti0, ti1): one tensor-memory wait for both, the
+  // same additions in the same order as two single closes.
+  auto close_seg2 = [&](const float* tab, int ti0, int ti1) {
+    const int sa = nseg & (NACC8 - 1), sb = (nseg + 1) & (NACC8 - 1);
+    const bool ga = pwait(a, pl, &P.accf[sa], (nseg / NACC8) & 1);
+    const bool gb = ga && pwait(a, pl, &P.accf[sb], ((nseg + 1) / NACC8) & 1);
+    nseg += 2;
+    if (!gb) return;
+    fence_after();
+    float d0[16], d1[16];
+    tm_ld16x2(trow + 16 * sa, trow + 16 * sb, d0, d1);
+    fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&P.accr[sa]);
+      mbar_arrive(&P.accr[sb]);
+    }
+    const float s0 = tab[ti0], s1 = tab[ti1];
+#pragma unroll
+    for (int t = 0; t < MAXB; ++t) {
+      acc[t] = fmaf(d0[t] + d0[8 + t] * kLoInv, s0, acc[t]);
+      acc[t] = fmaf(d1[t] + d1[8 + t] * kLoInv, s1, acc[t]);
+    }
+  };
   // Control flow here is the same in all four warps whatever happens (named barriers below): after an
   // expired wait the loop keeps walking the stream but skips the waits and the work.
   int g = 0;
@@ -1254,7 +1300,13 @@ __device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pi
             ++n4;
           }
         } else if (w13 || w2_aligned) {  // the stage is exactly one scale segment
-          close_seg(tab, 4 * (j - U.j0) + toff);
+          if (!fp4l && !last) {  // this stage and the next together (the SF look-ahead is FP4-only)
+            close_seg2(tab, 4 * (j - U.j0) + toff, 4 * (j + 1 - U.j0) + toff);
+            ++j;
+            ++g;
+          } else {
+            close_seg(tab, 4 * (j - U.j0) + toff);
+          }
         } else {  // w2 of a slice that starts inside a 128-row block: the same segments as the MMA issuer
           const int nk = ksteps(a.I_loc, k, j);
           for (int qk = 0; qk < nk; ++qk) {
@@ -1296,21 +1348,40 @@ __device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pi
         if (live && !pl.abort) {
           unsigned long long* cnt = w13 ? pl.cnt13 + (long long)si * a.P1 + U.tile : pl.cnt2 + U.tile;
           const unsigned long long total = w13 ? (unsigned long long)a.KB1 : (unsigned long long)((pl.nr + 1) * a.KB2);
-          // release: the partial of all 128 threads (ordered by the barrier); acquire: if this is the
-          // last contribution, the other contributors' partials
-          const unsigned long long c = atom_add_acq_rel(cnt, (unsigned long long)U.n) + (unsigned long long)U.n;
-          if (c == total) {
-            if (w13 || a.ar_world <= 1) {
-              fk = w13 ? 1 : 2;
-            } else {  // N > 1: the exchange of the output tile runs on this CTA's finisher warp
-              const int tail = *P.qtail;
-              P.queue[tail % QCAP] = U.tile;
-              __threadfence_block();
-              *P.qtail = tail + 1;
+          if (w13 && U.j0 != 0) {
+            // A w1|w3 tile is finished by the CTA holding its first blocks: in that CTA's range they
+            // come last, while every other contributor holds the tile's later blocks at the start of
+            // its own range. The others only add their count (release: this CTA's partial, ordered by
+            // the barrier) and go on.
+            red_add_release(cnt, (unsigned long long)U.n);
+          } else {
+            // release: the partial of all 128 threads (ordered by the barrier); acquire: the other
+            // contributors' partials once the count is complete
+            unsigned long long c = atom_add_acq_rel(cnt, (unsigned long long)U.n) + (unsigned long long)U.n;
+            if (w13 && c < total) {  // the tile's later blocks are still on their way (bounded wait)
+              const uint64_t t0 = globaltimer_ns();
+              while ((c = ld_relaxed64(cnt)) < total) {
+                if (ld_relaxed32(a.status) != 0u || globaltimer_ns() - t0 > kWait) {
+                  atomicOr(a.status, ST_CNT);
+                  pl.abort = 1;
+                  break;
+                }
+              }
+              fence_acq_rel_gpu();
             }
-          } else if (c > total) {
-            atomicOr(a.status, ST_CNT);
-            pl.abort = 1;
+            if (c == total) {
+              if (w13 || a.ar_world <= 1) {
+                fk = w13 ? 1 : 2;
+              } else {  // N > 1: the exchange of the output tile runs on this CTA's finisher warp
+                const int tail = *P.qtail;
+                P.queue[tail % QCAP] = U.tile;
+                __threadfence_block();
+                *P.qtail = tail + 1;
+              }
+            } else if (c > total) {
+              atomicOr(a.status, ST_CNT);
+              pl.abort = 1;
+            }
           }
         }
         pl.efl = fk;
@@ -1673,6 +1744,7 @@ __global__ void __launch_bounds__(NT, 1) moe_tc_kernel(const __grid_constant__ T
     for (int i = 0; i < NISS; ++i) mbar_init(&P.mdone[i], 1);
     ucnt[1] = ucnt[3] = 0;
     pl.nr = 0;
+    pl.efl = 0;
     pl.wk.init(a, 0);  // the shared expert's splits now; the routed ones once the plan is known
     pl.tag = 0u;
     pl.ar_epoch = 0u;
