@@ -60,7 +60,7 @@ constexpr int SA = 16384;                // stage A: 128 rows x 128 K (one byte 
 constexpr int SB = 2048;                 // stage B (w2 phase): 16 rows x 128 K e4m3
 constexpr int STAGE = SA + SB + 1024;    // + 1 KB for the stage's scales (FP4 512 B, FP8 16 B)
 constexpr int NACC8 = 16;                // FP8 block accumulators (16 TMEM columns each)
-constexpr int kDepth8 = 4;               // FP8 stages (16 KB) in flight per CTA
+constexpr int kDepth8 = 6;               // FP8 stages (16 KB) in flight per CTA
 // Tensor memory columns: FP8 block accumulators [0, 256), FP4 unit accumulators [2 parities][2 issuers]
 // at [256, 320), FP4 A scale factors 4 per ring slot from 320, B scale factors at 416.
 constexpr uint32_t TM_ACC4 = 256, TM_SFA = 320, TM_SFB = 416, TM_COLS = 512;
@@ -321,7 +321,7 @@ __host__ __device__ inline TcSmem tc_smem(int H, int S, int E, int B) {
   L.scr = o;  // the plan's scores and biased scores, [B][E] each
   o += ((size_t)2 * B * E * 4 + 15) & ~size_t(15);
   L.bars = o;
-  o += (size_t)(3 * S + 2 * NACC8 + 5 * NISS) * 8;
+  o += (size_t)(3 * S + 2 * NACC8 + 5 * NISS + 1) * 8;
   o = (o + 15) & ~size_t(15);
   L.plan = o;
   o += (sizeof(TcPlan) + 15) & ~size_t(15);
@@ -709,6 +709,7 @@ struct Pipe {
   uint64_t* a4f;    // [2 parities][NISS] FP4 unit accumulator of an issuer complete
   uint64_t* a4r;    // [2 parities][NISS] FP4 unit accumulator of an issuer read (4 epilogue warps)
   uint64_t* mdone;  // [NISS] every MMA of an issuer complete
+  uint64_t* rdy;    // the plan and the routed units are published (one arrival)
   int* queue;       // [QCAP] finisher jobs
   volatile int* qtail;
   volatile int* edone;   // the epilogue has queued its last job
@@ -768,29 +769,32 @@ struct Cur {
   }
 };
 
-__device__ __forceinline__ void backoff() { __nanosleep(64); }
+// Polls of shared or global words spin without sleeping: a sleeping thread wakes up late (measured
+// here at over a microsecond), and every such wait sits on the layer's critical path.
+__device__ __forceinline__ void backoff() {}
 
-// Waits (bounded) until the plan and the routed units are published.
-__device__ void wait_ready(const TcArgs& a, TcPlan& pl) {
-  const uint64_t t0 = globaltimer_ns();
-  while (!pl.ready && !pl.abort) {
-    backoff();
-    if (globaltimer_ns() - t0 > kWait) {
-      atomicOr(a.status, ST_PLAN);
-      pl.abort = 1;
-    }
+// Waits (bounded) until the plan and the routed units are published: the plan thread arrives on the
+// `rdy` barrier (release), the waiters' try_wait acquires.
+__device__ void wait_ready(const TcArgs& a, TcPlan& pl, uint64_t* rdy) {
+  if (!mbar_wait(rdy, 0, kWait)) {
+    atomicOr(a.status, ST_PLAN);
+    pl.abort = 1;
   }
-  __threadfence_block();  // the routed units and the plan, written before `ready`
 }
 
 // ---- warp 0, lane 0: TMA producer. One 128 x 128 tensor box per stage (plus an FP4 block's scales).
 __device__ __noinline__ void role_producer(const TcArgs& a, TcPlan& pl, const Pipe& Pin) {
   const Pipe P = Pin;
   const uint64_t pol = l2_evict_first();
+  // the four tensor maps into the TMA unit's descriptor cache now, not at their first copies
+  asm volatile("prefetch.tensormap [%0];" ::"l"(&a.tm_s13) : "memory");
+  asm volatile("prefetch.tensormap [%0];" ::"l"(&a.tm_r13) : "memory");
+  asm volatile("prefetch.tensormap [%0];" ::"l"(&a.tm_s2) : "memory");
+  asm volatile("prefetch.tensormap [%0];" ::"l"(&a.tm_r2) : "memory");
   int slot = 0, ph = 0, g = 0;
   for (int k = 0; k < 4 && !pl.abort; ++k) {
     if (k == 1) {  // routed work needs the plan
-      wait_ready(a, pl);
+      wait_ready(a, pl, P.rdy);
       if (pl.abort) break;
     }
     const bool w13 = k < 2, routed = k & 1;
@@ -913,7 +917,7 @@ __device__ __noinline__ void role_mma(const TcArgs& a, TcPlan& pl, const Pipe& P
   const bool w2_aligned = (a.row0 & 127) == 0;  // every w2 stage is then one FP8 scale segment
   for (int k = 0; k < 4 && ok; ++k) {
     if (k == 1) {  // the routed units exist once the plan is published
-      wait_ready(a, pl);
+      wait_ready(a, pl, P.rdy);
       if (pl.abort) break;
     }
     const bool f4 = (k & 1) && a.r_fmt == DSMOE_FMT_FP4;
@@ -1236,7 +1240,7 @@ __device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pi
   int g = 0;
   for (int k = 0; k < 4; ++k) {
     if (k == 1) {  // the routed units exist once the plan is published
-      if (m == 0) wait_ready(a, pl);
+      if (m == 0) wait_ready(a, pl, P.rdy);
       named_bar_sync(2, 128);
       if (fp4l) sf.start(P, 1, g);
     }
@@ -1337,47 +1341,54 @@ __device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pi
 #pragma unroll
         for (int t = 0; t < MAXB; ++t) acc[t] *= (U.slot >= 0 && live ? pl.w[U.slot][t] : 1.0f) * (1.0f / kHScale);
       }
-      if (live && !pl.abort) {
+      if (live && !pl.abort && !(w13 && U.j0 == 0)) {  // (a w1|w3 tile's finisher keeps its own in registers)
         float4* d4 = reinterpret_cast<float4*>(dst + m * 8);
         d4[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
         if (a.B > 4) d4[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
       }
       named_bar_sync(2, 128);
+      // A w1|w3 tile is finished by the CTA holding its first blocks: in that CTA's range they come
+      // last, while every other contributor holds the tile's later blocks at the start of its own
+      // range. At N = 1 an output tile is finished by its designated CTA once the stream is done (see
+      // below); at N > 1 by its last contributor's finisher warp. Units that cannot finish anything only
+      // add their count (release: this CTA's partial, ordered by the barrier) and go on.
+      const bool may_finish = w13 ? U.j0 == 0 : a.ar_world > 1;
       if (m == 0) {
-        int fk = 0;  // what this CTA finishes: 1 a w1|w3 tile, 2 a w2 tile (N = 1)
+        int fk = 0;  // what this CTA finishes: 1 a w1|w3 tile
         if (live && !pl.abort) {
           unsigned long long* cnt = w13 ? pl.cnt13 + (long long)si * a.P1 + U.tile : pl.cnt2 + U.tile;
           const unsigned long long total = w13 ? (unsigned long long)a.KB1 : (unsigned long long)((pl.nr + 1) * a.KB2);
-          if (w13 && U.j0 != 0) {
-            // A w1|w3 tile is finished by the CTA holding its first blocks: in that CTA's range they
-            // come last, while every other contributor holds the tile's later blocks at the start of
-            // its own range. The others only add their count (release: this CTA's partial, ordered by
-            // the barrier) and go on.
+          if (!may_finish) {
             red_add_release(cnt, (unsigned long long)U.n);
+          } else if (w13) {
+            // this CTA finishes the tile: it waits for the other contributors' counts (its own partial
+            // stays in registers and is never counted), then acquires their partials (bounded wait)
+            const unsigned long long others = total - (unsigned long long)U.n;
+            const uint64_t t0 = globaltimer_ns();
+            unsigned long long c;
+            while ((c = ld_relaxed64(cnt)) < others) {
+              if (ld_relaxed32(a.status) != 0u || globaltimer_ns() - t0 > kWait) {
+                atomicOr(a.status, ST_CNT);
+                pl.abort = 1;
+                break;
+              }
+            }
+            fence_acq_rel_gpu();
+            if (c == others) {
+              fk = 1;
+            } else if (c > others) {
+              atomicOr(a.status, ST_CNT);
+              pl.abort = 1;
+            }
           } else {
             // release: the partial of all 128 threads (ordered by the barrier); acquire: the other
             // contributors' partials once the count is complete
-            unsigned long long c = atom_add_acq_rel(cnt, (unsigned long long)U.n) + (unsigned long long)U.n;
-            if (w13 && c < total) {  // the tile's later blocks are still on their way (bounded wait)
-              const uint64_t t0 = globaltimer_ns();
-              while ((c = ld_relaxed64(cnt)) < total) {
-                if (ld_relaxed32(a.status) != 0u || globaltimer_ns() - t0 > kWait) {
-                  atomicOr(a.status, ST_CNT);
-                  pl.abort = 1;
-                  break;
-                }
-              }
-              fence_acq_rel_gpu();
-            }
-            if (c == total) {
-              if (w13 || a.ar_world <= 1) {
-                fk = w13 ? 1 : 2;
-              } else {  // N > 1: the exchange of the output tile runs on this CTA's finisher warp
-                const int tail = *P.qtail;
-                P.queue[tail % QCAP] = U.tile;
-                __threadfence_block();
-                *P.qtail = tail + 1;
-              }
+            const unsigned long long c = atom_add_acq_rel(cnt, (unsigned long long)U.n) + (unsigned long long)U.n;
+            if (c == total) {  // N > 1: the exchange of the output tile runs on this CTA's finisher warp
+              const int tail = *P.qtail;
+              P.queue[tail % QCAP] = U.tile;
+              __threadfence_block();
+              *P.qtail = tail + 1;
             } else if (c > total) {
               atomicOr(a.status, ST_CNT);
               pl.abort = 1;
@@ -1386,13 +1397,41 @@ __device__ __noinline__ void role_epilogue(const TcArgs& a, TcPlan& pl, const Pi
         }
         pl.efl = fk;
       }
-      named_bar_sync(2, 128);
-      const int fk = *reinterpret_cast<volatile int*>(&pl.efl);
-      if (fk == 1)
-        epi_finish_w13(a, pl, U.slot < 0 ? 0 : 1, si, U.tile, U.tile_id, U.jc, acc, m, efin);
-      else if (fk == 2)
-        epi_finish_w2(a, pl, U.tile, SH, m, reinterpret_cast<int*>(efin + 2 * 64 * 8));
+      if (may_finish) {
+        named_bar_sync(2, 128);
+        if (*reinterpret_cast<volatile int*>(&pl.efl) == 1)
+          epi_finish_w13(a, pl, U.slot < 0 ? 0 : 1, si, U.tile, U.tile_id, U.jc, acc, m, efin);
+      }
       ++unit;
+    }
+  }
+  // N = 1: the output tiles designated to this CTA (tile mt to CTA floor(mt G / MT2), at most one each
+  // while MT2 <= G), each once all its (nr + 1) KB2 stage contributions are counted (bounded wait).
+  if (a.ar_world <= 1) {
+    const int G = gridDim.x;
+    const int c = blockIdx.x;
+    for (int mt = (int)(((unsigned)c * (unsigned)a.MT2 + (unsigned)G - 1u) / (unsigned)G);
+         mt < a.MT2 && (int)((unsigned)mt * (unsigned)G / (unsigned)a.MT2) == c; ++mt) {
+      named_bar_sync(2, 128);
+      if (m == 0) {
+        int go = 0;
+        if (!pl.abort) {
+          const unsigned long long total = (unsigned long long)((pl.nr + 1) * a.KB2);
+          const uint64_t t0 = globaltimer_ns();
+          while (ld_relaxed64(pl.cnt2 + mt) < total) {
+            if (ld_relaxed32(a.status) != 0u || globaltimer_ns() - t0 > kWait) {
+              atomicOr(a.status, ST_CNT);
+              pl.abort = 1;
+              break;
+            }
+          }
+          fence_acq_rel_gpu();  // acquire: every contributor's partial
+          go = pl.abort ? 0 : 1;
+        }
+        pl.efl = go;
+      }
+      named_bar_sync(2, 128);
+      if (*reinterpret_cast<volatile int*>(&pl.efl) == 1) epi_finish_w2(a, pl, mt, SH, m, reinterpret_cast<int*>(efin + 2 * 64 * 8));
     }
   }
   named_bar_sync(2, 128);
@@ -1701,6 +1740,7 @@ __global__ void __launch_bounds__(NT, 1) moe_tc_kernel(const __grid_constant__ T
   P.a4f = P.accr + NACC8;
   P.a4r = P.a4f + 2 * NISS;
   P.mdone = P.a4r + 2 * NISS;
+  P.rdy = P.mdone + NISS;
   TcPlan& pl = *reinterpret_cast<TcPlan*>(sm + L.plan);
   unsigned* emask = reinterpret_cast<unsigned*>(sm + L.emask);
   float* etab = reinterpret_cast<float*>(sm + L.etab);
@@ -1742,6 +1782,7 @@ __global__ void __launch_bounds__(NT, 1) moe_tc_kernel(const __grid_constant__ T
       mbar_init(&P.a4r[i], 4);
     }
     for (int i = 0; i < NISS; ++i) mbar_init(&P.mdone[i], 1);
+    mbar_init(P.rdy, 1);
     ucnt[1] = ucnt[3] = 0;
     pl.nr = 0;
     pl.efl = 0;
@@ -1829,6 +1870,7 @@ __global__ void __launch_bounds__(NT, 1) moe_tc_kernel(const __grid_constant__ T
             pl.wk.sp[3].init(nr * a.MT2 * a.KB2, a.KB2, G);
             __threadfence_block();
             pl.ready = 1;
+            mbar_arrive(P.rdy);
           }
           if (lane == 0) role_hcopy(a, pl, P, SH);
         } else if (a.ar_world > 1) {
