@@ -79,6 +79,9 @@ def parse():
     ap.add_argument("--decode-store", choices=["tc", "frag"], default="frag",
                     help="resident store of decode layers of 1..8 tokens: the fragment layout (mma.sync kernel, "
                          "default) or the tensor-core layout (tcgen05 kernel)")
+    ap.add_argument("--no-alt-store", dest="alt_store", action="store_false",
+                    help="N = 1, 1..8 tokens: skip the second decode store's timing and parity (reported as "
+                         "alt_store beside the line)")
     ap.add_argument("--no-stack", dest="stack_in_bench", action="store_false",
                     help="decode mode at N >= 4: skip the 40-layer stack measurement reported beside the line")
     return ap.parse_args()
@@ -91,6 +94,13 @@ def decode_layouts(B):
     """Resident store of a decode benchmark layer: ``--decode-store`` for 1..8 tokens, the fragment
     layout for larger batches."""
     return (DECODE_STORE,) if B <= 8 else ("frag",)
+
+
+def alt_layouts(args, B, world):
+    """The other decode store, kept too at N = 1 and 1..8 tokens so the line also reports it."""
+    if world != 1 or B > 8 or not args.alt_store:
+        return ()
+    return ("frag",) if DECODE_STORE == "tc" else ("tc",)
 
 
 def layer_formats(args):
@@ -374,7 +384,8 @@ def ours(args):
     for li, fmt in enumerate(layer_formats(args)):
         NE = args.experts
         m = dsmoe.MoE(H, I, NE, TOPK, fmt, "sigmoid", ROUTE_SCALE, rank=rank, world=world, device=dev, max_tokens=B,
-                      layouts=decode_layouts(B))
+                      layouts=decode_layouts(B) + alt_layouts(args, B, world))
+        m.use_decode_store(decode_layouts(B)[0])
         rw = dsmoe.make_router(NE, H, gen, device=dev)
         m.load_router(rw)
         sh = dsmoe.make_expert("fp8", H, I, gen, device=dev)
@@ -567,6 +578,26 @@ def ours(args):
     achieved = dom["gbs"]
     traffic = read_traffic(dom_name, B, world)
 
+    # ---- the other decode store (N = 1): the same layers, tokens and routing through its kernel
+    alt = None
+    alts = alt_layouts(args, B, world)
+    if alts:
+        for m in layers:
+            m.use_decode_store(alts[0])
+        aparity = check_parity(args, layers, refs, layer_launch, xin, yout, idx_st, comm, rank, world, dev)
+        ams = variant_times([lambda v, li=li: layer_launch(li, v) for li in range(n_layers)], NV, K, W, dev)
+        for m in layers:
+            m.check(B)
+            m.use_decode_store(decode_layouts(B)[0])
+        akern = {}
+        for li, nm in enumerate(names):
+            t = ams[li]
+            byts = kern[f"{nm}_layer"]["bytes"]
+            akern[f"{nm}_layer"] = {"us": round(t * 1e3, 2), "bytes": byts, "gbs": round(byts / (t * 1e-3) / 1e9, 1)}
+        alt = {"store": alts[0], "dtype": DTYPE_TC if alts[0] == "tc" else DTYPE_FRAG, "kernels": akern,
+               "us_per_layer_token": round(sum(ams) * 1e3 / (n_layers * B), 3), "parity": aparity,
+               "timing": "CUDA graphs per token variant with timestamp nodes between the layers, replayed round-robin"}
+
     # ---- e2e through the public API: every step copies its layers' tokens from pinned host memory
     # (one copy for the step), runs MoE.forward per layer and reads every layer's output back
     xh = torch.empty((NV, n_layers * B, H), dtype=torch.bfloat16).pin_memory()
@@ -632,6 +663,7 @@ def ours(args):
                     "d2h_bytes_per_step": n_layers * B * H * 2},
             "gpu_launches": K * n_layers * launches_per_layer,
             "parity": parity,
+            "alt_store": alt,
             "stack40_ms_per_token": stack40["ms_per_token"] if stack40 else None,
             "stack40": stack40,
             "timing": timing_mode,
@@ -700,6 +732,35 @@ def graph_times(fns, steps, warmup, dev):
             for i in range(len(fns)):
                 t[i].append(ev[i].elapsed_time(ev[i + 1]))
     del g
+    return [statistics.mean(x) for x in t]
+
+
+def variant_times(fns, NV, steps, warmup, dev):
+    """Per-fn mean ms: fns[i](v) launches layer i on token variant v; one CUDA graph per variant with
+    timestamp nodes between the layers, replayed round-robin over the variants (sync per replay)."""
+    import torch
+    for v in range(NV):
+        for f in fns:
+            f(v)
+    torch.cuda.synchronize(dev)
+    evs = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(len(fns) + 1)] for _ in range(NV)]
+    gs = [torch.cuda.CUDAGraph() for _ in range(NV)]
+    for v in range(NV):
+        with torch.cuda.graph(gs[v]):
+            for i, f in enumerate(fns):
+                evs[v][i].record()
+                f(v)
+            evs[v][-1].record()
+    torch.cuda.synchronize(dev)
+    t = [[] for _ in fns]
+    for s in range(warmup + steps):
+        v = s % NV
+        gs[v].replay()
+        torch.cuda.synchronize(dev)
+        if s >= warmup:
+            for i in range(len(fns)):
+                t[i].append(evs[v][i].elapsed_time(evs[v][i + 1]))
+    del gs
     return [statistics.mean(x) for x in t]
 
 

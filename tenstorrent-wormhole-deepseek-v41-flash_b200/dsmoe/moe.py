@@ -87,6 +87,13 @@ class MoE:
         self.comm = None  # tp.PeerComm: all-reduce inside the decode kernel
         self._prefill_ws: Optional[torch.Tensor] = None  # grown on demand by prefill()
 
+    def use_decode_store(self, layout: str) -> None:
+        """Serve decode calls from the given resident store ("tc" or "frag"; it must have been kept)."""
+        if layout not in self.stores:
+            raise ValueError(f"store {layout!r} is not resident (kept: {tuple(self.stores)})")
+        self._dec_layout = layout
+        self._bind()
+
     def _bind(self):
         """The decode layer (tensor-core store when kept) and the batched layer (fragment store)."""
         self._layer = self._layers[self._dec_layout]
