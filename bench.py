@@ -13,7 +13,9 @@ per-layer time. Weights are seeded synthetic N(0, 0.02), generated and resident 
 Prints one JSON line (rank 0). ``value`` is device time (CUDA events on the launching stream,
 max over ranks; every step streams more weight bytes than L2 holds, so no flush is needed --
 ``--l2-flush`` adds one); ``e2e`` is the same metric through the public API
-with the step's tokens copied from pinned host memory and its outputs read back every step.
+with the step's tokens copied from pinned host memory and its outputs read back every step: the
+traced decode step (``dsmoe.DecodeTrace``) when it applies, with the eager ``MoE.forward`` figure
+beside it.
 """
 import argparse
 import ctypes
@@ -613,15 +615,40 @@ def ours(args):
             yh[li].copy_(m.forward(xd[li * B:(li + 1) * B]), non_blocking=True)
         torch.cuda.synchronize()
 
-    for s in range(W):
-        e2e_step(s)
-    if world > 1:
-        dist.barrier()
-    t0 = time.perf_counter()
-    for s in range(K):
-        e2e_step(W + s)
-    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / K, dev)
-    e2e_val = e2e_ms * 1e3 / (n_layers * B)
+    def e2e_time(step_fn):
+        for s in range(W):
+            step_fn(s)
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for s in range(K):
+            step_fn(W + s)
+        return max_over_ranks((time.perf_counter() - t0) * 1e3 / K, dev) * 1e3 / (n_layers * B)
+
+    # eager: MoE.forward per layer per step
+    e2e_eager = e2e_time(e2e_step)
+    # traced: dsmoe.DecodeTrace (the reference's traced decode step); the step's host tokens are
+    # copied into the trace's pinned input, and the graph copies them in and every output out
+    e2e_traced, trace_err = None, None
+    if B <= 8 and (world == 1 or comm is not None):
+        tr = None
+        try:
+            tr = dsmoe.DecodeTrace(layers, B)
+            xv = xh.view(NV, n_layers, B, H)
+            e2e_traced = e2e_time(lambda s: tr.step(xv[s % NV]))
+            tr.check()
+            for li in range(n_layers):  # the trace's last step equals the eager forward on its tokens
+                y_e = layers[li].forward(xv[(W + K - 1) % NV, li].to(dev))
+                if not torch.equal(tr.y_host[li], y_e.cpu()):
+                    trace_err = f"layer {li}: traced output differs from MoE.forward"
+        except Exception as ex:  # reported in the line; the eager figure stands
+            trace_err = repr(ex)[:200]
+        finally:
+            if tr is not None:
+                tr.release()
+    if trace_err is not None:
+        e2e_traced = None
+    e2e_val = e2e_traced if e2e_traced is not None else e2e_eager
 
     # ---- the 40-layer resident stack (config 4) when it fits: layers 2..39 hold copies of the two
     # benchmark layers' expert bytes in their own memory, each with its own router
@@ -660,7 +687,13 @@ def ours(args):
                          "traffic": traffic},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_val, 3), "unit": UNIT, "h2d_bytes_per_step": n_layers * B * H * 2,
-                    "d2h_bytes_per_step": n_layers * B * H * 2},
+                    "d2h_bytes_per_step": n_layers * B * H * 2,
+                    "api": "dsmoe.DecodeTrace.step" if e2e_traced is not None else "dsmoe.MoE.forward",
+                    "eager_forward": round(e2e_eager, 3),
+                    "traced": round(e2e_traced, 3) if e2e_traced is not None else None,
+                    "trace_error": trace_err,
+                    "timing": "host wall clock per step (max over ranks), tokens from pinned host memory "
+                              "in and every layer's output out each step"},
             "gpu_launches": K * n_layers * launches_per_layer,
             "parity": parity,
             "alt_store": alt,

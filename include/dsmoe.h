@@ -229,6 +229,12 @@ DSMOE_API int dsmoe_moe_decode_profiled(const dsmoe_layer_t* layer, const void* 
 /* fp32 [n] -> bf16 [n] (the last step after an fp32 all-reduce of the partial sums). */
 DSMOE_API int dsmoe_f32_to_bf16(const float* src, void* dst, long long n, void* stream);
 
+/* One asynchronous copy of n bytes between addresses the device can reach (device memory or
+ * page-locked host memory), ordered on the stream. Under CUDA-graph capture it becomes one memcpy
+ * node: the traced decode step (the role of DecodeTrace, dsv41/tt/model.py:262-330) copies its
+ * tokens in and its outputs out with it. Pageable host memory is rejected during capture. */
+DSMOE_API int dsmoe_copy_async(void* dst, const void* src, long long n, void* stream);
+
 /* ---- prefill / batched layer on the 5th-generation tensor cores --------------------------- */
 
 /* Workspace bytes for dsmoe_moe_prefill with P tokens (0 if the layer or P is unsupported). */

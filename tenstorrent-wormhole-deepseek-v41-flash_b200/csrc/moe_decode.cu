@@ -624,6 +624,14 @@ extern "C" int dsmoe_moe_check(const dsmoe_layer_t* L, int B, void* workspace, s
   return DSMOE_ERR_TIMEOUT;
 }
 
+extern "C" int dsmoe_copy_async(void* dst, const void* src, long long n, void* stream) {
+  DSMOE_REQUIRE(dst && src && n >= 0, DSMOE_ERR_ARG, "copy_async: bad arguments");
+  if (n == 0) return DSMOE_OK;
+  if (cudaMemcpyAsync(dst, src, (size_t)n, cudaMemcpyDefault, (cudaStream_t)stream) != cudaSuccess)
+    return cuda_status("copy_async");
+  return DSMOE_OK;
+}
+
 extern "C" int dsmoe_f32_to_bf16(const float* src, void* dst, long long n, void* stream) {
   DSMOE_REQUIRE(src && dst && n >= 0, DSMOE_ERR_ARG, "f32_to_bf16: bad arguments");
   if (n == 0) return DSMOE_OK;

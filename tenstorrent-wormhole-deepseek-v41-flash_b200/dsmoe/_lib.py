@@ -66,6 +66,7 @@ _SIGS = {
                                    ctypes.POINTER(_P)], _I),
     "dsmoe_moe_check": ([ctypes.POINTER(Layer), _I, _P, ctypes.c_size_t, _P], _I),
     "dsmoe_f32_to_bf16": ([_P, _P, _LL, _P], _I),
+    "dsmoe_copy_async": ([_P, _P, _LL, _P], _I),
     "dsmoe_moe_prefill_workspace_bytes": ([ctypes.POINTER(Layer), _I], ctypes.c_size_t),
     "dsmoe_moe_prefill": ([ctypes.POINTER(Layer), _P, _I, _P, _P, _P, _I, _P, ctypes.c_size_t, _P], _I),
     "dsmoe_moe_prefill_check": ([ctypes.POINTER(Layer), _I, _P, ctypes.c_size_t, _P], _I),

@@ -42,6 +42,12 @@ def _check_x(x: torch.Tensor, hidden: int, device) -> torch.Tensor:
     return x if x.is_contiguous() else x.contiguous()
 
 
+def _check_out(out: torch.Tensor, B: int, hidden: int, device) -> None:
+    if (out.dtype != torch.bfloat16 or out.shape != (B, hidden) or not out.is_contiguous()
+            or out.device != device):
+        raise ValueError(f"out must be a contiguous [{B}, {hidden}] bfloat16 tensor on {device}")
+
+
 class MoE:
     """One MoE layer resident on one GPU (one tensor-parallel rank).
 
@@ -219,19 +225,24 @@ class MoE:
             raise ValueError("comm does not match this layer's rank, world or hidden size")
         self.comm = comm
 
-    def forward(self, x: torch.Tensor, image_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """y [B, H] bf16: the full layer output (partials all-reduced when world > 1).
+    def forward(self, x: torch.Tensor, image_mask: Optional[torch.Tensor] = None,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """y [B, H] bf16: the full layer output (partials all-reduced when world > 1), written into
+        ``out`` (a contiguous [B, H] bf16 tensor on the layer's GPU) when given.
 
         If a bounded device wait of an earlier call on this layer's workspace expired, the kernel
         writes NaN rows instead of y until ``check()`` resets the workspace."""
+        if out is not None:
+            _check_out(out, x.shape[0], self.hidden, self.device)
         if self.world == 1:
-            return self._run(x, image_mask, None, L.DTYPE_BF16)
+            return self._run(x, image_mask, out, L.DTYPE_BF16)
         if self.comm is not None and self.comm.handle is not None:
             x = _check_x(x, self.hidden, self.device)
             B = x.shape[0]
             if B <= self._dec_max and L.lib.dsmoe_moe_allreduce_supported(self._layer, self.comm.handle,
                                                                            x.data_ptr(), B):
-                y = torch.empty((B, self.hidden), dtype=torch.bfloat16, device=self.device)
+                y = out if out is not None else torch.empty((B, self.hidden), dtype=torch.bfloat16,
+                                                            device=self.device)
                 mask = self._mask(image_mask, B)
                 L.check(L.lib.dsmoe_moe_decode_allreduce(
                     self._layer, self.comm.handle, x.data_ptr(), B, L.ptr(mask), y.data_ptr(), L.DTYPE_BF16, None,
@@ -239,7 +250,7 @@ class MoE:
                 return y
         part = self._run(x, image_mask, None, L.DTYPE_F32)
         torch.distributed.all_reduce(part, group=self.group)
-        y = torch.empty(part.shape, dtype=torch.bfloat16, device=self.device)
+        y = out if out is not None else torch.empty(part.shape, dtype=torch.bfloat16, device=self.device)
         L.call("dsmoe_f32_to_bf16", L.ptr(part), L.ptr(y), part.numel(), L.stream_of(part))
         return y
 
