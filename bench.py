@@ -67,7 +67,7 @@ def parse():
     ap.add_argument("--l2-flush", action="store_true",
                     help="write 256 MiB between steps (default: off; each step already streams more than L2)")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline sampling")
-    ap.add_argument("--mode", choices=["decode", "prefill", "sweep", "stack"], default="decode",
+    ap.add_argument("--mode", choices=["decode", "prefill", "sweep", "stack", "gemm"], default="decode",
                     help="decode: the headline config (default); prefill: P tokens with Zipf routing through the "
                          "tcgen05 grouped GEMMs; sweep: decode batch 1..64 and the batched path under uniform / Zipf routing")
     ap.add_argument("--tokens", type=int, default=126, help="prefill mode: tokens per layer call")
@@ -847,6 +847,109 @@ def prefill_mode(args):
     print(json.dumps(line), flush=True)
 
 
+def gemm_mode(args):
+    """The kernel-surface GEMMs (fp8_gemm / fp4_gemm, dsv41/ref/kernel.py:105-112) at a DeepSeek linear
+    shape, N = K = 5120, for M in {1, 126, 2048} tokens: e4m3 activations with fp32 scales per 128-K
+    block (act_quant's output, the form model.py passes), bf16 output. Enough distinct weight
+    matrices rotate through the timed calls that every call reads its weights from HBM, not L2.
+    Each call is one launch; the calls are replayed from a CUDA graph and timed with CUDA events.
+    ``cublas_bf16_us`` is torch.matmul of bf16 activations with weights already dequantized to bf16
+    (the same flops, twice the weight bytes of FP8), for context."""
+    import torch
+    import dsmoe  # noqa: F401  (loads libdsmoe.so)
+    from dsmoe import _lib as L
+    from dsmoe import synth
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    N = K = H
+    peak, peak_kind = measured_peak()
+    with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+        tf_peak = float(json.load(f).get("bf16_tflops", 1590.0))
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    res = {}
+    for fmt in ("fp8", "fp4"):
+        w = torch.randn((N, K), generator=gen, device=dev) * 0.02
+        q, sc = synth.quant_fp8_block(w) if fmt == "fp8" else synth.quant_fp4_e8m0(w)
+        wbytes = q.numel() + sc.numel() * sc.element_size()
+        nmat = max(2, -(-3 * 126 * 2 ** 20 // wbytes))  # > 3x L2 in rotation
+        qs = [q.clone() for _ in range(nmat)]
+        scs = [sc.clone() for _ in range(nmat)]
+        del w
+        fn = L.lib.dsmoe_fp8_gemm if fmt == "fp8" else L.lib.dsmoe_fp4_gemm
+        for M in (1, 126, 2048):
+            x = torch.randn((M, K), generator=gen, device=dev) * 2
+            xb = x.view(M, K // 128, 128)
+            a_s = (xb.abs().amax(-1).clamp(min=1e-4) / 448.0).contiguous()
+            xq = (xb / a_s.unsqueeze(-1)).clamp(-448, 448).to(torch.float8_e4m3fn).view(M, K).view(torch.uint8)
+            out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            st = torch.cuda.current_stream(dev).cuda_stream
+            call = lambda i: L.check(fn(xq.data_ptr(), L.DTYPE_E4M3, a_s.data_ptr(), M, K, qs[i].data_ptr(),
+                                        scs[i].data_ptr(), N, out.data_ptr(), L.DTYPE_BF16,
+                                        torch.cuda.current_stream(dev).cuda_stream))
+            call(0)  # first call outside capture (the split-K workspace is allocated here)
+            torch.cuda.synchronize(dev)
+            reps = nmat
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for r in range(reps):
+                    call(r % nmat)
+            for _ in range(max(3, args.warmup)):
+                g.replay()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            us = e0.elapsed_time(e1) * 1e3 / (args.steps * reps)
+            del g
+            flops = 2.0 * M * N * K
+            byts = wbytes + M * K + M * (K // 128) * 4 + M * N * 2
+            r = {"us": round(us, 2), "bytes": int(byts), "gbs": round(byts / (us * 1e-6) / 1e9, 1),
+                 "hbm_frac_of_measured": round(byts / (us * 1e-6) / 1e9 / peak, 3),
+                 "tflops": round(flops / (us * 1e-6) / 1e12, 1),
+                 "weight_matrices_rotated": nmat}
+            if fmt == "fp8":  # kind::f8f6f4 on the codes: the FP8 rate, twice the measured bf16 figure
+                r["mma"] = "kind::f8f6f4 (e4m3 x e4m3), no conversion"
+                r["tensor_frac"] = round(flops / (us * 1e-6) / 1e12 / (2 * tf_peak), 3)
+                r["tensor_peak_tflops"] = 2 * tf_peak
+            else:  # kind::f16 on converted weights, activations as bf16 hi + lo: 2x the GEMM's flops issued
+                r["mma"] = "kind::f16 (bf16), weights converted in shared memory, activation hi + lo"
+                r["tensor_frac"] = round(2 * flops / (us * 1e-6) / 1e12 / tf_peak, 3)
+                r["tensor_peak_tflops"] = tf_peak
+            # context: cuBLAS bf16 on pre-dequantized weights (same shape)
+            if fmt == "fp8":
+                wb = torch.empty((N, K), dtype=torch.bfloat16, device=dev)
+                L.call("dsmoe_fp8_block_dequant", q.data_ptr(), sc.data_ptr(), N, K, 128, wb.data_ptr(),
+                       L.DTYPE_BF16, st)
+                xbf = x.to(torch.bfloat16)
+                for _ in range(3):
+                    torch.matmul(xbf, wb.T)
+                torch.cuda.synchronize(dev)
+                e0.record()
+                for _ in range(args.steps):
+                    torch.matmul(xbf, wb.T)
+                e1.record()
+                torch.cuda.synchronize(dev)
+                r["cublas_bf16_us"] = round(e0.elapsed_time(e1) * 1e3 / args.steps, 2)
+                r["cublas_bf16_note"] = "one weight matrix (L2-resident for M <= 126), bf16 x bf16"
+                del wb
+            res[f"{fmt}_m{M}"] = r
+        del qs, scs
+        torch.cuda.empty_cache()
+    line = {"mode": "gemm", "metric": "kernel-surface fp8_gemm / fp4_gemm us per call (tcgen05)",
+            "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+            "config": {"workload": "out[M, 5120] = (e4m3 a * a_s) @ dequant(W[5120, 5120])^T, bf16 out",
+                       "M": [1, 126, 2048], "activations": "e4m3 + fp32 scale per 128-K block",
+                       "l2": "weights rotate over > 3x L2 of distinct matrices"},
+            "kernels": res, "peak_hbm_gbs": peak, "peak_source": peak_kind, "peak_bf16_tflops": tf_peak,
+            "tensor_frac_note": "FP8: GEMM flops over 2x the measured bf16 peak (the FP8 rate); FP4: issued flops "
+                                "(2x the GEMM's, bf16 hi + lo activation terms) over the measured bf16 peak",
+            "timing": "CUDA graph of back-to-back calls, CUDA events around the replays"}
+    print(json.dumps(line), flush=True)
+
+
 def sweep_mode(args):
     """Config: decode batch 1..64 on one FP8 and one FP4 layer (router routing, ~uniform), and the
     batched tcgen05 path under forced uniform and Zipf(1.1) routing at the same batches."""
@@ -1099,6 +1202,8 @@ def main():
         prefill_mode(args)
     elif args.mode == "sweep":
         sweep_mode(args)
+    elif args.mode == "gemm":
+        gemm_mode(args)
     elif args.mode == "stack":
         stack_mode(args)
     else:

@@ -74,6 +74,8 @@ def _gemm(fn, a, a_s, b, b_s, block):
         adt, a2 = _L.DTYPE_BF16, a2.contiguous()
     else:
         adt, a2 = _L.DTYPE_F32, a2.float().contiguous()
+    if a2.data_ptr() % 16:  # the GEMM reads activations with 16-byte aligned tensor-memory-access tiles
+        a2 = a2.clone()
     M, N = a2.shape[0], b.shape[0]
     as2 = None
     if a_s is not None:
