@@ -910,14 +910,11 @@ def gemm_mode(args):
                  "hbm_frac_of_measured": round(byts / (us * 1e-6) / 1e9 / peak, 3),
                  "tflops": round(flops / (us * 1e-6) / 1e12, 1),
                  "weight_matrices_rotated": nmat}
-            if fmt == "fp8":  # kind::f8f6f4 on the codes: the FP8 rate, twice the measured bf16 figure
-                r["mma"] = "kind::f8f6f4 (e4m3 x e4m3), no conversion"
-                r["tensor_frac"] = round(flops / (us * 1e-6) / 1e12 / (2 * tf_peak), 3)
-                r["tensor_peak_tflops"] = 2 * tf_peak
-            else:  # kind::f16 on converted weights, activations as bf16 hi + lo: 2x the GEMM's flops issued
-                r["mma"] = "kind::f16 (bf16), weights converted in shared memory, activation hi + lo"
-                r["tensor_frac"] = round(2 * flops / (us * 1e-6) / 1e12 / tf_peak, 3)
-                r["tensor_peak_tflops"] = tf_peak
+            # the codes go to the tensor core as they are: the FP8 rate, twice the measured bf16 figure
+            r["mma"] = ("kind::f8f6f4 (e4m3 x e4m3)" if fmt == "fp8" else
+                        "kind::mxf8f6f4.block_scale (e2m1 x e4m3, e8m0 group scales in TMEM)") + ", no conversion"
+            r["tensor_frac"] = round(flops / (us * 1e-6) / 1e12 / (2 * tf_peak), 3)
+            r["tensor_peak_tflops"] = 2 * tf_peak
             # context: cuBLAS bf16 on pre-dequantized weights (same shape)
             if fmt == "fp8":
                 wb = torch.empty((N, K), dtype=torch.bfloat16, device=dev)
@@ -944,8 +941,7 @@ def gemm_mode(args):
                        "M": [1, 126, 2048], "activations": "e4m3 + fp32 scale per 128-K block",
                        "l2": "weights rotate over > 3x L2 of distinct matrices"},
             "kernels": res, "peak_hbm_gbs": peak, "peak_source": peak_kind, "peak_bf16_tflops": tf_peak,
-            "tensor_frac_note": "FP8: GEMM flops over 2x the measured bf16 peak (the FP8 rate); FP4: issued flops "
-                                "(2x the GEMM's, bf16 hi + lo activation terms) over the measured bf16 peak",
+            "tensor_frac_note": "GEMM flops over 2x the measured bf16 peak (the dense FP8 rate)",
             "timing": "CUDA graph of back-to-back calls, CUDA events around the replays"}
     print(json.dumps(line), flush=True)
 

@@ -435,15 +435,22 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
   }
 }
 
-// ------------------------------------------------------------------ FP8 weights x e4m3 activations
+// ------------------------------------------------------------------ FP8 / FP4 weights x e4m3 activations
 // The fake-quant form model.py passes (act_quant's e4m3 codes + fp32 scale per 128-K block) needs
 // no conversion: the TMA lands both operands in the canonical K-major 128-byte-swizzled layout and
-// tcgen05.mma kind::f8f6f4 (K 32 per instruction) multiplies the codes exactly. One accumulator per
-// 128-K block (a ring of F8ACC in tensor memory); the epilogue warps fold each block into fp32
-// registers with its scales, acc += D * a_s[t][kb] * b_s[kb], while the next blocks' MMAs run.
+// the tensor core multiplies the codes exactly, K 32 per instruction. FP8 weights: kind::f8f6f4.
+// FP4 weights: kind::mxf8f6f4.block_scale with A = e2m1 (the TMA widens the packed codes into the
+// padded form the tensor core reads) and the checkpoint's e8m0 group scales as A scale factors in
+// tensor memory (written two stages ahead by the epilogue warps; B scale factors 1.0). One
+// accumulator per 128-K block (a ring of F8ACC in tensor memory); the epilogue warps fold each block
+// into fp32 registers with its scales, acc += D * a_s[t][kb] (* b_s[kb] for FP8), while the next
+// blocks' MMAs run.
 constexpr int F8ACC = 4;
 constexpr int F8MAXRS = 10;
+constexpr uint32_t F4_SFA = 320, F4_SFB = 416;  // tensor-memory columns of the scale factors (FP4)
+constexpr int F4_LOOK = 2;                       // stages of A scale factors written ahead
 
+template <bool F4>
 __global__ void __launch_bounds__(NT, 1) gemm_f8_kernel(const __grid_constant__ Args a) {
   extern __shared__ __align__(1024) uint8_t gsm[];
   uint8_t* base = gsm + ((1024 - (smem_u32(gsm) & 1023)) & 1023);
@@ -455,7 +462,8 @@ __global__ void __launch_bounds__(NT, 1) gemm_f8_kernel(const __grid_constant__ 
   uint64_t* accf = empty + F8MAXRS;      // [F8ACC] block accumulator ready
   uint64_t* acce = accf + F8ACC;         // [F8ACC] block accumulator read (one arrival per epilogue warp)
   uint64_t* mdone = acce + F8ACC;        // [1] every MMA of this CTA done
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(mdone + 1);
+  uint64_t* sfr = mdone + 1;             // [F8MAXRS] FP4: the stage's A scale factors stored (one arrival per quadrant)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sfr + F8MAXRS);
   volatile int* abortf = reinterpret_cast<volatile int*>(tslot + 1);
   volatile int* lastf = abortf + 1;
 
@@ -476,11 +484,14 @@ __global__ void __launch_bounds__(NT, 1) gemm_f8_kernel(const __grid_constant__ 
       mbar_init(&acce[s], 8);
     }
     mbar_init(mdone, 1);
+    for (int s = 0; s < F8MAXRS; ++s) mbar_init(&sfr[s], 4);
     *abortf = 0;
     *lastf = 0;
     fence_mbar_init();
   }
-  const uint32_t ncols = (uint32_t)(F8ACC * TT);  // 64, 128, 256 or 512 columns
+  // FP8: 64, 128, 256 or 512 accumulator columns; FP4 (TT <= 64): accumulators in [0, 256), scale
+  // factors from column 320
+  const uint32_t ncols = F4 ? 512u : (uint32_t)(F8ACC * TT);
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
                  "r"(ncols)
@@ -511,7 +522,8 @@ __global__ void __launch_bounds__(NT, 1) gemm_f8_kernel(const __grid_constant__ 
         if (i >= a.RS && !wait(&empty[s], ((i / a.RS) - 1) & 1)) break;
         uint8_t* st = base + s * RB;
         const int kb = kb0 + i;
-        mbar_expect_tx(&full[s], (uint32_t)RB);
+        // an FP4 box counts its packed global bytes (the widened shared-memory tile is 16 KB)
+        mbar_expect_tx(&full[s], (uint32_t)((F4 ? TM * 64 : a.w_bytes) + a.a_bytes));
         tma_2d(st, &a.tw, kb * 128, n0, &full[s]);
         tma_2d(st + a.w_bytes, &a.ta, kb * 128, m0, &full[s]);
         ++issued;
@@ -521,22 +533,38 @@ __global__ void __launch_bounds__(NT, 1) gemm_f8_kernel(const __grid_constant__ 
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = (1u << 4) | ((uint32_t)(TT >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
+      const uint32_t idesc = F4 ? (5u << 7) | ((uint32_t)(TT >> 3) << 17) | (1u << 23) | ((uint32_t)(TM >> 4) << 24)
+                                : (1u << 4) | ((uint32_t)(TT >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
       const uint64_t d0 = desc_sw128(smem_u32(base));
       for (int i = 0; i < nk; ++i) {
         const int s = i % a.RS, ac = i % F8ACC;
         if (!wait(&full[s], (i / a.RS) & 1)) break;
+        if (F4 && !wait(&sfr[s], (i / a.RS) & 1)) break;
         if (i >= F8ACC && !wait(&acce[ac], ((i / F8ACC) - 1) & 1)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint64_t da = d0 + (uint64_t)((s * RB) >> 4), db = da + (uint64_t)(a.w_bytes >> 4);
         const uint32_t d = tmem + (uint32_t)(ac * TT);
+        if (F4) {
+          const uint32_t sfa = tmem + F4_SFA + 4u * (uint32_t)s, sfb = tmem + F4_SFB;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          asm volatile(
-              "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-              "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-              "l"(da + 2u * q), "l"(db + 2u * q), "r"(idesc), "r"(q > 0 ? 1u : 0u)
-              : "memory");
+          for (int q = 0; q < 4; ++q) {
+            // K step q reads byte q of every scale-factor word
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+                "l"(da + 2u * q), "l"(db + 2u * q), "r"(idesc | ((uint32_t)q << 29) | ((uint32_t)q << 4)),
+                "r"(q > 0 ? 1u : 0u), "r"(sfa | ((uint32_t)q << 30)), "r"(sfb | ((uint32_t)q << 30))
+                : "memory");
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+                "l"(da + 2u * q), "l"(db + 2u * q), "r"(idesc), "r"(q > 0 ? 1u : 0u)
+                : "memory");
+          }
         }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                      ::"r"(smem_u32(&empty[s])) : "memory");
@@ -564,9 +592,48 @@ __global__ void __launch_bounds__(NT, 1) gemm_f8_kernel(const __grid_constant__ 
     auto block_scale = [&](int kb, int h) -> float {
       const int c = 32 * h + lane, t = m0 + c0 + c;
       if (c >= nc || t >= a.M) return 0.f;
-      const float bs = reinterpret_cast<const float*>(a.b_s)[(long long)(n0 / 128) * KS + kb];
+      const float bs = F4 ? 1.f : reinterpret_cast<const float*>(a.b_s)[(long long)(n0 / 128) * KS + kb];
       return a.a_s ? a.a_s[(long long)t * KS + kb] * bs : bs;
     };
+    // FP4: warps 2-5 (one per lane quadrant) keep the A scale factors in tensor memory. Word c of
+    // lane l holds the four 32-K group scales of tile row 32 c + l for one 128-K block; every
+    // quadrant holds the same words.
+    const bool sf_warp = F4 && half == 0;
+    const uint32_t tsf = tmem + ((uint32_t)(32 * qd) << 16);
+    auto sf_words = [&](int j, uint32_t (&w)[4]) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int r = n0 + 32 * c + lane;
+        w[c] = r < a.N ? *reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(a.b_s) +
+                                                            (long long)r * (a.K / 32) + 4 * (kb0 + j))
+                       : 0x7F7F7F7Fu;
+      }
+    };
+    auto sf_store = [&](int j, const uint32_t (&w)[4]) -> bool {
+      const int s = j % a.RS;
+      // the slot's previous stage must be done with its scale factors
+      if (j >= a.RS && !wait(&empty[s], ((j / a.RS) - 1) & 1)) return false;
+      asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(tsf + F4_SFA + 4u * (uint32_t)s),
+                   "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                   : "memory");
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sfr[s]);
+      return true;
+    };
+    uint32_t swn[4] = {0u, 0u, 0u, 0u};
+    if (sf_warp) {
+      asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(tsf + F4_SFB),
+                   "r"(0x7F7F7F7Fu), "r"(0x7F7F7F7Fu), "r"(0x7F7F7F7Fu), "r"(0x7F7F7F7Fu)
+                   : "memory");
+      for (int j = 0; j < F4_LOOK && j < nk; ++j) {
+        uint32_t w[4];
+        sf_words(j, w);
+        sf_store(j, w);
+      }
+      if (F4_LOOK < nk) sf_words(F4_LOOK, swn);
+    }
     float sn0 = 0.f, sn1 = 0.f;
     if (nk > 0) {
       sn0 = block_scale(kb0, 0);
@@ -575,6 +642,13 @@ __global__ void __launch_bounds__(NT, 1) gemm_f8_kernel(const __grid_constant__ 
     bool ok = true;
     for (int i = 0; i < nk; ++i) {
       const int ac = i % F8ACC;
+      if (sf_warp && i + F4_LOOK < nk) {
+        if (!sf_store(i + F4_LOOK, swn)) {
+          ok = false;
+          break;
+        }
+        if (i + F4_LOOK + 1 < nk) sf_words(i + F4_LOOK + 1, swn);
+      }
       const float s0 = sn0, s1 = sn1;
       if (i + 1 < nk) {
         sn0 = block_scale(kb0 + i + 1, 0);
@@ -672,7 +746,7 @@ struct DevState {
   float* part = nullptr;
   unsigned* cnt = nullptr;
   bool attr[2][3] = {{false, false, false}, {false, false, false}};
-  bool attr_f8 = false;
+  bool attr_f8[2] = {false, false};
 };
 DevState g_dev[64];
 
@@ -741,8 +815,10 @@ int launch_gemm(int fmt, const void* x, int a_dtype, const float* a_s, long long
   a.M = (int)M;
   a.N = (int)N;
   a.K = (int)K;
-  const bool f8 = fmt == DSMOE_FMT_FP8 && a_dtype == DSMOE_DTYPE_E4M3;  // no conversion: gemm_f8_kernel
-  a.TT = M <= 16 ? 16 : M <= 32 ? 32 : (M <= 192 || !f8) ? TTMAX : F8TTMAX;
+  // e4m3 activations need no conversion: gemm_f8_kernel (FP4 scale words are read 4 bytes at a time)
+  const bool f8 = a_dtype == DSMOE_DTYPE_E4M3 && (fmt == DSMOE_FMT_FP8 || ((uintptr_t)b_s & 3) == 0);
+  const bool f4n = f8 && fmt == DSMOE_FMT_FP4;
+  a.TT = M <= 16 ? 16 : M <= 32 ? 32 : (M <= 192 || !f8 || f4n) ? TTMAX : F8TTMAX;
   a.tiles_n = (int)((N + TM - 1) / TM);
   const long long tiles = (long long)a.tiles_n * ((M + a.TT - 1) / a.TT);
   DSMOE_REQUIRE(tiles < (1LL << 31), DSMOE_ERR_ARG, "gemm: too many tiles");
@@ -778,19 +854,24 @@ int launch_gemm(int fmt, const void* x, int a_dtype, const float* a_s, long long
     a.w_bytes = TM * 128;
     a.a_bytes = a.TT * 128;
     const size_t rb = (size_t)a.w_bytes + a.a_bytes;
-    const int RS = (int)std::min<size_t>(F8MAXRS, ((size_t)d.optin - 1024 - 256) / rb);
-    DSMOE_REQUIRE(RS >= 2, DSMOE_ERR_UNSUPPORTED, "gemm: shared memory for %d stages only", RS);
+    const int RS = (int)std::min<size_t>(F8MAXRS, ((size_t)d.optin - 1024 - 512) / rb);
+    DSMOE_REQUIRE(RS > F4_LOOK, DSMOE_ERR_UNSUPPORTED, "gemm: shared memory for %d stages only", RS);
     a.RS = RS;
-    rc = encode2d(&a.tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, K, N, K, 128, TM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (f4n)  // packed e2m1: K 4-bit elements per row, K / 2 bytes apart; widened by the TMA
+      rc = encode2d(&a.tw, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, b, K, N, K / 2, 128, TM, CU_TENSOR_MAP_SWIZZLE_128B);
+    else
+      rc = encode2d(&a.tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, K, N, K, 128, TM, CU_TENSOR_MAP_SWIZZLE_128B);
     if (!rc) rc = encode2d(&a.ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, x, K, M, K, 128, a.TT, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    const size_t smem = 1024 + (size_t)RS * rb + 256;
-    if (!d.attr_f8) {
-      if (cudaFuncSetAttribute(gemm_f8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, d.optin) != cudaSuccess)
+    const size_t smem = 1024 + (size_t)RS * rb + 512;
+    if (!d.attr_f8[f4n]) {
+      if (cudaFuncSetAttribute(f4n ? gemm_f8_kernel<true> : gemm_f8_kernel<false>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, d.optin) != cudaSuccess)
         return cuda_status("gemm: set smem");
-      d.attr_f8 = true;
+      d.attr_f8[f4n] = true;
     }
-    gemm_f8_kernel<<<a.tiles * S, NT, smem, st>>>(a);
+    if (f4n) gemm_f8_kernel<true><<<a.tiles * S, NT, smem, st>>>(a);
+    else gemm_f8_kernel<false><<<a.tiles * S, NT, smem, st>>>(a);
     return cuda_status("gemm");
   }
   a.w_bytes = fmt == DSMOE_FMT_FP8 ? TM * 128 : TM * 64;

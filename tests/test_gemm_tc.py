@@ -97,12 +97,13 @@ def test_gemm_dtypes(dev, fmt, adt, scaled, out_f32):
     _run(dev, fmt, adt, 9, 256, 512, scaled, out_f32, seed=seed)
 
 
+@pytest.mark.parametrize("fmt", ["fp8", "fp4"])
 @pytest.mark.parametrize("M,N,K", [(1, 384, 640), (20, 384, 640), (40, 256, 512), (65, 384, 640), (100, 1000, 384),
                                    (300, 1000, 384), (600, 7680, 256)])
-def test_gemm_fp8_e4m3_tiles(dev, M, N, K):
-    """FP8 weights x e4m3 activations (the no-conversion kernel): 16 / 32 / 64 / 128 tokens per tile,
-    split and unsplit K, ragged M and N."""
-    _run(dev, "fp8", "e4m3", M, N, K, True, False, seed=M + N + K)
+def test_gemm_e4m3_tiles(dev, fmt, M, N, K):
+    """FP8 / FP4 weights x e4m3 activations (the no-conversion kernel; FP4 through the block-scaled
+    MMA): 16 / 32 / 64 / 128 tokens per tile, split and unsplit K, ragged M and N."""
+    _run(dev, fmt, "e4m3", M, N, K, True, False, seed=M + N + K + (fmt == "fp4"))
 
 
 @pytest.mark.parametrize("fmt", ["fp8", "fp4"])
