@@ -206,8 +206,8 @@ class ClockSampler:
 
     A background ``nvidia-smi -lms 200`` runs across the region; rows whose timestamp falls inside
     [first step, last step] are kept. Timed regions are often shorter than the 200 ms period, so
-    ``mark()`` -- called between two timed steps, outside every step's events -- also takes one
-    synchronous sample, which is inside the region by construction."""
+    ``mark()`` -- called right after the timed steps are queued, while the GPU runs them -- also
+    takes one sample, which is inside the region by construction."""
     Q = ("index,uuid,timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -235,6 +235,26 @@ class ClockSampler:
         return self
 
     def mark(self):
+        """One sample now. NVML in-process (tens of microseconds, so it can be taken while queued
+        steps run); nvidia-smi when NVML is unavailable. Reads only."""
+        try:
+            import datetime
+            import pynvml as N
+            N.nvmlInit()
+            h = N.nvmlDeviceGetHandleByUUID(self.uuid) if self.uuid else N.nvmlDeviceGetHandleByIndex(0)
+            sm = N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
+            smax = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+            pw = N.nvmlDeviceGetPowerUsage(h) / 1000.0
+            r = N.nvmlDeviceGetCurrentClocksEventReasons(h)
+            act = lambda bit: "Active" if r & bit else "Not Active"
+            ts = datetime.datetime.now().strftime("%Y/%m/%d %H:%M:%S.%f")
+            self.marks.append(", ".join([
+                "0", self.uuid or "", ts, str(sm), str(smax), f"{pw:.2f}", hex(r),
+                act(N.nvmlClocksEventReasonHwSlowdown), act(N.nvmlClocksEventReasonHwThermalSlowdown),
+                act(N.nvmlClocksEventReasonSwThermalSlowdown), act(N.nvmlClocksEventReasonSwPowerCap)]))
+            return
+        except Exception:
+            pass
         try:
             out = subprocess.run(self._cmd(False), capture_output=True, text=True, timeout=10).stdout
             self.marks += [ln for ln in out.splitlines() if ln.strip()]
@@ -281,7 +301,7 @@ class ClockSampler:
         reasons = sorted({n for r in rows for n, v in zip(names, r[7:11]) if v.lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(rows[0][4]),
                 "reasons": reasons, "samples": len(rows), "in_region": "timestamped background samples inside "
-                "the timed region plus one synchronous sample between two timed steps"}
+                "the timed region plus one in-process NVML sample taken while the queued timed steps run"}
 
 
 def _oracle_expert(ew):
@@ -460,9 +480,11 @@ def ours(args):
     gev =[[torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_layers + 1)] for _ in range(NV)]
     pev = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)] for _ in range(NV)]
     graphs, pgraphs = None, None
-    timing_mode = ("cuda-graph replay per step: the step time from graphs with timestamp nodes at their ends only, "
-                   "so consecutive layer kernels overlap (programmatic dependent launch); the per-layer split "
-                   "from a second pass of graphs with timestamp nodes between the layers")
+    timing_mode = ("cuda-graph replay: the K timed steps (every layer of each, token variants in step order) "
+                   "captured as one graph and replayed once between two CUDA events (barrier + synchronize "
+                   "before, synchronize after), so consecutive layer kernels overlap (programmatic dependent "
+                   "launch); the per-layer split from a second pass of per-step graphs with timestamp nodes "
+                   "between the layers, synchronized per step")
     try:
         graphs = [torch.cuda.CUDAGraph() for _ in range(NV)]
         pgraphs = [torch.cuda.CUDAGraph() for _ in range(NV)]
@@ -527,17 +549,52 @@ def ours(args):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(uuid) as clk:
-        for s in range(W, W + K):
-            if s == W + K // 2:  # between two steps: outside every timed event pair
-                if rank == 0:
-                    clk.mark()
-                if world > 1:  # the ranks' kernels exchange tiles: all of them resume together
-                    dist.barrier()
-                    torch.cuda.synchronize()
-            step(s, True)
         torch.cuda.synchronize()
+        dist.barrier()  # the barrier's own work has completed on every rank before the first step
+    torch.cuda.synchronize()
+    # The K timed steps run back to back (no host synchronisation between them), bracketed by a
+    # barrier and a synchronize: at N > 1 the ranks then run in lockstep through the in-kernel
+    # exchange, and a host-side delay on one rank is not charged to every step.
+    # With graphs, the K steps (their token variants in step order) are one graph, as a decode loop
+    # replays one graph per token: no launch gap between steps.
+    kgraph = None
+    if graphs is not None:
+        try:
+            kgraph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(kgraph):
+                for s in range(W, W + K):
+                    for li in range(n_layers):
+                        layer_launch(li, s % NV)
+            torch.cuda.synchronize()
+        except Exception:  # pragma: no cover - depends on the driver
+            kgraph = None
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+            torch.cuda.synchronize()
+            dist.barrier()
+        torch.cuda.synchronize()
+    t_beg, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(uuid) as clk:
+        t_beg.record(stream)
+        if kgraph is not None:
+            kgraph.replay()
+        else:
+            for s in range(W, W + K):
+                v = s % NV
+                if graphs is not None:
+                    pgraphs[v].replay()
+                else:
+                    for li in range(n_layers):
+                        layer_launch(li, v)
+        t_end.record(stream)
+        if rank == 0:
+            clk.mark()  # while the queued steps run
+        torch.cuda.synchronize()
+    step_t = [t_beg.elapsed_time(t_end) / K] * K
+    for s in range(W, W + K):  # every replay of a token variant routes the same way
+        for li in range(n_layers):
+            idx_log[s, li].copy_(idx_st[li][s % NV])
     if graphs is not None:  # second pass: the per-layer split (timestamp nodes between the layers)
         for s in range(W):
             step(s, False, split=True)
@@ -548,7 +605,7 @@ def ours(args):
     torch.cuda.synchronize()
     for m in layers:
         m.check(B)
-    graphs = pgraphs = None  # released before the process group goes away
+    graphs = pgraphs = kgraph = None  # released before the process group goes away
 
     # ---- per-step and per-layer device times
     step_ms = step_t
@@ -629,23 +686,34 @@ def ours(args):
     e2e_eager = e2e_time(e2e_step)
     # traced: dsmoe.DecodeTrace (the reference's traced decode step); the step's host tokens are
     # copied into the trace's pinned input, and the graph copies them in and every output out
+    # Every rank takes the same collective steps: the trace is timed only if every rank built it,
+    # and its verdict is agreed before it is used (the replays and the eager check run the exchange).
     e2e_traced, trace_err = None, None
     if B <= 8 and (world == 1 or comm is not None):
         tr = None
         try:
             tr = dsmoe.DecodeTrace(layers, B)
-            xv = xh.view(NV, n_layers, B, H)
-            e2e_traced = e2e_time(lambda s: tr.step(xv[s % NV]))
-            tr.check()
-            for li in range(n_layers):  # the trace's last step equals the eager forward on its tokens
-                y_e = layers[li].forward(xv[(W + K - 1) % NV, li].to(dev))
-                if not torch.equal(tr.y_host[li], y_e.cpu()):
-                    trace_err = f"layer {li}: traced output differs from MoE.forward"
         except Exception as ex:  # reported in the line; the eager figure stands
             trace_err = repr(ex)[:200]
-        finally:
-            if tr is not None:
-                tr.release()
+        if max_over_ranks(1.0 if tr is None else 0.0, dev) == 0.0:
+            xv = xh.view(NV, n_layers, B, H)
+            e2e_traced = e2e_time(lambda s: tr.step(xv[s % NV]))
+            bad = 0.0
+            try:
+                tr.check()
+            except L.DsmoeError as ex:
+                trace_err, bad = repr(ex)[:200], 1.0
+            # the trace's last step equals the eager forward on its tokens (every layer on every rank)
+            same = [torch.equal(tr.y_host[li], layers[li].forward(xv[(W + K - 1) % NV, li].to(dev)).cpu())
+                    for li in range(n_layers)]
+            if not all(same):
+                trace_err, bad = "traced output differs from MoE.forward", 1.0
+            if max_over_ranks(bad, dev) != 0.0:
+                trace_err = trace_err or "the trace failed on another rank"
+        elif trace_err is None:
+            trace_err = "the trace could not be built on another rank"
+        if tr is not None:
+            tr.release()
     if trace_err is not None:
         e2e_traced = None
     e2e_val = e2e_traced if e2e_traced is not None else e2e_eager
