@@ -90,3 +90,33 @@ def test_slot_plan_rule_restated():
         counts = np.bincount(idx.ravel(), minlength=384)
         slots = int(np.sum((counts + 7) // 8)) + (B + 7) // 8
         assert slots <= B * 6 + (B + 7) // 8
+
+
+class _FakeLayer:
+    """Just the attributes DecodeTrace checks before it touches a GPU."""
+
+    def __init__(self, hidden=1024, world=1, comm=None, max_tokens=64, device="cuda:0"):
+        self.hidden, self.world, self.comm, self.max_tokens, self.device = hidden, world, comm, max_tokens, device
+
+
+def test_decode_trace_rejects_bad_layer_sets():
+    from dsmoe import DecodeTrace
+    with pytest.raises(ValueError):
+        DecodeTrace([], 1)
+    with pytest.raises(ValueError):  # one trace, one hidden size
+        DecodeTrace([_FakeLayer(1024), _FakeLayer(2048)], 1)
+    with pytest.raises(ValueError):  # one trace, one GPU
+        DecodeTrace([_FakeLayer(device="cuda:0"), _FakeLayer(device="cuda:1")], 1)
+    for bad in (0, 65):
+        with pytest.raises(ValueError):
+            DecodeTrace([_FakeLayer()], bad)
+    with pytest.raises(ValueError):  # world > 1: the all-reduce must run inside the decode kernel
+        DecodeTrace([_FakeLayer(world=2)], 1)
+    with pytest.raises(ValueError):  # ... which takes at most 8 tokens
+        DecodeTrace([_FakeLayer(world=2, comm=object())], 9)
+
+
+def test_copy_async_rejects_null_arguments():
+    from dsmoe import _lib as L
+    assert L.lib.dsmoe_copy_async(None, None, 16, None) == L.ERR_ARG
+    assert L.lib.dsmoe_copy_async(None, None, -1, None) == L.ERR_ARG
