@@ -6,9 +6,12 @@
 // imports them by name for every quantized linear); the MoE hot path itself runs on the resident
 // stores.
 //
-// One CTA computes a tile of 128 weight rows x TT tokens (TT = 16..64) over a range of 128-K blocks
-// on the 5th-generation tensor cores (tcgen05.mma kind::f16, bf16 operands, fp32 accumulator in
-// tensor memory):
+// Two kernels, both on the 5th-generation tensor cores with fp32 accumulators in tensor memory:
+// gemm_f8_kernel takes e4m3 activations (act_quant's output) and multiplies the codes as they are
+// (further down); gemm_tc_kernel takes fp32 or bf16 activations and converts. In both, one CTA
+// computes a tile of 128 weight rows x TT tokens over a range of 128-K blocks.
+//
+// gemm_tc_kernel (TT = 16, 32 or 64; tcgen05.mma kind::f16, bf16 operands):
 //   warp 0      TMA producer: per 128-K block, one tiled load of the raw weight tile (e4m3 bytes, or
 //               packed e2m1 bytes) and one of the raw activation tile (fp32 / bf16 / e4m3), rows past
 //               N or M read as zero; a ring of RS stages.
