@@ -26,8 +26,9 @@
 //   warps 2-9   epilogue: tcgen05.ld of the accumulator (two warps per 32-lane quadrant, splitting
 //               the tokens), hi column + lo column, coalesced stores of out[token][row].
 // Few tiles (small M): the K blocks are split over S CTAs per tile; each writes its fp32 partial to a
-// per-device workspace and the last to arrive on the tile's counter sums the S partials in split
-// order (deterministic) and writes the tile.
+// static device array and the last to arrive on the tile's counter sums the S partials in split
+// order (deterministic), writes the tile and resets the counter. Calls on one device must therefore
+// be ordered (one stream).
 // Every wait is bounded; a CTA whose wait expired writes NaN into its share of the output.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -46,7 +47,7 @@ constexpr int TTMAX = 64;               // tokens per tile (MMA N)
 constexpr int CS = 2;                   // converted stages
 constexpr int A_BYTES = TM * 128 * 2;   // bf16 weights of one 128-K block: two 64-K SW128 atoms
 constexpr int MAXRS = 4;                // raw stages
-constexpr int MAXSLOT = 160;            // split-K partial tiles in the workspace
+constexpr int MAXSLOT = 160;            // split-K partial tiles (static device array)
 constexpr int F8TTMAX = 128;            // tokens per tile of the FP8 x e4m3 kernel
 constexpr int PART = TM * F8TTMAX;      // floats per partial tile ([col][row])
 constexpr uint64_t kWaitNs = 1000000000ull;
@@ -741,6 +742,11 @@ __global__ void __launch_bounds__(NT, 1) gemm_f8_kernel(const __grid_constant__ 
   }
 }
 
+// Split-K partial tiles and per-tile arrival counters: static device arrays (10.5 MB, zero at module
+// load; the last CTA of a tile resets its counter), so no call allocates.
+__device__ float g_split_part[MAXSLOT * PART];
+__device__ unsigned g_split_cnt[MAXSLOT];
+
 // ------------------------------------------------------------------ host side
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::mutex g_mu;
@@ -827,23 +833,26 @@ int launch_gemm(int fmt, const void* x, int a_dtype, const float* a_s, long long
   DSMOE_REQUIRE(tiles < (1LL << 31), DSMOE_ERR_ARG, "gemm: too many tiles");
   a.tiles = (int)tiles;
   a.nkb = (int)(K / 128);
-  // split K over CTAs while the tiles alone leave SMs idle (partials in a per-device workspace)
+  // split K over CTAs while the tiles alone leave SMs idle (partials in the static device array)
   int S = 1;
   if (tiles < d.sms) S = (int)std::max<long long>(1, std::min<long long>(std::min<long long>(a.nkb, d.sms / tiles), MAXSLOT / tiles));
   if (S > 1 && !d.part) {
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     cudaStreamIsCapturing(st, &cap);
     if (cap == cudaStreamCaptureStatusNone) {
-      // allocated once per device (first uncaptured call that splits), kept for the process
-      if (cudaMalloc(&d.part, (size_t)MAXSLOT * PART * 4 + MAXSLOT * 4) != cudaSuccess) {
-        d.part = nullptr;
-        return cuda_status("gemm: workspace");
+      // the static partials and counters of this device (nothing is allocated); looked up once
+      void* p = nullptr;
+      void* c = nullptr;
+      if (cudaGetSymbolAddress(&p, g_split_part) != cudaSuccess || cudaGetSymbolAddress(&c, g_split_cnt) != cudaSuccess) {
+        cudaGetLastError();
+        p = c = nullptr;
       }
-      d.cnt = reinterpret_cast<unsigned*>(d.part + (size_t)MAXSLOT * PART);
-      if (cudaMemset(d.cnt, 0, MAXSLOT * 4) != cudaSuccess) return cuda_status("gemm: workspace");
+      d.part = static_cast<float*>(p);
+      d.cnt = static_cast<unsigned*>(c);
+      if (!d.part || !d.cnt) d.part = nullptr, d.cnt = nullptr;
     }
   }
-  if (!d.part) S = 1;  // first call inside a graph capture: no workspace yet, no split
+  if (!d.part) S = 1;  // first call inside a graph capture: address not looked up yet, no split
   a.S = S;
   a.part = d.part;
   a.cnt = d.cnt;
