@@ -496,6 +496,9 @@ __global__ void __launch_bounds__(NT, 1) gemm_f8_kernel(const __grid_constant__ 
   // FP8: 64, 128, 256 or 512 accumulator columns; FP4 (TT <= 64): accumulators in [0, 256), scale
   // factors from column 320
   const uint32_t ncols = F4 ? 512u : (uint32_t)(F8ACC * TT);
+  // accumulators in the ring: four, or two of 128 columns for FP4 at 128 tokens (the scale factors
+  // sit from column 320)
+  const int nacc = (F4 && TT > 64) ? 2 : F8ACC;
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
                  "r"(ncols)
@@ -541,10 +544,10 @@ __global__ void __launch_bounds__(NT, 1) gemm_f8_kernel(const __grid_constant__ 
                                 : (1u << 4) | ((uint32_t)(TT >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
       const uint64_t d0 = desc_sw128(smem_u32(base));
       for (int i = 0; i < nk; ++i) {
-        const int s = i % a.RS, ac = i % F8ACC;
+        const int s = i % a.RS, ac = i % nacc;
         if (!wait(&full[s], (i / a.RS) & 1)) break;
         if (F4 && !wait(&sfr[s], (i / a.RS) & 1)) break;
-        if (i >= F8ACC && !wait(&acce[ac], ((i / F8ACC) - 1) & 1)) break;
+        if (i >= nacc && !wait(&acce[ac], ((i / nacc) - 1) & 1)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint64_t da = d0 + (uint64_t)((s * RB) >> 4), db = da + (uint64_t)(a.w_bytes >> 4);
         const uint32_t d = tmem + (uint32_t)(ac * TT);
@@ -645,7 +648,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_f8_kernel(const __grid_constant__ 
     }
     bool ok = true;
     for (int i = 0; i < nk; ++i) {
-      const int ac = i % F8ACC;
+      const int ac = i % nacc;
       if (sf_warp && i + F4_LOOK < nk) {
         if (!sf_store(i + F4_LOOK, swn)) {
           ok = false;
@@ -658,7 +661,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_f8_kernel(const __grid_constant__ 
         sn0 = block_scale(kb0 + i + 1, 0);
         sn1 = block_scale(kb0 + i + 1, 1);
       }
-      if (!wait(&accf[ac], (i / F8ACC) & 1)) {
+      if (!wait(&accf[ac], (i / nacc) & 1)) {
         ok = false;
         break;
       }
@@ -827,7 +830,7 @@ int launch_gemm(int fmt, const void* x, int a_dtype, const float* a_s, long long
   // e4m3 activations need no conversion: gemm_f8_kernel (FP4 scale words are read 4 bytes at a time)
   const bool f8 = a_dtype == DSMOE_DTYPE_E4M3 && (fmt == DSMOE_FMT_FP8 || ((uintptr_t)b_s & 3) == 0);
   const bool f4n = f8 && fmt == DSMOE_FMT_FP4;
-  a.TT = M <= 16 ? 16 : M <= 32 ? 32 : (M <= 192 || !f8 || f4n) ? TTMAX : F8TTMAX;
+  a.TT = M <= 16 ? 16 : M <= 32 ? 32 : (M <= 192 || !f8) ? TTMAX : F8TTMAX;
   a.tiles_n = (int)((N + TM - 1) / TM);
   const long long tiles = (long long)a.tiles_n * ((M + a.TT - 1) / a.TT);
   DSMOE_REQUIRE(tiles < (1LL << 31), DSMOE_ERR_ARG, "gemm: too many tiles");
